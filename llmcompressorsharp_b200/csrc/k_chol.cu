@@ -1,0 +1,292 @@
+// Damped Cholesky inverse and the GPTQ upper factor.
+//
+// Reference: HessianInverseSolver.Compute (src/LLMCompressorSharp.TorchExtensions/Hessian/
+// HessianInverseSolver.cs:44-92) and the factor U = chol(Hinv)^T of GptqBlockQuantizer.cs:105-118.
+//
+// Recursive blocked factorisation that produces L and L^-1 together:
+//   chol_inv([[A11, .], [A21, A22]]):
+//     (L11, L11^-1) = chol_inv(A11)
+//     L21   = A21 L11^-T                       (GEMM, triangular operand)
+//     A22  -= L21 L21^T                        (GEMM, lower output only)
+//     (L22, L22^-1) = chol_inv(A22)
+//     (L^-1)21 = -L22^-1 (L21 L11^-1)          (two GEMMs)
+// with a one-CTA shared-memory kernel for blocks of <= 64.  All O(d^3) work is GEMM.
+//
+// U directly: with P the index-reversal permutation and L' = chol(P H' P), the matrix
+// U = P L'^-1 P is upper triangular and U^T U = H'^-1, i.e. U is exactly the upper
+// Cholesky factor of H'^-1 that GptqBlockQuantizer computes through Hinv.  One
+// factorisation + inverse replaces the reference's four O(d^3) steps.
+#include "ops.h"
+
+namespace llmc {
+namespace {
+
+constexpr int NB = 64;
+
+__global__ void diag_lambda_kernel(const float* H, int64_t d, int64_t ldh, float damp, float* lam) {
+    // mean(diag H) read back as a float, times the damping fraction as C# float math
+    // (HessianInverseSolver.cs:64-65).  The sum is taken in double, then rounded.
+    __shared__ double part[256];
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) s += (double)H[i * ldh + i];
+    part[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if ((int)threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const float mean = (float)(part[0] / (double)d);
+        lam[0] = damp > 0.f ? __fmul_rn(damp, mean) : 0.f;
+    }
+}
+
+// A[i][j] = H'[p(i)][p(j)] for i >= j, 0 above the diagonal; p flips when `flip`.
+__global__ void prep_kernel(const float* H, int64_t d, int64_t ldh, int upper_only, int flip, const float* lam,
+                            float* A, int64_t lda) {
+    const int64_t total = d * d;
+    const float l = lam[0];
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / d, j = t % d;
+        float v = 0.f;
+        if (i >= j) {
+            int64_t pi = flip ? d - 1 - i : i, pj = flip ? d - 1 - j : j;
+            if (upper_only && pi > pj) {
+                int64_t tmp = pi;
+                pi = pj;
+                pj = tmp;
+            }
+            v = H[pi * ldh + pj];
+            if (i == j) v = __fadd_rn(v, l);
+        }
+        A[i * lda + j] = v;
+    }
+}
+
+// Cholesky + triangular inverse of one n x n (n <= NB) diagonal block in shared memory.
+// A's lower triangle is read; L (zeros above) goes back to A and L^-1 to I.  A pivot that
+// is not > 0 (or NaN) raises flags[0] and the block continues with a unit pivot, so the
+// kernel always terminates; the host reports the failure.
+__global__ void __launch_bounds__(256) chol_inv_base_kernel(float* A, float* I, int64_t ld, int n, int* flags) {
+    __shared__ float sL[NB][NB + 1];
+    __shared__ float sX[NB][NB + 1];
+    const int tid = threadIdx.x;
+    for (int t = tid; t < n * n; t += blockDim.x) {
+        const int i = t / n, j = t % n;
+        sL[i][j] = (j <= i) ? A[i * ld + j] : 0.f;
+        sX[i][j] = 0.f;
+    }
+    __syncthreads();
+    for (int k = 0; k < n; k++) {
+        __shared__ float piv;
+        if (tid == 0) {
+            float p = sL[k][k];
+            if (!(p > 0.f)) {
+                atomicOr(flags, 1);
+                p = 1.f;
+            }
+            piv = __fsqrt_rn(p);
+            sL[k][k] = piv;
+        }
+        __syncthreads();
+        for (int i = k + 1 + tid; i < n; i += blockDim.x) sL[i][k] = __fdiv_rn(sL[i][k], piv);
+        __syncthreads();
+        const int r = n - k - 1;  // trailing size
+        for (int t = tid; t < r * r; t += blockDim.x) {
+            const int i = k + 1 + t / r, j = k + 1 + t % r;
+            if (j <= i) sL[i][j] = fmaf(-sL[i][k], sL[j][k], sL[i][j]);
+        }
+        __syncthreads();
+    }
+    // X = L^-1 row by row: X[i][j] = (delta_ij - sum_{k=j}^{i-1} L[i][k] X[k][j]) / L[i][i].
+    for (int i = 0; i < n; i++) {
+        for (int j = tid; j <= i; j += blockDim.x) {
+            float s = (i == j) ? 1.f : 0.f;
+            for (int k = j; k < i; k++) s = fmaf(-sL[i][k], sX[k][j], s);
+            sX[i][j] = __fdiv_rn(s, sL[i][i]);
+        }
+        __syncthreads();
+    }
+    for (int t = tid; t < n * n; t += blockDim.x) {
+        const int i = t / n, j = t % n;
+        A[i * ld + j] = sL[i][j];
+        I[i * ld + j] = sX[i][j];
+    }
+}
+
+// out[i][j] = src[d-1-i][d-1-j] (flip) or src[j][i] (transpose); src lower -> out upper.
+__global__ void remap_kernel(const float* src, int64_t d, int64_t lds, int mode, float* out, int64_t ldo) {
+    const int64_t total = d * d;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / d, j = t % d;
+        float v;
+        if (mode == 0) v = src[(d - 1 - i) * lds + (d - 1 - j)];
+        else v = (j >= i) ? src[j * lds + i] : 0.f;
+        out[i * ldo + j] = v;
+    }
+}
+
+__global__ void copy2d_kernel(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd) {
+    const int64_t total = rows * cols;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / cols, j = t % cols;
+        dst[i * ldd + j] = src[i * lds + j];
+    }
+}
+
+// flags[1] = 1 when any element of the (symmetric) input is nonzero.
+__global__ void nonzero_kernel(const float* H, int64_t d, int64_t ldh, int* flags) {
+    const int64_t total = d * d;
+    int any = 0;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / d, j = t % d;
+        if (H[i * ldh + j] != 0.f) any = 1;
+    }
+    if (__syncthreads_or(any) && threadIdx.x == 0) atomicOr(flags + 1, 1);
+}
+
+int grid_for(llmc_ctx* ctx, int64_t items) {
+    int64_t b = (items + 255) / 256;
+    int64_t cap = (int64_t)ctx->sm_count * 8;
+    return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+struct CholWs {
+    float* A;
+    float* I;
+    float* tmp;  // n2 x n1 scratch when L must be kept
+    int64_t ld;
+};
+
+llmc_status rec(llmc_ctx* ctx, const CholWs& w, int64_t off, int64_t n, int keep_L) {
+    float* A = w.A + off * w.ld + off;
+    float* I = w.I + off * w.ld + off;
+    if (n <= NB) {
+        chol_inv_base_kernel<<<1, 256, 0, ctx->stream>>>(A, I, w.ld, (int)n, ctx->dflags);
+        return check_launch(ctx, "chol_inv_base");
+    }
+    int64_t n1 = ((n / 2 + NB - 1) / NB) * NB;
+    if (n1 >= n) n1 = n - NB;
+    const int64_t n2 = n - n1;
+    float* A21 = A + n1 * w.ld;
+    float* I11 = I;
+    float* I21 = I + n1 * w.ld;
+    float* I22 = I21 + n1;
+
+    LLMC_TRY(rec(ctx, w, off, n1, keep_L));
+    GemmArgs g{};
+    // L21 = A21 L11^-T  -> held in I21 (free until the end of this frame)
+    g = GemmArgs{n2, n1, n1, A21, w.ld, 0, LLMC_DTYPE_F32, I11, w.ld, 1, LLMC_DTYPE_F32, I21, w.ld, 1.f, 0.f};
+    g.b_tri = TRI_KLE;
+    LLMC_TRY(gemm_f32(ctx, g));
+    // A22 -= L21 L21^T (lower triangle)
+    g = GemmArgs{n2, n2, n1, I21, w.ld, 0, LLMC_DTYPE_F32, I21, w.ld, 1, LLMC_DTYPE_F32, A21 + n1, w.ld, -1.f, 1.f};
+    g.c_mode = 1;
+    LLMC_TRY(gemm_f32(ctx, g));
+    float* T = A21;  // A21 is dead once L21 lives in I21 ...
+    if (keep_L) {    // ... unless the caller wants L back, then A21 <- L21 and T is scratch.
+        copy2d_kernel<<<grid_for(ctx, n2 * n1), 256, 0, ctx->stream>>>(I21, n2, n1, w.ld, A21, w.ld);
+        LLMC_TRY(check_launch(ctx, "copy2d"));
+        T = w.tmp;
+    }
+    LLMC_TRY(rec(ctx, w, off + n1, n2, keep_L));
+    const int64_t ldt = keep_L ? n1 : w.ld;
+    // T = L21 L11^-1
+    g = GemmArgs{n2, n1, n1, I21, w.ld, 0, LLMC_DTYPE_F32, I11, w.ld, 0, LLMC_DTYPE_F32, T, ldt, 1.f, 0.f};
+    g.b_tri = TRI_KGE;
+    LLMC_TRY(gemm_f32(ctx, g));
+    // (L^-1)21 = -L22^-1 T
+    g = GemmArgs{n2, n1, n2, I22, w.ld, 0, LLMC_DTYPE_F32, T, ldt, 0, LLMC_DTYPE_F32, I21, w.ld, -1.f, 0.f};
+    g.a_tri = TRI_KLE;
+    return gemm_f32(ctx, g);
+}
+
+llmc_status read_flags(llmc_ctx* ctx, int* f0, int* f1) {
+    LLMC_CUDA_TRY(cudaMemcpyAsync(ctx->hflags, ctx->dflags, 2 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    *f0 = ctx->hflags[0];
+    *f1 = ctx->hflags[1];
+    return LLMC_OK;
+}
+
+// Factor the prepared lower matrix in w.A; on a non-positive pivot decide between the
+// all-zero case (pinv(0) = 0) and a genuine failure.
+llmc_status factor(llmc_ctx* ctx, const CholWs& w, int64_t d, int keep_L, int* not_pd, int* all_zero) {
+    LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags, 0, 2 * sizeof(int), ctx->stream));
+    LLMC_CUDA_TRY(cudaMemsetAsync(w.I, 0, (size_t)d * w.ld * sizeof(float), ctx->stream));
+    LLMC_TRY(rec(ctx, w, 0, d, keep_L));
+    int f0, f1;
+    LLMC_TRY(read_flags(ctx, &f0, &f1));
+    *not_pd = f0 != 0;
+    *all_zero = 0;
+    return LLMC_OK;
+}
+
+}  // namespace
+
+llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, float damp, int upper_only, float* out,
+                         int64_t ldo, int want_upper) {
+    void* wsp;
+    const size_t dd = (size_t)d * d;
+    LLMC_TRY(workspace(ctx, 2 * dd * sizeof(float) + 4096, &wsp));
+    Carver cv{(char*)wsp};
+    CholWs w{cv.take<float>(dd), cv.take<float>(dd), nullptr, d};
+    float* lam = cv.take<float>(4);
+    diag_lambda_kernel<<<1, 256, 0, ctx->stream>>>(H, d, ldh, damp, lam);
+    LLMC_TRY(check_launch(ctx, "diag_lambda"));
+    prep_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(H, d, ldh, upper_only, want_upper ? 1 : 0, lam, w.A, d);
+    LLMC_TRY(check_launch(ctx, "prep"));
+    int not_pd = 0, all_zero = 0;
+    LLMC_TRY(factor(ctx, w, d, 0, &not_pd, &all_zero));
+    if (not_pd) {
+        // HessianInverseSolver.cs:85-91 falls back to pinv(H').  pinv of the zero matrix is
+        // zero (the no-calibration-data case); anything else is reported.
+        LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags, 0, 2 * sizeof(int), ctx->stream));
+        prep_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(H, d, ldh, upper_only, 0, lam, w.A, d);
+        LLMC_TRY(check_launch(ctx, "prep"));
+        nonzero_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.A, d, d, ctx->dflags);
+        LLMC_TRY(check_launch(ctx, "nonzero"));
+        int f0, f1;
+        LLMC_TRY(read_flags(ctx, &f0, &f1));
+        if (f1 == 0) {
+            LLMC_CUDA_TRY(cudaMemset2DAsync(out, ldo * sizeof(float), 0, d * sizeof(float), d, ctx->stream));
+            return LLMC_OK;
+        }
+        return fail(LLMC_ERR_NOT_PD, "damped Hessian (d=%lld) is not positive definite; pseudo-inverse fallback "
+                    "is only available for the all-zero matrix", (long long)d);
+    }
+    if (want_upper) {
+        remap_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.I, d, d, 0, out, ldo);
+        return check_launch(ctx, "remap_flip");
+    }
+    // Hinv = L^-T L^-1 (HessianInverseSolver.cs:83)
+    GemmArgs g{d, d, d, w.I, d, 1, LLMC_DTYPE_F32, w.I, d, 0, LLMC_DTYPE_F32, out, ldo, 1.f, 0.f};
+    g.a_tri = TRI_KGE;
+    g.b_tri = TRI_KGE;
+    return gemm_f32(ctx, g);
+}
+
+llmc_status upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ldh, float* out, int64_t ldo) {
+    void* wsp;
+    const size_t dd = (size_t)d * d;
+    const int64_t half = (d + 1) / 2 + NB;
+    LLMC_TRY(workspace(ctx, (2 * dd + (size_t)half * half) * sizeof(float) + 4096, &wsp));
+    Carver cv{(char*)wsp};
+    CholWs w{cv.take<float>(dd), cv.take<float>(dd), cv.take<float>((size_t)half * half), d};
+    float* lam = cv.take<float>(4);
+    diag_lambda_kernel<<<1, 256, 0, ctx->stream>>>(hinv, d, ldh, 0.f, lam);
+    LLMC_TRY(check_launch(ctx, "diag_lambda"));
+    prep_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(hinv, d, ldh, 0, 0, lam, w.A, d);
+    LLMC_TRY(check_launch(ctx, "prep"));
+    int not_pd = 0, all_zero = 0;
+    LLMC_TRY(factor(ctx, w, d, 1, &not_pd, &all_zero));
+    if (not_pd) {
+        // GptqBlockQuantizer.cs:112-118: fall back to Hinv itself.
+        copy2d_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(hinv, d, d, ldh, out, ldo);
+        return check_launch(ctx, "copy2d");
+    }
+    remap_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.A, d, d, 1, out, ldo);
+    return check_launch(ctx, "remap_transpose");
+}
+
+}  // namespace llmc

@@ -1,0 +1,437 @@
+// Observers, affine parameters, fake quantisation, RTN quantise+pack, int4 packing.
+//
+// Reference: MinMaxObserver.cs:24-45, PerChannelMinMaxObserver.cs:38-76, Observer.cs:47-75,
+// FakeQuantizeFunction.cs:30-47, RtnModifier.cs:44-122, Int4PackedTensor.cs:47-161.
+//
+// These are HBM-bound streams.  A "segment" is the set of elements that share one
+// (scale, zero-point): a whole row (per-channel), a (row, group) slice (group) or a row as
+// the first level of a per-tensor reduction.  A group of L lanes (L a power of two <= 32)
+// owns one segment and walks it with 16-byte vector loads, so a warp covers 32*16 bytes
+// of consecutive columns per step; the segment's min/max is combined with xor shuffles
+// inside the lane group.
+#include "ops.h"
+
+namespace llmc {
+namespace {
+
+constexpr int NT = 256;
+
+template <typename T, int VEC>
+struct Vec {
+    float v[VEC];
+    __device__ __forceinline__ void load(const T* p) {
+        if constexpr (VEC == 1) {
+            v[0] = to_f<T>(p[0]);
+        } else {
+            static_assert(VEC * sizeof(T) == 16, "16-byte vectors");
+            uint4 q = *reinterpret_cast<const uint4*>(p);
+            const T* h = reinterpret_cast<const T*>(&q);
+#pragma unroll
+            for (int i = 0; i < VEC; i++) v[i] = to_f<T>(h[i]);
+        }
+    }
+};
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+// Segment geometry shared by the min/max and the fused RTN kernels.
+struct SegGeom {
+    int64_t rows, cols, ld, gs, nseg;  // nseg = segments per row
+    int L;                              // lanes per segment
+};
+
+template <typename T, int VEC>
+__device__ __forceinline__ void seg_reduce(const T* x, const SegGeom& g, int64_t seg, bool active, float& mn,
+                                           float& mx) {
+    mn = INFINITY;
+    mx = -INFINITY;
+    const int sub = lane_id() % g.L;
+    int64_t r = 0, c0 = 0, c1 = 0;
+    if (active) {
+        r = seg / g.nseg;
+        const int64_t s = seg % g.nseg;
+        c0 = s * g.gs;
+        c1 = min(g.cols, c0 + g.gs);
+    }
+    const T* row = x + r * g.ld;
+    for (int64_t c = c0 + (int64_t)sub * VEC; c < c1; c += (int64_t)g.L * VEC) {
+        if (c + VEC <= c1) {
+            Vec<T, VEC> v;
+            v.load(row + c);
+#pragma unroll
+            for (int i = 0; i < VEC; i++) {
+                mn = fminf(mn, v.v[i]);
+                mx = fmaxf(mx, v.v[i]);
+            }
+        } else {
+            for (int64_t i = c; i < c1; i++) {
+                float f = to_f<T>(row[i]);
+                mn = fminf(mn, f);
+                mx = fmaxf(mx, f);
+            }
+        }
+    }
+    for (int off = g.L / 2; off > 0; off >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    }
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(NT) seg_minmax_kernel(const T* x, SegGeom g, float* mins, float* maxs, int accumulate) {
+    const int64_t groups_per_block = NT / g.L;
+    const int64_t total = g.rows * g.nseg;
+    const int64_t lg = threadIdx.x / g.L;
+    for (int64_t base = (int64_t)blockIdx.x * groups_per_block; base < total;
+         base += (int64_t)gridDim.x * groups_per_block) {
+        // Loop bound is uniform across the block, so every lane reaches the shuffles.
+        const int64_t seg = base + lg;
+        const bool active = seg < total;
+        float mn, mx;
+        seg_reduce<T, VEC>(x, g, seg, active, mn, mx);
+        if (active && (lane_id() % g.L) == 0) {
+            if (accumulate) {
+                mn = fminf(mn, mins[seg]);
+                mx = fmaxf(mx, maxs[seg]);
+            }
+            mins[seg] = mn;
+            maxs[seg] = mx;
+        }
+    }
+}
+
+__global__ void affine_kernel(const float* mins, const float* maxs, int64_t count, int bits, int sym, float* scales,
+                              int32_t* zps) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        float s;
+        int z;
+        affine_params(mins[i], maxs[i], bits, sym, &s, &z);
+        scales[i] = s;
+        zps[i] = z;
+    }
+}
+
+// Writes VEC codes of one row starting at column c (c even when packing nibbles).
+template <int VEC>
+__device__ __forceinline__ void store_codes(uint8_t* row_codes, int64_t c, const int* q, int zp, int bits, int n_valid) {
+    if (bits <= 4) {
+        if (n_valid == VEC && (VEC % 2) == 0) {
+            uint8_t b[VEC / 2 > 0 ? VEC / 2 : 1];
+#pragma unroll
+            for (int i = 0; i < VEC / 2; i++)
+                b[i] = (uint8_t)((((q[2 * i] - zp) & 0xF) << 4) | ((q[2 * i + 1] - zp) & 0xF));
+            uint8_t* p = row_codes + c / 2;
+            if constexpr (VEC == 8) *reinterpret_cast<uint32_t*>(p) = *reinterpret_cast<uint32_t*>(b);
+            else if constexpr (VEC == 4) *reinterpret_cast<uint16_t*>(p) = *reinterpret_cast<uint16_t*>(b);
+            else
+#pragma unroll
+                for (int i = 0; i < VEC / 2; i++) p[i] = b[i];
+        } else {
+            for (int i = 0; i < n_valid; i++) {
+                const int64_t col = c + i;
+                uint8_t nib = (uint8_t)((q[i] - zp) & 0xF);
+                uint8_t* p = row_codes + col / 2;
+                if (col % 2 == 0) *p = (uint8_t)((*p & 0x0F) | (nib << 4));
+                else *p = (uint8_t)((*p & 0xF0) | nib);
+            }
+        }
+    } else {
+        for (int i = 0; i < n_valid; i++) row_codes[c + i] = (uint8_t)q[i];
+    }
+}
+
+__host__ __device__ inline int64_t code_row_bytes(int bits, int64_t n) { return bits <= 4 ? (n + 1) / 2 : n; }
+
+// Fused observer + fake-quant for CHANNEL / GROUP, or fake-quant with one scale (TENSOR,
+// params precomputed into scales[0]/zps[0]).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(NT) rtn_kernel(const T* x, SegGeom g, int bits, int sym, int tensor_mode,
+                                                  float* scales, int32_t* zps, uint8_t* codes, T* deq, int64_t ld_deq) {
+    const int64_t groups_per_block = NT / g.L;
+    const int64_t total = g.rows * g.nseg;
+    const int64_t lg = threadIdx.x / g.L;
+    const int sub = lane_id() % g.L;
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    const int64_t crow = code_row_bytes(bits, g.cols);
+    for (int64_t base = (int64_t)blockIdx.x * groups_per_block; base < total;
+         base += (int64_t)gridDim.x * groups_per_block) {
+        const int64_t seg = base + lg;
+        const bool active = seg < total;
+        float s;
+        int z;
+        if (tensor_mode) {
+            s = scales[0];
+            z = zps[0];
+        } else {
+            float mn, mx;
+            seg_reduce<T, VEC>(x, g, seg, active, mn, mx);
+            affine_params(mn, mx, bits, sym, &s, &z);
+            if (active && sub == 0) {
+                scales[seg] = s;
+                zps[seg] = z;
+            }
+        }
+        if (!active) continue;
+        const float zf = (float)z;
+        const int64_t r = seg / g.nseg;
+        const int64_t c0 = (seg % g.nseg) * g.gs, c1 = min(g.cols, c0 + g.gs);
+        const T* row = x + r * g.ld;
+        for (int64_t c = c0 + (int64_t)sub * VEC; c < c1; c += (int64_t)g.L * VEC) {
+            const int nv = (int)min((int64_t)VEC, c1 - c);
+            float v[VEC];
+            if (nv == VEC) {
+                Vec<T, VEC> vv;
+                vv.load(row + c);
+#pragma unroll
+                for (int i = 0; i < VEC; i++) v[i] = vv.v[i];
+            } else {
+                for (int i = 0; i < VEC; i++) v[i] = i < nv ? to_f<T>(row[c + i]) : 0.f;
+            }
+            int q[VEC];
+            float o[VEC];
+#pragma unroll
+            for (int i = 0; i < VEC; i++) o[i] = fq_chain<T>(v[i], s, zf, qmin, qmax, &q[i]);
+            if (codes) store_codes<VEC>(codes + r * crow, c, q, z, bits, nv);
+            if (deq) {
+                T* d = deq + r * ld_deq + c;
+                if (nv == VEC && VEC * sizeof(T) == 16) {
+                    uint4 pk;
+                    T* h = reinterpret_cast<T*>(&pk);
+#pragma unroll
+                    for (int i = 0; i < VEC; i++) h[i] = from_f<T>(o[i]);
+                    *reinterpret_cast<uint4*>(d) = pk;
+                } else {
+                    for (int i = 0; i < nv; i++) d[i] = from_f<T>(o[i]);
+                }
+            }
+        }
+    }
+}
+
+template <typename T>
+__global__ void fake_quant_flat_kernel(const T* x, int64_t n, float s, float zf, float qmin, float qmax, T* out,
+                                       int32_t* codes) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int q;
+        const float v = fq_chain<T>(to_f<T>(x[i]), s, zf, qmin, qmax, &q);
+        if (out) out[i] = from_f<T>(v);
+        if (codes) codes[i] = q;
+    }
+}
+
+__global__ void int4_pack_kernel(const int32_t* q, int64_t n, int zp, uint8_t* out) {
+    const int64_t nb = (n + 1) / 2;
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+        const int hi = (q[2 * b] - zp) & 0xF;
+        const int lo = (2 * b + 1 < n) ? ((q[2 * b + 1] - zp) & 0xF) : 0;
+        out[b] = (uint8_t)((hi << 4) | lo);
+    }
+}
+
+__global__ void int4_unpack_kernel(const uint8_t* p, int64_t n, float s, int sym, float* out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t b = p[i / 2];
+        int nib = (i % 2 == 0) ? (b >> 4) : (b & 0xF);
+        if (sym && (nib & 0x8)) nib -= 16;  // Int4PackedTensor.cs:132-136: sign-extend only if symmetric
+        out[i] = __fmul_rn((float)nib, s);
+    }
+}
+
+template <typename T>
+__global__ void convert_kernel(const T* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd) {
+    const int64_t total = rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / cols, c = i % cols;
+        dst[r * ldd + c] = to_f<T>(src[r * lds + c]);
+    }
+}
+
+__global__ void symmetrize_kernel(const float* src, int64_t d, int64_t lds, float* dst, int64_t ldd) {
+    const int64_t total = d * d;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / d, c = i % d;
+        dst[r * ldd + c] = (r <= c) ? src[r * lds + c] : src[c * lds + r];
+    }
+}
+
+int grid_for(llmc_ctx* ctx, int64_t items, int per_block) {
+    int64_t b = (items + per_block - 1) / per_block;
+    int64_t cap = (int64_t)ctx->sm_count * 16;
+    if (b > cap) b = cap;
+    if (b < 1) b = 1;
+    return (int)b;
+}
+
+// Lanes per segment: the power of two <= 32 closest to (segment length / VEC) from below.
+int lanes_for(int64_t seglen, int vec) {
+    int64_t chunks = (seglen + vec - 1) / vec;
+    int L = 1;
+    while (L < 32 && L * 2 <= chunks) L *= 2;
+    return L;
+}
+
+template <typename T>
+bool vec_ok(const void* x, int64_t ld, int64_t gs, int64_t cols) {
+    constexpr int V = 16 / sizeof(T);
+    return ((uintptr_t)x % 16 == 0) && (ld % V == 0) && (gs % V == 0) && (cols % V == 0 || gs >= cols);
+}
+
+template <typename T>
+llmc_status launch_minmax(llmc_ctx* ctx, const void* x, int64_t rows, int64_t cols, int64_t ld, int64_t gs,
+                          float* mins, float* maxs, int accumulate) {
+    constexpr int V = 16 / sizeof(T);
+    SegGeom g{rows, cols, ld, gs, (cols + gs - 1) / gs, 1};
+    const int64_t total = rows * g.nseg;
+    if (vec_ok<T>(x, ld, gs, cols)) {
+        g.L = lanes_for(gs < cols ? gs : cols, V);
+        seg_minmax_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+            reinterpret_cast<const T*>(x), g, mins, maxs, accumulate);
+    } else {
+        g.L = lanes_for(gs < cols ? gs : cols, 1);
+        seg_minmax_kernel<T, 1><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+            reinterpret_cast<const T*>(x), g, mins, maxs, accumulate);
+    }
+    return check_launch(ctx, "seg_minmax");
+}
+
+llmc_status dispatch_minmax(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, int64_t gs,
+                            float* mins, float* maxs, int accumulate) {
+    switch (dtype) {
+        case LLMC_DTYPE_F32: return launch_minmax<float>(ctx, x, rows, cols, ld, gs, mins, maxs, accumulate);
+        case LLMC_DTYPE_BF16: return launch_minmax<__nv_bfloat16>(ctx, x, rows, cols, ld, gs, mins, maxs, accumulate);
+        case LLMC_DTYPE_F16: return launch_minmax<__half>(ctx, x, rows, cols, ld, gs, mins, maxs, accumulate);
+    }
+    return fail(LLMC_ERR_INVALID_ARG, "bad dtype %d", dtype);
+}
+
+template <typename T>
+llmc_status launch_rtn(llmc_ctx* ctx, const void* x, int64_t m, int64_t n, int64_t ldw, int64_t gs, int bits, int sym,
+                       int tensor_mode, float* scales, int32_t* zps, uint8_t* codes, void* deq) {
+    constexpr int V = 16 / sizeof(T);
+    SegGeom g{m, n, ldw, gs, (n + gs - 1) / gs, 1};
+    const int64_t total = m * g.nseg;
+    // Vector path also needs whole code bytes per lane (even column starts) and aligned output.
+    const bool deq_ok = deq == nullptr || ((uintptr_t)deq % 16 == 0);
+    const bool codes_ok = codes == nullptr || bits > 4 || (n % 2 == 0);
+    if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok) {
+        g.L = lanes_for(gs < n ? gs : n, V);
+        rtn_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+            reinterpret_cast<const T*>(x), g, bits, sym, tensor_mode, scales, zps, codes, reinterpret_cast<T*>(deq), n);
+    } else {
+        g.L = lanes_for(gs < n ? gs : n, 1);
+        // The scalar path packs nibbles one at a time (read-modify-write of a byte), so
+        // one lane owns each segment's codes; segments start on even columns (odd group
+        // sizes with packed codes are rejected by the caller), so no byte is shared.
+        if (codes && bits <= 4) g.L = 1;
+        rtn_kernel<T, 1><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+            reinterpret_cast<const T*>(x), g, bits, sym, tensor_mode, scales, zps, codes, reinterpret_cast<T*>(deq), n);
+    }
+    return check_launch(ctx, "rtn");
+}
+
+}  // namespace
+
+size_t minmax_scratch_floats(int strategy, int64_t rows) {
+    return strategy == LLMC_STRATEGY_TENSOR ? (size_t)(2 * rows + 64) : 0;
+}
+
+llmc_status minmax(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, int strategy,
+                   int64_t group_size, float* mins, float* maxs, int accumulate, float* scratch) {
+    if (strategy == LLMC_STRATEGY_TENSOR) {
+        // Level 1: per-row min/max into scratch; level 2: min over the row minima and max
+        // over the row maxima (each level-2 call also produces one unused value).
+        float* rmin = scratch;
+        float* rmax = scratch + rows;
+        float* unused = scratch + 2 * rows + 32;
+        LLMC_TRY(dispatch_minmax(ctx, x, dtype, rows, cols, ld, cols, rmin, rmax, 0));
+        LLMC_TRY(dispatch_minmax(ctx, rmin, LLMC_DTYPE_F32, 1, rows, rows, rows, mins, unused, accumulate));
+        LLMC_TRY(dispatch_minmax(ctx, rmax, LLMC_DTYPE_F32, 1, rows, rows, rows, unused, maxs, accumulate));
+        return LLMC_OK;
+    }
+    const int64_t gs = strategy == LLMC_STRATEGY_GROUP ? group_size : cols;
+    return dispatch_minmax(ctx, x, dtype, rows, cols, ld, gs, mins, maxs, accumulate);
+}
+
+llmc_status affine(llmc_ctx* ctx, const float* mins, const float* maxs, int64_t count, int bits, int sym, float* scales,
+                   int32_t* zps) {
+    affine_kernel<<<grid_for(ctx, count, NT), NT, 0, ctx->stream>>>(mins, maxs, count, bits, sym, scales, zps);
+    return check_launch(ctx, "affine");
+}
+
+llmc_status rtn(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64_t n, int64_t ldw, const llmc_qconfig* cfg,
+                uint8_t* codes, float* scales, int32_t* zps, void* deq, float* scratch) {
+    const int bits = cfg->num_bits, sym = cfg->symmetric;
+    int tensor_mode = 0;
+    int64_t gs = n;
+    if (cfg->strategy == LLMC_STRATEGY_TENSOR) {
+        // scratch: [2m + 64] for the two-level reduction, then 2 device scalars.
+        float* mn = scratch + 2 * m + 64;
+        float* mx = mn + 1;
+        LLMC_TRY(minmax(ctx, W, dtype, m, n, ldw, LLMC_STRATEGY_TENSOR, n, mn, mx, 0, scratch));
+        LLMC_TRY(affine(ctx, mn, mx, 1, bits, sym, scales, zps));
+        tensor_mode = 1;
+    } else if (cfg->strategy == LLMC_STRATEGY_GROUP) {
+        gs = cfg->group_size;
+    }
+    switch (dtype) {
+        case LLMC_DTYPE_F32: return launch_rtn<float>(ctx, W, m, n, ldw, gs, bits, sym, tensor_mode, scales, zps, codes, deq);
+        case LLMC_DTYPE_BF16: return launch_rtn<__nv_bfloat16>(ctx, W, m, n, ldw, gs, bits, sym, tensor_mode, scales, zps, codes, deq);
+        case LLMC_DTYPE_F16: return launch_rtn<__half>(ctx, W, m, n, ldw, gs, bits, sym, tensor_mode, scales, zps, codes, deq);
+    }
+    return fail(LLMC_ERR_INVALID_ARG, "bad dtype");
+}
+
+llmc_status fake_quant_flat(llmc_ctx* ctx, const void* x, int dtype, int64_t count, float s, int zp, int bits, int sym,
+                            void* out, int32_t* codes) {
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    const int g = grid_for(ctx, count, NT);
+    switch (dtype) {
+        case LLMC_DTYPE_F32:
+            fake_quant_flat_kernel<float><<<g, NT, 0, ctx->stream>>>((const float*)x, count, s, (float)zp, qmin, qmax,
+                                                                     (float*)out, codes);
+            break;
+        case LLMC_DTYPE_BF16:
+            fake_quant_flat_kernel<__nv_bfloat16><<<g, NT, 0, ctx->stream>>>((const __nv_bfloat16*)x, count, s, (float)zp,
+                                                                             qmin, qmax, (__nv_bfloat16*)out, codes);
+            break;
+        case LLMC_DTYPE_F16:
+            fake_quant_flat_kernel<__half><<<g, NT, 0, ctx->stream>>>((const __half*)x, count, s, (float)zp, qmin, qmax,
+                                                                      (__half*)out, codes);
+            break;
+        default: return fail(LLMC_ERR_INVALID_ARG, "bad dtype");
+    }
+    return check_launch(ctx, "fake_quant");
+}
+
+llmc_status int4_pack(llmc_ctx* ctx, const int32_t* q, int64_t n, int zp, uint8_t* out) {
+    int4_pack_kernel<<<grid_for(ctx, (n + 1) / 2, NT), NT, 0, ctx->stream>>>(q, n, zp, out);
+    return check_launch(ctx, "int4_pack");
+}
+
+llmc_status int4_unpack(llmc_ctx* ctx, const uint8_t* p, int64_t n, float s, int sym, float* out) {
+    int4_unpack_kernel<<<grid_for(ctx, n, NT), NT, 0, ctx->stream>>>(p, n, s, sym, out);
+    return check_launch(ctx, "int4_unpack");
+}
+
+llmc_status convert_to_f32(llmc_ctx* ctx, const void* src, int dtype, int64_t rows, int64_t cols, int64_t lds, float* dst,
+                           int64_t ldd) {
+    const int g = grid_for(ctx, rows * cols, NT);
+    switch (dtype) {
+        case LLMC_DTYPE_F32: convert_kernel<float><<<g, NT, 0, ctx->stream>>>((const float*)src, rows, cols, lds, dst, ldd); break;
+        case LLMC_DTYPE_BF16:
+            convert_kernel<__nv_bfloat16><<<g, NT, 0, ctx->stream>>>((const __nv_bfloat16*)src, rows, cols, lds, dst, ldd);
+            break;
+        case LLMC_DTYPE_F16: convert_kernel<__half><<<g, NT, 0, ctx->stream>>>((const __half*)src, rows, cols, lds, dst, ldd); break;
+        default: return fail(LLMC_ERR_INVALID_ARG, "bad dtype");
+    }
+    return check_launch(ctx, "convert_to_f32");
+}
+
+llmc_status symmetrize_from_upper(llmc_ctx* ctx, const float* src, int64_t d, int64_t lds, float* dst, int64_t ldd) {
+    symmetrize_kernel<<<grid_for(ctx, d * d, NT), NT, 0, ctx->stream>>>(src, d, lds, dst, ldd);
+    return check_launch(ctx, "symmetrize");
+}
+
+}  // namespace llmc

@@ -1,0 +1,263 @@
+// SmoothQuant activation statistics / smoothing and the AWQ scale grid search.
+//
+// Reference: SmoothQuantModifier.UpdateActivationMax (src/LLMCompressorSharp.Core/Algorithms/
+// SmoothQuant/SmoothQuantModifier.cs:71-115), ApplyMapping (:117-182); AWQ per the design
+// sketch docs/llmcompressorsharp/algorithm-mapping.md:214-249.
+#include "ops.h"
+
+namespace llmc {
+namespace {
+
+constexpr int NT = 256;
+
+// Column-wise max |x| over rows, folded into out with an integer atomicMax on the float
+// bits (valid because every value is >= 0).  Each thread owns VEC consecutive columns
+// and a slice of rows, so a warp reads 32*16 contiguous bytes per row.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(NT) col_absmax_kernel(const T* x, int64_t rows, int64_t cols, int64_t ld,
+                                                        int64_t rows_per_block, float* out) {
+    const int64_t c0 = ((int64_t)blockIdx.x * NT + threadIdx.x) * VEC;
+    if (c0 >= cols) return;
+    const int64_t r0 = (int64_t)blockIdx.y * rows_per_block;
+    const int64_t r1 = min(rows, r0 + rows_per_block);
+    float mx[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; i++) mx[i] = 0.f;
+    const bool full = c0 + VEC <= cols;
+    for (int64_t r = r0; r < r1; r++) {
+        const T* p = x + r * ld + c0;
+        if (VEC > 1 && full) {
+            uint4 q = *reinterpret_cast<const uint4*>(p);
+            const T* h = reinterpret_cast<const T*>(&q);
+#pragma unroll
+            for (int i = 0; i < VEC; i++) mx[i] = fmaxf(mx[i], fabsf(to_f<T>(h[i])));
+        } else {
+            for (int i = 0; i < VEC && c0 + i < cols; i++) mx[i] = fmaxf(mx[i], fabsf(to_f<T>(p[i])));
+        }
+    }
+    for (int i = 0; i < VEC && c0 + i < cols; i++)
+        atomicMax(reinterpret_cast<int*>(out + c0 + i), __float_as_int(mx[i]));
+}
+
+// MathF.Pow result: pow evaluated in double and rounded once to float (the correctly
+// rounded single-precision power that the host C library returns in practice).
+__device__ __forceinline__ float powf_cr(float a, float b) { return (float)pow((double)a, (double)b); }
+
+__global__ void smooth_scales_kernel(const float* act, const float* wmax, int64_t n, float alpha, float* s) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float num = powf_cr(fmaxf(act[i], 1e-5f), alpha);
+        const float den = powf_cr(fmaxf(wmax[i], 1e-5f), __fsub_rn(1.f, alpha));
+        s[i] = fmaxf(__fdiv_rn(num, den), 1e-5f);  // SmoothQuantModifier.cs:165-172
+    }
+}
+
+// smooth /= s ; balance *= s, with s first rounded to the smooth weight's dtype
+// (tensor(s).to(smoothW.dtype), SmoothQuantModifier.cs:174-178).
+template <typename TS, typename TB>
+__global__ void scale_apply_kernel(const float* s, TS* smooth, TB* balance, int64_t m, int64_t hidden) {
+    const int64_t total = m * hidden;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total + hidden;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        if (t < total) {
+            const int64_t c = t % hidden;
+            const float sc = rnd<TS>(s[c]);
+            balance[t] = from_f<TB>(__fmul_rn(to_f<TB>(balance[t]), sc));
+        } else if (smooth) {
+            const int64_t c = t - total;
+            const float sc = rnd<TS>(s[c]);
+            smooth[c] = from_f<TS>(__fdiv_rn(to_f<TS>(smooth[c]), sc));
+        }
+    }
+}
+
+// AWQ: s_k[c] = max(a_c^(k/G) / wmax_c^(1-k/G), 1e-4) for k = 1..G (torch fp32 pow).
+__global__ void awq_scales_kernel(const float* act, const float* wmax, int64_t n, int grid_pts, float* sk) {
+    const int64_t total = (int64_t)grid_pts * n;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int k = (int)(t / n) + 1;
+        const int64_t c = t % n;
+        const float alpha = __fdiv_rn((float)k, (float)grid_pts);
+        const float v = __fdiv_rn(powf_cr(act[c], alpha), powf_cr(wmax[c], __fsub_rn(1.f, alpha)));
+        sk[t] = fmaxf(v, 1e-4f);
+    }
+}
+
+// One pass per grid point over W: segment (row, group) min/max of W*s, affine params,
+// fake-quant in fp32, squared error of FQ(W*s)/s - W accumulated in double.
+// One warp per segment; lanes stride over the segment's columns.
+template <typename T>
+__global__ void __launch_bounds__(NT) awq_err_kernel(const T* W, int64_t m, int64_t n, int64_t ldw, int64_t gs,
+                                                     const float* s, int bits, int sym, double* mse_acc) {
+    const int64_t nseg = (n + gs - 1) / gs;
+    const int64_t total = m * nseg;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * NT + threadIdx.x) / 32;
+    const int64_t nwarps = (int64_t)gridDim.x * NT / 32;
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    double acc = 0.0;
+    for (int64_t seg = warp; seg < total; seg += nwarps) {
+        const int64_t r = seg / nseg, c0 = (seg % nseg) * gs, c1 = min(n, c0 + gs);
+        float mn = INFINITY, mx = -INFINITY;
+        for (int64_t c = c0 + lane; c < c1; c += 32) {
+            const float v = __fmul_rn(to_f<T>(W[r * ldw + c]), s[c]);
+            mn = fminf(mn, v);
+            mx = fmaxf(mx, v);
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        float sc;
+        int z;
+        affine_params(mn, mx, bits, sym, &sc, &z);
+        for (int64_t c = c0 + lane; c < c1; c += 32) {
+            const float w = to_f<T>(W[r * ldw + c]);
+            const float v = __fmul_rn(w, s[c]);
+            int code;
+            const float fq = fq_chain<float>(v, sc, (float)z, qmin, qmax, &code);
+            const float e = __fsub_rn(__fdiv_rn(fq, s[c]), w);
+            acc += (double)e * (double)e;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) atomicAdd(mse_acc, acc);
+}
+
+__global__ void awq_pick_kernel(const double* sums, int grid_pts, double denom, const float* sk, int64_t n, double* mse_out,
+                                float* best_s, int* best_k) {
+    __shared__ int kbest;
+    if (threadIdx.x == 0) {
+        double best = INFINITY;
+        int kb = 1;
+        for (int k = 0; k < grid_pts; k++) {
+            const double v = sums[k] / denom;
+            if (mse_out) mse_out[k] = v;
+            if (v < best) {
+                best = v;
+                kb = k + 1;
+            }
+        }
+        kbest = kb;
+        best_k[0] = kb;
+    }
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < n; c += blockDim.x) best_s[c] = sk[(int64_t)(kbest - 1) * n + c];
+}
+
+int grid_for(llmc_ctx* ctx, int64_t items) {
+    int64_t b = (items + NT - 1) / NT;
+    int64_t cap = (int64_t)ctx->sm_count * 8;
+    return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+template <typename T>
+llmc_status launch_col_absmax(llmc_ctx* ctx, const void* x, int64_t rows, int64_t cols, int64_t ld, float* out) {
+    constexpr int V = 16 / sizeof(T);
+    const bool vec = ((uintptr_t)x % 16 == 0) && (ld % V == 0);
+    const int vv = vec ? V : 1;
+    const int64_t col_threads = (cols + vv - 1) / vv;
+    const unsigned gx = (unsigned)((col_threads + NT - 1) / NT);
+    int64_t want_blocks = (int64_t)ctx->sm_count * 8;
+    int64_t gy = want_blocks / gx;
+    if (gy < 1) gy = 1;
+    if (gy > rows) gy = rows > 0 ? rows : 1;
+    if (gy > 65535) gy = 65535;
+    const int64_t rpb = (rows + gy - 1) / gy;
+    gy = (rows + rpb - 1) / rpb;
+    if (gy < 1) gy = 1;
+    dim3 grid(gx, (unsigned)gy);
+    if (vec) col_absmax_kernel<T, V><<<grid, NT, 0, ctx->stream>>>((const T*)x, rows, cols, ld, rpb, out);
+    else col_absmax_kernel<T, 1><<<grid, NT, 0, ctx->stream>>>((const T*)x, rows, cols, ld, rpb, out);
+    return check_launch(ctx, "col_absmax");
+}
+
+}  // namespace
+
+llmc_status col_absmax(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* out,
+                       int accumulate) {
+    if (!accumulate) LLMC_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)cols * sizeof(float), ctx->stream));
+    if (rows <= 0) return LLMC_OK;
+    switch (dtype) {
+        case LLMC_DTYPE_F32: return launch_col_absmax<float>(ctx, x, rows, cols, ld, out);
+        case LLMC_DTYPE_BF16: return launch_col_absmax<__nv_bfloat16>(ctx, x, rows, cols, ld, out);
+        case LLMC_DTYPE_F16: return launch_col_absmax<__half>(ctx, x, rows, cols, ld, out);
+    }
+    return fail(LLMC_ERR_INVALID_ARG, "bad dtype");
+}
+
+llmc_status scale_apply(llmc_ctx* ctx, const float* s, void* smooth, int sdt, void* balance, int bdt, int64_t m,
+                        int64_t hidden) {
+    const int g = grid_for(ctx, m * hidden + hidden);
+#define LLMC_SA(TS, TB) \
+    scale_apply_kernel<TS, TB><<<g, NT, 0, ctx->stream>>>(s, (TS*)smooth, (TB*)balance, m, hidden)
+    if (sdt == LLMC_DTYPE_F32 && bdt == LLMC_DTYPE_F32) LLMC_SA(float, float);
+    else if (sdt == LLMC_DTYPE_BF16 && bdt == LLMC_DTYPE_BF16) LLMC_SA(__nv_bfloat16, __nv_bfloat16);
+    else if (sdt == LLMC_DTYPE_F16 && bdt == LLMC_DTYPE_F16) LLMC_SA(__half, __half);
+    else if (sdt == LLMC_DTYPE_F32 && bdt == LLMC_DTYPE_BF16) LLMC_SA(float, __nv_bfloat16);
+    else if (sdt == LLMC_DTYPE_BF16 && bdt == LLMC_DTYPE_F32) LLMC_SA(__nv_bfloat16, float);
+    else return fail(LLMC_ERR_UNSUPPORTED, "scale_apply: dtype pair (%d, %d) not supported", sdt, bdt);
+#undef LLMC_SA
+    return check_launch(ctx, "scale_apply");
+}
+
+llmc_status smooth_apply(llmc_ctx* ctx, const float* act_max, void* smooth, int sdt, void* balance, int bdt, int64_t m,
+                         int64_t hidden, float alpha, float* s_out) {
+    void* wsp;
+    LLMC_TRY(workspace(ctx, (size_t)hidden * 8 + 1024, &wsp));
+    Carver cv{(char*)wsp};
+    float* wmax = cv.take<float>(hidden);
+    float* s = s_out ? s_out : cv.take<float>(hidden);
+    LLMC_TRY(col_absmax(ctx, balance, bdt, m, hidden, hidden, wmax, 0));
+    smooth_scales_kernel<<<grid_for(ctx, hidden), NT, 0, ctx->stream>>>(act_max, wmax, hidden, alpha, s);
+    LLMC_TRY(check_launch(ctx, "smooth_scales"));
+    return scale_apply(ctx, s, smooth, sdt, balance, bdt, m, hidden);
+}
+
+llmc_status awq_search(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64_t n, int64_t ldw, const float* act_max,
+                       int grid_pts, const llmc_qconfig* cfg, float* best_s, double* mse_out, int32_t* best_k) {
+    void* wsp;
+    LLMC_TRY(workspace(ctx, (size_t)n * 4 + (size_t)grid_pts * n * 4 + (size_t)grid_pts * 8 + 2048, &wsp));
+    Carver cv{(char*)wsp};
+    float* wmax = cv.take<float>(n);
+    float* sk = cv.take<float>((size_t)grid_pts * n);
+    double* sums = cv.take<double>(grid_pts);
+    int* kdev = cv.take<int>(4);
+    LLMC_TRY(col_absmax(ctx, W, dtype, m, n, ldw, wmax, 0));
+    awq_scales_kernel<<<grid_for(ctx, (int64_t)grid_pts * n), NT, 0, ctx->stream>>>(act_max, wmax, n, grid_pts, sk);
+    LLMC_TRY(check_launch(ctx, "awq_scales"));
+    LLMC_CUDA_TRY(cudaMemsetAsync(sums, 0, (size_t)grid_pts * sizeof(double), ctx->stream));
+    const int64_t gs = cfg->strategy == LLMC_STRATEGY_GROUP ? cfg->group_size : n;
+    const int64_t segs = m * ((n + gs - 1) / gs);
+    int64_t nb = (segs + 7) / 8;
+    if (nb > (int64_t)ctx->sm_count * 8) nb = (int64_t)ctx->sm_count * 8;
+    int blocks = (int)nb;
+    if (blocks < 1) blocks = 1;
+    for (int k = 0; k < grid_pts; k++) {
+        const float* s = sk + (int64_t)k * n;
+        switch (dtype) {
+            case LLMC_DTYPE_F32:
+                awq_err_kernel<float><<<blocks, NT, 0, ctx->stream>>>((const float*)W, m, n, ldw, gs, s, cfg->num_bits,
+                                                                      cfg->symmetric, sums + k);
+                break;
+            case LLMC_DTYPE_BF16:
+                awq_err_kernel<__nv_bfloat16><<<blocks, NT, 0, ctx->stream>>>((const __nv_bfloat16*)W, m, n, ldw, gs, s,
+                                                                              cfg->num_bits, cfg->symmetric, sums + k);
+                break;
+            case LLMC_DTYPE_F16:
+                awq_err_kernel<__half><<<blocks, NT, 0, ctx->stream>>>((const __half*)W, m, n, ldw, gs, s, cfg->num_bits,
+                                                                       cfg->symmetric, sums + k);
+                break;
+            default: return fail(LLMC_ERR_INVALID_ARG, "bad dtype");
+        }
+        LLMC_TRY(check_launch(ctx, "awq_err"));
+    }
+    awq_pick_kernel<<<1, NT, 0, ctx->stream>>>(sums, grid_pts, (double)m * (double)n, sk, n, mse_out, best_s, kdev);
+    LLMC_TRY(check_launch(ctx, "awq_pick"));
+    LLMC_CUDA_TRY(cudaMemcpyAsync(ctx->hflags, kdev, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    *best_k = ctx->hflags[0];
+    return LLMC_OK;
+}
+
+}  // namespace llmc

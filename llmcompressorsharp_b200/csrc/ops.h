@@ -1,0 +1,53 @@
+// Internal launchers shared between the translation units of libllmc_b200.
+#pragma once
+#include "common.cuh"
+
+namespace llmc {
+
+// ---- fp32 SIMT GEMM (k_gemm.cu) --------------------------------------------------------
+// C[M,N] = alpha * op(A) @ op(B) + beta * C, row-major, op(X) = X or X^T.
+// Triangular hints restrict each tile's K range (the skipped region must hold zeros):
+//   a_tri: 0 none, 1 op(A)[i][k] == 0 for k > i, 2 op(A)[i][k] == 0 for k < i
+//   b_tri: 0 none, 1 op(B)[k][j] == 0 for k > j, 2 op(B)[k][j] == 0 for k < j
+// c_mode: 0 full, 1 only i >= j is written (lower), 2 only tiles with i-tile <= j-tile (upper
+// blocks of a symmetric product; diagonal tiles written in full).
+// split_k > 1 partitions K; partial products are added with atomics (beta must be 1).
+enum { TRI_NONE = 0, TRI_KLE = 1, TRI_KGE = 2 };
+struct GemmArgs {
+    int64_t M, N, K;
+    const void* A; int64_t lda; int a_trans; int a_dtype;
+    const void* B; int64_t ldb; int b_trans; int b_dtype;
+    float* C; int64_t ldc;
+    float alpha, beta;
+    int a_tri = 0, b_tri = 0, c_mode = 0, split_k = 1;
+};
+llmc_status gemm_f32(llmc_ctx* ctx, const GemmArgs& g);
+
+// ---- tcgen05 symmetric rank-k update (k_hessian_tc.cu) ------------------------------------
+// H[upper tiles] += X^T X for bf16/f16 X [rows, d] (row stride ld).  Returns
+// LLMC_ERR_UNSUPPORTED when the shape/alignment is outside the kernel's contract.
+llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t d, int64_t ld, float* H, int64_t ldh);
+
+// ---- observers / quantisation (k_quant.cu) -----------------------------------------------
+// scratch: minmax_scratch_floats(strategy, rows) floats (only the per-tensor reduction uses it)
+llmc_status minmax(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                   int strategy, int64_t group_size, float* mins, float* maxs, int accumulate, float* scratch);
+size_t minmax_scratch_floats(int strategy, int64_t rows);
+llmc_status affine(llmc_ctx* ctx, const float* mins, const float* maxs, int64_t count, int bits, int sym,
+                   float* scales, int32_t* zps);
+// Number of (scale, zp) entries per row and per-row stride for a strategy over n columns.
+inline int64_t n_groups(int strategy, int64_t n, int64_t gs) {
+    return strategy == LLMC_STRATEGY_GROUP ? (n + gs - 1) / gs : 1;
+}
+
+// ---- Cholesky / inverse (k_chol.cu) -------------------------------------------------------
+llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, float damp, int upper_only,
+                         float* out, int64_t ldo, int want_upper);
+llmc_status upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ldh, float* out, int64_t ldo);
+
+// ---- misc ----------------------------------------------------------------------------------
+llmc_status symmetrize_from_upper(llmc_ctx* ctx, const float* src, int64_t d, int64_t lds, float* dst, int64_t ldd);
+llmc_status convert_to_f32(llmc_ctx* ctx, const void* src, int dtype, int64_t rows, int64_t cols, int64_t lds,
+                           float* dst, int64_t ldd);
+
+}  // namespace llmc

@@ -1,0 +1,530 @@
+"""GPU parity: every CUDA entry point against the CPU oracle on the same seeded inputs.
+
+Bars (per the task's acceptance rules):
+  * RTN / observers / fake-quant / packing: bit-exact (torch.equal).
+  * Hessian: fp32 sums in a different order -> relative Frobenius error <= 1e-6 (fp32 input)
+    and exact for small-integer inputs; bf16 input products are exact in fp32.
+  * Cholesky inverse / U factor: relative error <= 1e-4 (conditioning-limited, fp32).
+  * GPTQ / SparseGPT: scales and zero-points equal the oracle's (they come from the original
+    weight); int codes / masks agree on >= 99.9% of elements; reconstruction error
+    tr(dW H dW^T) within 1% of the oracle's.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from oracle import affine as o_aff, fakequant as o_fq, gptq as o_gptq, hessian as o_hess, rtn as o_rtn
+from oracle import smoothquant as o_sq, sparsegpt as o_sp, awq as o_awq
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def rel_fro(a, b):
+    a = a.double().cpu()
+    b = b.double().cpu()
+    return float((a - b).norm() / max(b.norm(), 1e-30))
+
+
+# --------------------------------------------------------------------------- Hessian
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("d,rows", [(3, 1), (64, 1000), (129, 777), (576, 4096), (300, 5)])
+def test_hessian_matches_oracle(dtype, d, rows):
+    from llmcompressorsharp_b200 import HessianAccumulator
+
+    g = gen(d * 7 + rows)
+    x = torch.randn(rows, d, generator=g).to(dtype)
+    acc = HessianAccumulator(d, DEV)
+    acc.update(x.to(DEV))
+    acc.update(x[: rows // 2 + 1].to(DEV))
+    ref = o_hess.HessianAccumulator(d)
+    ref.update(x)
+    ref.update(x[: rows // 2 + 1])
+    h = acc.get_hessian()
+    assert acc.sample_count == ref.sample_count
+    assert torch.equal(h, h.t())
+    assert rel_fro(h, ref.get_hessian()) < 1e-6
+
+
+def test_hessian_kats():  # HessianAccumulatorTests.cs
+    from llmcompressorsharp_b200 import HessianAccumulator
+    from llmcompressorsharp_b200.errors import ArgumentOutOfRangeError, ShapeError
+
+    acc = HessianAccumulator(3, DEV)
+    assert torch.count_nonzero(acc.get_hessian()) == 0
+    acc.update(torch.tensor([[1.0, 2.0, 3.0]], device=DEV))
+    assert acc.get_hessian().flatten().tolist() == [1, 2, 3, 2, 4, 6, 3, 6, 9]
+    acc = HessianAccumulator(2, DEV)
+    blk = [[1.0, 0.0], [0.0, 1.0], [1.0, 1.0]]
+    acc.update(torch.tensor([blk, blk], device=DEV))  # rank-3 input flattens
+    assert acc.sample_count == 6 and acc.get_hessian().flatten().tolist() == [4, 2, 2, 4]
+    acc.update(torch.tensor([[1.0, 2.0]]).to(torch.float16))  # host fp16 input
+    assert acc.get_hessian().dtype == torch.float32
+    acc.reset()
+    assert acc.sample_count == 0 and torch.count_nonzero(acc.get_hessian()) == 0
+    with pytest.raises(ShapeError, match="last dim"):
+        HessianAccumulator(3, DEV).update(torch.ones(1, 2, device=DEV))
+    with pytest.raises(ArgumentOutOfRangeError):
+        HessianAccumulator(0, DEV)
+
+
+def test_hessian_bf16_large_entries_exact_sample():
+    """Size-independent property at a benchmark width: entries of H for bf16 X equal fp64
+    dot products of the columns (products exact in fp32, fp32 accumulation)."""
+    from llmcompressorsharp_b200 import HessianAccumulator
+
+    d, rows = 4096, 16384
+    x = torch.randn(rows, d, device=DEV, generator=torch.Generator(DEV).manual_seed(11)).to(torch.bfloat16)
+    acc = HessianAccumulator(d, DEV)
+    acc.update(x)
+    h = acc.get_hessian()
+    idx = torch.randint(0, d, (256, 2), generator=gen(12))
+    xc = x.double().cpu()
+    ref = (xc[:, idx[:, 0]] * xc[:, idx[:, 1]]).sum(0)
+    got = h[idx[:, 0], idx[:, 1]].double().cpu()
+    scale = (xc[:, idx[:, 0]].abs() * xc[:, idx[:, 1]].abs()).sum(0)
+    assert float(((got - ref).abs() / scale).max()) < 1e-5
+    assert torch.equal(h, h.t())
+
+
+# --------------------------------------------------------------------------- inverse
+
+def spd(d, seed, rows=None):
+    g = gen(seed)
+    x = torch.randn(rows or 2 * d, d, generator=g)
+    return x.t() @ x
+
+
+@pytest.mark.parametrize("d", [1, 7, 64, 65, 200, 576])
+def test_inverse_matches_oracle(d):
+    from llmcompressorsharp_b200 import HessianInverseSolver
+
+    h = spd(d, d)
+    hinv = HessianInverseSolver.compute(h.to(DEV), 0.01)
+    ref = o_hess.hessian_inverse(h, 0.01)
+    assert rel_fro(hinv, ref) < 1e-4
+    u = HessianInverseSolver.upper(h.to(DEV), 0.01)
+    uref = o_hess.upper_factor(ref)
+    assert rel_fro(u, uref) < 1e-4
+    assert torch.count_nonzero(torch.tril(u.cpu(), -1)) == 0
+
+
+def test_inverse_upper_only_reads_upper_triangle():
+    from llmcompressorsharp_b200 import HessianInverseSolver
+
+    h = spd(100, 3)
+    garbage = torch.triu(h) + torch.tril(torch.full_like(h, 123.0), -1)
+    a = HessianInverseSolver.upper(garbage.to(DEV), 0.01, upper_only=True)
+    b = HessianInverseSolver.upper(h.to(DEV), 0.01)
+    assert torch.equal(a, b)
+
+
+def test_inverse_kats():  # HessianInverseSolverTests.cs
+    from llmcompressorsharp_b200 import HessianInverseSolver
+    from llmcompressorsharp_b200.errors import ShapeError
+
+    assert (HessianInverseSolver.compute(torch.eye(4, device=DEV), 0.0) - torch.eye(4, device=DEV)).abs().max() < 1e-5
+    assert (HessianInverseSolver.compute(2 * torch.eye(3, device=DEV), 0.0) - 0.5 * torch.eye(3, device=DEV)).abs().max() < 1e-5
+    assert torch.isfinite(HessianInverseSolver.compute(torch.ones(2, 2, device=DEV), 0.01)).all()
+    assert torch.isfinite(HessianInverseSolver.compute(torch.eye(4, device=DEV) * 1e-10, 0.0)).all()
+    z = HessianInverseSolver.compute(torch.zeros(5, 5, device=DEV), 0.01)  # pinv(0) = 0
+    assert torch.count_nonzero(z) == 0
+    with pytest.raises(ShapeError, match="square"):
+        HessianInverseSolver.compute(torch.ones(3, 4, device=DEV), 0.01)
+
+
+def test_upper_factor_fallback_to_hinv():  # GptqBlockQuantizer.cs:112-118
+    from llmcompressorsharp_b200 import upper_factor
+
+    hinv = torch.zeros(6, 6, device=DEV)
+    assert torch.equal(upper_factor(hinv), hinv)
+
+
+# --------------------------------------------------------------------------- observers / fq / rtn
+
+def outlier_weight(m, n, seed, dtype):
+    g = gen(seed)
+    w = torch.randn(m, n, generator=g) * 0.02
+    mask = torch.rand(m, n, generator=g) < 0.001
+    w = torch.where(mask, w * 20, w)
+    return w.to(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("strategy", ["tensor", "channel", "group"])
+@pytest.mark.parametrize("bits,sym", [(4, True), (4, False), (8, True), (8, False)])
+@pytest.mark.parametrize("shape", [(192, 576), (37, 300), (5, 1536)])
+def test_rtn_bit_exact(dtype, strategy, bits, sym, shape):
+    from llmcompressorsharp_b200 import RtnConfig, rtn_quantize
+
+    m, n = shape
+    w = outlier_weight(m, n, m * n + bits, dtype)
+    gs = 128 if n % 128 == 0 else 100
+    cfg = RtnConfig(num_bits=bits, symmetric=sym, strategy=strategy, group_size=gs)
+    deq, codes, scales, zps = rtn_quantize(w.to(DEV), cfg)
+    rdeq, rcodes, rs, rz = o_rtn.rtn_quantize(w, o_rtn.RtnConfig(bits, sym, strategy, group_size=gs))
+    assert torch.equal(deq.cpu(), rdeq)
+    n_par = 1 if strategy == "tensor" else None
+    assert np.array_equal(scales.cpu().numpy().reshape(-1), np.asarray(rs, np.float32).reshape(-1)[:n_par])
+    assert np.array_equal(zps.cpu().numpy().reshape(-1), np.asarray(rz).reshape(-1)[:n_par])
+    if bits <= 4:
+        zp_e = torch.from_numpy(np.asarray(rz))
+        if zp_e.shape[1] > 1:
+            zp_e = zp_e[:, torch.arange(n) // gs]
+        ref_codes = o_fq.pack_int4_rows(rcodes, zp_e)
+    else:
+        ref_codes = rcodes.to(torch.uint8)
+    assert torch.equal(codes.cpu(), ref_codes)
+
+
+def test_rtn_kats():  # RtnModifierTests.cs
+    from llmcompressorsharp_b200 import RtnConfig, RtnModifier, CompressionState
+
+    st = CompressionState({"layer.weight": torch.tensor([-127.0, -64.4, 0.0, 64.6, 127.0, 127.0])})
+    m = RtnModifier(RtnConfig(8, True, "tensor"))
+    for f in (m.initialize, m.on_start, m.on_end, m.finalize):
+        f(st)
+    assert st.named_weights["layer.weight"].tolist() == [-127, -64, 0, 65, 127, 127]
+    st = CompressionState({"model.layer.0.q_proj.weight": torch.tensor([-10.0, 0.0, 10.0]),
+                           "model.lm_head.weight": torch.tensor([-10.0, 0.0, 10.0])})
+    m = RtnModifier(RtnConfig(4, True, targets=["model.layer.*"], ignore=["*.lm_head.*"]))
+    for f in (m.initialize, m.on_start, m.on_end, m.finalize):
+        f(st)
+    assert st.named_weights["model.lm_head.weight"].tolist() == [-10, 0, 10]
+    q = st.named_weights["model.layer.0.q_proj.weight"]
+    assert abs(q[0] + 10) <= 2 and abs(q[1]) <= 2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_fake_quantize_bit_exact(dtype):
+    from llmcompressorsharp_b200 import FakeQuantize
+
+    x = (torch.randn(100_003, generator=gen(5)) * 0.05).to(dtype)
+    for bits, sym, z in ((4, True, 0), (4, False, 7), (8, True, 0), (8, False, 131), (2, False, 1), (16, True, 0)):
+        s = float(np.float32(0.0071234))
+        got = FakeQuantize.apply(x.to(DEV), s, z, bits, sym)
+        ref = o_fq.fake_quantize_torch_chain(x, s, z, bits, sym)
+        assert got.dtype == dtype and torch.equal(got.cpu(), ref)
+
+
+def test_fake_quantize_kats_and_ste():  # FakeQuantizeFunctionTests.cs
+    from llmcompressorsharp_b200 import FakeQuantize
+    from llmcompressorsharp_b200.errors import ArgumentOutOfRangeError
+
+    y = FakeQuantize.apply(torch.tensor([-127.4, -127.6, 0.4, 0.6, 127.4, 127.6], device=DEV), 1.0, 0, 8, True)
+    assert y.tolist() == [-127, -127, 0, 1, 127, 127]
+    assert FakeQuantize.apply(torch.tensor([-3.6, 0.0, 3.6], device=DEV), 0.5, 0, 4, True).tolist() == [-3.5, 0, 3.5]
+    assert FakeQuantize.apply(torch.tensor([-8.0, 0.0, 7.0], device=DEV), 1.0, 8, 4, False).tolist() == [-8, 0, 7]
+    x = torch.tensor([-2.0, -1.0, 0.0, 1.0, 2.0], device=DEV, requires_grad=True)
+    FakeQuantize.apply(x, 1.0, 0, 4, True).sum().backward()
+    assert x.grad.tolist() == [1, 1, 1, 1, 1]
+    with pytest.raises(ArgumentOutOfRangeError):
+        FakeQuantize.apply(torch.ones(2, device=DEV), 1.0, 0, 1, True)
+
+
+def test_observer_kats():  # MinMaxObserverTests.cs, PerChannelMinMaxObserverTests.cs, MovingAverage...
+    from llmcompressorsharp_b200 import MinMaxObserver, MovingAverageMinMaxObserver, PerChannelMinMaxObserver
+    from llmcompressorsharp_b200.errors import ArgumentOutOfRangeError, InvalidOperationError
+
+    o = MinMaxObserver()
+    for b in ([-2.0, 0.0, 3.0], [-5.0, 1.0, 2.0], [-1.0, 7.0, 0.0]):
+        o.update(torch.tensor(b, device=DEV))
+    s, z = o.get_quant_params(8, False)
+    assert abs(s - 12 / 255) < 1e-5 and z == 106
+    assert o.get_quant_params(8, True) == o_aff.compute_affine_params(-5, 7, 8, True)
+    with pytest.raises(InvalidOperationError):
+        MinMaxObserver().get_quant_params(8, True)
+    o = MinMaxObserver()
+    o.update(torch.zeros(3, device=DEV))
+    assert o.get_quant_params(8, True) == (1.0, 0)
+    p = PerChannelMinMaxObserver(0)
+    p.update(torch.tensor([[-1.0, 2.0], [-3.0, 5.0]], device=DEV))
+    p.update(torch.tensor([[-5.0, 1.0], [-2.0, 8.0]], device=DEV))
+    s, _ = p.get_quant_params(8, True)
+    assert abs(s[0].item() - 5 / 127) < 1e-6 and abs(s[1].item() - 8 / 127) < 1e-6
+    with pytest.raises(ArgumentOutOfRangeError):
+        PerChannelMinMaxObserver(5).update(torch.ones(2, 2, device=DEV))
+    e = MovingAverageMinMaxObserver(0.5)
+    e.update(torch.tensor([-10.0, 10.0], device=DEV))
+    e.update(torch.tensor([-2.0, 2.0], device=DEV))
+    assert abs(e.get_quant_params(8, True)[0] - 6 / 127) < 1e-6
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_observer_minmax_and_affine_exact(dtype):
+    from llmcompressorsharp_b200 import GroupMinMaxObserver, PerChannelMinMaxObserver
+
+    w = outlier_weight(300, 1000, 9, dtype)
+    go = GroupMinMaxObserver(128)
+    go.update(w.to(DEV))
+    mins, maxs = o_aff.group_minmax(w, 128)
+    assert torch.equal(go._min.cpu(), mins) and torch.equal(go._max.cpu(), maxs)
+    for bits, sym in ((4, False), (8, True), (3, False)):
+        s, z = go.get_quant_params(bits, sym)
+        rs, rz = o_aff.affine_params_array(mins.numpy(), maxs.numpy(), bits, sym)
+        assert np.array_equal(s.cpu().numpy(), rs) and np.array_equal(z.cpu().numpy(), rz)
+    pc = PerChannelMinMaxObserver(0)
+    pc.update(w.to(DEV))
+    ref = o_aff.PerChannelMinMaxObserver(0)
+    ref.update(w)
+    s, z = pc.get_quant_params(4, False)
+    rs, rz = ref.get_quant_params(4, False)
+    assert np.array_equal(s.cpu().numpy(), rs) and np.array_equal(z.cpu().numpy(), rz)
+
+
+def test_int4_pack_kats():  # Int4PackedTensorTests.cs
+    from llmcompressorsharp_b200 import Int4PackedTensor
+
+    p = Int4PackedTensor.from_float(torch.tensor([-8.5, -7.0, 0.0, 7.0, 9.0], device=DEV), 1.0, 0, True)
+    assert p.dequantize().tolist() == [-7, -7, 0, 7, 7]
+    assert len(Int4PackedTensor.from_float(torch.arange(1.0, 9.0, device=DEV), 1.0, 0, True).packed_bytes) == 4
+    vals = [-7.0, -3.0, 0.0, 4.0, 7.0, -2.0]
+    p = Int4PackedTensor.from_float(torch.tensor(vals, device=DEV), 1.0, 0, True)
+    r = Int4PackedTensor.from_packed_bytes(p.packed_bytes, 6, 1.0, 0, True)
+    assert r.dequantize().tolist() == vals
+    ref = o_fq.Int4PackedTensor.from_float(torch.tensor(vals), 1.0, 0, True)
+    assert p.packed_bytes == ref.packed_bytes
+    p = Int4PackedTensor.from_float(torch.tensor([-8.0, 0.0, 7.0], device=DEV), 1.0, 8, False)
+    assert p.packed_bytes == o_fq.Int4PackedTensor.from_float(torch.tensor([-8.0, 0.0, 7.0]), 1.0, 8, False).packed_bytes
+
+
+# --------------------------------------------------------------------------- GPTQ
+
+def gptq_case(m, n, seed, dtype=torch.float32):
+    g = gen(seed)
+    x = torch.randn(4 * n, n, generator=g) @ (torch.eye(n) + 0.2 * torch.randn(n, n, generator=g) / n ** 0.5)
+    h = x.t() @ x
+    w = (torch.randn(m, n, generator=g) * 0.02).to(dtype)
+    return w, h
+
+
+def check_gptq(w, h, cfg_kw, dev_res=None, min_agree=0.999):
+    from llmcompressorsharp_b200 import GPTQConfig, gptq_quantize_u
+
+    hinv = o_hess.hessian_inverse(h, 0.01)
+    u = o_hess.upper_factor(hinv)
+    ocfg = o_gptq.GPTQConfig(**cfg_kw)
+    wq_r, codes_r, s_r, z_r = o_gptq.gptq_quantize_u(w, u, ocfg)
+    res = dev_res or gptq_quantize_u(w.to(DEV), u.to(DEV), GPTQConfig(**cfg_kw))
+    n_par = 1 if cfg_kw.get("strategy") == "tensor" else None
+    assert np.array_equal(res.scales.cpu().numpy().reshape(-1), s_r.reshape(-1)[:n_par])
+    assert np.array_equal(res.zero_points.cpu().numpy().reshape(-1), z_r.reshape(-1)[:n_par])
+    m, n = w.shape
+    # unpack device codes and compare integer codes
+    if res.codes is not None and ocfg.num_bits <= 4:
+        zp_e = torch.from_numpy(np.asarray(z_r))
+        zp_e = zp_e.expand(m, 1) if zp_e.shape[1] == 1 else zp_e[:, torch.arange(n) // ocfg.group_size]
+        ref_codes = o_fq.pack_int4_rows(codes_r, zp_e)
+        agree_bytes = (res.codes.cpu() == ref_codes).float().mean().item()
+        assert agree_bytes >= 1 - 2 * (1 - min_agree)
+    agree = (res.wq.cpu() == wq_r).float().mean().item()
+    assert agree >= min_agree, agree
+    e_dev = o_gptq.reconstruction_error(w, res.wq.cpu(), h)
+    e_ref = o_gptq.reconstruction_error(w, wq_r, h)
+    assert abs(e_dev / e_ref - 1) < 0.01
+    return res
+
+
+@pytest.mark.parametrize("strategy", ["tensor", "channel", "group"])
+@pytest.mark.parametrize("bits,sym", [(4, True), (4, False), (8, True)])
+@pytest.mark.parametrize("m,n,bs", [(192, 576, 128), (100, 300, 128), (33, 70, 16), (64, 256, 4)])
+def test_gptq_matches_oracle(strategy, bits, sym, m, n, bs):
+    w, h = gptq_case(m, n, m + n + bits)
+    gs = 128 if n % 128 == 0 else 50
+    check_gptq(w, h, dict(num_bits=bits, symmetric=sym, strategy=strategy, block_size=bs, group_size=gs))
+
+
+def test_gptq_bf16_weight_smollm_shape():
+    w, h = gptq_case(576, 1536, 21, torch.bfloat16)
+    check_gptq(w, h, dict(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128))
+
+
+def test_gptq_kats():  # GptqBlockQuantizerTests.cs
+    from llmcompressorsharp_b200 import GPTQConfig, GptqBlockQuantizer
+    from llmcompressorsharp_b200.errors import NotSupportedError
+
+    cfg = GPTQConfig(num_bits=8, symmetric=True, strategy="tensor", block_size=128)
+    assert GptqBlockQuantizer.quantize(torch.zeros(2, 4, device=DEV), torch.eye(4, device=DEV), cfg).abs().max() < 1e-6
+    w = torch.randn(2, 4, generator=gen(1)).to(DEV)
+    cfg16 = GPTQConfig(num_bits=16, symmetric=True, strategy="tensor", block_size=4)
+    assert (GptqBlockQuantizer.quantize(w, torch.eye(4, device=DEV), cfg16) - w).abs().max() < 1e-3
+    w = torch.tensor([[1.0, 2.0], [3.0, 4.0]], device=DEV)
+    cfg1 = GPTQConfig(num_bits=16, symmetric=True, strategy="tensor", block_size=1)
+    assert torch.allclose(GptqBlockQuantizer.quantize(w, torch.eye(2, device=DEV), cfg1), w, atol=0.01)
+    out = GptqBlockQuantizer.quantize(torch.randn(3, 6, device=DEV), torch.eye(6, device=DEV),
+                                      GPTQConfig(num_bits=4, strategy="tensor", block_size=2))
+    assert out.shape == (3, 6) and torch.isfinite(out).all()
+    with pytest.raises(NotSupportedError, match="ActOrder"):
+        GptqBlockQuantizer.quantize(w, torch.eye(2, device=DEV), GPTQConfig(act_order=True))
+
+
+def test_gptq_identity_hinv_equals_rtn():
+    from llmcompressorsharp_b200 import GPTQConfig, RtnConfig, gptq_quantize_u, rtn_quantize
+
+    w = torch.randn(64, 384, generator=gen(3)) * 0.02
+    for strategy in ("tensor", "channel", "group"):
+        res = gptq_quantize_u(w.to(DEV), torch.eye(384, device=DEV),
+                              GPTQConfig(num_bits=4, symmetric=False, strategy=strategy, group_size=128))
+        deq, codes, s, z = rtn_quantize(w.to(DEV), RtnConfig(4, False, strategy, group_size=128))
+        assert torch.equal(res.wq, deq) and torch.equal(res.codes, codes)
+
+
+def test_gptq_modifier_lifecycle():  # GPTQModifierTests.cs / GPTQEndToEndTests.cs
+    from llmcompressorsharp_b200 import (CompressionSession, CompressionState, GPTQConfig, GPTQModifier,
+                                         SessionStatus)
+    from llmcompressorsharp_b200.errors import InvalidOperationError
+
+    torch.manual_seed(0)
+    layer = torch.nn.Linear(16, 8, bias=False).to(DEV)
+    orig = layer.weight.detach().clone()
+    st = CompressionState({"fc.weight": orig.clone()})
+    st.named_modules = {"fc": layer}
+    mod = GPTQModifier(GPTQConfig(num_bits=4, symmetric=True, strategy="tensor", block_size=4))
+    mod.initialize(st)
+    mod.on_start(st)
+    xs = [torch.randn(4, 16, device=DEV) for _ in range(10)]
+    for x in xs:
+        layer(x)
+        mod.on_batch(st)
+    mod.on_end(st)
+    mod.finalize(st)
+    wq = st.named_weights["fc.weight"]
+    assert torch.isfinite(wq).all() and (wq - orig).abs().max() > 1e-6
+    # same result as the oracle given the same calibration inputs
+    acc = o_hess.HessianAccumulator(16)
+    for x in xs:
+        acc.update(x.cpu())
+    hinv = o_hess.hessian_inverse(acc.get_hessian(), 0.01)
+    ref, *_ = o_gptq.gptq_quantize(orig.cpu(), hinv, o_gptq.GPTQConfig(4, True, "tensor", block_size=4))
+    assert (wq.cpu() == ref).float().mean() >= 0.99
+    # no batches -> H = 0 -> pure RTN (GPTQModifierTests.cs:92-110)
+    st2 = CompressionState({"fc.weight": orig.clone()})
+    st2.named_modules = {"fc": layer}
+    s = CompressionSession([GPTQModifier(GPTQConfig(num_bits=8, strategy="tensor", block_size=4))])
+    assert s.run(st2, []) == SessionStatus.COMPLETED
+    rq, *_ = o_rtn.rtn_quantize(orig.cpu(), o_rtn.RtnConfig(8, True, "tensor"))
+    assert torch.equal(st2.named_weights["fc.weight"].cpu(), rq)
+    st3 = CompressionState({"fc.weight": orig.clone()})
+    m3 = GPTQModifier(GPTQConfig())
+    m3.initialize(st3)
+    with pytest.raises(InvalidOperationError, match="NamedModules"):
+        m3.on_start(st3)
+
+
+def test_gptq_modifier_shared_inputs_match_separate():
+    from llmcompressorsharp_b200 import CompressionState, GPTQConfig, GPTQModifier
+
+    torch.manual_seed(1)
+    q = torch.nn.Linear(64, 32, bias=False).to(DEV)
+    k = torch.nn.Linear(64, 16, bias=False).to(DEV)
+    outs = []
+    for share in (False, True):
+        st = CompressionState({"q.weight": q.weight.detach().clone(), "k.weight": k.weight.detach().clone()})
+        st.named_modules = {"q": q, "k": k}
+        mod = GPTQModifier(GPTQConfig(num_bits=4, strategy="group", group_size=32, symmetric=False), share_inputs=share)
+        mod.initialize(st)
+        mod.on_start(st)
+        g = torch.Generator(DEV).manual_seed(5)
+        for _ in range(4):
+            x = torch.randn(8, 64, device=DEV, generator=g)
+            q(x)
+            k(x)
+        mod.on_end(st)
+        mod.finalize(st)
+        outs.append((st.named_weights["q.weight"], st.named_weights["k.weight"]))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+# --------------------------------------------------------------------------- SmoothQuant / AWQ / SparseGPT
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_act_absmax_exact(dtype):
+    from llmcompressorsharp_b200 import act_absmax
+
+    x1 = (torch.randn(3000, 520, generator=gen(1)) * torch.rand(520, generator=gen(2)) * 5).to(dtype)
+    x2 = (torch.randn(2, 100, 520, generator=gen(3))).to(dtype)
+    r = act_absmax(x1.to(DEV))
+    r = act_absmax(x2.to(DEV), r)
+    ref = o_sq.update_running_max(o_sq.update_running_max(None, x1), x2)
+    assert np.array_equal(r.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_smooth_apply_matches_oracle(dtype):
+    from llmcompressorsharp_b200 import act_absmax, smooth_apply
+
+    g = torch.rand(512, generator=gen(4)).to(dtype) + 0.5
+    w = (torch.randn(96, 512, generator=gen(5)) * 0.05).to(dtype)
+    x = torch.randn(256, 512, generator=gen(6)) * torch.where(torch.rand(512, generator=gen(7)) < 0.02, 50.0, 1.0)
+    amax = act_absmax(x.to(dtype).to(DEV))
+    ref_amax = o_sq.act_absmax(x.to(dtype))
+    sw, bw, s = smooth_apply(g.to(DEV), w.to(DEV), amax, 0.5)
+    rg, rw, rs = o_sq.apply_mapping(g, w, ref_amax, 0.5)
+    assert np.abs(s.cpu().numpy() / rs - 1).max() <= 2 ** -22
+    assert torch.equal(sw.cpu(), rg) or rel_fro(sw, rg) < 1e-6
+    assert torch.equal(bw.cpu(), rw) or rel_fro(bw, rw) < 1e-6
+
+
+def test_smoothquant_modifier_kats():  # SmoothQuantModifierTests.cs
+    from llmcompressorsharp_b200 import (CompressionState, SmoothQuantConfig, SmoothQuantMapping,
+                                         SmoothQuantModifier)
+    from llmcompressorsharp_b200.errors import ArgumentOutOfRangeError, InvalidOperationError
+
+    st = CompressionState({"norm.weight": torch.tensor([2.0, 4.0]), "proj.weight": torch.ones(2, 2)})
+    st.layer_activations = {"proj": torch.tensor([[1.0, 4.0], [-0.5, -2.0]])}
+    m = SmoothQuantModifier(SmoothQuantConfig(0.5, [SmoothQuantMapping("norm.weight", "proj.weight", "proj")]))
+    m.initialize(st)
+    m.on_start(st)
+    m.on_batch(st)
+    m.on_end(st)
+    m.finalize(st)
+    assert torch.allclose(st.named_weights["norm.weight"], torch.tensor([2.0, 2.0]), atol=1e-4)
+    assert torch.allclose(st.named_weights["proj.weight"], torch.tensor([[1.0, 2.0], [1.0, 2.0]]), atol=1e-4)
+    st = CompressionState({"g.weight": torch.ones(2), "proj.weight": torch.ones(1, 2)})
+    st.layer_activations = {}
+    m = SmoothQuantModifier(SmoothQuantConfig(0.5, [SmoothQuantMapping("g.weight", "proj.weight", "proj")]))
+    m.initialize(st)
+    m.on_start(st)
+    with pytest.raises(InvalidOperationError, match="activation.*proj"):
+        m.on_end(st)
+    with pytest.raises(ArgumentOutOfRangeError):
+        SmoothQuantModifier(SmoothQuantConfig(1.1))
+
+
+@pytest.mark.parametrize("structure", ["unstructured", "2:4"])
+def test_sparsegpt_matches_oracle(structure):
+    from llmcompressorsharp_b200 import SparseGPTConfig, sparsegpt_prune_u
+
+    w, h = gptq_case(96, 384, 17)
+    u = o_hess.upper_factor(o_hess.hessian_inverse(h, 0.01))
+    cfg = SparseGPTConfig(sparsity=0.5, mask_structure=structure)
+    out, mask = sparsegpt_prune_u(w.to(DEV), u.to(DEV), cfg)
+    n_, m_ = cfg.nm()
+    rout, rmask = o_sp.sparsegpt_prune_u(w, u, 128, 0.5, n_, m_)
+    assert (mask.cpu().bool() == rmask).float().mean() >= 0.999
+    assert rel_fro(out, rout) < 1e-3
+    kept = mask.cpu().reshape(96, -1, 4).sum(-1) if structure == "2:4" else mask.cpu().reshape(96, 3, 128).sum(-1)
+    assert (kept == (2 if structure == "2:4" else 64)).all()
+    assert torch.count_nonzero(out.cpu()[mask.cpu() == 0]) == 0
+
+
+def test_awq_search_matches_oracle():
+    from llmcompressorsharp_b200 import RtnConfig, awq_search
+
+    w = (torch.randn(128, 512, generator=gen(8)) * 0.02).to(torch.bfloat16)
+    a = (torch.rand(512, generator=gen(9)) * 3 + 0.1) * torch.where(torch.rand(512, generator=gen(10)) < 0.02, 30.0, 1.0)
+    cfg = RtnConfig(4, False, "group", group_size=128)
+    s, k, mse = awq_search(w.to(DEV), a.to(DEV), 20, cfg)
+    rs, rk, rmse = o_awq.awq_search(w, a.numpy(), 20, o_rtn.RtnConfig(4, False, "group", group_size=128))
+    assert np.allclose(mse.cpu().numpy(), np.asarray(rmse), rtol=1e-4)
+    assert k == rk or abs(rmse[k - 1] / rmse[rk - 1] - 1) < 1e-4
+    if k == rk:
+        assert rel_fro(s, rs) < 1e-6

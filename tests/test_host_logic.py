@@ -1,0 +1,99 @@
+"""Host-side control flow that needs no GPU: modifier lifecycle, session failure handling,
+target matching (ModifierBaseTests.cs, CompressionSessionTests.cs, TargetMatcherTests.cs)."""
+
+import pytest
+import torch
+
+from llmcompressorsharp_b200.session import (CompressionSession, CompressionState, ModifierBase,
+                                             ModifierLifecycleError, SessionStatus, TargetMatcher)
+
+
+class Recording(ModifierBase):
+    def __init__(self, log, fail_on=None):
+        super().__init__("rec")
+        self.log = log
+        self.fail_on = fail_on
+
+    def _rec(self, what):
+        self.log.append(what)
+        if what == self.fail_on:
+            raise RuntimeError("boom")
+
+    def on_initialize(self, state):
+        self._rec("init")
+
+    def on_start_core(self, state):
+        self._rec("start")
+
+    def on_batch_core(self, state):
+        self._rec(f"batch{state.current_batch_index}")
+
+    def on_end_core(self, state):
+        self._rec("end")
+
+    def on_finalize_core(self, state):
+        self._rec("final")
+
+
+def test_session_lifecycle_order():  # CompressionSessionTests.cs
+    log = []
+    st = CompressionState({"w": torch.zeros(1)})
+    s = CompressionSession([Recording(log)])
+    assert s.run(st, [1, 2]) == SessionStatus.COMPLETED
+    assert log == ["init", "start", "batch0", "batch1", "end", "final"]
+    with pytest.raises(ModifierLifecycleError):
+        s.run(st, [])
+
+
+def test_session_failure_still_finalizes():  # CompressionSession.cs:91-99
+    log = []
+    s = CompressionSession([Recording(log, fail_on="batch1")])
+    assert s.run(CompressionState({}), [1, 2, 3]) == SessionStatus.FAILED
+    assert isinstance(s.failure, RuntimeError)
+    assert log[-1] == "final" and "end" not in log
+
+
+def test_modifier_guards():  # ModifierBase.cs:47-116
+    m = Recording([])
+    st = CompressionState({})
+    with pytest.raises(ModifierLifecycleError):
+        m.on_start(st)
+    m.initialize(st)
+    with pytest.raises(ModifierLifecycleError):
+        m.initialize(st)
+    with pytest.raises(ModifierLifecycleError):
+        m.on_batch(st)
+    m.on_start(st)
+    m.on_end(st)
+    with pytest.raises(ModifierLifecycleError):
+        m.on_batch(st)
+    m.finalize(st)
+    with pytest.raises(ModifierLifecycleError):
+        m.finalize(st)
+
+
+def test_target_matcher():  # TargetMatcher.cs:22-86
+    names = ["model.layer.0.q_proj.weight", "model.lm_head.weight", "fc.weight"]
+    assert TargetMatcher.filter(names, [], []) == names
+    assert TargetMatcher.filter(names, ["model.layer.*"], ["*.lm_head.*"]) == ["model.layer.0.q_proj.weight"]
+    assert TargetMatcher.filter(names, ["fc.weight"], []) == ["fc.weight"]
+    assert TargetMatcher.filter(names, ["*"], ["*.weight"]) == []
+
+
+def test_rtn_config_rejects_token():
+    from llmcompressorsharp_b200.errors import NotSupportedError
+    from llmcompressorsharp_b200.rtn import RtnConfig
+
+    with pytest.raises(NotSupportedError):
+        RtnConfig(strategy="token").to_c()
+
+
+def test_gptq_config_defaults():  # GPTQConfig.cs:22-59
+    from llmcompressorsharp_b200.gptq import GPTQConfig
+
+    c = GPTQConfig()
+    assert (c.num_bits, c.symmetric, c.strategy, c.channel_axis, c.block_size, c.act_order) == (4, True, "channel", 0,
+                                                                                                 128, False)
+    assert abs(c.dampening_frac - 0.01) < 1e-9
+    q = c.to_c()
+    assert q.num_bits == 4 and q.strategy == 1 and q.block_size == 128
