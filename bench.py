@@ -1,0 +1,470 @@
+#!/usr/bin/env python
+"""GPTQ W4A16 (asym int4, group 128, damp 0.01, block 128) on a random-init Llama-3-8B-shaped
+model with 512 x 2048 = 1,048,576 calibration tokens: wall-clock seconds per full job, with
+the Hessian kernel's throughput and roofline.
+
+One step = the whole one-shot job for all 32 decoder layers: per layer, the Hessian of each
+of the 4 distinct input sites (attention input -> q/k/v, o input, MLP input -> gate/up, down
+input) over all calibration tokens on tcgen05 tensor cores, the damped Cholesky factor U of
+each, and the GPTQ column-block solve of all 7 weights producing packed int4 codes, scales
+and zero-points.
+
+Synthetic data (no network): weights bf16 ~N(0, 0.02) per layer; activations bf16 ~N(0, 1),
+one seeded [tokens, d] set per input site, shared by all layers.  The activations (52 GiB)
+are far larger than L2, so every timed step streams them from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun): calibration tokens are split across ranks, each rank accumulates partial
+Hessians for every layer, the partials are summed onto each layer's owner over NCCL, and the
+owners (layers dealt round-robin) solve their layers: total work fixed ("strong").
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MODEL = {"name": "llama3-8b", "hidden": 4096, "intermediate": 14336, "heads": 32, "kv_heads": 8, "layers": 32}
+METRIC = "GPTQ W4A16 wall-clock s (Llama-3-8B shape)"
+UNIT = "s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--layers", type=int, default=MODEL["layers"])
+    p.add_argument("--tokens", type=int, default=512 * 2048)
+    p.add_argument("--chunk", type=int, default=65536, help="calibration rows per Hessian update call")
+    p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of this GPU during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+                power.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        loaded = [s for s, p in zip(sm, power) if p > 300] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ------------------------------------------------------------------------------ helpers
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            j = json.load(f)
+        return float(j["bf16_tflops"]), float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def sites_for(model):
+    from llmcompressorsharp_b200.pipeline import llama_sites
+
+    return llama_sites(model["hidden"], model["intermediate"], model["heads"], model["kv_heads"])
+
+
+# ------------------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from llmcompressorsharp_b200 import _lib
+    from llmcompressorsharp_b200.gptq import GPTQConfig
+    from llmcompressorsharp_b200.pipeline import GptqPipeline
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    sites = sites_for(MODEL)
+    L = args.layers
+    T_local = args.tokens // world
+    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128,
+                     dampening_frac=0.01)
+    owners = {l: l % world for l in range(L)}
+    mine = [l for l in range(L) if owners[l] == rank]
+
+    # ---- synthetic inputs, resident in HBM
+    g = torch.Generator(dev)
+    acts = {}
+    for i, s in enumerate(sites):
+        g.manual_seed(1000 + 17 * rank + i)
+        acts[s.name] = _randn_bf16(T_local, s.d, dev, g)
+    weights = {}
+    for l in mine:
+        weights[l] = {}
+        for si, s in enumerate(sites):
+            for wi, (wname, m) in enumerate(s.weights):
+                g.manual_seed(10_000 + 97 * l + 7 * si + wi)
+                weights[l][wname] = _randn_bf16(m, s.d, dev, g, std=0.02)
+    pipe = GptqPipeline(sites, cfg, dev, chunk_rows=args.chunk)
+    outputs = {l: pipe.alloc_outputs(weights[l]) for l in mine}
+    hbufs = None
+    if world > 1:
+        hbufs = {l: {s.name: torch.empty(s.d, s.d, dtype=torch.float32, device=dev) for s in sites} for l in range(L)}
+    torch.cuda.synchronize()
+
+    hess_events = []
+
+    def step(record=False):
+        """One full job; returns nothing (work is enqueued on the current stream)."""
+        if world == 1:
+            for l in range(L):
+                for s in sites:
+                    if record:
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                    pipe.accumulate(s, acts[s.name])
+                    if record:
+                        e1.record()
+                        hess_events.append((e0, e1, s.d, acts[s.name].shape[0]))
+                    pipe.solve_site(s, pipe.hessian_ptr(s.name), weights[l], outputs[l])
+            return
+        # phase 1: partial Hessians of every layer over this rank's tokens
+        for l in range(L):
+            for s in sites:
+                if record:
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                pipe.accumulate(s, acts[s.name], out_h=hbufs[l][s.name])
+                if record:
+                    e1.record()
+                    hess_events.append((e0, e1, s.d, acts[s.name].shape[0]))
+        # phase 2: sum partials onto each layer's owner (NCCL reduce, one group)
+        reqs = []
+        for l in range(L):
+            for s in sites:
+                reqs.append(dist.reduce(hbufs[l][s.name], dst=owners[l], op=dist.ReduceOp.SUM, async_op=True))
+        for r in reqs:
+            r.wait()
+        # phase 3: owners solve
+        for l in mine:
+            for s in sites:
+                pipe.solve_site(s, hbufs[l][s.name].data_ptr(), weights[l], outputs[l])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    launches0 = _lib.launch_count(local)
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step(record=True)
+    t1.record()
+    barrier()
+    clk = clocks.stop()
+    launches = _lib.launch_count(local) - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    hess_ms = sum(a.elapsed_time(b) for a, b, _, _ in hess_events) / args.steps
+    hess_launches = sum((rows + args.chunk - 1) // args.chunk for _, _, _, rows in hess_events)
+    hess_flops_computed = sum(d * (d + 1) * rows for _, _, d, rows in hess_events)  # SYRK: d(d+1)T
+    hess_flops_full = sum(2 * d * d * rows for _, _, d, rows in hess_events)
+    tot_hess_ms = sum(a.elapsed_time(b) for a, b, _, _ in hess_events)
+    if world > 1:
+        t = torch.tensor([ms, hess_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, hess_ms = float(t[0]), float(t[1])
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local, hbufs)
+    if world > 1:
+        et = torch.tensor([e2e["value"] if e2e else 0.0], device=dev, dtype=torch.float64)
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        if e2e:
+            e2e["value"] = float(et[0])
+
+    if rank == 0:
+        burst, sustained, hbm, src = peaks()
+        per_launch_flops = hess_flops_computed / max(1, hess_launches)
+        per_launch_ms = tot_hess_ms / max(1, hess_launches)
+        achieved = per_launch_flops / (per_launch_ms * 1e-3) / 1e12
+        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(args)
+        line = {
+            "metric": METRIC, "value": round(ms / 1e3, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "GPTQ W4A16 asym g128 damp 0.01 block 128, Llama-3-8B shape "
+                                   f"({args.layers} layers x 7 Linear, hidden 4096, intermediate 14336, 32/8 heads), "
+                                   f"{args.tokens} calibration tokens (512 x 2048), bf16",
+                       "layers": args.layers, "tokens": args.tokens, "update_rows": args.chunk,
+                       "parallelism": f"tokens split over {world} GPU(s), layers dealt round-robin",
+                       "activations": "one seeded bf16 [tokens, d] set per input site, shared by all layers",
+                       "l2": "inputs larger than L2 (52 GiB of activations streamed per step)"},
+            "hessian_tflops": round(hess_flops_full / (tot_hess_ms * 1e-3) / 1e12 if tot_hess_ms else 0, 1),
+            "hessian_tflops_note": "Hessian TFLOP/s with the full-GEMM count 2*d^2*T (the metric's definition); "
+                                   "the kernel computes the symmetric half",
+            "hessian_ms_per_step": round(hess_ms, 2),
+            "roofline": {"kernel": "syrk_tc_kernel (Hessian H += X^T X, tcgen05)", "bound": "tensor",
+                         "achieved": round(achieved, 1), "peak": sustained, "unit": "TFLOP/s",
+                         "frac": round(achieved / sustained, 3),
+                         "peak_note": f"{src} sustained bf16 (kernel runs inside a ~{ms / 1e3:.0f} s step)",
+                         "algorithmic": "d(d+1)T FLOP per launch (symmetric rank-k update of T tokens)",
+                         "traffic": SYRK_TRAFFIC_PER_LAUNCH},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    pipe.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+# DRAM bytes per syrk_tc launch (d = 4096, 65,536 tokens) from the committed ncu capture
+# profiles/syrk_tc_kernel.md; filled in when that capture exists.
+SYRK_TRAFFIC_PER_LAUNCH = None
+
+
+def _randn_bf16(m, n, dev, g, std=1.0):
+    import torch
+
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    rows = max(1, (1 << 28) // n)
+    for r0 in range(0, m, rows):
+        r1 = min(m, r0 + rows)
+        out[r0:r1] = (torch.randn(r1 - r0, n, device=dev, generator=g) * std).to(torch.bfloat16)
+    return out
+
+
+# ------------------------------------------------------------------------------ end to end
+def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local, hbufs):
+    """Same job through the public API with HOST buffers: every step copies the weights of
+    this rank's layers and the calibration activations from pinned host memory, runs the
+    job, and copies codes/scales/zero-points back to pinned host memory."""
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local)
+    h_acts = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in acts.items()}
+    for k in acts:
+        h_acts[k].copy_(acts[k])
+    h_w = {l: {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in weights[l].items()} for l in mine}
+    for l in mine:
+        for k in weights[l]:
+            h_w[l][k].copy_(weights[l][k])
+    h_out = {l: {k: {f: torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for f, t in o.items()}
+                 for k, o in outputs[l].items()} for l in mine}
+    h2d = sum(t.numel() * t.element_size() for t in h_acts.values())
+    h2d += sum(t.numel() * t.element_size() for l in mine for t in h_w[l].values())
+    d2h = sum(t.numel() * t.element_size() for l in mine for o in h_out[l].values() for t in o.values())
+    owners = {l: l % world for l in range(args.layers)}
+
+    def e2e_step():
+        for k in acts:
+            acts[k].copy_(h_acts[k], non_blocking=True)
+        if world == 1:
+            for l in mine:
+                for k in weights[l]:
+                    weights[l][k].copy_(h_w[l][k], non_blocking=True)
+                pipe.run_layer(acts, weights[l], outputs[l])
+                for k, o in outputs[l].items():
+                    for f, t in o.items():
+                        h_out[l][k][f].copy_(t, non_blocking=True)
+            return
+        for l in range(args.layers):
+            for s in sites:
+                pipe.accumulate(s, acts[s.name], out_h=hbufs[l][s.name])
+        reqs = [dist.reduce(hbufs[l][s.name], dst=owners[l], async_op=True) for l in range(args.layers) for s in sites]
+        for r in reqs:
+            r.wait()
+        for l in mine:
+            for k in weights[l]:
+                weights[l][k].copy_(h_w[l][k], non_blocking=True)
+            for s in sites:
+                pipe.solve_site(s, hbufs[l][s.name].data_ptr(), weights[l], outputs[l])
+            for k, o in outputs[l].items():
+                for f, t in o.items():
+                    h_out[l][k][f].copy_(t, non_blocking=True)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    e2e_step()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    t1.record()
+    barrier()
+    ms = t0.elapsed_time(t1) / args.e2e_steps
+    return {"value": round(ms / 1e3, 4), "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "steps": args.e2e_steps, "api": "llmcompressorsharp_b200.pipeline.GptqPipeline over the C ABI, host buffers"}
+
+
+# ------------------------------------------------------------------------------ CPU side
+def cpu_sample_seconds(threads: int, sample_tokens: int = 4096):
+    """Times the oracle (a PyTorch-CPU restatement of the reference's TorchSharp path) on a
+    bounded sample of the job and extrapolates to the full job linearly in tokens, layers
+    and weights.  Returns (seconds for the full job, description)."""
+    import torch
+
+    from oracle import gptq as o_gptq, hessian as o_hess
+
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    d = MODEL["hidden"]
+    x = torch.randn(sample_tokens, d, generator=g).to(torch.bfloat16)
+    acc = o_hess.HessianAccumulator(d)
+    t = time.perf_counter()
+    acc.update(x)
+    t_h = time.perf_counter() - t  # d=4096 site, sample_tokens rows
+    h = acc.get_hessian()
+    t = time.perf_counter()
+    hinv = o_hess.hessian_inverse(h, 0.01)
+    u = o_hess.upper_factor(hinv)
+    t_chol = time.perf_counter() - t  # d = 4096
+    m_s = 256
+    w = (torch.randn(m_s, d, generator=g) * 0.02).to(torch.bfloat16)
+    cfg = o_gptq.GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128)
+    t = time.perf_counter()
+    o_gptq.gptq_quantize_u(w, u, cfg)
+    t_gptq = time.perf_counter() - t  # 256 x 4096
+    hid, inter, L, T = MODEL["hidden"], MODEL["intermediate"], MODEL["layers"], 512 * 2048
+    # Hessian: 3 sites of width hidden + 1 of width intermediate, time ~ d^2 T
+    hess = t_h * (T / sample_tokens) * (3 + (inter / hid) ** 2) * L
+    chol = t_chol * (3 + (inter / hid) ** 3) * L
+    # GPTQ column loop: per-column vector ops over m rows; time ~ n * (c0 + c1 * m) ~ m * n for
+    # large m; tail GEMMs ~ m n^2.  Scale by m*n (lower bound for the n^2 tail).
+    kv = MODEL["kv_heads"] * (hid // MODEL["heads"])
+    mn = (2 * hid * hid + 2 * kv * hid + 2 * inter * hid) + inter * hid * (inter / hid)
+    gptq_t = t_gptq * (mn / (m_s * d)) * L
+    total = hess + chol + gptq_t
+    desc = (f"oracle on {threads} host threads: Hessian of {sample_tokens} tokens at d={d} ({t_h:.2f} s), damped "
+            f"Cholesky inverse + U at d={d} ({t_chol:.2f} s), GPTQ of a {m_s}x{d} weight ({t_gptq:.2f} s); "
+            "extrapolated to 32 layers x 4 sites x 1,048,576 tokens (d^2 T), 128 factorisations (d^3) and 224 "
+            "weights (m n^2 tail at n=14336 scaled from m n) — a lower bound on the reference, whose per-row "
+            "P/Invoke loops this vectorised restatement does not pay")
+    return total, desc
+
+
+def cpu_baseline(args):
+    threads = os.cpu_count() or 1
+    total, desc = cpu_sample_seconds(threads)
+    return {"value": round(total, 1), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU algorithm (the oracle restatement; the C#/.NET
+    reference cannot be built in this image) on all host threads, same metric and config."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    steps = []
+    desc = ""
+    threads = os.cpu_count() or 1
+    if args.warmup > 0:
+        cpu_sample_seconds(threads, 1024)  # warm the CPU kernels once; a step is already seconds long
+    for _ in range(args.steps):
+        total, desc = cpu_sample_seconds(threads)
+        steps.append(total)
+    v = statistics.median(steps)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "GPTQ W4A16 asym g128, Llama-3-8B shape, 1,048,576 calibration tokens",
+                       "layers": MODEL["layers"], "tokens": 512 * 2048},
+            "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
+            "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

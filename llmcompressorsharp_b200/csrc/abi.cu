@@ -30,6 +30,20 @@ llmc_status fail(llmc_status st, const char* fmt, ...) {
     return st;
 }
 
+// Synchronises the stream and reports a bounded device wait that gave up (error word 2,
+// written by the tensor-core kernels) as LLMC_ERR_TIMEOUT, clearing the word.
+llmc_status device_error_check(llmc_ctx* ctx) {
+    LLMC_CUDA_TRY(cudaMemcpyAsync(ctx->hflags + 2, ctx->dflags + 2, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (ctx->hflags[2] != 0) {
+        ctx->hflags[2] = 0;
+        LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags + 2, 0, sizeof(int), ctx->stream));
+        return fail(LLMC_ERR_TIMEOUT, "a bounded wait inside a tensor-core kernel gave up; results of the "
+                    "affected calls are incomplete");
+    }
+    return LLMC_OK;
+}
+
 llmc_status workspace(llmc_ctx* ctx, size_t bytes, void** out) {
     if (bytes > ctx->ws_bytes) {
         if (ctx->ws) {
@@ -124,6 +138,7 @@ llmc_status llmc_init(int32_t device, llmc_ctx** out) {
     c->sm_count = prop.multiProcessorCount;
     cudaError_t e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&c->dflags, 16 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->dflags, 0, 16 * sizeof(int));
     if (e == cudaSuccess) e = cudaMallocHost(&c->hflags, 16 * sizeof(int));
     if (e != cudaSuccess) {
         if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -156,8 +171,7 @@ llmc_status llmc_set_stream(llmc_ctx* ctx, void* stream) {
 
 llmc_status llmc_sync(llmc_ctx* ctx) {
     CTX_CHECK(ctx);
-    LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-    return LLMC_OK;
+    return device_error_check(ctx);
 }
 
 llmc_status llmc_launch_count(llmc_ctx* ctx, int64_t* out) {
@@ -208,6 +222,10 @@ llmc_status llmc_hessian_update(llmc_hessian* h, const void* x, int32_t dtype, i
             int64_t split = (2 * (int64_t)ctx->sm_count + upper - 1) / upper;
             const int64_t max_split = (rows + 1023) / 1024;
             if (split > max_split) split = max_split;
+            // Each split sums <= 2048 products sequentially in fp32 before one atomic add,
+            // which keeps the accumulated rounding near the oracle's blocked sgemm.
+            const int64_t min_split = (rows + 2047) / 2048;
+            if (split < min_split) split = min_split;
             if (split < 1) split = 1;
             GemmArgs g{h->d, h->d, rows, x, ld, 1, dtype, x, ld, 0, dtype, h->h, h->d, 1.f, 1.f};
             g.c_mode = 2;
@@ -224,6 +242,7 @@ llmc_status llmc_hessian_get(llmc_hessian* h, float* out) {
     NULL_CHECK(h, "hessian");
     CTX_CHECK(h->ctx);
     NULL_CHECK(out, "out");
+    LLMC_TRY(device_error_check(h->ctx));
     return symmetrize_from_upper(h->ctx, h->h, h->d, h->d, out, h->d);
 }
 

@@ -202,6 +202,7 @@ llmc_status rec(llmc_ctx* ctx, const CholWs& w, int64_t off, int64_t n, int keep
 }
 
 llmc_status read_flags(llmc_ctx* ctx, int* f0, int* f1) {
+    LLMC_TRY(device_error_check(ctx));
     LLMC_CUDA_TRY(cudaMemcpyAsync(ctx->hflags, ctx->dflags, 2 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
     LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     *f0 = ctx->hflags[0];

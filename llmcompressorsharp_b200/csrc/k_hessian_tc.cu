@@ -1,8 +1,452 @@
-// tcgen05 symmetric rank-k update (placeholder until the tensor-core kernel lands).
+// Hessian accumulation H += X^T X on the 5th-generation tensor cores (sm_100a).
+//
+// Reference: HessianAccumulator.Update (src/LLMCompressorSharp.TorchExtensions/Hessian/
+// HessianAccumulator.cs:47-67) — x.to(fp32).reshape(-1, d); H.add_(flat^T flat).  For bf16 /
+// fp16 activations every product is exact in fp32, so an fp32-accumulating tensor-core
+// GEMM gives the reference's result up to summation order.
+//
+// Shape of the work: C[d, d] += A[d, T] B[T, d] with A = X^T and B = X, i.e. both operands
+// are the same row-major X [T, d] read "MN-major" (features contiguous, tokens = K).  Only
+// tiles that touch the upper triangle are computed (the symmetric lower half is implied).
+//
+// Per CTA (one per SM, 128 threads):
+//   * tile 128 (rows of H) x 256 (columns of H), K-block 64 tokens, 4-stage ring in shared
+//     memory filled by TMA (2 + 4 boxes of 64 features x 64 tokens, 128-byte swizzle, no
+//     multicast, cluster of one);
+//   * one elected thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16)
+//     into a 128 x 256 fp32 accumulator in TMEM and releases each stage with
+//     tcgen05.commit;
+//   * accuracy: the tensor core's fp32 accumulation truncates, so TMEM only ever holds the
+//     sum of KF = 8 k-blocks (512 tokens).  Two TMEM accumulators alternate: while the MMA
+//     issuer fills one, eight epilogue warps fold the other into fp32 registers with
+//     round-to-nearest adds (each warp owns 32 rows x 128 columns);
+//   * end of a unit: registers -> padded shared staging -> one bulk reduce-add
+//     (cp.reduce.async.bulk .add.f32) per half row into H, so H accumulates across calls
+//     and across token splits without a read pass.
+// Work units are (tile, token split); units of one split run in the same wave so that the
+// X rows they stream are shared through L2.
+// Every wait is bounded: on expiry the kernel raises an error word, drains its own
+// in-flight copies (again bounded), frees TMEM and returns.
 #include "ops.h"
 
+#include <cuda.h>
+
 namespace llmc {
-llmc_status syrk_tc(llmc_ctx*, const void*, int, int64_t, int64_t, int64_t, float*, int64_t) {
-    return LLMC_ERR_UNSUPPORTED;
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int EPI_WARPS = 8, NT = 32 * (2 + EPI_WARPS);  // producer, MMA issuer, 8 epilogue warps
+constexpr int KF = 8;          // k-blocks (512 tokens) accumulated in TMEM before promotion
+constexpr int TMEM_COLS = 2 * BN;  // two 128 x 256 fp32 accumulators
+constexpr int A_BYTES = BM * BK * 2;             // 16 KB
+constexpr int B_BYTES = BN * BK * 2;             // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
+constexpr int BOX_BYTES = 64 * BK * 2;           // 8 KB: 64 features x 64 tokens
+constexpr int STG_LD = BN + 4;                   // fp32 staging row stride (floats)
+constexpr int SMEM_MAIN = STAGES * STAGE_BYTES;  // 192 KB (reused as 130 KB staging)
+constexpr int SMEM_BYTES = SMEM_MAIN + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr unsigned WAIT_LIMIT = 1u << 26;        // try_wait attempts before giving up
+constexpr int MAX_TJ = 160;                      // d <= 40960
+
+static_assert(BM * STG_LD * 4 <= SMEM_MAIN, "epilogue staging must fit in the stage ring");
+
+struct SyrkArgs {
+    float* H;
+    int64_t ldh;
+    int d;
+    int nti, ntj;
+    int ntiles;
+    int kb_total;     // k-blocks over all rows
+    int splits;       // token splits
+    int kb_per_split;
+    int tile_off[MAX_TJ + 1];  // first tile index of column-panel tj
+    int* err;         // device error word (bit 0: a wait timed out)
+    uint32_t idesc;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; returns false (and raises the abort flag) when it gives up or when
+// another thread has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
+    for (unsigned i = 0; i < WAIT_LIMIT; i++) {
+        if (mbar_try_wait(b, parity)) return true;
+        if ((i & 255u) == 255u && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    atomicOr(err, 1);
+    return false;
+}
+
+// Bounded wait that ignores the abort flag (used only to drain after an abort).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* b, uint32_t parity) {
+    for (unsigned i = 0; i < WAIT_LIMIT; i++)
+        if (mbar_try_wait(b, parity)) return;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// UMMA shared-memory descriptor for an MN-major, 128-byte-swizzled operand whose 64-element
+// MN chunks are `lbo` bytes apart and whose 8-row K groups are 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);             // start address  [0,14)
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;        // leading byte offset [16,30)
+    d |= (uint64_t)((1024u >> 4) & 0x3FFFu) << 32;      // stride byte offset  [32,46)
+    d |= (uint64_t)1 << 46;                             // descriptor version (sm100)
+    d |= (uint64_t)2 << 61;                             // layout: SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const float* ssrc, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;"
+                 ::"l"(reinterpret_cast<uint64_t>(gdst)), "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void unit_tile(const SyrkArgs& a, int tile, int* ti, int* tj) {
+    int lo = 0, hi = a.ntj - 1;  // find tj with tile_off[tj] <= tile < tile_off[tj+1]
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.tile_off[mid] <= tile) lo = mid;
+        else hi = mid - 1;
+    }
+    *tj = lo;
+    *ti = tile - a.tile_off[lo];
+}
+
+__global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ CUtensorMap xmap, const SyrkArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SMEM_MAIN);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;   // [2] accumulator b ready for promotion
+    uint64_t* tempty = tfull + 2;       // [2] accumulator b folded, MMA may reuse it
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* staging = reinterpret_cast<float*>(smem);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], EPI_WARPS);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int total_units = a.ntiles * a.splits;
+    uint32_t prod_it = 0, mma_it = 0, cc = 0;  // cc: chunks processed (MMA issuer / epilogue)
+    int pend_par[STAGES];  // producer: parity of the latest load issued into each stage (-1: none)
+#pragma unroll
+    for (int s = 0; s < STAGES; s++) pend_par[s] = -1;
+    int commit_par[2] = {-1, -1};  // MMA issuer: parity of its latest commit to tfull[b]
+
+    for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
+        const int split = u / a.ntiles, tile = u % a.ntiles;
+        int ti, tj;
+        unit_tile(a, tile, &ti, &tj);
+        const int kb0 = split * a.kb_per_split;
+        const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
+        const int nchunks = (kb1 - kb0 + KF - 1) / KF;
+        const int i0 = ti * BM, j0 = tj * BN;
+
+        if (warp == 0) {
+            if (lane == 0) {
+                // ---- TMA producer
+                for (int kb = kb0; kb < kb1; kb++, prod_it++) {
+                    const int s = prod_it % STAGES;
+                    const uint32_t ph = (prod_it / STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    unsigned char* st = smem + s * STAGE_BYTES;
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    const int y = kb * BK;
+#pragma unroll
+                    for (int b = 0; b < BM / 64; b++) tma_load_2d(st + b * BOX_BYTES, &xmap, i0 + 64 * b, y, &full[s]);
+#pragma unroll
+                    for (int b = 0; b < BN / 64; b++)
+                        tma_load_2d(st + A_BYTES + b * BOX_BYTES, &xmap, j0 + 64 * b, y, &full[s]);
+                    pend_par[s] = (int)((prod_it / STAGES) & 1u);
+                }
+            }
+            __syncwarp();
+        } else if (warp == 1) {
+            if (lane == 0) {
+                // ---- MMA issuer: chunk c accumulates into TMEM buffer (cc & 1)
+                uint32_t c_it = cc;
+                for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
+                    const int b = (int)(c_it & 1u);
+                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    tc_fence_after();
+                    const uint32_t dst = tmem + (uint32_t)(b * BN);
+                    const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
+                    bool ok = true;
+                    for (int kb = k0; kb < k1; kb++, mma_it++) {
+                        const int s = mma_it % STAGES;
+                        const uint32_t ph = (mma_it / STAGES) & 1u;
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t abase = smem_u32(smem + s * STAGE_BYTES);
+                        const uint32_t bbase = abase + A_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            // 16 tokens = 2 swizzle atoms of 8 rows x 128 B
+                            const uint64_t da = smem_desc_mn_sw128(abase + kk * 2048, BOX_BYTES);
+                            const uint64_t db = smem_desc_mn_sw128(bbase + kk * 2048, BOX_BYTES);
+                            umma_f16(dst, da, db, a.idesc, (kb > k0 || kk > 0) ? 1u : 0u);
+                        }
+                        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                    }
+                    umma_commit(&tfull[b]);  // chunk complete (fires even if the loop broke early)
+                    commit_par[b] = (int)((c_it >> 1) & 1u);
+                    if (!ok) break;
+                }
+            }
+            __syncwarp();
+        } else {
+            // ---- epilogue warps: TMEM lane quadrant q (a warp may only touch lanes
+            // [32*(warp%4), +32)), column half h.
+            const int e = warp - 2, q = warp % 4, h = e / 4;
+            float acc[BN / 2];
+#pragma unroll
+            for (int i = 0; i < BN / 2; i++) acc[i] = 0.f;
+            uint32_t c_it = cc;
+            for (int c = 0; c < nchunks; c++, c_it++) {
+                const int b = (int)(c_it & 1u);
+                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
+                if (!__all_sync(0xffffffffu, have ? 1 : 0)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int part = 0; part < 4; part++) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + h * 128 + part * 32), v);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) acc[part * 32 + i] = __fadd_rn(acc[part * 32 + i], __uint_as_float(v[i]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+            }
+            // Every stage of this unit has been read by its MMAs (the last tfull implies it),
+            // so the stage ring is free for staging.
+            const int r = q * 32 + lane;
+            const int64_t gi = (int64_t)i0 + r;
+            float* srow = staging + (size_t)r * STG_LD + h * 128;
+            if (!*abort_flag) {
+#pragma unroll
+                for (int i = 0; i < BN / 2; i += 4)
+                    *reinterpret_cast<float4*>(srow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                const int jc = j0 + h * 128;
+                const int ncols = min(BN / 2, a.d - jc);
+                if (gi < a.d && ncols > 0) {
+                    bulk_reduce_add_f32(a.H + gi * a.ldh + jc, srow, (uint32_t)ncols * 4u);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                }
+            }
+        }
+        cc += (uint32_t)nchunks;
+        __syncthreads();  // staging consumed before the next unit's loads reuse the ring
+    }
+
+    // Drain: every bulk reduce finishes; after an abort, also wait (bounded) for the TMA
+    // loads this CTA issued and for its MMAs, so that nothing touches shared memory or
+    // TMEM after they are released.
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (*abort_flag) {
+        if (warp == 0 && lane == 0)
+            for (int s = 0; s < STAGES; s++)
+                if (pend_par[s] >= 0) mbar_wait_drain(&full[s], (uint32_t)pend_par[s]);
+        if (warp == 1 && lane == 0)
+            for (int b = 0; b < 2; b++)
+                if (commit_par[b] >= 0) mbar_wait_drain(&tfull[b], (uint32_t)commit_par[b]);
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+// ---- host side -------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+uint32_t make_idesc(int dtype) {
+    const uint32_t fmt = dtype == LLMC_DTYPE_BF16 ? 1u : 0u;  // kind::f16 operand: 0 = F16, 1 = BF16
+    uint32_t d = 0;
+    d |= 1u << 4;                 // D format: F32
+    d |= fmt << 7;                // A format
+    d |= fmt << 10;               // B format
+    d |= 1u << 15;                // A major: MN
+    d |= 1u << 16;                // B major: MN
+    d |= (uint32_t)(BN >> 3) << 17;
+    d |= (uint32_t)(BM >> 4) << 24;
+    return d;
+}
+
+}  // namespace
+
+int syrk_tc_error_word_index() { return 2; }
+
+llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t d, int64_t ld, float* H, int64_t ldh) {
+    if (dtype != LLMC_DTYPE_BF16 && dtype != LLMC_DTYPE_F16) return LLMC_ERR_UNSUPPORTED;
+    // Contract of the tensor map and of the bulk reduce epilogue.
+    if (((uintptr_t)x % 16) != 0 || (ld % 8) != 0 || (d % 4) != 0 || (ldh % 4) != 0 || ((uintptr_t)H % 16) != 0)
+        return LLMC_ERR_UNSUPPORTED;
+    if (d < 64 || rows < BK || rows > (int64_t)INT32_MAX) return LLMC_ERR_UNSUPPORTED;
+    const int ntj = (int)((d + BN - 1) / BN), nti = (int)((d + BM - 1) / BM);
+    if (ntj > MAX_TJ) return LLMC_ERR_UNSUPPORTED;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return LLMC_ERR_UNSUPPORTED;
+
+    SyrkArgs a{};
+    a.H = H;
+    a.ldh = ldh;
+    a.d = (int)d;
+    a.nti = nti;
+    a.ntj = ntj;
+    int off = 0;
+    for (int tj = 0; tj < ntj; tj++) {
+        a.tile_off[tj] = off;
+        off += min(2 * tj + 2, nti);  // row panels ti with 128*ti <= 256*tj + 255
+    }
+    a.tile_off[ntj] = off;
+    a.ntiles = off;
+    a.kb_total = (int)((rows + BK - 1) / BK);
+    // Token splits: balance the last wave while keeping >= 32 k-blocks (2048 tokens) per unit.
+    const int grid_cap = ctx->sm_count;
+    int best_s = 1;
+    double best_eff = 0.0;
+    for (int s = 1; s <= 16; s++) {
+        const int kps = (a.kb_total + s - 1) / s;
+        if (s > 1 && kps < 32) break;
+        const int units = a.ntiles * s;
+        const int waves = (units + grid_cap - 1) / grid_cap;
+        const double eff = (double)units / ((double)waves * grid_cap);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best_s = s;
+        }
+    }
+    a.splits = best_s;
+    a.kb_per_split = (a.kb_total + best_s - 1) / best_s;
+    a.err = ctx->dflags + 2;
+    a.idesc = make_idesc(dtype);
+
+    CUtensorMap map;
+    const cuuint64_t gdim[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {64, BK};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult cr = enc(&map, dtype == LLMC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                      const_cast<void*>(x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(LLMC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
+
+    static bool attr = false;
+    if (!attr) {
+        LLMC_CUDA_TRY(cudaFuncSetAttribute(syrk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr = true;
+    }
+    const int units = a.ntiles * a.splits;
+    const int grid = units < grid_cap ? units : grid_cap;
+    syrk_tc_kernel<<<grid, NT, SMEM_BYTES, ctx->stream>>>(map, a);
+    return check_launch(ctx, "syrk_tc");
+}
+
 }  // namespace llmc

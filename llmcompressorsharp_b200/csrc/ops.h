@@ -46,6 +46,7 @@ llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, 
 llmc_status upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ldh, float* out, int64_t ldo);
 
 // ---- misc ----------------------------------------------------------------------------------
+llmc_status device_error_check(llmc_ctx* ctx);
 llmc_status symmetrize_from_upper(llmc_ctx* ctx, const float* src, int64_t d, int64_t lds, float* dst, int64_t ldd);
 llmc_status convert_to_f32(llmc_ctx* ctx, const void* src, int dtype, int64_t rows, int64_t cols, int64_t lds,
                            float* dst, int64_t ldd);
