@@ -328,8 +328,9 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
     for l in mine:
         for k in weights[l]:
             h_w[l][k].copy_(weights[l][k])
+    stacked = {l: {k: o for k, o in outputs[l].items() if k.startswith("__stacked__")} for l in mine}
     h_out = {l: {k: {f: torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for f, t in o.items()}
-                 for k, o in outputs[l].items()} for l in mine}
+                 for k, o in stacked[l].items()} for l in mine}
     h2d = sum(t.numel() * t.element_size() for t in h_acts.values())
     h2d += sum(t.numel() * t.element_size() for l in mine for t in h_w[l].values())
     d2h = sum(t.numel() * t.element_size() for l in mine for o in h_out[l].values() for t in o.values())
@@ -343,7 +344,7 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
                 for k in weights[l]:
                     weights[l][k].copy_(h_w[l][k], non_blocking=True)
                 pipe.run_layer(acts, weights[l], outputs[l])
-                for k, o in outputs[l].items():
+                for k, o in stacked[l].items():
                     for f, t in o.items():
                         h_out[l][k][f].copy_(t, non_blocking=True)
             return
@@ -358,7 +359,7 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
                 weights[l][k].copy_(h_w[l][k], non_blocking=True)
             for s in sites:
                 pipe.solve_site(s, hbufs[l][s.name].data_ptr(), weights[l], outputs[l])
-            for k, o in outputs[l].items():
+            for k, o in stacked[l].items():
                 for f, t in o.items():
                     h_out[l][k][f].copy_(t, non_blocking=True)
 

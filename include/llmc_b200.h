@@ -147,6 +147,18 @@ llmc_status llmc_gptq_quantize(llmc_ctx* ctx, const void* W, int32_t dtype, int6
                                const float* U, int64_t ldu, const llmc_qconfig* cfg,
                                float* wq_out, int64_t ldq, uint8_t* codes_out, float* scales_out, int32_t* zps_out);
 
+/* Several weights that share one Hessian (q/k/v read the attention input, gate/up the MLP
+ * input) solved in one call as a stacked matrix: weight k is W[k] [m[k], n] (row stride
+ * ldw[k]); every output is stacked in weight order over sum(m) rows (wq_out row stride ldq,
+ * codes/scales/zero-points as llmc_gptq_quantize for the stacked matrix), except that the
+ * TENSOR strategy returns one scale / zero-point per weight.  Results equal `count` separate
+ * llmc_gptq_quantize calls (GptqBlockQuantizer.Quantize per weight, GPTQModifier.cs:119-136).
+ * W, m and ldw are host arrays of `count` entries; W[k] are device pointers. */
+llmc_status llmc_gptq_quantize_batch(llmc_ctx* ctx, int32_t count, const void* const* W, const int64_t* m,
+                                     const int64_t* ldw, int32_t dtype, int64_t n, const float* U, int64_t ldu,
+                                     const llmc_qconfig* cfg, float* wq_out, int64_t ldq, uint8_t* codes_out,
+                                     float* scales_out, int32_t* zps_out);
+
 /* ---- SparseGPT (plan docs/superpowers/plans/2026-05-18-phase-4c-sparsegpt.md:37-59,1584-1656,
  * in the U-factor form of GptqBlockQuantizer.cs:124-181).  out fp32 [m,n] pruned weight,
  * mask_out (optional) one byte per element, 1 = kept. */

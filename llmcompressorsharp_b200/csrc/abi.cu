@@ -44,25 +44,30 @@ llmc_status device_error_check(llmc_ctx* ctx) {
     return LLMC_OK;
 }
 
-llmc_status workspace(llmc_ctx* ctx, size_t bytes, void** out) {
-    if (bytes > ctx->ws_bytes) {
-        if (ctx->ws) {
+static llmc_status grow(llmc_ctx* ctx, void** buf, size_t* cap, size_t bytes, void** out) {
+    if (bytes > *cap) {
+        if (*buf) {
             // The old block may still be in use by queued work on this stream.
             LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-            LLMC_CUDA_TRY(cudaFree(ctx->ws));
-            ctx->ws = nullptr;
-            ctx->ws_bytes = 0;
+            LLMC_CUDA_TRY(cudaFree(*buf));
+            *buf = nullptr;
+            *cap = 0;
         }
         size_t want = align_up(bytes, (size_t)1 << 20);
-        cudaError_t e = cudaMalloc(&ctx->ws, want);
+        cudaError_t e = cudaMalloc(buf, want);
         if (e != cudaSuccess) {
-            ctx->ws = nullptr;
+            *buf = nullptr;
             return fail(LLMC_ERR_CUDA, "workspace allocation of %zu bytes failed: %s", want, cudaGetErrorString(e));
         }
-        ctx->ws_bytes = want;
+        *cap = want;
     }
-    *out = ctx->ws;
+    *out = *buf;
     return LLMC_OK;
+}
+
+llmc_status workspace(llmc_ctx* ctx, size_t bytes, void** out) { return grow(ctx, &ctx->ws, &ctx->ws_bytes, bytes, out); }
+llmc_status workspace2(llmc_ctx* ctx, size_t bytes, void** out) {
+    return grow(ctx, &ctx->ws2, &ctx->ws2_bytes, bytes, out);
 }
 
 // Internal launchers implemented in the kernel translation units.
@@ -73,6 +78,8 @@ llmc_status int4_pack(llmc_ctx*, const int32_t*, int64_t, int, uint8_t*);
 llmc_status int4_unpack(llmc_ctx*, const uint8_t*, int64_t, float, int, float*);
 llmc_status gptq(llmc_ctx*, const void*, int, int64_t, int64_t, int64_t, const float*, int64_t, const llmc_qconfig*,
                  float*, int64_t, uint8_t*, float*, int32_t*, int, uint8_t*);
+llmc_status gptq_batch(llmc_ctx*, int, const void* const*, const int64_t*, const int64_t*, int, int64_t, const float*,
+                       int64_t, const llmc_qconfig*, float*, int64_t, uint8_t*, float*, int32_t*, int, uint8_t*);
 llmc_status col_absmax(llmc_ctx*, const void*, int, int64_t, int64_t, int64_t, float*, int);
 llmc_status smooth_apply(llmc_ctx*, const float*, void*, int, void*, int, int64_t, int64_t, float, float*);
 llmc_status scale_apply(llmc_ctx*, const float*, void*, int, void*, int, int64_t, int64_t);
@@ -156,6 +163,7 @@ llmc_status llmc_destroy(llmc_ctx* ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->ws2) cudaFree(ctx->ws2);
     if (ctx->dflags) cudaFree(ctx->dflags);
     if (ctx->hflags) cudaFreeHost(ctx->hflags);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -316,6 +324,31 @@ llmc_status llmc_gptq_quantize(llmc_ctx* ctx, const void* W, int32_t dtype, int6
     if (codes_out && cfg->num_bits <= 4 && cfg->strategy == LLMC_STRATEGY_GROUP && (cfg->group_size % 2))
         return fail(LLMC_ERR_UNSUPPORTED, "packed int4 codes need an even group size");
     return gptq(ctx, W, dtype, m, n, ldw, U, ldu, cfg, wq_out, ldq, codes_out, scales_out, zps_out, 0, nullptr);
+}
+
+llmc_status llmc_gptq_quantize_batch(llmc_ctx* ctx, int32_t count, const void* const* W, const int64_t* m,
+                                     const int64_t* ldw, int32_t dtype, int64_t n, const float* U, int64_t ldu,
+                                     const llmc_qconfig* cfg, float* wq_out, int64_t ldq, uint8_t* codes_out,
+                                     float* scales_out, int32_t* zps_out) {
+    CTX_CHECK(ctx);
+    NULL_CHECK(W, "weights");
+    NULL_CHECK(m, "m");
+    NULL_CHECK(ldw, "ldw");
+    NULL_CHECK(U, "hinv");
+    LLMC_TRY(check_qconfig(cfg, 1));
+    if (count < 1 || count > 64) return fail(LLMC_ERR_INVALID_ARG, "count must be in [1, 64]");
+    if (!dtype_ok(dtype)) return fail(LLMC_ERR_INVALID_ARG, "unsupported dtype %d", dtype);
+    if (n <= 0 || ldu < n) return fail(LLMC_ERR_SHAPE, "bad U shape");
+    for (int k = 0; k < count; k++) {
+        NULL_CHECK(W[k], "weight");
+        if (m[k] <= 0 || ldw[k] < n) return fail(LLMC_ERR_SHAPE, "bad shape of weight %d", k);
+    }
+    if (wq_out && ldq < n) return fail(LLMC_ERR_SHAPE, "ldq < n");
+    if (codes_out && cfg->num_bits > 8) return fail(LLMC_ERR_UNSUPPORTED, "integer codes are produced for num_bits <= 8");
+    if (codes_out && cfg->num_bits <= 4 && cfg->strategy == LLMC_STRATEGY_GROUP && (cfg->group_size % 2))
+        return fail(LLMC_ERR_UNSUPPORTED, "packed int4 codes need an even group size");
+    return gptq_batch(ctx, count, W, m, ldw, dtype, n, U, ldu, cfg, wq_out, ldq, codes_out, scales_out, zps_out, 0,
+                      nullptr);
 }
 
 llmc_status llmc_sparsegpt_prune(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t m, int64_t n, int64_t ldw,

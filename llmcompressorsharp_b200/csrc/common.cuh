@@ -43,6 +43,9 @@ struct llmc_ctx {
     // Growable scratch owned by the context (stream-ordered reuse: one op at a time).
     void* ws = nullptr;
     size_t ws_bytes = 0;
+    // Second scratch area for operand copies made by routines called while ws is in use.
+    void* ws2 = nullptr;
+    size_t ws2_bytes = 0;
     // Device status words (flags written by kernels, e.g. a non-positive pivot).
     int* dflags = nullptr;
     int* hflags = nullptr;  // pinned mirror
@@ -59,6 +62,8 @@ namespace llmc {
 
 // Returns scratch of at least `bytes`, valid until the next workspace() call on ctx.
 llmc_status workspace(llmc_ctx* ctx, size_t bytes, void** out);
+// Same for the second scratch area (used by the tensor-core GEMM's operand split).
+llmc_status workspace2(llmc_ctx* ctx, size_t bytes, void** out);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

@@ -10,7 +10,7 @@
 //     A22  -= L21 L21^T                        (GEMM, lower output only)
 //     (L22, L22^-1) = chol_inv(A22)
 //     (L^-1)21 = -L22^-1 (L21 L11^-1)          (two GEMMs)
-// with a one-CTA shared-memory kernel for blocks of <= 64.  All O(d^3) work is GEMM.
+// with a one-CTA shared-memory kernel for blocks of <= 128.  All O(d^3) work is GEMM.
 //
 // U directly: with P the index-reversal permutation and L' = chol(P H' P), the matrix
 // U = P L'^-1 P is upper triangular and U^T U = H'^-1, i.e. U is exactly the upper
@@ -21,7 +21,7 @@
 namespace llmc {
 namespace {
 
-constexpr int NB = 64;
+constexpr int NB = 128;  // diagonal block size of the recursion's base case
 
 __global__ void diag_lambda_kernel(const float* H, int64_t d, int64_t ldh, float damp, float* lam) {
     // mean(diag H) read back as a float, times the damping fraction as C# float math
@@ -63,55 +63,66 @@ __global__ void prep_kernel(const float* H, int64_t d, int64_t ldh, int upper_on
     }
 }
 
-// Cholesky + triangular inverse of one n x n (n <= NB) diagonal block in shared memory.
-// A's lower triangle is read; L (zeros above) goes back to A and L^-1 to I.  A pivot that
-// is not > 0 (or NaN) raises flags[0] and the block continues with a unit pivot, so the
-// kernel always terminates; the host reports the failure.
-__global__ void __launch_bounds__(256) chol_inv_base_kernel(float* A, float* I, int64_t ld, int n, int* flags) {
-    __shared__ float sL[NB][NB + 1];
-    __shared__ float sX[NB][NB + 1];
-    const int tid = threadIdx.x;
-    for (int t = tid; t < n * n; t += blockDim.x) {
-        const int i = t / n, j = t % n;
-        sL[i][j] = (j <= i) ? A[i * ld + j] : 0.f;
-        sX[i][j] = 0.f;
-    }
+// Cholesky + triangular inverse of one n x n (n <= NB) diagonal block in shared memory,
+// 1024 threads viewed as 32 x 32.  A's lower triangle is read; L (zeros above) goes back to
+// A and L^-1 to I.  A pivot that is not > 0 (or NaN) raises flags[0] and the block continues
+// with a unit pivot, so the kernel always terminates; the host reports the failure.
+//
+// Factorisation: outer-product form with one barrier per step; step k updates the trailing
+// lower triangle with a_ij -= (a_ik / a_kk) a_jk from the (still unscaled) column k, and the
+// columns are scaled by 1/sqrt(a_kk) at the end.  Inverse: forward elimination of L X = I
+// applied to all right-hand sides at once (row k scaled, then eliminated from rows > k).
+constexpr int BASE_THREADS = 1024;
+constexpr int BLD = NB + 1;
+
+size_t base_smem_bytes() { return (size_t)2 * NB * BLD * sizeof(float) + NB * sizeof(float); }
+
+__global__ void __launch_bounds__(BASE_THREADS) chol_inv_base_kernel(float* A, float* I, int64_t ld, int n, int* flags) {
+    extern __shared__ float sm[];
+    float* sL = sm;               // [NB][BLD]
+    float* sX = sm + NB * BLD;    // [NB][BLD]
+    float* sdiag = sX + NB * BLD; // [NB]
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+    for (int i = ty; i < n; i += 32)
+        for (int j = tx; j < n; j += 32) {
+            sL[i * BLD + j] = (j <= i) ? A[i * ld + j] : 0.f;
+            sX[i * BLD + j] = (i == j) ? 1.f : 0.f;
+        }
     __syncthreads();
     for (int k = 0; k < n; k++) {
-        __shared__ float piv;
-        if (tid == 0) {
-            float p = sL[k][k];
-            if (!(p > 0.f)) {
-                atomicOr(flags, 1);
-                p = 1.f;
-            }
-            piv = __fsqrt_rn(p);
-            sL[k][k] = piv;
+        float akk = sL[k * BLD + k];
+        if (!(akk > 0.f)) {
+            if (threadIdx.x == 0) atomicOr(flags, 1);
+            akk = 1.f;
         }
+        const float inv = __frcp_rn(akk);
+        for (int i = k + 1 + ty; i < n; i += 32) {
+            const float lik = __fmul_rn(sL[i * BLD + k], inv);
+            for (int j = k + 1 + tx; j <= i; j += 32) sL[i * BLD + j] = fmaf(-lik, sL[j * BLD + k], sL[i * BLD + j]);
+        }
+        if (threadIdx.x == 0) sdiag[k] = __fsqrt_rn(akk);
         __syncthreads();
-        for (int i = k + 1 + tid; i < n; i += blockDim.x) sL[i][k] = __fdiv_rn(sL[i][k], piv);
+    }
+    for (int i = ty; i < n; i += 32)
+        for (int j = tx; j <= i; j += 32)
+            sL[i * BLD + j] = (i == j) ? sdiag[i] : __fdiv_rn(sL[i * BLD + j], sdiag[j]);
+    __syncthreads();
+    for (int k = 0; k < n; k++) {
+        const float rk = __frcp_rn(sL[k * BLD + k]);
+        if (ty == 0)
+            for (int j = tx; j <= k; j += 32) sX[k * BLD + j] = __fmul_rn(sX[k * BLD + j], rk);
         __syncthreads();
-        const int r = n - k - 1;  // trailing size
-        for (int t = tid; t < r * r; t += blockDim.x) {
-            const int i = k + 1 + t / r, j = k + 1 + t % r;
-            if (j <= i) sL[i][j] = fmaf(-sL[i][k], sL[j][k], sL[i][j]);
+        for (int i = k + 1 + ty; i < n; i += 32) {
+            const float lik = sL[i * BLD + k];
+            for (int j = tx; j <= k; j += 32) sX[i * BLD + j] = fmaf(-lik, sX[k * BLD + j], sX[i * BLD + j]);
         }
         __syncthreads();
     }
-    // X = L^-1 row by row: X[i][j] = (delta_ij - sum_{k=j}^{i-1} L[i][k] X[k][j]) / L[i][i].
-    for (int i = 0; i < n; i++) {
-        for (int j = tid; j <= i; j += blockDim.x) {
-            float s = (i == j) ? 1.f : 0.f;
-            for (int k = j; k < i; k++) s = fmaf(-sL[i][k], sX[k][j], s);
-            sX[i][j] = __fdiv_rn(s, sL[i][i]);
+    for (int i = ty; i < n; i += 32)
+        for (int j = tx; j < n; j += 32) {
+            A[i * ld + j] = sL[i * BLD + j];
+            I[i * ld + j] = sX[i * BLD + j];
         }
-        __syncthreads();
-    }
-    for (int t = tid; t < n * n; t += blockDim.x) {
-        const int i = t / n, j = t % n;
-        A[i * ld + j] = sL[i][j];
-        I[i * ld + j] = sX[i][j];
-    }
 }
 
 // out[i][j] = src[d-1-i][d-1-j] (flip) or src[j][i] (transpose); src lower -> out upper.
@@ -162,7 +173,13 @@ llmc_status rec(llmc_ctx* ctx, const CholWs& w, int64_t off, int64_t n, int keep
     float* A = w.A + off * w.ld + off;
     float* I = w.I + off * w.ld + off;
     if (n <= NB) {
-        chol_inv_base_kernel<<<1, 256, 0, ctx->stream>>>(A, I, w.ld, (int)n, ctx->dflags);
+        static bool attr = false;
+        if (!attr) {
+            LLMC_CUDA_TRY(cudaFuncSetAttribute(chol_inv_base_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)base_smem_bytes()));
+            attr = true;
+        }
+        chol_inv_base_kernel<<<1, BASE_THREADS, base_smem_bytes(), ctx->stream>>>(A, I, w.ld, (int)n, ctx->dflags);
         return check_launch(ctx, "chol_inv_base");
     }
     int64_t n1 = ((n / 2 + NB - 1) / NB) * NB;

@@ -177,6 +177,11 @@ llmc_status gemm_f32(llmc_ctx* ctx, const GemmArgs& g) {
         // C = beta * C: run with an empty K range (all accumulators zero).
     }
     if (g.a_dtype != g.b_dtype) return fail(LLMC_ERR_INTERNAL, "gemm: mixed operand dtypes");
+    // Large fp32 products go to the tensor cores (3 x TF32); small ones stay on the SIMT kernel.
+    if (g.a_dtype == LLMC_DTYPE_F32 && g.K > 0 && (double)g.M * (double)g.N * (double)g.K >= (double)(1 << 26)) {
+        llmc_status st = gemm_tc(ctx, g);
+        if (st != LLMC_ERR_UNSUPPORTED) return st;
+    }
     switch (g.a_dtype) {
         case LLMC_DTYPE_F32: return launch<float, float>(ctx, g);
         case LLMC_DTYPE_BF16: return launch<__nv_bfloat16, __nv_bfloat16>(ctx, g);

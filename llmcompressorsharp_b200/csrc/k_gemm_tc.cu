@@ -1,0 +1,400 @@
+// fp32 GEMM on the 5th-generation tensor cores with a 3 x TF32 split (sm_100a).
+//
+// Serves the O(d^3) fp32 parts of the hot path: the Cholesky / triangular-inverse recursion
+// (HessianInverseSolver.cs:62-90) and the GPTQ lazy tail update W[:, i2:] -= Err1 U[i1:i2, i2:]
+// (GptqBlockQuantizer.cs:173-180).
+//
+// C[M,N] = alpha * op(A) op(B) + beta * C with fp32 operands split (by split2d_kernel) into
+// x = hi + lo, hi = x rounded to TF32 (low 13 mantissa bits zero) and lo = x - hi (exact in
+// fp32).  The product is hi_a hi_b + hi_a lo_b + lo_a hi_b: three tcgen05.mma kind::tf32
+// per K step, error ~2^-21 relative per product (the dropped lo_a lo_b and the TF32 view of
+// the lo terms), i.e. fp32-grade.
+//
+// Per CTA (one output tile of 128 x 128, 192 threads):
+//   warp 0: TMA producer, 3-stage ring of {A hi, A lo, B hi, B lo} tiles of 32 K-elements,
+//           128-byte swizzle, K-major or MN-major per operand, no multicast;
+//   warp 1: one thread issues the MMAs into one of two TMEM accumulators (128 columns each);
+//   warps 2-5: fold each accumulator into fp32 registers every KF k-blocks (the tensor core's
+//           accumulation truncates; folding bounds that to KF*32 K-elements), then write
+//           C = alpha*acc + beta*C (optionally only the lower triangle).
+// Triangular operands restrict each tile's K range (the skipped region must be zero).
+// Every wait is bounded (error word + drain + TMEM release, as in the Hessian kernel).
+#include "ops.h"
+#include "tc_common.cuh"
+
+#include <cuda.h>
+
+namespace llmc {
+namespace {
+
+using namespace tc;
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int EPI_WARPS = 4, NT = 32 * (2 + EPI_WARPS);
+constexpr int KF = 2;                       // k-blocks (64 K-elements, 24 MMAs) per TMEM accumulation
+constexpr int TILE_BYTES = BM * BK * 4;     // 16 KB per operand part
+constexpr int STAGE_BYTES = 4 * TILE_BYTES; // A hi, A lo, B hi, B lo
+constexpr int SMEM_MAIN = STAGES * STAGE_BYTES;
+constexpr int SMEM_BYTES = SMEM_MAIN + 1024 + 256;
+constexpr int TMEM_COLS = 2 * BN;
+
+struct TcGemmArgs {
+    int64_t M, N, K;
+    float* C;
+    int64_t ldc;
+    float alpha, beta;
+    int a_tri, b_tri, c_mode;
+    int* err;
+    uint32_t idesc;
+};
+
+// Loads one operand part (128 rows of the MN dimension x 32 K-elements, K contiguous) for a
+// k-block: box {32 K, 128 rows}, i.e. 128 rows of 128 B in 8-row 128-byte-swizzle atoms.
+__device__ __forceinline__ void load_part(unsigned char* dst, const CUtensorMap* map, int mn0, int k0, uint64_t* bar) {
+    tma_load_2d(dst, map, k0, mn0, bar);
+}
+
+// K step of 8 TF32 elements = 32 bytes inside each 128-byte K-major row.
+__device__ __forceinline__ uint64_t part_desc(uint32_t base, int kk) { return smem_desc_k_sw128(base + kk * 32); }
+
+__global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap ahi,
+                                                        const __grid_constant__ CUtensorMap alo,
+                                                        const __grid_constant__ CUtensorMap bhi,
+                                                        const __grid_constant__ CUtensorMap blo, const TcGemmArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SMEM_MAIN);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+    if (a.c_mode == 1 && m0 + BM - 1 < n0) return;  // tile entirely above the diagonal
+    if (a.c_mode == 2 && m0 > n0 + BN - 1) return;  // tile entirely below the diagonal
+
+    int64_t kb_lo = 0, kb_hi = a.K;
+    if (a.a_tri == TRI_KLE) kb_hi = min(kb_hi, m0 + BM);
+    if (a.a_tri == TRI_KGE) kb_lo = max(kb_lo, m0);
+    if (a.b_tri == TRI_KLE) kb_hi = min(kb_hi, n0 + BN);
+    if (a.b_tri == TRI_KGE) kb_lo = max(kb_lo, n0);
+    const int kb0 = (int)(kb_lo / BK);
+    const int kb1 = kb_hi > kb_lo ? (int)((kb_hi + BK - 1) / BK) : kb0;
+    const int nchunks = (kb1 - kb0 + KF - 1) / KF;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], EPI_WARPS);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int pend_par[STAGES];
+#pragma unroll
+    for (int s = 0; s < STAGES; s++) pend_par[s] = -1;
+    int commit_par[2] = {-1, -1};
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int kb = kb0; kb < kb1; kb++, it++) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                unsigned char* st = smem + s * STAGE_BYTES;
+                mbar_expect_tx(&full[s], STAGE_BYTES);
+                const int k0 = kb * BK;
+                load_part(st + 0 * TILE_BYTES, &ahi, (int)m0, k0, &full[s]);
+                load_part(st + 1 * TILE_BYTES, &alo, (int)m0, k0, &full[s]);
+                load_part(st + 2 * TILE_BYTES, &bhi, (int)n0, k0, &full[s]);
+                load_part(st + 3 * TILE_BYTES, &blo, (int)n0, k0, &full[s]);
+                pend_par[s] = (int)ph;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int c = 0; c < nchunks && !*abort_flag; c++) {
+                const int b = c & 1;
+                if (!mbar_wait(&tempty[b], ((uint32_t)(c >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                tc_fence_after();
+                const uint32_t dst = tmem + (uint32_t)(b * BN);
+                const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
+                bool ok = true;
+                for (int kb = k0; kb < k1; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; kk++) {
+                        const uint64_t dah = part_desc(base + 0 * TILE_BYTES, kk);
+                        const uint64_t dal = part_desc(base + 1 * TILE_BYTES, kk);
+                        const uint64_t dbh = part_desc(base + 2 * TILE_BYTES, kk);
+                        const uint64_t dbl = part_desc(base + 3 * TILE_BYTES, kk);
+                        const uint32_t first = (kb == k0 && kk == 0) ? 0u : 1u;
+                        umma_tf32(dst, dah, dbh, a.idesc, first);
+                        umma_tf32(dst, dah, dbl, a.idesc, 1u);
+                        umma_tf32(dst, dal, dbh, a.idesc, 1u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&tfull[b]);
+                commit_par[b] = (c >> 1) & 1;
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // epilogue warps: TMEM lane quadrant q = warp % 4 = rows [32q, 32q + 32) of the tile
+        const int q = warp % 4;
+        float acc[BN];
+#pragma unroll
+        for (int i = 0; i < BN; i++) acc[i] = 0.f;
+        for (int c = 0; c < nchunks; c++) {
+            const int b = c & 1;
+            const bool have = mbar_wait(&tfull[b], (uint32_t)(c >> 1) & 1u, abort_flag, a.err);
+            if (!__all_sync(0xffffffffu, have ? 1 : 0)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int part = 0; part < BN / 32; part++) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + part * 32), v);
+#pragma unroll
+                for (int i = 0; i < 32; i++) acc[part * 32 + i] = __fadd_rn(acc[part * 32 + i], __uint_as_float(v[i]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+        const int64_t r = m0 + q * 32 + lane;
+        if (r < a.M && !*abort_flag) {
+            float* crow = a.C + r * a.ldc + n0;
+            const bool vec = ((reinterpret_cast<uintptr_t>(crow) & 15u) == 0) && n0 + BN <= a.N &&
+                             !(a.c_mode == 1 && r < n0 + BN - 1);
+            if (vec) {
+#pragma unroll
+                for (int i = 0; i < BN; i += 4) {
+                    float4 o = make_float4(a.alpha * acc[i], a.alpha * acc[i + 1], a.alpha * acc[i + 2],
+                                           a.alpha * acc[i + 3]);
+                    if (a.beta != 0.f) {
+                        const float4 c = *reinterpret_cast<const float4*>(crow + i);
+                        o.x = fmaf(a.beta, c.x, o.x);
+                        o.y = fmaf(a.beta, c.y, o.y);
+                        o.z = fmaf(a.beta, c.z, o.z);
+                        o.w = fmaf(a.beta, c.w, o.w);
+                    }
+                    *reinterpret_cast<float4*>(crow + i) = o;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < BN; i++) {
+                    const int64_t col = n0 + i;
+                    if (col < a.N && !(a.c_mode == 1 && r < col)) {
+                        const float v = a.alpha * acc[i];
+                        crow[i] = (a.beta == 0.f) ? v : fmaf(a.beta, crow[i], v);
+                    }
+                }
+            }
+        }
+    }
+
+    if (*abort_flag) {
+        if (warp == 0 && lane == 0)
+            for (int s = 0; s < STAGES; s++)
+                if (pend_par[s] >= 0) mbar_wait_drain(&full[s], (uint32_t)pend_par[s]);
+        if (warp == 1 && lane == 0)
+            for (int b = 0; b < 2; b++)
+                if (commit_par[b] >= 0) mbar_wait_drain(&tfull[b], (uint32_t)commit_par[b]);
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+// hi = x rounded to TF32 (round to nearest, ties away), lo = x - hi (exact in fp32).
+__device__ __forceinline__ void tf32_split(float x, float* h, float* l) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;  // finite: keep 10 mantissa bits
+    *h = __uint_as_float(u);
+    *l = __fsub_rn(x, *h);
+}
+
+// Split a K-major operand [rows, cols] (K = cols) into packed hi / lo copies (row stride ldd).
+__global__ void split2d_kernel(const float* src, int64_t rows, int64_t cols, int64_t lds, float* hi, float* lo,
+                               int64_t ldd) {
+    const int64_t total = rows * cols;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / cols, j = t % cols;
+        float h, l;
+        tf32_split(src[i * lds + j], &h, &l);
+        hi[i * ldd + j] = h;
+        lo[i * ldd + j] = l;
+    }
+}
+
+// Split an MN-major operand [K rows, MN cols] into K-major hi / lo copies [MN rows, K cols]
+// (32 x 32 tiles through shared memory so both sides are coalesced).
+__global__ void split2d_transpose_kernel(const float* src, int64_t rows, int64_t cols, int64_t lds, float* hi,
+                                         float* lo, int64_t ldd) {
+    __shared__ float th[32][33];
+    __shared__ float tl[32][33];
+    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+    for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+        const int64_t r = r0 + y, c = c0 + threadIdx.x;
+        float h = 0.f, l = 0.f;
+        if (r < rows && c < cols) tf32_split(src[r * lds + c], &h, &l);
+        th[y][threadIdx.x] = h;
+        tl[y][threadIdx.x] = l;
+    }
+    __syncthreads();
+    for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+        const int64_t orow = c0 + y, ocol = r0 + threadIdx.x;  // output [cols, rows]
+        if (orow < cols && ocol < rows) {
+            hi[orow * ldd + ocol] = th[threadIdx.x][y];
+            lo[orow * ldd + ocol] = tl[threadIdx.x][y];
+        }
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Tensor map of a packed K-major fp32 operand [rows, cols = K] (row stride ld floats), box
+// {32 K, 128 rows}.
+llmc_status make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(LLMC_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)ld * 4};
+    const cuuint32_t box[2] = {32, 128};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult cr = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride, box, estride,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(LLMC_ERR_CUDA, "cuTensorMapEncodeTiled (fp32) failed (%d)", (int)cr);
+    return LLMC_OK;
+}
+
+// hi / lo K-major copies [mn, k] of an operand stored either K-major ([mn, k], ld) or
+// MN-major ([k, mn], ld).
+llmc_status split_operand(llmc_ctx* ctx, const float* src, int64_t mn, int64_t k, int64_t ld, int mn_major, float* hi,
+                          float* lo, int64_t ldd);
+
+int grid_for(llmc_ctx* ctx, int64_t items) {
+    int64_t b = (items + 255) / 256;
+    int64_t cap = (int64_t)ctx->sm_count * 8;
+    return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+llmc_status split_operand(llmc_ctx* ctx, const float* src, int64_t mn, int64_t k, int64_t ld, int mn_major, float* hi,
+                          float* lo, int64_t ldd) {
+    if (!mn_major) {
+        split2d_kernel<<<grid_for(ctx, mn * k), 256, 0, ctx->stream>>>(src, mn, k, ld, hi, lo, ldd);
+    } else {
+        dim3 grid((unsigned)((mn + 31) / 32), (unsigned)((k + 31) / 32));
+        if (grid.y > 65535) return fail(LLMC_ERR_UNSUPPORTED, "split: K too large");
+        split2d_transpose_kernel<<<grid, dim3(32, 8), 0, ctx->stream>>>(src, k, mn, ld, hi, lo, ldd);
+    }
+    return check_launch(ctx, "split2d");
+}
+
+}  // namespace
+
+// Tensor-core path of gemm_f32 (fp32 operands).  Returns LLMC_ERR_UNSUPPORTED when the shape
+// is too small to pay for the split (the caller then runs the SIMT kernel).
+llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
+    if (g.a_dtype != LLMC_DTYPE_F32 || g.b_dtype != LLMC_DTYPE_F32) return LLMC_ERR_UNSUPPORTED;
+    if (g.split_k > 1 || g.M < 128 || g.N < 128 || g.K < 64) return LLMC_ERR_UNSUPPORTED;
+    if (g.M > (int64_t)INT32_MAX || g.N > (int64_t)INT32_MAX || g.K > (int64_t)INT32_MAX) return LLMC_ERR_UNSUPPORTED;
+    // Operands as stored: A is [M, K] (a_trans = 0) or [K, M] (a_trans = 1); B is [K, N]
+    // (b_trans = 0) or [N, K] (b_trans = 1).  The split copies are K-major [M, K] and [N, K].
+    const int64_t ldk = (g.K + 3) / 4 * 4;
+    const size_t need = (size_t)(2 * g.M * ldk + 2 * g.N * ldk) * 4 + 4096;
+    void* sp;
+    LLMC_TRY(workspace2(ctx, need, &sp));
+    Carver cv{(char*)sp};
+    float* ah = cv.take<float>((size_t)g.M * ldk);
+    float* al = cv.take<float>((size_t)g.M * ldk);
+    float* bh = cv.take<float>((size_t)g.N * ldk);
+    float* bl = cv.take<float>((size_t)g.N * ldk);
+    LLMC_TRY(split_operand(ctx, (const float*)g.A, g.M, g.K, g.lda, g.a_trans, ah, al, ldk));
+    LLMC_TRY(split_operand(ctx, (const float*)g.B, g.N, g.K, g.ldb, !g.b_trans, bh, bl, ldk));
+    CUtensorMap mah, mal, mbh, mbl;
+    LLMC_TRY(make_map(&mah, ah, g.M, g.K, ldk));
+    LLMC_TRY(make_map(&mal, al, g.M, g.K, ldk));
+    LLMC_TRY(make_map(&mbh, bh, g.N, g.K, ldk));
+    LLMC_TRY(make_map(&mbl, bl, g.N, g.K, ldk));
+
+    TcGemmArgs t{};
+    t.M = g.M;
+    t.N = g.N;
+    t.K = g.K;
+    t.C = g.C;
+    t.ldc = g.ldc;
+    t.alpha = g.alpha;
+    t.beta = g.beta;
+    t.a_tri = g.a_tri;
+    t.b_tri = g.b_tri;
+    t.c_mode = g.c_mode;
+    t.err = ctx->dflags + 2;
+    uint32_t d = 0;
+    d |= 1u << 4;          // D: F32
+    d |= 2u << 7;          // A: TF32
+    d |= 2u << 10;         // B: TF32
+    // A and B K-major (bits 15/16 clear)
+    d |= (uint32_t)(BN >> 3) << 17;
+    d |= (uint32_t)(BM >> 4) << 24;
+    t.idesc = d;
+
+    static bool attr = false;
+    if (!attr) {
+        LLMC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr = true;
+    }
+    dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM));
+    if (grid.y > 65535) return LLMC_ERR_UNSUPPORTED;
+    gemm_tc_kernel<<<grid, NT, SMEM_BYTES, ctx->stream>>>(mah, mal, mbh, mbl, t);
+    return check_launch(ctx, "gemm_tc");
+}
+
+}  // namespace llmc

@@ -5,21 +5,25 @@
 // (:240-274); SparseGPT per the plan docs/superpowers/plans/2026-05-18-phase-4c-sparsegpt.md
 // (:37-59, :1584-1656) in the same U-factor form.
 //
-// Rows are independent given U, so one thread owns one output row of the current block
-// of <= 128 columns and keeps that row segment in registers.  The 128 sequential column
-// steps (quantise, err = (w-q)/U[j][j], rank-1 update of the rest of the block) then run
-// with no global traffic: U's diagonal block sits in shared memory and is read as
-// broadcasts.  The block's W tile and its outputs move through shared memory so that
-// every global access is coalesced.  The lazy tail update W[:, i2:] -= Err1 U[i1:i2, i2:]
-// is a GEMM (gemm_f32) with Err1 stored transposed [cnt, m].
+// Rows are independent given U, so one thread owns one output row of the current block of
+// <= 128 columns.  The block is processed as four 32-column sub-blocks: a sub-block's row
+// segment lives in registers and its 32 sequential column steps (quantise, err = (w-q)/U[j][j],
+// rank-1 update of the rest of the sub-block) are fully unrolled; the sub-block's 32 errors
+// then update the block's later columns, which wait in shared memory, in a rolled loop
+// (U rows are shared-memory broadcasts).  This keeps the code small enough for the
+// instruction cache.  The lazy tail update W[:, i2:] -= Err1 U[i1:i2, i2:] is a GEMM with
+// Err1 stored transposed [cnt, m].
+//
+// Several weights that share one U (q/k/v, gate/up) are solved as one stacked matrix.
 #include "ops.h"
 
 namespace llmc {
 namespace {
 
-constexpr int BW = 128;     // columns per block held in registers
-constexpr int ROWS = 64;    // rows (threads) per CTA
-constexpr int WPAD = BW + 4;
+constexpr int BW = 128;      // columns per block
+constexpr int SB = 32;       // columns per register sub-block
+constexpr int ROWS = 64;     // rows (threads) per CTA
+constexpr int WLD = ROWS + 1;  // column-major W tile: element (row r, col c) at c*WLD + r
 
 struct BlockArgs {
     float* W; int64_t ldw;             // fp32 working copy; quantised values written back in place
@@ -29,30 +33,32 @@ struct BlockArgs {
     // quantisation
     int bits, sym;
     const float* scales; const int32_t* zps;
-    int64_t srow;   // scale entries per row (0 tensor, 1 channel, G group)
+    int64_t srow;   // scale entries per row (0 tensor, 1 channel / per-row, G group)
     int64_t gs;     // columns per scale entry along a row (n for tensor/channel)
     uint8_t* codes; int64_t crow;  // packed (bits<=4) or bytes; nullable
-    float* err1t;   // [BW, m]
+    float* err1t;   // [cnt, m] errors of the current block (inside the super-block's buffer)
     // SparseGPT
     float sparsity; int mask_n, mask_m;
     uint8_t* mask; int64_t mrow;   // nullable, one byte per element
 };
 
-size_t block_smem_bytes() { return (size_t)BW * BW * 4 + (size_t)ROWS * WPAD * 4 + (size_t)ROWS * BW; }
+template <int MODE>
+constexpr size_t block_smem_bytes() {
+    return (size_t)BW * BW * 4 + (size_t)BW * WLD * 4 + (size_t)BW * ROWS + (MODE == 1 ? (size_t)BW * WLD * 4 : 0);
+}
 
 // Keep mask of one row's block (SparseGPT): per-row top-k (unstructured) or N:M, ties to
-// the lower column index.  sal points at the row's non-negative saliencies in shared
-// memory (run-time indexed); the result is a 128-bit mask.
+// the lower column index.  sal[c * WLD] holds the row's non-negative saliencies.
 __device__ void select_keep(const float* sal, int cnt, float sparsity, int mask_n, int mask_m, unsigned (&bits)[BW / 32]) {
 #pragma unroll
     for (int i = 0; i < BW / 32; i++) bits[i] = 0u;
     if (mask_m > 0) {
         for (int c = 0; c < cnt; c++) {
             const int g0 = (c / mask_m) * mask_m;
-            const float sc = sal[c];
+            const float sc = sal[c * WLD];
             int rank = 0;
             for (int o = g0; o < g0 + mask_m && o < cnt; o++) {
-                const float so = sal[o];
+                const float so = sal[o * WLD];
                 if (so > sc || (so == sc && o < c)) rank++;
             }
             if (rank < mask_n) bits[c / 32] |= 1u << (c % 32);
@@ -66,14 +72,14 @@ __device__ void select_keep(const float* sal, int cnt, float sparsity, int mask_
     for (int bit = 31; bit >= 0; bit--) {
         const unsigned cand = prefix | (1u << bit);
         int count = 0;
-        for (int c = 0; c < cnt; c++) count += (__float_as_uint(sal[c]) >= cand) ? 1 : 0;
+        for (int c = 0; c < cnt; c++) count += (__float_as_uint(sal[c * WLD]) >= cand) ? 1 : 0;
         if (count >= k) prefix = cand;
     }
     int above = 0;
-    for (int c = 0; c < cnt; c++) above += (__float_as_uint(sal[c]) > prefix) ? 1 : 0;
+    for (int c = 0; c < cnt; c++) above += (__float_as_uint(sal[c * WLD]) > prefix) ? 1 : 0;
     int need = k - above;
     for (int c = 0; c < cnt; c++) {
-        const unsigned b = __float_as_uint(sal[c]);
+        const unsigned b = __float_as_uint(sal[c * WLD]);
         bool kp = b > prefix;
         if (!kp && b == prefix && need > 0) {
             kp = true;
@@ -86,9 +92,10 @@ __device__ void select_keep(const float* sal, int cnt, float sparsity, int mask_
 template <int MODE>  // 0 = GPTQ quantise, 1 = SparseGPT prune
 __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
-    float* Us = reinterpret_cast<float*>(smem);                 // [BW][BW]
-    float* Wt = Us + BW * BW;                                   // [ROWS][WPAD]
-    uint8_t* Ct = reinterpret_cast<uint8_t*>(Wt + ROWS * WPAD); // [ROWS][BW]
+    float* Us = reinterpret_cast<float*>(smem);                  // [BW][BW] row-major
+    float* Wt = Us + BW * BW;                                    // [BW][WLD] column-major tile
+    uint8_t* Ct = reinterpret_cast<uint8_t*>(Wt + BW * WLD);     // [BW][ROWS] codes / mask bytes
+    float* Sal = reinterpret_cast<float*>(Ct + BW * ROWS);       // MODE 1: [BW][WLD] saliencies
     const int tid = threadIdx.x;
     const int64_t r0 = (int64_t)blockIdx.x * ROWS;
     const int cnt = a.cnt;
@@ -100,29 +107,22 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
     for (int t = tid; t < ROWS * BW; t += ROWS) {
         const int rr = t / BW, c = t % BW;
         const int64_t R = r0 + rr;
-        Wt[rr * WPAD + c] = (R < a.m && c < cnt) ? a.W[R * a.ldw + a.i1 + c] : 0.f;
+        Wt[c * WLD + rr] = (R < a.m && c < cnt) ? a.W[R * a.ldw + a.i1 + c] : 0.f;
     }
     __syncthreads();
 
     const int64_t R = r0 + tid;
     const bool row_ok = R < a.m;
-    float w[BW];
-#pragma unroll
-    for (int c = 0; c < BW; c += 4) {
-        float4 v = *reinterpret_cast<const float4*>(&Wt[tid * WPAD + c]);
-        w[c] = v.x; w[c + 1] = v.y; w[c + 2] = v.z; w[c + 3] = v.w;
-    }
 
     unsigned keep[BW / 32] = {0u, 0u, 0u, 0u};
     if constexpr (MODE == 1) {
-        // Saliency w^2 / U[c][c]^2 from the block snapshot, staged in this thread's row of
-        // the W tile (the original values already live in registers).
-#pragma unroll
+        // Saliency w^2 / U[c][c]^2 from the block snapshot (before any in-block update).
         for (int c = 0; c < BW; c++) {
+            const float w = Wt[c * WLD + tid];
             const float d = Us[c * BW + c];
-            Wt[tid * WPAD + c] = __fdiv_rn(__fmul_rn(w[c], w[c]), fmaxf(__fmul_rn(d, d), 1e-10f));
+            Sal[c * WLD + tid] = __fdiv_rn(__fmul_rn(w, w), fmaxf(__fmul_rn(d, d), 1e-10f));
         }
-        select_keep(&Wt[tid * WPAD], cnt, a.sparsity, a.mask_n, a.mask_m, keep);
+        select_keep(&Sal[tid], cnt, a.sparsity, a.mask_n, a.mask_m, keep);
     }
 
     float qmin, qmax;
@@ -139,45 +139,69 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
         zf = (float)zi;
     }
 
+    for (int c0 = 0; c0 < cnt; c0 += SB) {
+        float w[SB], e[SB];
 #pragma unroll
-    for (int j = 0; j < BW; j++) {
-        if (j < cnt) {
-            float q;
-            uint8_t cb;
-            if constexpr (MODE == 0) {
-                if (j == next_edge) {
-                    g++;
-                    next_edge += a.gs;
-                    const int64_t si = row_ok ? R * a.srow + g : 0;
-                    s = a.scales[si];
-                    zi = a.zps[si];
-                    zf = (float)zi;
-                }
-                int code;
-                q = fq_chain<float>(w[j], s, zf, qmin, qmax, &code);
-                cb = a.bits <= 4 ? (uint8_t)((code - zi) & 0xF) : (uint8_t)code;
-            } else {
-                const bool kj = (keep[j / 32] >> (j % 32)) & 1u;
-                q = kj ? w[j] : 0.f;
-                cb = kj ? 1 : 0;
-            }
-            Wt[tid * WPAD + j] = q;
-            Ct[tid * BW + j] = cb;
-            const float piv = Us[j * BW + j];
-            float err = 0.f;
-            if (fabsf(piv) >= 1e-10f) {  // GptqBlockQuantizer.cs:146-150 (NumericEpsilon)
-                err = __fdiv_rn(__fsub_rn(w[j], q), piv);
+        for (int c = 0; c < SB; c++) w[c] = Wt[(c0 + c) * WLD + tid];
 #pragma unroll
-                for (int c4 = 0; c4 < BW / 4; c4++) {  // constant trip count: folds after unrolling
-                    if (4 * c4 + 3 <= j) continue;
-                    const float4 u = *reinterpret_cast<const float4*>(&Us[j * BW + 4 * c4]);
-                    if (4 * c4 + 0 > j) w[4 * c4 + 0] = fmaf(-err, u.x, w[4 * c4 + 0]);
-                    if (4 * c4 + 1 > j) w[4 * c4 + 1] = fmaf(-err, u.y, w[4 * c4 + 1]);
-                    if (4 * c4 + 2 > j) w[4 * c4 + 2] = fmaf(-err, u.z, w[4 * c4 + 2]);
-                    if (4 * c4 + 3 > j) w[4 * c4 + 3] = fmaf(-err, u.w, w[4 * c4 + 3]);
+        for (int j = 0; j < SB; j++) {
+            const int jj = c0 + j;
+            e[j] = 0.f;
+            if (jj < cnt) {
+                float q;
+                uint8_t cb;
+                if constexpr (MODE == 0) {
+                    if (jj == next_edge) {
+                        g++;
+                        next_edge += a.gs;
+                        const int64_t si = row_ok ? R * a.srow + g : 0;
+                        s = a.scales[si];
+                        zi = a.zps[si];
+                        zf = (float)zi;
+                    }
+                    int code;
+                    q = fq_chain<float>(w[j], s, zf, qmin, qmax, &code);
+                    cb = a.bits <= 4 ? (uint8_t)((code - zi) & 0xF) : (uint8_t)code;
+                } else {
+                    const bool kj = (keep[jj / 32] >> (jj % 32)) & 1u;
+                    q = kj ? w[j] : 0.f;
+                    cb = kj ? 1 : 0;
                 }
+                Wt[jj * WLD + tid] = q;
+                Ct[jj * ROWS + tid] = cb;
+                const float piv = Us[jj * BW + jj];
+                if (fabsf(piv) >= 1e-10f) {  // GptqBlockQuantizer.cs:146-150 (NumericEpsilon)
+                    const float err = __fdiv_rn(__fsub_rn(w[j], q), piv);
+                    e[j] = err;
+#pragma unroll
+                    for (int c4 = 0; c4 < SB / 4; c4++) {  // constant trip count: folds after unrolling
+                        if (4 * c4 + 3 <= j) continue;
+                        const float4 u = *reinterpret_cast<const float4*>(&Us[jj * BW + c0 + 4 * c4]);
+                        if (4 * c4 + 0 > j) w[4 * c4 + 0] = fmaf(-err, u.x, w[4 * c4 + 0]);
+                        if (4 * c4 + 1 > j) w[4 * c4 + 1] = fmaf(-err, u.y, w[4 * c4 + 1]);
+                        if (4 * c4 + 2 > j) w[4 * c4 + 2] = fmaf(-err, u.z, w[4 * c4 + 2]);
+                        if (4 * c4 + 3 > j) w[4 * c4 + 3] = fmaf(-err, u.w, w[4 * c4 + 3]);
+                    }
+                }
+                if (row_ok) a.err1t[(int64_t)jj * a.m + R] = e[j];
             }
-            if (row_ok) a.err1t[(int64_t)j * a.m + R] = err;
+        }
+        // This sub-block's errors update the block's later columns (shared memory).
+        for (int c = c0 + SB; c < cnt; c += 4) {
+            float v0 = Wt[(c + 0) * WLD + tid], v1 = Wt[(c + 1) * WLD + tid];
+            float v2 = Wt[(c + 2) * WLD + tid], v3 = Wt[(c + 3) * WLD + tid];
+#pragma unroll
+            for (int j = 0; j < SB; j++) {
+                const float4 u = *reinterpret_cast<const float4*>(&Us[(c0 + j) * BW + c]);
+                v0 = fmaf(-e[j], u.x, v0);
+                v1 = fmaf(-e[j], u.y, v1);
+                v2 = fmaf(-e[j], u.z, v2);
+                v3 = fmaf(-e[j], u.w, v3);
+            }
+            Wt[(c + 0) * WLD + tid] = v0;
+            Wt[(c + 1) * WLD + tid] = v1;
+            Wt[(c + 2) * WLD + tid] = v2;
+            Wt[(c + 3) * WLD + tid] = v3;
         }
     }
     __syncthreads();
@@ -186,7 +210,7 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
     for (int t = tid; t < ROWS * BW; t += ROWS) {
         const int rr = t / BW, c = t % BW;
         const int64_t RR = r0 + rr;
-        if (RR < a.m && c < cnt) a.W[RR * a.ldw + a.i1 + c] = Wt[rr * WPAD + c];
+        if (RR < a.m && c < cnt) a.W[RR * a.ldw + a.i1 + c] = Wt[c * WLD + rr];
     }
     if (MODE == 0 && a.codes) {
         if (a.bits <= 4) {
@@ -202,15 +226,15 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
                 const bool hi_in = ch >= a.i1 && ch < a.i1 + cnt;
                 const bool lo_in = cl >= a.i1 && cl < a.i1 + cnt && cl < a.n;
                 uint8_t v = (hi_in && (lo_in || cl >= a.n)) ? 0 : *p;
-                if (hi_in) v = (uint8_t)((v & 0x0F) | (Ct[rr * BW + (ch - a.i1)] << 4));
-                if (lo_in) v = (uint8_t)((v & 0xF0) | Ct[rr * BW + (cl - a.i1)]);
+                if (hi_in) v = (uint8_t)((v & 0x0F) | (Ct[(ch - a.i1) * ROWS + rr] << 4));
+                if (lo_in) v = (uint8_t)((v & 0xF0) | Ct[(cl - a.i1) * ROWS + rr]);
                 *p = v;
             }
         } else {
             for (int t = tid; t < ROWS * BW; t += ROWS) {
                 const int rr = t / BW, c = t % BW;
                 const int64_t RR = r0 + rr;
-                if (RR < a.m && c < cnt) a.codes[RR * a.crow + a.i1 + c] = Ct[rr * BW + c];
+                if (RR < a.m && c < cnt) a.codes[RR * a.crow + a.i1 + c] = Ct[c * ROWS + rr];
             }
         }
     }
@@ -218,33 +242,57 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
         for (int t = tid; t < ROWS * BW; t += ROWS) {
             const int rr = t / BW, c = t % BW;
             const int64_t RR = r0 + rr;
-            if (RR < a.m && c < cnt) a.mask[RR * a.mrow + a.i1 + c] = Ct[rr * BW + c];
+            if (RR < a.m && c < cnt) a.mask[RR * a.mrow + a.i1 + c] = Ct[c * ROWS + rr];
         }
     }
 }
 
+// Per-tensor parameters of one weight replicated over its rows (batched per-tensor GPTQ).
+__global__ void expand_rows_kernel(const float* s, const int32_t* z, int64_t rows, float* rs, int32_t* rz) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += (int64_t)gridDim.x * blockDim.x) {
+        rs[i] = s[0];
+        rz[i] = z[0];
+    }
+}
+
+// Columns whose block errors are applied to the far tail in one GEMM: the tail update
+// W[:, i2:] -= Err1 U[i1:i2, i2:] of GptqBlockQuantizer.cs:173-180 is split into a near part
+// (inside the super-block, after every block) and a far part (after the super-block, one
+// K = SUPER product).  The sum is the same; the fp32 tail of W is rewritten 4x less often.
+constexpr int SUPER_BLOCKS = 4;
+
 template <int MODE>
 llmc_status run_blocks(llmc_ctx* ctx, BlockArgs a, int block_size) {
     static bool attr_set = false;
-    const size_t smem = block_smem_bytes();
+    const size_t smem = block_smem_bytes<MODE>();
     if (!attr_set) {
         LLMC_CUDA_TRY(cudaFuncSetAttribute(block_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr_set = true;
     }
     const int bs = block_size < 1 ? BW : (block_size > BW ? BW : block_size);
+    const int64_t super = (int64_t)bs * SUPER_BLOCKS;
     const unsigned grid = (unsigned)((a.m + ROWS - 1) / ROWS);
-    for (int64_t i1 = 0; i1 < a.n; i1 += bs) {
-        const int cnt = (int)min((int64_t)bs, a.n - i1);
-        a.i1 = i1;
-        a.cnt = cnt;
-        block_kernel<MODE><<<grid, ROWS, smem, ctx->stream>>>(a);
-        LLMC_TRY(check_launch(ctx, "gptq_block"));
-        const int64_t i2 = i1 + cnt;
-        if (i2 < a.n) {
-            // W[:, i2:] -= Err1 @ U[i1:i2, i2:]   (GptqBlockQuantizer.cs:173-180)
-            GemmArgs g{a.m, a.n - i2, cnt, a.err1t, a.m, 1, LLMC_DTYPE_F32, a.U + i1 * a.ldu + i2, a.ldu, 0,
-                       LLMC_DTYPE_F32, a.W + i2, a.ldw, -1.f, 1.f};
-            LLMC_TRY(gemm_f32(ctx, g));
+    float* err_all = a.err1t;  // [super, m]: the super-block's errors, block after block
+    for (int64_t s0 = 0; s0 < a.n; s0 += super) {
+        const int64_t s1 = min(a.n, s0 + super);
+        for (int64_t i1 = s0; i1 < s1; i1 += bs) {
+            const int cnt = (int)min((int64_t)bs, s1 - i1);
+            a.i1 = i1;
+            a.cnt = cnt;
+            a.err1t = err_all + (i1 - s0) * a.m;
+            block_kernel<MODE><<<grid, ROWS, smem, ctx->stream>>>(a);
+            LLMC_TRY(check_launch(ctx, "gptq_block"));
+            const int64_t i2 = i1 + cnt;
+            if (i2 < s1) {  // near: W[:, i2:s1] -= Err1 U[i1:i2, i2:s1]
+                GemmArgs gm{a.m, s1 - i2, cnt, a.err1t, a.m, 1, LLMC_DTYPE_F32, a.U + i1 * a.ldu + i2, a.ldu, 0,
+                            LLMC_DTYPE_F32, a.W + i2, a.ldw, -1.f, 1.f};
+                LLMC_TRY(gemm_f32(ctx, gm));
+            }
+        }
+        if (s1 < a.n) {  // far: W[:, s1:] -= Err[s0:s1] U[s0:s1, s1:]
+            GemmArgs gm{a.m, a.n - s1, s1 - s0, err_all, a.m, 1, LLMC_DTYPE_F32, a.U + s0 * a.ldu + s1, a.ldu, 0,
+                        LLMC_DTYPE_F32, a.W + s1, a.ldw, -1.f, 1.f};
+            LLMC_TRY(gemm_f32(ctx, gm));
         }
     }
     return LLMC_OK;
@@ -252,54 +300,108 @@ llmc_status run_blocks(llmc_ctx* ctx, BlockArgs a, int block_size) {
 
 }  // namespace
 
-llmc_status gptq(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64_t n, int64_t ldw, const float* U, int64_t ldu,
-                 const llmc_qconfig* cfg, float* wq_out, int64_t ldq, uint8_t* codes, float* scales_out,
-                 int32_t* zps_out, int mode, uint8_t* mask_out) {
+// count weights [m_k, n] sharing U; outputs are stacked in weight order (rows sum(m_k)).
+// Per-tensor parameters come out one per weight; channel / group parameters per stacked row.
+llmc_status gptq_batch(llmc_ctx* ctx, int count, const void* const* Ws, const int64_t* ms, const int64_t* ldws, int dtype,
+                       int64_t n, const float* U, int64_t ldu, const llmc_qconfig* cfg, float* wq_out, int64_t ldq,
+                       uint8_t* codes, float* scales_out, int32_t* zps_out, int mode, uint8_t* mask_out) {
     const int strategy = cfg->strategy;
+    int64_t M = 0, mmax = 0;
+    for (int k = 0; k < count; k++) {
+        M += ms[k];
+        mmax = ms[k] > mmax ? ms[k] : mmax;
+    }
     const int64_t gs = strategy == LLMC_STRATEGY_GROUP ? cfg->group_size : n;
     const int64_t G = n_groups(strategy, n, gs);
-    const int64_t nparams = strategy == LLMC_STRATEGY_TENSOR ? 1 : m * G;
-    // Scratch: working copy (unless the caller's wq_out is used), Err1^T, params, reduction.
+    const bool tensor = strategy == LLMC_STRATEGY_TENSOR;
+    const int64_t nrow_params = tensor ? M : M * G;  // what the block kernel indexes
+    // Scratch: working copy (unless wq_out is used), Err1^T, params, reduction.
     const bool own_work = wq_out == nullptr;
     size_t need = 0;
-    need += own_work ? (size_t)m * n * 4 + 256 : 0;
-    need += (size_t)BW * m * 4 + 256;
-    need += (size_t)nparams * 2 * 8 + 512;        // mins/maxs (+ scales/zps when not returned)
-    need += (size_t)(2 * m + 128) * 4 + 256;      // per-tensor reduction scratch
+    need += own_work ? (size_t)M * n * 4 + 256 : 0;
+    need += (size_t)BW * SUPER_BLOCKS * M * 4 + 256;
+    need += (size_t)(tensor ? 2 * count : M * G) * 2 * 4 + 1024;  // mins/maxs
+    need += (size_t)nrow_params * 8 + 512;                          // per-row params (kernel side)
+    need += (size_t)(tensor ? count : 0) * 8 + 512;                 // per-weight params if not returned
+    need += (size_t)(2 * mmax + 128) * 4 + 256;                     // per-tensor reduction scratch
     void* wsp;
     LLMC_TRY(workspace(ctx, need, &wsp));
     Carver cv{(char*)wsp};
-    float* work = own_work ? cv.take<float>((size_t)m * n) : wq_out;
+    float* work = own_work ? cv.take<float>((size_t)M * n) : wq_out;
     const int64_t ldwork = own_work ? n : ldq;
-    float* err1t = cv.take<float>((size_t)BW * m);
-    float* mins = cv.take<float>(nparams);
-    float* maxs = cv.take<float>(nparams);
-    float* scales = scales_out ? scales_out : cv.take<float>(nparams);
-    int32_t* zps = zps_out ? zps_out : cv.take<int32_t>(nparams);
-    float* red = cv.take<float>(2 * m + 128);
+    float* err1t = cv.take<float>((size_t)BW * SUPER_BLOCKS * M);
+    float* mins = cv.take<float>(tensor ? 2 * count : M * G);
+    float* maxs = cv.take<float>(tensor ? 2 * count : M * G);
+    float* krs = nullptr;
+    int32_t* krz = nullptr;
+    float* ts = nullptr;
+    int32_t* tz = nullptr;
+    if (tensor) {
+        krs = cv.take<float>(M);
+        krz = cv.take<int32_t>(M);
+        ts = scales_out ? scales_out : cv.take<float>(count);
+        tz = zps_out ? zps_out : cv.take<int32_t>(count);
+    } else {
+        krs = scales_out ? scales_out : cv.take<float>(M * G);
+        krz = zps_out ? zps_out : cv.take<int32_t>(M * G);
+    }
+    float* red = cv.take<float>(2 * mmax + 128);
+
+    // Stacked fp32 working copy of the ORIGINAL weights.
+    int64_t off = 0;
+    for (int k = 0; k < count; k++) {
+        LLMC_TRY(convert_to_f32(ctx, Ws[k], dtype, ms[k], n, ldws[k], work + off * ldwork, ldwork));
+        off += ms[k];
+    }
 
     BlockArgs a{};
-    a.W = work; a.ldw = ldwork; a.m = m; a.n = n;
+    a.W = work; a.ldw = ldwork; a.m = M; a.n = n;
     a.U = U; a.ldu = ldu;
     a.bits = cfg->num_bits; a.sym = cfg->symmetric;
     a.err1t = err1t;
     if (mode == 0) {
-        // ComputeScaleZeroPoint from the ORIGINAL weight (GptqBlockQuantizer.cs:97, :196-234).
-        LLMC_TRY(minmax(ctx, W, dtype, m, n, ldw, strategy, gs, mins, maxs, 0, red));
-        LLMC_TRY(affine(ctx, mins, maxs, nparams, cfg->num_bits, cfg->symmetric, scales, zps));
-        a.scales = scales; a.zps = zps;
-        a.srow = strategy == LLMC_STRATEGY_TENSOR ? 0 : (strategy == LLMC_STRATEGY_CHANNEL ? 1 : G);
-        a.gs = strategy == LLMC_STRATEGY_GROUP ? gs : n;
+        // ComputeScaleZeroPoint from the ORIGINAL weight (GptqBlockQuantizer.cs:97, :196-234);
+        // the fp32 copy holds exactly the original values.
+        if (tensor) {
+            off = 0;
+            for (int k = 0; k < count; k++) {
+                LLMC_TRY(minmax(ctx, work + off * ldwork, LLMC_DTYPE_F32, ms[k], n, ldwork, LLMC_STRATEGY_TENSOR, n,
+                                mins + k, maxs + k, 0, red));
+                off += ms[k];
+            }
+            LLMC_TRY(affine(ctx, mins, maxs, count, cfg->num_bits, cfg->symmetric, ts, tz));
+            off = 0;
+            for (int k = 0; k < count; k++) {
+                expand_rows_kernel<<<(unsigned)((ms[k] + 255) / 256), 256, 0, ctx->stream>>>(ts + k, tz + k, ms[k],
+                                                                                              krs + off, krz + off);
+                LLMC_TRY(check_launch(ctx, "expand_rows"));
+                off += ms[k];
+            }
+            a.srow = 1;
+            a.gs = n;
+        } else {
+            LLMC_TRY(minmax(ctx, work, LLMC_DTYPE_F32, M, n, ldwork, strategy, gs, mins, maxs, 0, red));
+            LLMC_TRY(affine(ctx, mins, maxs, M * G, cfg->num_bits, cfg->symmetric, krs, krz));
+            a.srow = G;
+            a.gs = strategy == LLMC_STRATEGY_GROUP ? gs : n;
+        }
+        a.scales = krs; a.zps = krz;
         a.codes = codes;
         a.crow = cfg->num_bits <= 4 ? (n + 1) / 2 : n;
-    } else {
-        a.srow = 0; a.gs = n;
-        a.sparsity = cfg->sparsity; a.mask_n = cfg->mask_n; a.mask_m = cfg->mask_m;
-        a.mask = mask_out; a.mrow = n;
+        return run_blocks<0>(ctx, a, cfg->block_size);
     }
-    LLMC_TRY(convert_to_f32(ctx, W, dtype, m, n, ldw, work, ldwork));
-    if (mode == 0) return run_blocks<0>(ctx, a, cfg->block_size);
+    a.srow = 0; a.gs = n;
+    a.sparsity = cfg->sparsity; a.mask_n = cfg->mask_n; a.mask_m = cfg->mask_m;
+    a.mask = mask_out; a.mrow = n;
     return run_blocks<1>(ctx, a, cfg->block_size);
+}
+
+llmc_status gptq(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64_t n, int64_t ldw, const float* U, int64_t ldu,
+                 const llmc_qconfig* cfg, float* wq_out, int64_t ldq, uint8_t* codes, float* scales_out,
+                 int32_t* zps_out, int mode, uint8_t* mask_out) {
+    const void* ws[1] = {W};
+    const int64_t mm[1] = {m}, ll[1] = {ldw};
+    return gptq_batch(ctx, 1, ws, mm, ll, dtype, n, U, ldu, cfg, wq_out, ldq, codes, scales_out, zps_out, mode, mask_out);
 }
 
 }  // namespace llmc

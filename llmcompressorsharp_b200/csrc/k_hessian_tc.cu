@@ -28,11 +28,14 @@
 // Every wait is bounded: on expiry the kernel raises an error word, drains its own
 // in-flight copies (again bounded), frees TMEM and returns.
 #include "ops.h"
+#include "tc_common.cuh"
 
 #include <cuda.h>
 
 namespace llmc {
 namespace {
+
+using namespace tc;
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int EPI_WARPS = 8, NT = 32 * (2 + EPI_WARPS);  // producer, MMA issuer, 8 epilogue warps
@@ -45,7 +48,6 @@ constexpr int BOX_BYTES = 64 * BK * 2;           // 8 KB: 64 features x 64 token
 constexpr int STG_LD = BN + 4;                   // fp32 staging row stride (floats)
 constexpr int SMEM_MAIN = STAGES * STAGE_BYTES;  // 192 KB (reused as 130 KB staging)
 constexpr int SMEM_BYTES = SMEM_MAIN + 1024 /*align slack*/ + 256 /*barriers*/;
-constexpr unsigned WAIT_LIMIT = 1u << 26;        // try_wait attempts before giving up
 constexpr int MAX_TJ = 160;                      // d <= 40960
 
 static_assert(BM * STG_LD * 4 <= SMEM_MAIN, "epilogue staging must fit in the stage ring");
@@ -63,107 +65,6 @@ struct SyrkArgs {
     int* err;         // device error word (bit 0: a wait timed out)
     uint32_t idesc;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait; returns false (and raises the abort flag) when it gives up or when
-// another thread has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
-    for (unsigned i = 0; i < WAIT_LIMIT; i++) {
-        if (mbar_try_wait(b, parity)) return true;
-        if ((i & 255u) == 255u && *abort_flag) return false;
-    }
-    *abort_flag = 1;
-    atomicOr(err, 1);
-    return false;
-}
-
-// Bounded wait that ignores the abort flag (used only to drain after an abort).
-__device__ __forceinline__ void mbar_wait_drain(uint64_t* b, uint32_t parity) {
-    for (unsigned i = 0; i < WAIT_LIMIT; i++)
-        if (mbar_try_wait(b, parity)) return;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-// UMMA shared-memory descriptor for an MN-major, 128-byte-swizzled operand whose 64-element
-// MN chunks are `lbo` bytes apart and whose 8-row K groups are 1024 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t lbo) {
-    uint64_t d = 0;
-    d |= (uint64_t)((addr >> 4) & 0x3FFFu);             // start address  [0,14)
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;        // leading byte offset [16,30)
-    d |= (uint64_t)((1024u >> 4) & 0x3FFFu) << 32;      // stride byte offset  [32,46)
-    d |= (uint64_t)1 << 46;                             // descriptor version (sm100)
-    d |= (uint64_t)2 << 61;                             // layout: SWIZZLE_128B
-    return d;
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
-        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const float* ssrc, uint32_t bytes) {
-    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;"
-                 ::"l"(reinterpret_cast<uint64_t>(gdst)), "r"(smem_u32(ssrc)), "r"(bytes)
-                 : "memory");
-}
 
 __device__ __forceinline__ void unit_tile(const SyrkArgs& a, int tile, int* ti, int* tj) {
     int lo = 0, hi = a.ntj - 1;  // find tj with tile_off[tj] <= tile < tile_off[tj+1]

@@ -22,6 +22,8 @@ struct GemmArgs {
     int a_tri = 0, b_tri = 0, c_mode = 0, split_k = 1;
 };
 llmc_status gemm_f32(llmc_ctx* ctx, const GemmArgs& g);
+// Tensor-core (3 x TF32) path of gemm_f32; LLMC_ERR_UNSUPPORTED when the shape does not fit it.
+llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g);
 
 // ---- tcgen05 symmetric rank-k update (k_hessian_tc.cu) ------------------------------------
 // H[upper tiles] += X^T X for bf16/f16 X [rows, d] (row stride ld).  Returns

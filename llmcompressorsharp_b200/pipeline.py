@@ -62,8 +62,9 @@ class GptqPipeline:
             _lib.call("llmc_hessian_create", self.c, C.c_int64(s.d), C.byref(p))
             self.h[s.name] = p.value
         self.u = torch.empty(maxd * maxd, dtype=torch.float32, device=device)
-        maxm = max(m for s in sites for _, m in s.weights)
-        self.work = torch.empty(maxm * maxd, dtype=torch.float32, device=device)
+        # fp32 working copy of the largest stacked solve (rows of all weights of one site)
+        self.work = torch.empty(max(sum(m for _, m in s.weights) * s.d for s in sites), dtype=torch.float32,
+                                device=device)
 
     def close(self):
         for p in self.h.values():
@@ -89,41 +90,64 @@ class GptqPipeline:
             out_h.copy_(torch.as_tensor(_HView(self.hessian_ptr(site.name), site.d), device=self.device))
 
     def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict):
-        """U from the site's H (upper triangle), then GPTQ of each weight reading the site."""
+        """U from the site's H (upper triangle), then one stacked GPTQ solve of every weight
+        that reads the site (outputs are views into stacked per-site buffers)."""
         d = site.d
         _lib.ctx_for(self.device.index)
         _lib.call("llmc_chol_inverse", self.c, C.c_void_p(h_ptr), C.c_int64(d), C.c_int64(d),
                   C.c_float(self.cfg.dampening_frac), 1, _lib.ptr(self.u), C.c_int64(d), 1)
-        for wname, m in site.weights:
-            w = weights[wname]
-            out = outputs[wname]
-            wq = out.get("wq")
-            if wq is None:
-                wq = self.work[: m * d].view(m, d)
-            _lib.call("llmc_gptq_quantize", self.c, _lib.ptr(w), _lib.dtype_code(w.dtype), C.c_int64(m), C.c_int64(d),
-                      C.c_int64(w.stride(0)), _lib.ptr(self.u), C.c_int64(d), C.byref(self.qc), _lib.ptr(wq),
-                      C.c_int64(d), _lib.ptr(out["codes"]), _lib.ptr(out["scales"]), _lib.ptr(out["zero_points"]))
+        names = [w for w, _ in site.weights]
+        ms = [m for _, m in site.weights]
+        k = len(names)
+        wp = (C.c_void_p * k)(*[weights[w].data_ptr() for w in names])
+        mp = (C.c_int64 * k)(*ms)
+        lp = (C.c_int64 * k)(*[weights[w].stride(0) for w in names])
+        st = outputs[_stack_key(site)]
+        wq = st.get("wq")
+        if wq is None:
+            wq = self.work[: sum(ms) * d].view(sum(ms), d)
+        _lib.call("llmc_gptq_quantize_batch", self.c, C.c_int32(k), wp, mp, lp, _lib.dtype_code(weights[names[0]].dtype),
+                  C.c_int64(d), _lib.ptr(self.u), C.c_int64(d), C.byref(self.qc), _lib.ptr(wq), C.c_int64(d),
+                  _lib.ptr(st["codes"]), _lib.ptr(st["scales"]), _lib.ptr(st["zero_points"]))
 
     def alloc_outputs(self, layer_weights: dict):
+        """Stacked per-site output buffers plus per-weight views into them."""
         outs = {}
         for s in self.sites:
-            for wname, m in s.weights:
-                n = s.d
-                shp = param_shape(self.cfg.strategy, m, n, self.cfg.group_size)
-                outs[wname] = {
-                    "codes": torch.empty(m, (n + 1) // 2 if self.cfg.num_bits <= 4 else n, dtype=torch.uint8,
-                                         device=self.device),
-                    "scales": torch.empty(shp, dtype=torch.float32, device=self.device),
-                    "zero_points": torch.empty(shp, dtype=torch.int32, device=self.device),
-                }
-                if self.keep_wq:
-                    outs[wname]["wq"] = torch.empty(m, n, dtype=torch.float32, device=self.device)
+            n = s.d
+            M = sum(m for _, m in s.weights)
+            stacked = {
+                "codes": torch.empty(M, (n + 1) // 2 if self.cfg.num_bits <= 4 else n, dtype=torch.uint8,
+                                     device=self.device),
+                "scales": torch.empty(param_shape(self.cfg.strategy, M, n, self.cfg.group_size), dtype=torch.float32,
+                                      device=self.device),
+                "zero_points": torch.empty(param_shape(self.cfg.strategy, M, n, self.cfg.group_size), dtype=torch.int32,
+                                           device=self.device),
+            }
+            if self.cfg.strategy == "tensor":
+                stacked["scales"] = torch.empty(len(s.weights), dtype=torch.float32, device=self.device)
+                stacked["zero_points"] = torch.empty(len(s.weights), dtype=torch.int32, device=self.device)
+            if self.keep_wq:
+                stacked["wq"] = torch.empty(M, n, dtype=torch.float32, device=self.device)
+            outs[_stack_key(s)] = stacked
+            r0 = 0
+            for i, (wname, m) in enumerate(s.weights):
+                view = {}
+                for f, t in stacked.items():
+                    view[f] = t[i:i + 1] if (self.cfg.strategy == "tensor" and f in ("scales", "zero_points")) \
+                        else t[r0:r0 + m]
+                outs[wname] = view
+                r0 += m
         return outs
 
     def run_layer(self, acts: dict, weights: dict, outputs: dict):
         for s in self.sites:
             self.accumulate(s, acts[s.name])
             self.solve_site(s, self.hessian_ptr(s.name), weights, outputs)
+
+
+def _stack_key(site: SiteSpec) -> str:
+    return "__stacked__" + site.name
 
 
 class _HView:

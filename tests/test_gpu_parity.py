@@ -201,6 +201,23 @@ def test_inverse_matches_oracle(d):
     assert torch.count_nonzero(torch.tril(u.cpu(), -1)) == 0
 
 
+@pytest.mark.parametrize("d", [1024, 2048, 4096])
+def test_inverse_large_matches_oracle(d):
+    """Sizes whose recursion GEMMs run on the tensor cores (3 x TF32)."""
+    from llmcompressorsharp_b200 import HessianInverseSolver
+
+    g = torch.Generator().manual_seed(d)
+    x = torch.randn(2 * d, d, generator=g) @ (torch.eye(d) + 0.3 * torch.randn(d, d, generator=g) / d ** 0.5)
+    h = x.t() @ x
+    ref = o_hess.hessian_inverse(h, 0.01)
+    uref = o_hess.upper_factor(ref)
+    hinv = HessianInverseSolver.compute(h.to(DEV), 0.01)
+    u = HessianInverseSolver.upper(h.to(DEV), 0.01)
+    assert rel_fro(hinv, ref) < 1e-4
+    assert rel_fro(u, uref) < 1e-4
+    assert torch.count_nonzero(torch.tril(u.cpu(), -1)) == 0
+
+
 def test_inverse_upper_only_reads_upper_triangle():
     from llmcompressorsharp_b200 import HessianInverseSolver
 
@@ -426,9 +443,50 @@ def test_gptq_matches_oracle(strategy, bits, sym, m, n, bs):
     check_gptq(w, h, dict(num_bits=bits, symmetric=sym, strategy=strategy, block_size=bs, group_size=gs))
 
 
+@pytest.mark.parametrize("m,n", [(512, 2048), (384, 4096)])
+def test_gptq_large_matches_oracle(m, n):
+    """Tail updates large enough for the tensor-core GEMM."""
+    w, h = gptq_case(m, n, m + n, torch.bfloat16)
+    check_gptq(w, h, dict(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128))
+
+
 def test_gptq_bf16_weight_smollm_shape():
     w, h = gptq_case(576, 1536, 21, torch.bfloat16)
     check_gptq(w, h, dict(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128))
+
+
+@pytest.mark.parametrize("strategy", ["tensor", "channel", "group"])
+def test_gptq_batch_equals_separate(strategy):
+    """llmc_gptq_quantize_batch over q/k/v-like weights sharing one U gives exactly the
+    per-weight results (rows are independent given U)."""
+    import ctypes as C
+    from llmcompressorsharp_b200 import GPTQConfig, _lib, gptq_quantize_u
+    from llmcompressorsharp_b200.gptq import param_shape
+
+    n = 256
+    _, h = gptq_case(8, n, 41)
+    u = o_hess.upper_factor(o_hess.hessian_inverse(h, 0.01)).to(DEV)
+    g = torch.Generator().manual_seed(42)
+    ws = [(torch.randn(m, n, generator=g) * 0.02).to(torch.bfloat16).to(DEV) for m in (192, 64, 64)]
+    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy=strategy, group_size=128)
+    sep = [gptq_quantize_u(w, u, cfg) for w in ws]
+    M = sum(w.shape[0] for w in ws)
+    wq = torch.empty(M, n, device=DEV)
+    codes = torch.empty(M, n // 2, dtype=torch.uint8, device=DEV)
+    shp = (3,) if strategy == "tensor" else param_shape(strategy, M, n, 128)
+    sc = torch.empty(shp, device=DEV)
+    zp = torch.empty(shp, dtype=torch.int32, device=DEV)
+    wp = (C.c_void_p * 3)(*[w.data_ptr() for w in ws])
+    mp = (C.c_int64 * 3)(*[w.shape[0] for w in ws])
+    lp = (C.c_int64 * 3)(*[n] * 3)
+    qc = cfg.to_c()
+    _lib.call("llmc_gptq_quantize_batch", C.c_void_p(_lib.ctx_for(0)), C.c_int32(3), wp, mp, lp,
+              _lib.dtype_code(torch.bfloat16), C.c_int64(n), _lib.ptr(u), C.c_int64(n), C.byref(qc), _lib.ptr(wq),
+              C.c_int64(n), _lib.ptr(codes), _lib.ptr(sc), _lib.ptr(zp))
+    assert torch.equal(wq, torch.cat([r.wq for r in sep]))
+    assert torch.equal(codes, torch.cat([r.codes for r in sep]))
+    assert torch.equal(sc, torch.cat([r.scales for r in sep]))
+    assert torch.equal(zp, torch.cat([r.zero_points for r in sep]))
 
 
 def test_gptq_kats():  # GptqBlockQuantizerTests.cs
