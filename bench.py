@@ -283,7 +283,9 @@ def run_ours(args):
                          "frac": round(achieved / sustained, 3),
                          "peak_note": f"{src} sustained bf16 (kernel runs inside a ~{ms / 1e3:.0f} s step)",
                          "algorithmic": "d(d+1)T FLOP per launch (symmetric rank-k update of T tokens)",
-                         "traffic": SYRK_TRAFFIC_PER_LAUNCH},
+                         "traffic": SYRK_TRAFFIC_PER_LAUNCH,
+                         "traffic_note": "ncu DRAM read+write bytes of one d=4096, 65,536-token launch; "
+                                         "its algorithmic bytes are 0.60 GB (X once + H upper triangle)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
@@ -296,9 +298,9 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# DRAM bytes per syrk_tc launch (d = 4096, 65,536 tokens) from the committed ncu capture
-# profiles/syrk_tc_kernel.md; filled in when that capture exists.
-SYRK_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) of one syrk_tc launch at d = 4096 over 65,536 tokens, from the ncu
+# capture summarised in profiles/syrk_tc_kernel_d4096_t65536.md (965.5 MB read + 368.4 MB written).
+SYRK_TRAFFIC_PER_LAUNCH = 1.334e9
 
 
 def _randn_bf16(m, n, dev, g, std=1.0):
