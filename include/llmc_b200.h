@@ -174,6 +174,20 @@ llmc_status llmc_sparsegpt_prune(llmc_ctx* ctx, const void* W, int32_t dtype, in
  * observer), 0 overwrites. */
 llmc_status llmc_observer_minmax(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows, int64_t cols, int64_t ld,
                                  int32_t strategy, int64_t group_size, float* min_io, float* max_io, int32_t accumulate);
+
+/* Per-tensor llmc_observer_minmax that allocates no device memory when called.  It has no
+ * counterpart in the reference: it serves callers that may not allocate or free device
+ * memory mid-run (an activation hook on a model's stream, where cudaFree's device-wide wait
+ * would stall the forward; a host whose caching allocator owns a fixed memory budget).
+ * Its row buffer is a fixed array in the library, so rows <= LLMC_NOALLOC_MINMAX_MAX_ROWS
+ * (larger: LLMC_ERR_SHAPE, nothing launched).  The first call on a device looks up that
+ * array's address; make it before any stream capture.  All calls on a device share the
+ * array, so calls that can overlap (two streams, two threads) race: order them on one
+ * stream.  Arguments as llmc_observer_minmax with strategy TENSOR; output count 1. */
+#define LLMC_NOALLOC_MINMAX_MAX_ROWS 65536
+llmc_status llmc_observer_minmax_tensor_noalloc(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows,
+                                                int64_t cols, int64_t ld, float* min_io, float* max_io,
+                                                int32_t accumulate);
 /* Observer.ComputeAffineParams (Observer.cs:47-75), element-wise over count pairs. */
 llmc_status llmc_affine_params(llmc_ctx* ctx, const float* mins, const float* maxs, int64_t count, int32_t num_bits,
                                int32_t symmetric, float* scale_out, int32_t* zp_out);

@@ -65,6 +65,7 @@ _SIGS = {
     "llmc_gptq_quantize_batch": [P, I32, P, P, P, I32, I64, P, I64, C.POINTER(QConfig), P, I64, P, P, P],
     "llmc_sparsegpt_prune": [P, P, I32, I64, I64, I64, P, I64, C.POINTER(QConfig), P, I64, P],
     "llmc_observer_minmax": [P, P, I32, I64, I64, I64, I32, I64, P, P, I32],
+    "llmc_observer_minmax_tensor_noalloc": [P, P, I32, I64, I64, I64, P, P, I32],
     "llmc_affine_params": [P, P, P, I64, I32, I32, P, P],
     "llmc_fake_quantize": [P, P, I32, I64, F32, I32, I32, I32, P, P],
     "llmc_rtn_quantize": [P, P, I32, I64, I64, I64, C.POINTER(QConfig), P, P, P, P],
