@@ -86,6 +86,10 @@ llmc_status llmc_destroy(llmc_ctx* ctx);
  * (non-blocking) stream.  To run on the legacy default stream pass cudaStreamLegacy
  * ((void*)0x1), not NULL. */
 llmc_status llmc_set_stream(llmc_ctx* ctx, void* stream);
+/* Cap the number of SMs that this context's persistent Hessian kernel occupies (0 = all).
+ * No reference counterpart: it lets a second context on the same device (one solving the
+ * previous layer on another stream) run on the SMs left free while this one accumulates. */
+llmc_status llmc_set_sm_limit(llmc_ctx* ctx, int32_t sms);
 llmc_status llmc_sync(llmc_ctx* ctx);
 /* Number of kernels this context has launched since creation (diagnostics / bench). */
 llmc_status llmc_launch_count(llmc_ctx* ctx, int64_t* out);

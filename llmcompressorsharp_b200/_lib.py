@@ -49,6 +49,7 @@ _SIGS = {
     "llmc_init": [I32, C.POINTER(P)],
     "llmc_destroy": [P],
     "llmc_set_stream": [P, P],
+    "llmc_set_sm_limit": [P, I32],
     "llmc_sync": [P],
     "llmc_launch_count": [P, C.POINTER(I64)],
     "llmc_hessian_create": [P, I64, C.POINTER(P)],

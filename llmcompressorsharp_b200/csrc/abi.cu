@@ -177,6 +177,13 @@ llmc_status llmc_set_stream(llmc_ctx* ctx, void* stream) {
     return LLMC_OK;
 }
 
+llmc_status llmc_set_sm_limit(llmc_ctx* ctx, int32_t sms) {
+    CTX_CHECK(ctx);
+    if (sms < 0) return fail(LLMC_ERR_INVALID_ARG, "sm limit must be >= 0 (0 = no limit)");
+    ctx->sm_limit = sms;
+    return LLMC_OK;
+}
+
 llmc_status llmc_sync(llmc_ctx* ctx) {
     CTX_CHECK(ctx);
     return device_error_check(ctx);

@@ -37,6 +37,8 @@ llmc_status fail(llmc_status st, const char* fmt, ...);
 struct llmc_ctx {
     int device = 0;
     int sm_count = 148;
+    // SMs the persistent Hessian kernel may occupy (0 = all); see llmc_set_sm_limit.
+    int sm_limit = 0;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     int64_t launches = 0;
@@ -85,6 +87,11 @@ inline llmc_status check_launch(llmc_ctx* ctx, const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(LLMC_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(e));
     return LLMC_OK;
+}
+
+// Grid size for a persistent kernel of this context: the SM count, capped by llmc_set_sm_limit.
+inline int persistent_sms(const llmc_ctx* ctx) {
+    return (ctx->sm_limit > 0 && ctx->sm_limit < ctx->sm_count) ? ctx->sm_limit : ctx->sm_count;
 }
 
 inline int dtype_size(int32_t dt) { return dt == LLMC_DTYPE_F32 ? 4 : 2; }

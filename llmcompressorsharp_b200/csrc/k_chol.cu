@@ -64,62 +64,193 @@ __global__ void prep_kernel(const float* H, int64_t d, int64_t ldh, int upper_on
 }
 
 // Cholesky + triangular inverse of one n x n (n <= NB) diagonal block in shared memory,
-// 1024 threads viewed as 32 x 32.  A's lower triangle is read; L (zeros above) goes back to
-// A and L^-1 to I.  A pivot that is not > 0 (or NaN) raises flags[0] and the block continues
+// blocked in 32-column panels.  A's lower triangle is read; L (zeros above) goes back to A
+// and L^-1 to I.  A pivot that is not > 0 (or NaN) raises flags[0] and the block continues
 // with a unit pivot, so the kernel always terminates; the host reports the failure.
 //
-// Factorisation: outer-product form with one barrier per step; step k updates the trailing
-// lower triangle with a_ij -= (a_ik / a_kk) a_jk from the (still unscaled) column k, and the
-// columns are scaled by 1/sqrt(a_kk) at the end.  Inverse: forward elimination of L X = I
-// applied to all right-hand sides at once (row k scaled, then eliminated from rows > k).
-constexpr int BASE_THREADS = 1024;
+// Per panel p (columns c0 = 32p .. c0+31):
+//   1. warp 0 factors the 32 x 32 diagonal block in registers (lane i holds row i; column k
+//      of the factor is broadcast with shuffles) and then inverts it (lane j builds column j
+//      of L11^-1 by forward substitution against the shared-memory copy of L11);
+//   2. all warps form the panel below, L21 = A21 L11^-T, from the explicit inverse;
+//   3. all warps apply the trailing update A22 -= L21 L21^T (lower triangle).
+// The off-diagonal blocks of L^-1 follow block row by block row:
+//   X_ij = -X_ii (sum_{k=j..i-1} L_ik X_kj).
+// Rows and columns in [n, round_up(n, 32)) are identity padding and are never stored.
+constexpr int BASE_THREADS = 512;  // 16 warps; 128 registers per thread for the register-resident factor
+constexpr int BW = BASE_THREADS / 32;
 constexpr int BLD = NB + 1;
+constexpr unsigned FULL = 0xffffffffu;
 
-size_t base_smem_bytes() { return (size_t)2 * NB * BLD * sizeof(float) + NB * sizeof(float); }
+size_t base_smem_bytes() { return (size_t)2 * NB * BLD * sizeof(float); }
+
+// Unblocked Cholesky of the 32 x 32 lower block of sL at (c0, c0) by one warp: lane i keeps
+// row i in registers; step K broadcasts the pivot and column K of the factor with shuffles.
+template <int K>
+__device__ __forceinline__ void chol32_step(float (&r)[32], int lane, int& bad) {
+    float piv = __shfl_sync(FULL, r[K], K);
+    if (!(piv > 0.f)) {
+        bad = 1;
+        piv = 1.f;
+    }
+    const float s = __fsqrt_rn(piv);
+    const float inv_s = __frcp_rn(s);
+    r[K] = (lane == K) ? s : ((lane > K) ? __fmul_rn(r[K], inv_s) : 0.f);
+#pragma unroll
+    for (int j = K + 1; j < 32; j++) {
+        const float ljk = __shfl_sync(FULL, r[K], j);
+        r[j] = (lane >= j) ? fmaf(-r[K], ljk, r[j]) : r[j];
+    }
+    if constexpr (K + 1 < 32) chol32_step<K + 1>(r, lane, bad);
+}
+
+__device__ __forceinline__ void factor_diag32(float* sL, int c0, int lane, int* flags) {
+    float r[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++) r[j] = (j <= lane) ? sL[(c0 + lane) * BLD + c0 + j] : 0.f;
+    int bad = 0;
+    chol32_step<0>(r, lane, bad);
+    if (bad && lane == 0) atomicOr(flags, 1);
+#pragma unroll
+    for (int j = 0; j < 32; j++) sL[(c0 + lane) * BLD + c0 + j] = (j <= lane) ? r[j] : 0.f;
+}
+
+// Column `lane` of the inverse of the 32 x 32 lower block of sL at (c0, c0), into sX.
+__device__ __forceinline__ void invert_diag32(const float* sL, float* sX, int c0, int lane) {
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const float* Li = sL + (c0 + i) * BLD + c0;
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < i; k++) acc = fmaf(Li[k], x[k], acc);  // x[k] = 0 for k < lane
+        const float lii = Li[i];
+        x[i] = (i < lane) ? 0.f : ((i == lane) ? __frcp_rn(lii) : __fdiv_rn(-acc, lii));
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i++) sX[(c0 + i) * BLD + c0 + lane] = x[i];
+}
 
 __global__ void __launch_bounds__(BASE_THREADS) chol_inv_base_kernel(float* A, float* I, int64_t ld, int n, int* flags) {
     extern __shared__ float sm[];
-    float* sL = sm;               // [NB][BLD]
-    float* sX = sm + NB * BLD;    // [NB][BLD]
-    float* sdiag = sX + NB * BLD; // [NB]
-    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
-    for (int i = ty; i < n; i += 32)
-        for (int j = tx; j < n; j += 32) {
-            sL[i * BLD + j] = (j <= i) ? A[i * ld + j] : 0.f;
-            sX[i * BLD + j] = (i == j) ? 1.f : 0.f;
+    float* sL = sm;             // [NB][BLD]
+    float* sX = sm + NB * BLD;  // [NB][BLD]
+    const int tid = threadIdx.x;
+    const int lane = tid % 32, warp = tid / 32;
+    const int np = (n + 31) / 32 * 32;
+    const int P = np / 32;
+    for (int i = warp; i < np; i += BW)
+        for (int j = lane; j < np; j += 32) {
+            float v;
+            if (i < n && j < n) v = (j <= i) ? A[i * ld + j] : 0.f;
+            else v = (i == j) ? 1.f : 0.f;
+            sL[i * BLD + j] = v;
+            sX[i * BLD + j] = 0.f;
         }
     __syncthreads();
-    for (int k = 0; k < n; k++) {
-        float akk = sL[k * BLD + k];
-        if (!(akk > 0.f)) {
-            if (threadIdx.x == 0) atomicOr(flags, 1);
-            akk = 1.f;
+
+    constexpr int RPW = (NB - 32) / BW;  // panel rows per warp (6)
+    for (int p = 0; p < P; p++) {
+        const int c0 = 32 * p;
+        if (warp == 0) {
+            factor_diag32(sL, c0, lane, flags);
+            __syncwarp();
+            invert_diag32(sL, sX, c0, lane);
         }
-        const float inv = __frcp_rn(akk);
-        for (int i = k + 1 + ty; i < n; i += 32) {
-            const float lik = __fmul_rn(sL[i * BLD + k], inv);
-            for (int j = k + 1 + tx; j <= i; j += 32) sL[i * BLD + j] = fmaf(-lik, sL[j * BLD + k], sL[i * BLD + j]);
+        __syncthreads();
+        const int r0 = c0 + 32;
+        if (r0 >= np) break;
+        // Panel: L21[r][j] = sum_{k <= j} A21[r][k] X11[j][k]; warp -> rows, lane -> column.
+        float pv[RPW];
+        const float* Xj = sX + (c0 + lane) * BLD + c0;
+#pragma unroll
+        for (int a = 0; a < RPW; a++) {
+            const int r = r0 + warp + BW * a;
+            float acc = 0.f;
+            if (r < np) {
+                const float* Ar = sL + r * BLD + c0;
+#pragma unroll
+                for (int k = 0; k < 32; k++) acc = fmaf(Ar[k], Xj[k], acc);  // Xj[k] = 0 for k > lane
+            }
+            pv[a] = acc;
         }
-        if (threadIdx.x == 0) sdiag[k] = __fsqrt_rn(akk);
+        __syncthreads();
+#pragma unroll
+        for (int a = 0; a < RPW; a++) {
+            const int r = r0 + warp + BW * a;
+            if (r < np) sL[r * BLD + c0 + lane] = pv[a];
+        }
+        __syncthreads();
+        // Trailing update of the lower triangle: A22[r][s] -= sum_k L21[r][k] L21[s][k].
+#pragma unroll
+        for (int a = 0; a < RPW; a++) {
+            const int r = r0 + warp + BW * a;
+            if (r >= np) continue;
+            const float* Lr = sL + r * BLD + c0;
+#pragma unroll
+            for (int b = 0; b < 3; b++) {
+                const int s2 = r0 + lane + 32 * b;
+                if (s2 > r) continue;
+                const float* Ls = sL + s2 * BLD + c0;
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 32; k++) acc = fmaf(Lr[k], Ls[k], acc);
+                sL[r * BLD + s2] = __fsub_rn(sL[r * BLD + s2], acc);
+            }
+        }
         __syncthreads();
     }
-    for (int i = ty; i < n; i += 32)
-        for (int j = tx; j <= i; j += 32)
-            sL[i * BLD + j] = (i == j) ? sdiag[i] : __fdiv_rn(sL[i * BLD + j], sdiag[j]);
-    __syncthreads();
-    for (int k = 0; k < n; k++) {
-        const float rk = __frcp_rn(sL[k * BLD + k]);
-        if (ty == 0)
-            for (int j = tx; j <= k; j += 32) sX[k * BLD + j] = __fmul_rn(sX[k * BLD + j], rk);
+
+    // Off-diagonal blocks of L^-1, block row by block row.
+    for (int bi = 1; bi < P; bi++) {
+        const int i0 = 32 * bi;
+        // T_j[a][b] = sum_{m = 32 j .. i0-1} L[i0+a][m] X[m][32 j + b], for every block j < bi.
+        float tv[2][3];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const float* La = sL + (i0 + warp + BW * h) * BLD;
+#pragma unroll
+            for (int bj = 0; bj < 3; bj++) {
+                float acc = 0.f;
+                if (bj < bi) {
+                    const int col = 32 * bj + lane;
+                    for (int m = 32 * bj; m < i0; m++) acc = fmaf(La[m], sX[m * BLD + col], acc);
+                }
+                tv[h][bj] = acc;
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int bj = 0; bj < 3; bj++)
+                if (bj < bi) sX[(i0 + warp + BW * h) * BLD + 32 * bj + lane] = tv[h][bj];
         __syncthreads();
-        for (int i = k + 1 + ty; i < n; i += 32) {
-            const float lik = sL[i * BLD + k];
-            for (int j = tx; j <= k; j += 32) sX[i * BLD + j] = fmaf(-lik, sX[k * BLD + j], sX[i * BLD + j]);
+        // X_ij[a][b] = -sum_{c <= a} X_ii[a][c] T_j[c][b]
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int ar = warp + BW * h;
+            const float* Xa = sX + (i0 + ar) * BLD + i0;
+#pragma unroll
+            for (int bj = 0; bj < 3; bj++) {
+                float acc = 0.f;
+                if (bj < bi) {
+                    const int col = 32 * bj + lane;
+                    for (int c = 0; c <= ar; c++) acc = fmaf(Xa[c], sX[(i0 + c) * BLD + col], acc);
+                }
+                tv[h][bj] = -acc;
+            }
         }
         __syncthreads();
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int bj = 0; bj < 3; bj++)
+                if (bj < bi) sX[(i0 + warp + BW * h) * BLD + 32 * bj + lane] = tv[h][bj];
+        __syncthreads();
     }
-    for (int i = ty; i < n; i += 32)
-        for (int j = tx; j < n; j += 32) {
+
+    for (int i = warp; i < n; i += BW)
+        for (int j = lane; j < n; j += 32) {
             A[i * ld + j] = sL[i * BLD + j];
             I[i * ld + j] = sX[i * BLD + j];
         }

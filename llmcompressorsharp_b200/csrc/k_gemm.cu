@@ -147,6 +147,97 @@ __global__ void __launch_bounds__(NT) gemm_kernel(GemmArgs g, int a_vec, int b_v
     }
 }
 
+// ---- small GEMMs: 32 x 32 tiles, K split over the CTA's 8 warps ----------------------------
+// The lower levels of the Cholesky recursion and the GPTQ near-block updates of short weights
+// produce GEMMs of a few 128 x 128 tiles, which the kernel above runs on a handful of SMs.
+// Here every 32 x 32 output tile is its own CTA; the CTA stages KC-deep slabs of A and B in
+// shared memory, each warp accumulates a 32 x 32 partial over its KC/8 slice of the slab
+// (lane: 4 rows x 8 columns), and the 8 partials are summed through shared memory.
+constexpr int ST = 32, SKC = 128, SNT = 256;
+
+template <typename T>
+__device__ __forceinline__ float ld_el(const T* base, int64_t ld, int64_t r, int64_t c, int64_t R, int64_t Cc) {
+    return (r < R && c < Cc) ? to_f<T>(base[r * ld + c]) : 0.f;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(SNT) gemm_small_kernel(GemmArgs g) {
+    const int64_t m0 = (int64_t)blockIdx.y * ST, n0 = (int64_t)blockIdx.x * ST;
+    if (g.c_mode == 1 && m0 + ST - 1 < n0) return;
+    if (g.c_mode == 2 && m0 > n0 + ST - 1) return;
+    int64_t kb = 0, ke = g.K;
+    if (g.a_tri == TRI_KLE) ke = min(ke, m0 + ST);
+    if (g.a_tri == TRI_KGE) kb = max(kb, m0);
+    if (g.b_tri == TRI_KLE) ke = min(ke, n0 + ST);
+    if (g.b_tri == TRI_KGE) kb = max(kb, n0);
+
+    __shared__ __align__(16) float As[SKC][ST];  // As[k][m]
+    __shared__ __align__(16) float Bs[SKC][ST];  // Bs[k][n]
+    const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+    const int rg = lane / 4, cg = lane % 4;  // rows rg*4 .. +3, columns cg*8 .. +7
+    const T* A = reinterpret_cast<const T*>(g.A);
+    const T* B = reinterpret_cast<const T*>(g.B);
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+
+    for (int64_t k0 = kb; k0 < ke; k0 += SKC) {
+        const int64_t kc = min((int64_t)SKC, ke - k0);
+        // stage A[m0 .. +32, k0 .. +kc] as As[k][m] and B[k0 .. +kc, n0 .. +32] as Bs[k][n]
+        for (int e = tid; e < SKC * ST; e += SNT) {
+            int k, mm;
+            if (!g.a_trans) { mm = e / SKC; k = e % SKC; }  // contiguous along k
+            else { k = e / ST; mm = e % ST; }              // contiguous along m
+            float v = 0.f;
+            if (k < kc) v = g.a_trans ? ld_el(A, g.lda, k0 + k, m0 + mm, ke, g.M) : ld_el(A, g.lda, m0 + mm, k0 + k, g.M, ke);
+            As[k][mm] = v;
+            int nn;
+            if (g.b_trans) { nn = e / SKC; k = e % SKC; }  // B stored [n][k]
+            else { k = e / ST; nn = e % ST; }
+            v = 0.f;
+            if (k < kc) v = g.b_trans ? ld_el(B, g.ldb, n0 + nn, k0 + k, g.N, ke) : ld_el(B, g.ldb, k0 + k, n0 + nn, ke, g.N);
+            Bs[k][nn] = v;
+        }
+        __syncthreads();
+        const int ks = warp * (SKC / 8);
+#pragma unroll 4
+        for (int k = ks; k < ks + SKC / 8; k++) {
+            const float4 a = *reinterpret_cast<const float4*>(&As[k][rg * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&Bs[k][cg * 8]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&Bs[k][cg * 8 + 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+    // Sum the 8 warps' partials: red[w][r][c] reuses As/Bs (8 x 32 x 32 floats = 32 KB).
+    float* red = &As[0][0];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) red[(warp * ST + rg * 4 + i) * ST + cg * 8 + j] = acc[i][j];
+    __syncthreads();
+    for (int e = tid; e < ST * ST; e += SNT) {
+        const int r = e / ST, c = e % ST;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) s += red[(w * ST + r) * ST + c];
+        const int64_t gr = m0 + r, gc = n0 + c;
+        if (gr >= g.M || gc >= g.N) continue;
+        if (g.c_mode == 1 && gr < gc) continue;
+        if (g.c_mode == 2 && gr > gc) continue;
+        float* p = g.C + gr * g.ldc + gc;
+        const float v = g.alpha * s;
+        *p = (g.beta == 0.f) ? v : fmaf(g.beta, *p, v);
+    }
+}
+
 template <typename TA, typename TB>
 llmc_status launch(llmc_ctx* ctx, const GemmArgs& g) {
     auto aligned = [](const void* p, int64_t ld, int es) {
@@ -181,6 +272,13 @@ llmc_status gemm_f32(llmc_ctx* ctx, const GemmArgs& g) {
     if (g.a_dtype == LLMC_DTYPE_F32 && g.K > 0 && (double)g.M * (double)g.N * (double)g.K >= (double)(1 << 26)) {
         llmc_status st = gemm_tc(ctx, g);
         if (st != LLMC_ERR_UNSUPPORTED) return st;
+    }
+    // Few 128 x 128 tiles and no split-K: 32 x 32 tiles spread the product over more SMs.
+    const int64_t tiles128 = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+    if (g.a_dtype == LLMC_DTYPE_F32 && g.split_k <= 1 && tiles128 < ctx->sm_count && g.M <= 65535LL * ST) {
+        dim3 grid((unsigned)((g.N + ST - 1) / ST), (unsigned)((g.M + ST - 1) / ST));
+        gemm_small_kernel<float><<<grid, SNT, 0, ctx->stream>>>(g);
+        return check_launch(ctx, "gemm_small");
     }
     switch (g.a_dtype) {
         case LLMC_DTYPE_F32: return launch<float, float>(ctx, g);

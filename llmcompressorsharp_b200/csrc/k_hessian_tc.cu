@@ -310,7 +310,7 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
     a.ntiles = off;
     a.kb_total = (int)((rows + BK - 1) / BK);
     // Token splits: balance the last wave while keeping >= 32 k-blocks (2048 tokens) per unit.
-    const int grid_cap = ctx->sm_count;
+    const int grid_cap = persistent_sms(ctx);
     int best_s = 1;
     double best_eff = 0.0;
     for (int s = 1; s <= 16; s++) {

@@ -7,6 +7,14 @@ input); every weight that reads a site is quantised against that site's factor U
 result per weight is the packed int codes, scales and zero-points (plus, optionally, the
 fp32 fake-quantised weight the reference returns).
 
+Overlap (one GPU): ``run`` pipelines the layers over two library contexts on two streams.
+While layer l is solved (Cholesky factor + GPTQ, mostly latency-bound kernels) on the solve
+stream, layer l+1's Hessians accumulate on the Hessian stream; the Hessian context's
+persistent kernel is capped to ``sm_count - reserve_sms`` SMs so the solve always finds SMs
+free.  Hessians are double-buffered (two handle sets), and events order every hand-off:
+solve(l) waits for accumulate(l), and accumulate(l+2) waits for solve(l) before it resets
+the buffer set they share.
+
 Multi-GPU: calibration tokens are split across ranks; each rank accumulates its partial
 H for every site, the partial Hessians are summed onto the layer's owner rank
 (``torch.distributed.reduce`` over NCCL), and owners solve their layers (layers are dealt
@@ -65,11 +73,37 @@ class GptqPipeline:
         # fp32 working copy of the largest stacked solve (rows of all weights of one site)
         self.work = torch.empty(max(sum(m for _, m in s.weights) * s.d for s in sites), dtype=torch.float32,
                                 device=device)
+        self.overlap = None
+
+    def enable_overlap(self, reserve_sms: int = 24):
+        """Switch ``run`` to the two-stream schedule described in the module docstring;
+        ``reserve_sms`` SMs are kept free of the persistent Hessian kernel for the solve."""
+        if self.overlap is None:
+            self.overlap = _Overlap(self, reserve_sms)
+        return self
 
     def close(self):
         for p in self.h.values():
             _lib.call("llmc_hessian_destroy", C.c_void_p(p))
         self.h = {}
+        if self.overlap is not None:
+            self.overlap.close()
+            self.overlap = None
+
+    def launch_count(self) -> int:
+        """Kernels launched so far by the library contexts this pipeline uses."""
+        n = _lib.launch_count(self.device.index)
+        if self.overlap is not None:
+            for c in (self.overlap.ch, self.overlap.cs):
+                v = C.c_int64()
+                _lib.call("llmc_launch_count", C.c_void_p(c), C.byref(v))
+                n += int(v.value)
+        return n
+
+    def hessian_sms(self) -> int:
+        """SMs the Hessian kernel runs on."""
+        sm = torch.cuda.get_device_properties(self.device).multi_processor_count
+        return self.overlap.hessian_sms if self.overlap is not None else sm
 
     def hessian_ptr(self, site: str) -> int:
         p = C.c_void_p()
@@ -79,22 +113,29 @@ class GptqPipeline:
     def accumulate(self, site: SiteSpec, x: torch.Tensor, out_h: torch.Tensor | None = None):
         """H_site = sum over chunks of X^T X (reset first).  Optionally copy H out."""
         _lib.ctx_for(self.device.index)
-        h = C.c_void_p(self.h[site.name])
+        self._accumulate_into(self.h[site.name], x)
+        if out_h is not None:
+            out_h.copy_(torch.as_tensor(_HView(self.hessian_ptr(site.name), site.d), device=self.device))
+
+    def _accumulate_into(self, handle: int, x: torch.Tensor):
+        """Reset one Hessian handle and add X^T X over X in row chunks (on the handle's stream)."""
+        h = C.c_void_p(handle)
         _lib.call("llmc_hessian_reset", h)
         T = x.shape[0]
         for r0 in range(0, T, self.chunk):
             r1 = min(T, r0 + self.chunk)
             _lib.call("llmc_hessian_update", h, C.c_void_p(x.data_ptr() + r0 * x.stride(0) * x.element_size()),
                       _lib.dtype_code(x.dtype), C.c_int64(r1 - r0), C.c_int64(x.stride(0)))
-        if out_h is not None:
-            out_h.copy_(torch.as_tensor(_HView(self.hessian_ptr(site.name), site.d), device=self.device))
 
-    def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict):
+    def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict, ctx=None):
         """U from the site's H (upper triangle), then one stacked GPTQ solve of every weight
-        that reads the site (outputs are views into stacked per-site buffers)."""
+        that reads the site (outputs are views into stacked per-site buffers).  ``ctx`` is a
+        library context bound to the stream to run on (default: torch's current stream)."""
         d = site.d
-        _lib.ctx_for(self.device.index)
-        _lib.call("llmc_chol_inverse", self.c, C.c_void_p(h_ptr), C.c_int64(d), C.c_int64(d),
+        if ctx is None:
+            _lib.ctx_for(self.device.index)
+            ctx = self.c
+        _lib.call("llmc_chol_inverse", ctx, C.c_void_p(h_ptr), C.c_int64(d), C.c_int64(d),
                   C.c_float(self.cfg.dampening_frac), 1, _lib.ptr(self.u), C.c_int64(d), 1)
         names = [w for w, _ in site.weights]
         ms = [m for _, m in site.weights]
@@ -106,7 +147,7 @@ class GptqPipeline:
         wq = st.get("wq")
         if wq is None:
             wq = self.work[: sum(ms) * d].view(sum(ms), d)
-        _lib.call("llmc_gptq_quantize_batch", self.c, C.c_int32(k), wp, mp, lp, _lib.dtype_code(weights[names[0]].dtype),
+        _lib.call("llmc_gptq_quantize_batch", ctx, C.c_int32(k), wp, mp, lp, _lib.dtype_code(weights[names[0]].dtype),
                   C.c_int64(d), _lib.ptr(self.u), C.c_int64(d), C.byref(self.qc), _lib.ptr(wq), C.c_int64(d),
                   _lib.ptr(st["codes"]), _lib.ptr(st["scales"]), _lib.ptr(st["zero_points"]))
 
@@ -144,6 +185,133 @@ class GptqPipeline:
         for s in self.sites:
             self.accumulate(s, acts[s.name])
             self.solve_site(s, self.hessian_ptr(s.name), weights, outputs)
+
+    def run(self, layers, acts, weights, outputs, before_solve=None, after_solve=None, hess_events=None):
+        """The whole job over ``layers``: per layer, every site's Hessian, factor and stacked
+        GPTQ solve.  ``acts`` is {site: [T, d]} (shared by the layers) or a callable
+        layer -> {site: tensor}; ``weights[l]`` / ``outputs[l]`` per layer.  ``before_solve(l)``
+        and ``after_solve(l)`` run on the stream that solves layer l, just before / after it
+        (e.g. host->device weight copies and device->host result copies).  With
+        ``hess_events`` (a list), CUDA event pairs bracketing each site's accumulation are
+        appended as (start, end, d, rows).  Work is enqueued on the current stream (or, with
+        overlap enabled, on the two pipeline streams joined back into it)."""
+        acts_for = acts if callable(acts) else (lambda _l: acts)
+        if self.overlap is not None:
+            return self.overlap.run(list(layers), acts_for, weights, outputs, before_solve, after_solve, hess_events)
+        for l in layers:
+            a = acts_for(l)
+            for s in self.sites:
+                ev = _events() if hess_events is not None else None
+                if ev:
+                    ev[0].record()
+                self.accumulate(s, a[s.name])
+                if ev:
+                    ev[1].record()
+                    hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
+                if s is self.sites[0] and before_solve is not None:
+                    before_solve(l)
+                self.solve_site(s, self.hessian_ptr(s.name), weights[l], outputs[l])
+            if after_solve is not None:
+                after_solve(l)
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+class _Overlap:
+    """Two library contexts, two streams and two Hessian handle sets for ``GptqPipeline.run``."""
+
+    def __init__(self, pipe: GptqPipeline, reserve_sms: int):
+        self.pipe = pipe
+        dev = pipe.device
+        sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        pr = torch.cuda.Stream.priority_range()
+        hi, lo = min(pr), max(pr)  # a lower number is a higher priority
+        # The Hessian stream is first in line for SMs at launch boundaries; the solve runs on
+        # the reserved SMs (CTAs of a higher-priority stream do not overtake the pending CTAs
+        # of a grid that is already being dispatched, so the split has to be static).
+        self.sh = torch.cuda.Stream(dev, priority=hi)
+        self.ss = torch.cuda.Stream(dev, priority=lo)
+        self.ch = self._ctx(dev, self.sh)
+        self.cs = self._ctx(dev, self.ss)
+        limit = max(1, sm - int(reserve_sms))
+        self.hessian_sms = limit
+        _lib.call("llmc_set_sm_limit", C.c_void_p(self.ch), C.c_int32(limit))
+        self.h = [{}, {}]
+        for b in range(2):
+            for s in pipe.sites:
+                p = C.c_void_p()
+                _lib.call("llmc_hessian_create", C.c_void_p(self.ch), C.c_int64(s.d), C.byref(p))
+                self.h[b][s.name] = p.value
+
+    @staticmethod
+    def _ctx(dev, stream) -> int:
+        out = C.c_void_p()
+        _lib.call("llmc_init", C.c_int32(dev.index), C.byref(out))
+        _lib.call("llmc_set_stream", out, C.c_void_p(stream.cuda_stream))
+        return out.value
+
+    def close(self):
+        torch.cuda.synchronize(self.pipe.device)
+        for b in range(2):
+            for p in self.h[b].values():
+                _lib.call("llmc_hessian_destroy", C.c_void_p(p))
+        self.h = [{}, {}]
+        for c in (self.ch, self.cs):
+            _lib.call("llmc_destroy", C.c_void_p(c))
+        self.ch = self.cs = None
+
+    def _data(self, b: int, site: str) -> int:
+        p = C.c_void_p()
+        _lib.call("llmc_hessian_data", C.c_void_p(self.h[b][site]), C.byref(p))
+        return p.value
+
+    def run(self, layers, acts_for, weights, outputs, before_solve, after_solve, hess_events):
+        pipe = self.pipe
+        cur = torch.cuda.current_stream(pipe.device)
+        self.sh.wait_stream(cur)
+        self.ss.wait_stream(cur)
+        solved = [None, None]  # event: last solve that read buffer set b
+
+        def solve(item):
+            l, b, acc_done = item
+            with torch.cuda.stream(self.ss):
+                self.ss.wait_event(acc_done)
+                if before_solve is not None:
+                    before_solve(l)
+                for s in pipe.sites:
+                    pipe.solve_site(s, self._data(b, s.name), weights[l], outputs[l], ctx=C.c_void_p(self.cs))
+                if after_solve is not None:
+                    after_solve(l)
+                done = torch.cuda.Event()
+                done.record(self.ss)
+                solved[b] = done
+
+        pending = None
+        for i, l in enumerate(layers):
+            b = i % 2
+            a = acts_for(l)
+            with torch.cuda.stream(self.sh):
+                if solved[b] is not None:
+                    self.sh.wait_event(solved[b])
+                for s in pipe.sites:
+                    ev = _events() if hess_events is not None else None
+                    if ev:
+                        ev[0].record(self.sh)
+                    pipe._accumulate_into(self.h[b][s.name], a[s.name])
+                    if ev:
+                        ev[1].record(self.sh)
+                        hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
+                acc_done = torch.cuda.Event()
+                acc_done.record(self.sh)
+            if pending is not None:
+                solve(pending)  # may block the host (factor flags) while the Hessian stream runs on
+            pending = (l, b, acc_done)
+        if pending is not None:
+            solve(pending)
+        cur.wait_stream(self.sh)
+        cur.wait_stream(self.ss)
 
 
 def _stack_key(site: SiteSpec) -> str:

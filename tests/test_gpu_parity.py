@@ -187,7 +187,7 @@ def spd(d, seed, rows=None):
     return x.t() @ x
 
 
-@pytest.mark.parametrize("d", [1, 7, 64, 65, 200, 576])
+@pytest.mark.parametrize("d", [1, 7, 64, 65, 200, 300, 576, 1000])
 def test_inverse_matches_oracle(d):
     from llmcompressorsharp_b200 import HessianInverseSolver
 
@@ -240,6 +240,21 @@ def test_inverse_kats():  # HessianInverseSolverTests.cs
     assert torch.count_nonzero(z) == 0
     with pytest.raises(ShapeError, match="square"):
         HessianInverseSolver.compute(torch.ones(3, 4, device=DEV), 0.01)
+
+
+@pytest.mark.parametrize("d", [40, 300])
+def test_inverse_not_positive_definite_is_reported(d):
+    """A damped matrix with a negative eigenvalue: the reference's pinv fallback is only
+    reproduced for the all-zero matrix, anything else raises."""
+    from llmcompressorsharp_b200 import HessianInverseSolver
+    from llmcompressorsharp_b200.errors import NotPositiveDefiniteError
+
+    h = spd(d, 5)
+    h[d // 2, d // 2] = -10.0 * h.diagonal().mean()
+    with pytest.raises(NotPositiveDefiniteError):
+        HessianInverseSolver.compute(h.to(DEV), 0.01)
+    u = HessianInverseSolver.upper(spd(d, 6).to(DEV), 0.01)  # the context stays usable
+    assert torch.isfinite(u).all()
 
 
 def test_upper_factor_fallback_to_hinv():  # GptqBlockQuantizer.cs:112-118
@@ -487,6 +502,45 @@ def test_gptq_batch_equals_separate(strategy):
     assert torch.equal(codes, torch.cat([r.codes for r in sep]))
     assert torch.equal(sc, torch.cat([r.scales for r in sep]))
     assert torch.equal(zp, torch.cat([r.zero_points for r in sep]))
+
+
+def _pipeline_case(seed=50, layers=3, tokens=8192):
+    from llmcompressorsharp_b200.pipeline import SiteSpec
+
+    sites = [SiteSpec("a", 256, [("w1", 128), ("w2", 64)]), SiteSpec("b", 512, [("w3", 256)])]
+    g = torch.Generator().manual_seed(seed)
+    acts = {s.name: torch.randn(tokens, s.d, generator=g).to(torch.bfloat16).to(DEV) for s in sites}
+    weights = {l: {w: (torch.randn(m, s.d, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+                   for s in sites for w, m in s.weights} for l in range(layers)}
+    return sites, acts, weights
+
+
+@pytest.mark.parametrize("reserve", [0, 100])
+def test_pipeline_overlap_matches_oracle(reserve):
+    """GptqPipeline.run: sequential (reserve 0) and two-stream overlapped schedules (Hessian
+    kernel capped at sm_count - 100 SMs) both match the oracle per layer and weight."""
+    from llmcompressorsharp_b200 import GPTQConfig
+    from llmcompressorsharp_b200.pipeline import GptqPipeline
+
+    sites, acts, weights = _pipeline_case()
+    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128)
+    pipe = GptqPipeline(sites, cfg, torch.device(DEV), chunk_rows=4096, keep_wq=True)
+    if reserve:
+        pipe.enable_overlap(reserve)
+    outs = {l: pipe.alloc_outputs(weights[l]) for l in weights}
+    pipe.run(range(len(weights)), acts, weights, outs)
+    torch.cuda.synchronize()
+    pipe.close()
+    from types import SimpleNamespace
+
+    for s in sites:
+        h = o_hess.HessianAccumulator(s.d)
+        h.update(acts[s.name].cpu())
+        for l in weights:
+            for w, _ in s.weights:
+                got = SimpleNamespace(**outs[l][w])
+                check_gptq(weights[l][w].cpu(), h.get_hessian(),
+                           dict(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128), got)
 
 
 def test_gptq_kats():  # GptqBlockQuantizerTests.cs
