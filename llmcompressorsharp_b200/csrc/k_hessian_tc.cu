@@ -20,9 +20,11 @@
 //     sum of KF = 8 k-blocks (512 tokens).  Two TMEM accumulators alternate: while the MMA
 //     issuer fills one, eight epilogue warps fold the other into fp32 registers with
 //     round-to-nearest adds (each warp owns 32 rows x 128 columns);
-//   * end of a unit: registers -> padded shared staging -> one bulk reduce-add
-//     (cp.reduce.async.bulk .add.f32) per half row into H, so H accumulates across calls
-//     and across token splits without a read pass.
+//   * end of a unit: each epilogue warp writes its 32 x 128 block out in four 32 x 32 boxes
+//     through its own 4 KB shared buffer (128-byte swizzle) and a tiled TMA reduce-add into
+//     H, so H accumulates across calls and token splits without a read pass.  The buffers
+//     are separate from the stage ring: the producer and the MMA issuer run on into the next
+//     unit while the previous one drains.
 // Work units are (tile, token split); units of one split run in the same wave so that the
 // X rows they stream are shared through L2.
 // Every wait is bounded: on expiry the kernel raises an error word, drains its own
@@ -31,6 +33,8 @@
 #include "tc_common.cuh"
 
 #include <cuda.h>
+
+#include <mutex>
 
 namespace llmc {
 namespace {
@@ -45,12 +49,13 @@ constexpr int A_BYTES = BM * BK * 2;             // 16 KB
 constexpr int B_BYTES = BN * BK * 2;             // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
 constexpr int BOX_BYTES = 64 * BK * 2;           // 8 KB: 64 features x 64 tokens
-constexpr int STG_LD = BN + 4;                   // fp32 staging row stride (floats)
-constexpr int SMEM_MAIN = STAGES * STAGE_BYTES;  // 192 KB (reused as 130 KB staging)
-constexpr int SMEM_BYTES = SMEM_MAIN + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int SMEM_MAIN = STAGES * STAGE_BYTES;  // 192 KB
+constexpr int OUT_BOX = 32;                      // epilogue write-out box: 32 rows x 32 fp32
+constexpr int OUT_BYTES = OUT_BOX * OUT_BOX * 4; // 4 KB per epilogue warp
+constexpr int SMEM_BYTES = SMEM_MAIN + EPI_WARPS * OUT_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 constexpr int MAX_TJ = 160;                      // d <= 40960
 
-static_assert(BM * STG_LD * 4 <= SMEM_MAIN, "epilogue staging must fit in the stage ring");
+static_assert(SMEM_BYTES <= 232448, "shared memory above the per-block limit");
 
 struct SyrkArgs {
     float* H;
@@ -77,16 +82,17 @@ __device__ __forceinline__ void unit_tile(const SyrkArgs& a, int tile, int* ti, 
     *ti = tile - a.tile_off[lo];
 }
 
-__global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ CUtensorMap xmap, const SyrkArgs a) {
+__global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                       const __grid_constant__ CUtensorMap hmap, const SyrkArgs a) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SMEM_MAIN);
+    unsigned char* outbufs = smem + SMEM_MAIN;  // EPI_WARPS x 4 KB, 1024-byte aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(outbufs + EPI_WARPS * OUT_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;   // [2] accumulator b ready for promotion
     uint64_t* tempty = tfull + 2;       // [2] accumulator b folded, MMA may reuse it
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* staging = reinterpret_cast<float*>(smem);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     if (threadIdx.x == 0) {
@@ -206,27 +212,32 @@ __global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ 
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);
             }
-            // Every stage of this unit has been read by its MMAs (the last tfull implies it),
-            // so the stage ring is free for staging.
-            const int r = q * 32 + lane;
-            const int64_t gi = (int64_t)i0 + r;
-            float* srow = staging + (size_t)r * STG_LD + h * 128;
+            // Write-out: rounds of one 32 x 32 box (rows of quadrant q, columns
+            // j0 + 128 h + 32 round ..) through this warp's buffer.  The buffer is reused only
+            // after the previous reduce has read it; TMA clips rows / columns beyond d.
             if (!*abort_flag) {
+                unsigned char* ob = outbufs + e * OUT_BYTES;
+                const uint32_t ob_s = smem_u32(ob);
 #pragma unroll
-                for (int i = 0; i < BN / 2; i += 4)
-                    *reinterpret_cast<float4*>(srow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                const int jc = j0 + h * 128;
-                const int ncols = min(BN / 2, a.d - jc);
-                if (gi < a.d && ncols > 0) {
-                    bulk_reduce_add_f32(a.H + gi * a.ldh + jc, srow, (uint32_t)ncols * 4u);
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                for (int round = 0; round < 4; round++) {
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const int i = round * 32 + c * 4;
+                        *reinterpret_cast<float4*>(ob + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                            make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_reduce_add_2d(&hmap, ob_s, j0 + h * 128 + round * 32, i0 + q * 32);
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
                 }
             }
         }
         cc += (uint32_t)nchunks;
-        __syncthreads();  // staging consumed before the next unit's loads reuse the ring
     }
 
     // Drain: every bulk reduce finishes; after an abort, also wait (bounded) for the TMA
@@ -250,6 +261,222 @@ __global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ 
     }
 }
 
+// ---- CTA-pair variant ----------------------------------------------------------------------
+// A cluster of two CTAs computes 256 x 256 tiles of the upper triangle with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16): CTA r holds rows 128 r .. of the tile
+// (its A panel) and columns 128 r .. of the B panel, so per 64-token k-block each SM loads
+// 32 KB instead of 48 KB for the same FLOPs, and the tensor cores read each B half once for
+// both SMs.  Protocol (the pair leader is CTA rank 0):
+//   * full[s]  (leader): armed once per stage by the leader with both CTAs' bytes; both
+//     CTAs' TMA loads complete on it;
+//   * empty[s] (each CTA): one arrive from the leader's multicast commit when the MMAs that
+//     read stage s have completed;
+//   * tfull[b] (each CTA): one arrive from the leader's multicast commit when accumulator b
+//     is complete;
+//   * tempty[b] (leader): one arrive per epilogue warp of both CTAs after folding b.
+// TMEM is allocated for the pair (same 512 columns in both SMs); each CTA's epilogue reads
+// its own 128 rows.  Before exit each producer waits until every stage it filled has been
+// released, so no arrive or load targets a CTA that has left.
+constexpr int P_STAGES = 6;
+constexpr int P_HALF_BYTES = 128 * BK * 2;         // 16 KB: 128 features x 64 tokens
+constexpr int P_STAGE_BYTES = 2 * P_HALF_BYTES;    // A half + B half
+constexpr int P_SMEM_MAIN = P_STAGES * P_STAGE_BYTES;  // 192 KB
+constexpr int P_SMEM_BYTES = P_SMEM_MAIN + EPI_WARPS * OUT_BYTES + 1024 + 256;
+static_assert(P_SMEM_BYTES <= 232448, "shared memory above the per-block limit");
+
+struct PairArgs {
+    float* H;
+    int64_t ldh;
+    int d;
+    int nt;        // 256-wide blocks per side
+    int ntiles;    // nt (nt + 1) / 2 upper-triangle tiles
+    int kb_total;
+    int splits;
+    int kb_per_split;
+    int* err;
+    uint32_t idesc;
+};
+
+__device__ __forceinline__ void pair_tile(int tile, int* ti, int* tj) {
+    int j = (int)((sqrtf(8.f * (float)tile + 1.f) - 1.f) * 0.5f);
+    while ((j + 1) * (j + 2) / 2 <= tile) j++;
+    while (j * (j + 1) / 2 > tile) j--;
+    *tj = j;
+    *ti = tile - j * (j + 1) / 2;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
+    syrk_tc2_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap, const PairArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* outbufs = smem + P_SMEM_MAIN;
+    uint64_t* full = reinterpret_cast<uint64_t*>(outbufs + EPI_WARPS * OUT_BYTES);
+    uint64_t* empty = full + P_STAGES;
+    uint64_t* tfull = empty + P_STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * EPI_WARPS);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int total_units = a.ntiles * a.splits;
+    uint32_t prod_it = 0, mma_it = 0, cc = 0;
+    int pend_par[P_STAGES];
+#pragma unroll
+    for (int s = 0; s < P_STAGES; s++) pend_par[s] = -1;
+    int commit_par[2] = {-1, -1};
+
+    for (int u = pair; u < total_units && !*abort_flag; u += npairs) {
+        const int split = u / a.ntiles, tile = u % a.ntiles;
+        int ti, tj;
+        pair_tile(tile, &ti, &tj);
+        const int kb0 = split * a.kb_per_split;
+        const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
+        const int nchunks = (kb1 - kb0 + KF - 1) / KF;
+        const int i0 = ti * 256 + (int)rank * 128;  // this CTA's rows of H
+        const int j0 = tj * 256;                    // the pair's columns
+        const int jb = j0 + (int)rank * 128;        // this CTA's half of the B panel
+
+        if (warp == 0) {
+            if (lane == 0) {
+                for (int kb = kb0; kb < kb1; kb++, prod_it++) {
+                    const int s = prod_it % P_STAGES;
+                    const uint32_t ph = (prod_it / P_STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    unsigned char* st = smem + s * P_STAGE_BYTES;
+                    if (rank == 0) mbar_expect_tx(&full[s], 2 * P_STAGE_BYTES);
+                    const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
+                    const int y = kb * BK;
+                    tma_load_2d_pair(st, &xmap, i0, y, fbar);
+                    tma_load_2d_pair(st + BOX_BYTES, &xmap, i0 + 64, y, fbar);
+                    tma_load_2d_pair(st + P_HALF_BYTES, &xmap, jb, y, fbar);
+                    tma_load_2d_pair(st + P_HALF_BYTES + BOX_BYTES, &xmap, jb + 64, y, fbar);
+                    pend_par[s] = (int)ph;
+                }
+            }
+            __syncwarp();
+        } else if (warp == 1) {
+            if (lane == 0 && rank == 0) {
+                uint32_t c_it = cc;
+                for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
+                    const int b = (int)(c_it & 1u);
+                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    tc_fence_after();
+                    const uint32_t dst = tmem + (uint32_t)(b * BN);
+                    const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
+                    bool ok = true;
+                    for (int kb = k0; kb < k1; kb++, mma_it++) {
+                        const int s = mma_it % P_STAGES;
+                        const uint32_t ph = (mma_it / P_STAGES) & 1u;
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t abase = smem_u32(smem + s * P_STAGE_BYTES);
+                        const uint32_t bbase = abase + P_HALF_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            const uint64_t da = smem_desc_mn_sw128(abase + kk * 2048, BOX_BYTES);
+                            const uint64_t db = smem_desc_mn_sw128(bbase + kk * 2048, BOX_BYTES);
+                            umma2_f16(dst, da, db, a.idesc, (kb > k0 || kk > 0) ? 1u : 0u);
+                        }
+                        umma2_commit_mc(&empty[s], 0x3);
+                    }
+                    umma2_commit_mc(&tfull[b], 0x3);
+                    commit_par[b] = (int)((c_it >> 1) & 1u);
+                    if (!ok) break;
+                }
+            }
+            __syncwarp();
+        } else {
+            const int e = warp - 2, q = warp % 4, h = e / 4;
+            float acc[BN / 2];
+#pragma unroll
+            for (int i = 0; i < BN / 2; i++) acc[i] = 0.f;
+            uint32_t c_it = cc;
+            for (int c = 0; c < nchunks; c++, c_it++) {
+                const int b = (int)(c_it & 1u);
+                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
+                if (!__all_sync(0xffffffffu, have ? 1 : 0)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int part = 0; part < 4; part++) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + h * 128 + part * 32), v);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) acc[part * 32 + i] = __fadd_rn(acc[part * 32 + i], __uint_as_float(v[i]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+            }
+            if (!*abort_flag) {
+                unsigned char* ob = outbufs + e * OUT_BYTES;
+                const uint32_t ob_s = smem_u32(ob);
+#pragma unroll
+                for (int round = 0; round < 4; round++) {
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const int i = round * 32 + c * 4;
+                        *reinterpret_cast<float4*>(ob + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                            make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_reduce_add_2d(&hmap, ob_s, j0 + h * 128 + round * 32, i0 + q * 32);
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                }
+            }
+        }
+        cc += (uint32_t)nchunks;
+    }
+
+    // Tail: the producer waits until the MMAs have released every stage it filled (so no
+    // commit arrive is still on its way here), after an abort also for its loads (bounded).
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (warp == 0 && lane == 0)
+        for (int s = 0; s < P_STAGES; s++)
+            if (pend_par[s] >= 0) mbar_wait_drain(&empty[s], (uint32_t)pend_par[s]);
+    if (*abort_flag && warp == 1 && lane == 0 && rank == 0)
+        for (int b = 0; b < 2; b++)
+            if (commit_par[b] >= 0) mbar_wait_drain(&tfull[b], (uint32_t)commit_par[b]);
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
 // ---- host side -------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -267,7 +494,7 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-uint32_t make_idesc(int dtype) {
+uint32_t make_idesc(int dtype, int m = BM, int n = BN) {
     const uint32_t fmt = dtype == LLMC_DTYPE_BF16 ? 1u : 0u;  // kind::f16 operand: 0 = F16, 1 = BF16
     uint32_t d = 0;
     d |= 1u << 4;                 // D format: F32
@@ -275,9 +502,70 @@ uint32_t make_idesc(int dtype) {
     d |= fmt << 10;               // B format
     d |= 1u << 15;                // A major: MN
     d |= 1u << 16;                // B major: MN
-    d |= (uint32_t)(BN >> 3) << 17;
-    d |= (uint32_t)(BM >> 4) << 24;
+    d |= (uint32_t)(n >> 3) << 17;
+    d |= (uint32_t)(m >> 4) << 24;
     return d;
+}
+
+// Token splits: balance the last wave over `cap` workers while keeping >= 32 k-blocks (2048
+// tokens) per unit.
+int pick_splits(int ntiles, int kb_total, int cap) {
+    int best_s = 1;
+    double best_eff = 0.0;
+    for (int s = 1; s <= 16; s++) {
+        const int kps = (kb_total + s - 1) / s;
+        if (s > 1 && kps < 32) break;
+        const int units = ntiles * s;
+        const int waves = (units + cap - 1) / cap;
+        const double eff = (double)units / ((double)waves * cap);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best_s = s;
+        }
+    }
+    return best_s;
+}
+
+// CTA pairs of syrk_tc2_kernel that can be resident at once on the context's device (0 when
+// the pair kernel cannot be used); computed once per device.
+int max_pairs(llmc_ctx* ctx) {
+    static std::mutex mu;
+    static int cache[64];
+    static bool known[64];
+    const int dev = ctx->device;
+    if (dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!known[dev]) {
+        known[dev] = true;
+        cache[dev] = 0;
+        if (cudaFuncSetAttribute(syrk_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (unsigned)ctx->sm_count, 1, 1);
+        cfg.blockDim = dim3(NT, 1, 1);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (const void*)syrk_tc2_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            cfg.numAttrs = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, (const void*)syrk_tc2_kernel, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+        }
+        cache[dev] = n;
+    }
+    return cache[dev];
 }
 
 }  // namespace
@@ -309,23 +597,9 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
     a.tile_off[ntj] = off;
     a.ntiles = off;
     a.kb_total = (int)((rows + BK - 1) / BK);
-    // Token splits: balance the last wave while keeping >= 32 k-blocks (2048 tokens) per unit.
     const int grid_cap = persistent_sms(ctx);
-    int best_s = 1;
-    double best_eff = 0.0;
-    for (int s = 1; s <= 16; s++) {
-        const int kps = (a.kb_total + s - 1) / s;
-        if (s > 1 && kps < 32) break;
-        const int units = a.ntiles * s;
-        const int waves = (units + grid_cap - 1) / grid_cap;
-        const double eff = (double)units / ((double)waves * grid_cap);
-        if (eff > best_eff + 1e-9) {
-            best_eff = eff;
-            best_s = s;
-        }
-    }
-    a.splits = best_s;
-    a.kb_per_split = (a.kb_total + best_s - 1) / best_s;
+    a.splits = pick_splits(a.ntiles, a.kb_total, grid_cap);
+    a.kb_per_split = (a.kb_total + a.splits - 1) / a.splits;
     a.err = ctx->dflags + 2;
     a.idesc = make_idesc(dtype);
 
@@ -338,7 +612,35 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
                       const_cast<void*>(x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return fail(LLMC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
+    // H [d, d] fp32 (row stride ldh) as the target of the epilogue's 32 x 32 reduce-adds.
+    CUtensorMap hmap;
+    const cuuint64_t hdim[2] = {(cuuint64_t)d, (cuuint64_t)d};
+    const cuuint64_t hstride[1] = {(cuuint64_t)ldh * 4};
+    const cuuint32_t hbox[2] = {OUT_BOX, OUT_BOX};
+    cr = enc(&hmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, H, hdim, hstride, hbox, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(LLMC_ERR_CUDA, "cuTensorMapEncodeTiled (H) failed (%d)", (int)cr);
 
+    if (d >= 256) {
+        const int pcap = min(persistent_sms(ctx) / 2, max_pairs(ctx));
+        if (pcap >= 1) {
+            PairArgs p{};
+            p.H = H;
+            p.ldh = ldh;
+            p.d = (int)d;
+            p.nt = (int)((d + 255) / 256);
+            p.ntiles = p.nt * (p.nt + 1) / 2;
+            p.kb_total = a.kb_total;
+            p.splits = pick_splits(p.ntiles, p.kb_total, pcap);
+            p.kb_per_split = (p.kb_total + p.splits - 1) / p.splits;
+            p.err = ctx->dflags + 2;
+            p.idesc = make_idesc(dtype, 256, 256);
+            const int punits = p.ntiles * p.splits;
+            const int pairs = punits < pcap ? punits : pcap;
+            syrk_tc2_kernel<<<2 * pairs, NT, P_SMEM_BYTES, ctx->stream>>>(map, hmap, p);
+            return check_launch(ctx, "syrk_tc2");
+        }
+    }
     static bool attr = false;
     if (!attr) {
         LLMC_CUDA_TRY(cudaFuncSetAttribute(syrk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
@@ -346,7 +648,7 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
     }
     const int units = a.ntiles * a.splits;
     const int grid = units < grid_cap ? units : grid_cap;
-    syrk_tc_kernel<<<grid, NT, SMEM_BYTES, ctx->stream>>>(map, a);
+    syrk_tc_kernel<<<grid, NT, SMEM_BYTES, ctx->stream>>>(map, hmap, a);
     return check_launch(ctx, "syrk_tc");
 }
 
