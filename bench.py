@@ -285,8 +285,9 @@ def run_ours(args):
                          "frac_of_its_sms": round(achieved / (sustained * pipe.hessian_sms() / sm_count), 3),
                          "algorithmic": "d(d+1)T FLOP per launch (symmetric rank-k update of T tokens)",
                          "traffic": SYRK_TRAFFIC_PER_LAUNCH,
-                         "traffic_note": "ncu DRAM read+write bytes of one d=4096, 65,536-token launch; "
-                                         "its algorithmic bytes are 0.60 GB (X once + H upper triangle)"},
+                         "traffic_note": "ncu DRAM read+write bytes per launch, averaged over the step's mix of "
+                                         "d=4096 (1.30 GB) and d=14336 (29.4 GB) launches of 65,536 tokens; their "
+                                         "algorithmic bytes are 0.60 GB and 2.29 GB (X once + H upper triangle)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
@@ -299,9 +300,12 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# DRAM bytes (read + write) of one syrk_tc launch at d = 4096 over 65,536 tokens, from the ncu
-# capture summarised in profiles/syrk_tc_kernel_d4096_t65536.md (965.5 MB read + 368.4 MB written).
-SYRK_TRAFFIC_PER_LAUNCH = 1.334e9
+# DRAM bytes (read + write) per Hessian launch of this workload, from one ncu capture of the
+# four site launches of a 65,536-token step (profiles/syrk_tc2_kernel_llama3_8b_sites.md):
+# d = 4096: 0.944 GB read + 0.355 GB written; d = 14336: 26.38 GB + 2.99 GB.  A step has three
+# d = 4096 launches for every d = 14336 launch, so the average launch moves
+# (3 * 1.299 + 29.37) / 4 GB.
+SYRK_TRAFFIC_PER_LAUNCH = (3 * 1.299e9 + 29.37e9) / 4
 
 
 def _randn_bf16(m, n, dev, g, std=1.0):

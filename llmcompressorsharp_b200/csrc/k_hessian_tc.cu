@@ -284,6 +284,9 @@ constexpr int P_SMEM_MAIN = P_STAGES * P_STAGE_BYTES;  // 192 KB
 constexpr int P_SMEM_BYTES = P_SMEM_MAIN + EPI_WARPS * OUT_BYTES + 1024 + 256;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory above the per-block limit");
 
+constexpr int P_MAX_NT = 160;                                // d <= 40960
+constexpr int P_MAX_TILES = P_MAX_NT * (P_MAX_NT + 1) / 2;   // 12,880
+
 struct PairArgs {
     float* H;
     int64_t ldh;
@@ -295,15 +298,11 @@ struct PairArgs {
     int kb_per_split;
     int* err;
     uint32_t idesc;
+    // Tile order, (ti << 8) | tj: compact G x G blocks of tiles one after another, so that
+    // the tiles one wave of pairs works on share few X panels and the panels stay in L2.
+    uint16_t tiles[P_MAX_TILES];
 };
-
-__device__ __forceinline__ void pair_tile(int tile, int* ti, int* tj) {
-    int j = (int)((sqrtf(8.f * (float)tile + 1.f) - 1.f) * 0.5f);
-    while ((j + 1) * (j + 2) / 2 <= tile) j++;
-    while (j * (j + 1) / 2 > tile) j--;
-    *tj = j;
-    *ti = tile - j * (j + 1) / 2;
-}
+static_assert(sizeof(PairArgs) + 2 * sizeof(CUtensorMap) <= 32764, "kernel parameters above the limit");
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
     syrk_tc2_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap, const PairArgs a) {
@@ -351,8 +350,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
 
     for (int u = pair; u < total_units && !*abort_flag; u += npairs) {
         const int split = u / a.ntiles, tile = u % a.ntiles;
-        int ti, tj;
-        pair_tile(tile, &ti, &tj);
+        const int ti = a.tiles[tile] >> 8, tj = a.tiles[tile] & 0xFF;
         const int kb0 = split * a.kb_per_split;
         const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
         const int nchunks = (kb1 - kb0 + KF - 1) / KF;
@@ -621,7 +619,7 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return fail(LLMC_ERR_CUDA, "cuTensorMapEncodeTiled (H) failed (%d)", (int)cr);
 
-    if (d >= 256) {
+    if (d >= 256 && d <= 256 * P_MAX_NT) {
         const int pcap = min(persistent_sms(ctx) / 2, max_pairs(ctx));
         if (pcap >= 1) {
             PairArgs p{};
@@ -630,6 +628,15 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
             p.d = (int)d;
             p.nt = (int)((d + 255) / 256);
             p.ntiles = p.nt * (p.nt + 1) / 2;
+            // Blocks of G x G tiles (G ~ sqrt(pairs)), column of blocks by column of blocks.
+            int G = 1;
+            while ((G + 1) * (G + 1) <= pcap) G++;
+            int n = 0;
+            for (int bj = 0; bj < p.nt; bj += G)
+                for (int bi = 0; bi <= bj; bi += G)
+                    for (int tj = bj; tj < min(p.nt, bj + G); tj++)
+                        for (int ti = bi; ti < min(bi + G, tj + 1); ti++) p.tiles[n++] = (uint16_t)((ti << 8) | tj);
+            if (n != p.ntiles) return fail(LLMC_ERR_INTERNAL, "syrk pair tile order: %d of %d tiles", n, p.ntiles);
             p.kb_total = a.kb_total;
             p.splits = pick_splits(p.ntiles, p.kb_total, pcap);
             p.kb_per_split = (p.kb_total + p.splits - 1) / p.splits;
