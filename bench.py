@@ -287,7 +287,7 @@ def run_ours(args):
                          "traffic": SYRK_TRAFFIC_PER_LAUNCH,
                          "traffic_note": "ncu DRAM read+write bytes per launch, averaged over the step's mix of "
                                          "d=4096 (1.30 GB) and d=14336 (29.4 GB) launches of 65,536 tokens; their "
-                                         "algorithmic bytes are 0.60 GB and 2.29 GB (X once + H upper triangle)"},
+                                         "algorithmic bytes are 0.60 GB and 2.70 GB (X once + H upper triangle)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
