@@ -141,7 +141,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from llmcompressorsharp_b200 import _lib
+    from llmcompressorsharp_b200.distributed import owned_layers, reduce_hessians, token_shard
     from llmcompressorsharp_b200.gptq import GPTQConfig
     from llmcompressorsharp_b200.pipeline import GptqPipeline
 
@@ -154,11 +154,11 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     sites = sites_for(MODEL)
     L = args.layers
-    T_local = args.tokens // world
+    r0, r1 = token_shard(args.tokens, world, rank)
+    T_local = r1 - r0
     cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128,
                      dampening_frac=0.01)
-    owners = {l: l % world for l in range(L)}
-    mine = [l for l in range(L) if owners[l] == rank]
+    mine = owned_layers(range(L), world, rank)
 
     # ---- synthetic inputs, resident in HBM
     g = torch.Generator(dev)
@@ -200,12 +200,7 @@ def run_ours(args):
                     e1.record()
                     hess_events.append((e0, e1, s.d, acts[s.name].shape[0]))
         # phase 2: sum partials onto each layer's owner (NCCL reduce, one group)
-        reqs = []
-        for l in range(L):
-            for s in sites:
-                reqs.append(dist.reduce(hbufs[l][s.name], dst=owners[l], op=dist.ReduceOp.SUM, async_op=True))
-        for r in reqs:
-            r.wait()
+        reduce_hessians(hbufs, sites, range(L), world)
         # phase 3: owners solve
         for l in mine:
             for s in sites:
@@ -327,6 +322,8 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
     import torch
     import torch.distributed as dist
 
+    from llmcompressorsharp_b200.distributed import reduce_hessians
+
     dev = torch.device("cuda", local)
     h_acts = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in acts.items()}
     for k in acts:
@@ -341,7 +338,6 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
     h2d = sum(t.numel() * t.element_size() for t in h_acts.values())
     h2d += sum(t.numel() * t.element_size() for l in mine for t in h_w[l].values())
     d2h = sum(t.numel() * t.element_size() for l in mine for o in h_out[l].values() for t in o.values())
-    owners = {l: l % world for l in range(args.layers)}
 
     def e2e_step():
         for k in acts:
@@ -361,9 +357,7 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
         for l in range(args.layers):
             for s in sites:
                 pipe.accumulate(s, acts[s.name], out_h=hbufs[l][s.name])
-        reqs = [dist.reduce(hbufs[l][s.name], dst=owners[l], async_op=True) for l in range(args.layers) for s in sites]
-        for r in reqs:
-            r.wait()
+        reduce_hessians(hbufs, sites, range(args.layers), world)
         for l in mine:
             for k in weights[l]:
                 weights[l][k].copy_(h_w[l][k], non_blocking=True)
