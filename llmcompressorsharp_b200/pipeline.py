@@ -186,21 +186,28 @@ class GptqPipeline:
             self.accumulate(s, acts[s.name])
             self.solve_site(s, self.hessian_ptr(s.name), weights, outputs)
 
-    def run(self, layers, acts, weights, outputs, before_solve=None, after_solve=None, hess_events=None):
+    def run(self, layers, acts, weights, outputs, before_solve=None, after_solve=None, hess_events=None,
+            acts_ready=None):
         """The whole job over ``layers``: per layer, every site's Hessian, factor and stacked
         GPTQ solve.  ``acts`` is {site: [T, d]} (shared by the layers) or a callable
         layer -> {site: tensor}; ``weights[l]`` / ``outputs[l]`` per layer.  ``before_solve(l)``
         and ``after_solve(l)`` run on the stream that solves layer l, just before / after it
         (e.g. host->device weight copies and device->host result copies).  With
         ``hess_events`` (a list), CUDA event pairs bracketing each site's accumulation are
-        appended as (start, end, d, rows).  Work is enqueued on the current stream (or, with
-        overlap enabled, on the two pipeline streams joined back into it)."""
+        appended as (start, end, d, rows).  ``acts_ready`` ({site: CUDA event}) makes the first
+        accumulation of each site wait for that event (activations still being copied in on
+        another stream).  Work is enqueued on the current stream (or, with overlap enabled,
+        on the two pipeline streams joined back into it)."""
         acts_for = acts if callable(acts) else (lambda _l: acts)
+        pending = dict(acts_ready or {})
         if self.overlap is not None:
-            return self.overlap.run(list(layers), acts_for, weights, outputs, before_solve, after_solve, hess_events)
+            return self.overlap.run(list(layers), acts_for, weights, outputs, before_solve, after_solve, hess_events,
+                                    pending)
         for l in layers:
             a = acts_for(l)
             for s in self.sites:
+                if s.name in pending:
+                    torch.cuda.current_stream(self.device).wait_event(pending.pop(s.name))
                 ev = _events() if hess_events is not None else None
                 if ev:
                     ev[0].record()
@@ -267,7 +274,7 @@ class _Overlap:
         _lib.call("llmc_hessian_data", C.c_void_p(self.h[b][site]), C.byref(p))
         return p.value
 
-    def run(self, layers, acts_for, weights, outputs, before_solve, after_solve, hess_events):
+    def run(self, layers, acts_for, weights, outputs, before_solve, after_solve, hess_events, acts_ready):
         pipe = self.pipe
         cur = torch.cuda.current_stream(pipe.device)
         self.sh.wait_stream(cur)
@@ -296,6 +303,8 @@ class _Overlap:
                 if solved[b] is not None:
                     self.sh.wait_event(solved[b])
                 for s in pipe.sites:
+                    if s.name in acts_ready:
+                        self.sh.wait_event(acts_ready.pop(s.name))
                     ev = _events() if hess_events is not None else None
                     if ev:
                         ev[0].record(self.sh)
