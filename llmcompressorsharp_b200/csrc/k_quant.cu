@@ -11,6 +11,8 @@
 // inside the lane group.
 #include "ops.h"
 
+#include <type_traits>
+
 namespace llmc {
 namespace {
 
@@ -98,6 +100,89 @@ __global__ void __launch_bounds__(NT) seg_minmax_kernel(const T* x, SegGeom g, f
             maxs[seg] = mx;
         }
     }
+}
+
+// Division of a segment index by the (runtime) number of segments per row with one
+// multiply-high, add and shift (Granlund and Montgomery, "Division by invariant integers
+// using multiplication", 1994): for 1 <= d < 2^31, l = ceil(log2 d), m = floor(2^32 (2^l - d)
+// / d) + 1, n / d = (mulhi(n, m) + n) >> l for every n < 2^31.
+struct FastDiv {
+    uint32_t m, l;
+};
+
+FastDiv make_fastdiv(uint32_t d) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) l++;
+    const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+    return FastDiv{(uint32_t)m, l};
+}
+
+__device__ __forceinline__ uint32_t fastdiv(uint32_t n, FastDiv f) { return (__umulhi(n, f.m) + n) >> f.l; }
+
+// Lanes of one segment load RV vectors each per step (segments of RV * L * VEC elements take
+// one step; longer ones loop), with one min/max pair per vector slot to keep the dependency
+// chains short.  Segment s of the launch is row s / nseg, columns (s % nseg) * seglen ...
+constexpr int RV = 4;
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(NT) seg_minmax_reg_kernel(const T* x, SegGeom g, FastDiv fd, float* mins,
+                                                            float* maxs, int accumulate) {
+    const int L = g.L;
+    const uint32_t gpb = NT / L;
+    const uint32_t total = (uint32_t)(g.rows * g.nseg);
+    const uint32_t lg = threadIdx.x / L;
+    const int sub = lane_id() % L;
+    const int64_t seglen = g.gs < g.cols ? g.gs : g.cols;
+    for (uint32_t base = blockIdx.x * gpb; base < total; base += gridDim.x * gpb) {
+        const uint32_t seg = base + lg;
+        const bool active = seg < total;
+        const uint32_t sg = active ? seg : 0;
+        const uint32_t r = fastdiv(sg, fd);
+        const T* row = x + (int64_t)r * g.ld + (int64_t)(sg - r * (uint32_t)g.nseg) * seglen;
+        float mn[RV], mx[RV];
+#pragma unroll
+        for (int j = 0; j < RV; j++) {
+            mn[j] = INFINITY;
+            mx[j] = -INFINITY;
+        }
+        if (active) {
+            for (int64_t c = (int64_t)sub * VEC; c < seglen; c += (int64_t)L * VEC * RV) {
+                Vec<T, VEC> v[RV];
+#pragma unroll
+                for (int j = 0; j < RV; j++) v[j].load(row + c + (int64_t)j * L * VEC);
+#pragma unroll
+                for (int j = 0; j < RV; j++)
+#pragma unroll
+                    for (int i = 0; i < VEC; i++) {
+                        mn[j] = fminf(mn[j], v[j].v[i]);
+                        mx[j] = fmaxf(mx[j], v[j].v[i]);
+                    }
+            }
+        }
+        float a = fminf(fminf(mn[0], mn[1]), fminf(mn[2], mn[3]));
+        float b = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        for (int off = L / 2; off > 0; off >>= 1) {
+            a = fminf(a, __shfl_xor_sync(0xffffffffu, a, off));
+            b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, off));
+        }
+        if (active && sub == 0) {
+            if (accumulate) {
+                a = fminf(a, mins[seg]);
+                b = fmaxf(b, maxs[seg]);
+            }
+            mins[seg] = a;
+            maxs[seg] = b;
+        }
+    }
+}
+
+// Lanes per segment for the register kernels: segments of RV * L * VEC elements (L a power of
+// two <= 32), or L = 32 for segments that are a multiple of 32 * RV * VEC; 0 = not eligible.
+int reg_lanes(int64_t seglen, int vec) {
+    if (seglen % ((int64_t)RV * vec) != 0) return 0;
+    if (seglen % ((int64_t)32 * RV * vec) == 0) return 32;
+    const int64_t l = seglen / ((int64_t)RV * vec);
+    return (l >= 1 && l <= 32 && (l & (l - 1)) == 0) ? (int)l : 0;
 }
 
 __global__ void affine_kernel(const float* mins, const float* maxs, int64_t count, int bits, int sym, float* scales,
@@ -209,6 +294,222 @@ __global__ void __launch_bounds__(NT) rtn_kernel(const T* x, SegGeom g, int bits
     }
 }
 
+// The op-by-op FakeQuantizeFunction chain, out of line (the register RTN kernel calls it
+// only for the rare elements its integer path does not cover).
+struct FqOut {
+    float value;
+    int code;
+};
+
+template <typename T>
+__device__ __noinline__ FqOut fq_chain_call(float x, float s, float zpf, float qmin, float qmax) {
+    FqOut r;
+    r.value = fq_chain<T>(x, s, zpf, qmin, qmax, &r.code);
+    return r;
+}
+
+// RTN with every segment held in registers: each lane loads RV vectors of its segment
+// (segment length = RV * L * VEC), so a thread keeps RV loads in flight and the per-segment
+// parameter math is shared by RV * VEC elements.  Elements follow the op-by-op chain (the
+// bf16 kernel below has the integer path).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(NT) rtn_reg_kernel(const T* x, SegGeom g, FastDiv fd, int bits, int sym,
+                                                     int tensor_mode, float* scales, int32_t* zps, uint8_t* codes,
+                                                     T* deq, int64_t ld_deq) {
+    const int L = g.L;
+    const uint32_t gpb = NT / L;
+    const uint32_t total = (uint32_t)(g.rows * g.nseg);
+    const uint32_t lg = threadIdx.x / L;
+    const int sub = lane_id() % L;
+    const int64_t seglen = g.gs < g.cols ? g.gs : g.cols;
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    const int64_t crow = code_row_bytes(bits, g.cols);
+    for (uint32_t base = blockIdx.x * gpb; base < total; base += gridDim.x * gpb) {
+        const uint32_t seg = base + lg;
+        const bool active = seg < total;
+        const uint32_t sg = active ? seg : 0;
+        const uint32_t r = fastdiv(sg, fd);
+        const int64_t c0 = (int64_t)(sg - r * (uint32_t)g.nseg) * seglen;
+        const T* row = x + (int64_t)r * g.ld + c0;
+        Vec<T, VEC> v[RV];
+        float mn[RV], mx[RV];
+#pragma unroll
+        for (int j = 0; j < RV; j++) {
+            mn[j] = INFINITY;
+            mx[j] = -INFINITY;
+        }
+        if (active) {
+#pragma unroll
+            for (int j = 0; j < RV; j++) v[j].load(row + (int64_t)(j * L + sub) * VEC);
+#pragma unroll
+            for (int j = 0; j < RV; j++)
+#pragma unroll
+                for (int i = 0; i < VEC; i++) {
+                    mn[j] = fminf(mn[j], v[j].v[i]);
+                    mx[j] = fmaxf(mx[j], v[j].v[i]);
+                }
+        }
+        float smin = fminf(fminf(mn[0], mn[1]), fminf(mn[2], mn[3]));
+        float smax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        for (int off = L / 2; off > 0; off >>= 1) {
+            smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, off));
+            smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+        }
+        if (!active) continue;
+        float s;
+        int z;
+        if (tensor_mode) {
+            s = scales[0];
+            z = zps[0];
+        } else {
+            affine_params(smin, smax, bits, sym, &s, &z);
+            if (sub == 0) {
+                scales[seg] = s;
+                zps[seg] = z;
+            }
+        }
+        const float zf = (float)z;
+        uint8_t* crow_p = codes ? codes + (int64_t)r * crow : nullptr;
+#pragma unroll
+        for (int j = 0; j < RV; j++) {
+            const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
+            int q[VEC];
+            float o[VEC];
+#pragma unroll
+            for (int i = 0; i < VEC; i++) o[i] = fq_chain<T>(v[j].v[i], s, zf, qmin, qmax, &q[i]);
+            if (crow_p) store_codes<VEC>(crow_p, c, q, z, bits, VEC);
+            if (deq) {
+                T* d = deq + (int64_t)r * ld_deq + c;
+                uint4 pk;
+                T* h = reinterpret_cast<T*>(&pk);
+#pragma unroll
+                for (int i = 0; i < VEC; i++) h[i] = from_f<T>(o[i]);
+                *reinterpret_cast<uint4*>(d) = pk;
+            }
+        }
+    }
+}
+
+// bf16 RTN, register-resident like rtn_reg_kernel, with an integer path that is exact by
+// construction.  With r = rcp_rn(s), f = x * r is within 3 units in the last place of
+// fl(x / s), so bf16(f) == bf16(fl(x / s)) unless the low 16 bits of f lie within 4 of the
+// bf16 rounding midpoint 0x8000 (those elements, and NaN / Inf, take the op-by-op chain).  If
+// every quotient of the segment satisfies -256 <= x / s + zp <= 256 (checked from its min and
+// max with a 2^-20 relative margin), every intermediate of FakeQuantizeFunction's chain (rint,
+// + zp, clamp, - zp) is an integer of magnitude <= 256, which bf16 represents exactly, so
+// the chain reduces to integer arithmetic on rint(bf16(x / s)) and the dequantised value to
+// bf16((q - zp) * s).  The bf16 rounding of f is done on its bit pattern (round to nearest
+// even at bit 16) and rint by adding 1.5 * 2^23 (ties to even, exact for |v| < 2^22), so the
+// path needs no conversion instructions.
+template <bool DEQ>
+__global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, SegGeom g, FastDiv fd, int bits, int sym,
+                                                      int tensor_mode, float* scales, int32_t* zps, uint8_t* codes,
+                                                      __nv_bfloat16* deq, int64_t ld_deq) {
+    constexpr int VEC = 8;
+    const int L = g.L;
+    const uint32_t gpb = NT / L;
+    const uint32_t total = (uint32_t)(g.rows * g.nseg);
+    const uint32_t lg = threadIdx.x / L;
+    const int sub = lane_id() % L;
+    const int64_t seglen = g.gs < g.cols ? g.gs : g.cols;
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    const int iqmin = (int)qmin, iqmax = (int)qmax;
+    const int64_t crow = code_row_bytes(bits, g.cols);
+    const __nv_bfloat162 pinf = __float2bfloat162_rn(INFINITY), ninf = __float2bfloat162_rn(-INFINITY);
+    for (uint32_t base = blockIdx.x * gpb; base < total; base += gridDim.x * gpb) {
+        const uint32_t seg = base + lg;
+        const bool active = seg < total;
+        const uint32_t sg = active ? seg : 0;
+        const uint32_t r = fastdiv(sg, fd);
+        const int64_t c0 = (int64_t)(sg - r * (uint32_t)g.nseg) * seglen;
+        const __nv_bfloat16* row = x + (int64_t)r * g.ld + c0;
+        uint4 w[RV];
+        __nv_bfloat162 mn2[2] = {pinf, pinf}, mx2[2] = {ninf, ninf};
+        if (active) {
+#pragma unroll
+            for (int j = 0; j < RV; j++) w[j] = *reinterpret_cast<const uint4*>(row + (int64_t)(j * L + sub) * VEC);
+#pragma unroll
+            for (int j = 0; j < RV; j++) {
+                const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(&ww[k]);
+                    mn2[k & 1] = __hmin2(mn2[k & 1], p);
+                    mx2[k & 1] = __hmax2(mx2[k & 1], p);
+                }
+            }
+        }
+        const __nv_bfloat162 mnp = __hmin2(mn2[0], mn2[1]), mxp = __hmax2(mx2[0], mx2[1]);
+        float smin = fminf(__low2float(mnp), __high2float(mnp));
+        float smax = fmaxf(__low2float(mxp), __high2float(mxp));
+        for (int off = L / 2; off > 0; off >>= 1) {
+            smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, off));
+            smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+        }
+        if (!active) continue;
+        float s;
+        int z;
+        if (tensor_mode) {
+            s = scales[0];
+            z = zps[0];
+        } else {
+            affine_params(smin, smax, bits, sym, &s, &z);
+            if (sub == 0) {
+                scales[seg] = s;
+                zps[seg] = z;
+            }
+        }
+        const float zf = (float)z;
+        const float rcp = __frcp_rn(s);
+        const float k = 1.f + 0x1p-20f;
+        const float hi = fmaxf(smax, 0.f) * rcp * k + zf;  // NaN / Inf fail the tests below
+        const float lo = fminf(smin, 0.f) * rcp * k + zf;
+        const bool fast = bits <= 8 && hi <= 256.f && lo >= -256.f;
+        uint8_t* crow_p = codes ? codes + (int64_t)r * crow : nullptr;
+#pragma unroll
+        for (int j = 0; j < RV; j++) {
+            const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
+            const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+            int q[VEC];
+            float o[VEC];
+            uint32_t slow = fast ? 0u : (1u << VEC) - 1u;
+#pragma unroll
+            for (int i = 0; i < VEC; i++) {
+                const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+                const float f = __fmul_rn(xv, rcp);
+                const uint32_t b = __float_as_uint(f);
+                if (((b - 0x7FFCu) & 0xFFFFu) <= 8u || !(fabsf(f) <= 3.0e38f)) slow |= 1u << i;
+                const float t1 = __uint_as_float((b + 0x7FFFu + ((b >> 16) & 1u)) & 0xFFFF0000u);
+                int t = __float_as_int(__fadd_rn(t1, 12582912.f)) - 0x4B400000 + z;
+                t = t < iqmin ? iqmin : (t > iqmax ? iqmax : t);
+                q[i] = t;
+                if (DEQ) o[i] = __fmul_rn(__int_as_float(0x4B400000 + (t - z)) - 12582912.f, s);
+            }
+            if (slow) {
+#pragma unroll
+                for (int i = 0; i < VEC; i++)
+                    if ((slow >> i) & 1u) {
+                        const float xv =
+                            (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+                        const FqOut e = fq_chain_call<__nv_bfloat16>(xv, s, zf, qmin, qmax);
+                        o[i] = e.value;
+                        q[i] = e.code;
+                    }
+            }
+            if (crow_p) store_codes<VEC>(crow_p, c, q, z, bits, VEC);
+            if (DEQ) {
+                uint4 pk;
+                __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&pk);
+#pragma unroll
+                for (int i = 0; i < VEC; i++) h[i] = __float2bfloat16_rn(o[i]);
+                *reinterpret_cast<uint4*>(deq + (int64_t)r * ld_deq + c) = pk;
+            }
+        }
+    }
+}
+
 template <typename T>
 __global__ void fake_quant_flat_kernel(const T* x, int64_t n, float s, float zf, float qmin, float qmax, T* out,
                                        int32_t* codes) {
@@ -284,9 +585,17 @@ llmc_status launch_minmax(llmc_ctx* ctx, const void* x, int64_t rows, int64_t co
     SegGeom g{rows, cols, ld, gs, (cols + gs - 1) / gs, 1};
     const int64_t total = rows * g.nseg;
     if (vec_ok<T>(x, ld, gs, cols)) {
-        g.L = lanes_for(gs < cols ? gs : cols, V);
-        seg_minmax_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
-            reinterpret_cast<const T*>(x), g, mins, maxs, accumulate);
+        const int64_t seglen = gs < cols ? gs : cols;
+        g.L = lanes_for(seglen, V);
+        const int rl = reg_lanes(seglen, V);
+        if (cols % seglen == 0 && rl > 0 && total < (int64_t(1) << 31) && g.nseg < (int64_t(1) << 31)) {
+            g.L = rl;
+            seg_minmax_reg_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+                reinterpret_cast<const T*>(x), g, make_fastdiv((uint32_t)g.nseg), mins, maxs, accumulate);
+        } else {
+            seg_minmax_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+                reinterpret_cast<const T*>(x), g, mins, maxs, accumulate);
+        }
     } else {
         g.L = lanes_for(gs < cols ? gs : cols, 1);
         seg_minmax_kernel<T, 1><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
@@ -314,7 +623,30 @@ llmc_status launch_rtn(llmc_ctx* ctx, const void* x, int64_t m, int64_t n, int64
     // Vector path also needs whole code bytes per lane (even column starts) and aligned output.
     const bool deq_ok = deq == nullptr || ((uintptr_t)deq % 16 == 0);
     const bool codes_ok = codes == nullptr || bits > 4 || (n % 2 == 0);
-    if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok) {
+    const int64_t seglen = gs < n ? gs : n;
+    const int64_t lanes = seglen / (RV * V);
+    const bool reg_ok = seglen % (RV * V) == 0 && lanes >= 1 && lanes <= 32 && (lanes & (lanes - 1)) == 0 &&
+                        n % seglen == 0 && total < (int64_t(1) << 31) && g.nseg < (int64_t(1) << 31);
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && reg_ok) {
+            g.L = (int)lanes;
+            const FastDiv fd = make_fastdiv((uint32_t)g.nseg);
+            if (deq)
+                rtn_bf16_kernel<true><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+                    reinterpret_cast<const T*>(x), g, fd, bits, sym, tensor_mode, scales, zps, codes,
+                    reinterpret_cast<T*>(deq), n);
+            else
+                rtn_bf16_kernel<false><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+                    reinterpret_cast<const T*>(x), g, fd, bits, sym, tensor_mode, scales, zps, codes, nullptr, n);
+            return check_launch(ctx, "rtn_bf16");
+        }
+    }
+    if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && reg_ok) {
+        g.L = (int)lanes;
+        rtn_reg_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+            reinterpret_cast<const T*>(x), g, make_fastdiv((uint32_t)g.nseg), bits, sym, tensor_mode, scales, zps, codes,
+            reinterpret_cast<T*>(deq), n);
+    } else if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok) {
         g.L = lanes_for(gs < n ? gs : n, V);
         rtn_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
             reinterpret_cast<const T*>(x), g, bits, sym, tensor_mode, scales, zps, codes, reinterpret_cast<T*>(deq), n);

@@ -301,6 +301,60 @@ def test_rtn_bit_exact(dtype, strategy, bits, sym, shape):
     assert torch.equal(codes.cpu(), ref_codes)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("strategy,gs,n", [("group", 128, 4096), ("group", 64, 1024), ("group", 256, 2048),
+                                           ("channel", 0, 512), ("channel", 0, 1024)])
+@pytest.mark.parametrize("bits,sym", [(4, False), (4, True), (8, False), (8, True)])
+def test_rtn_register_path_bit_exact(dtype, strategy, gs, n, bits, sym):
+    """Shapes whose segments fit the register-resident RTN kernel; rows 0-7 are offset far from
+    zero (|x / s| too large for the integer fast path) and rows 8-15 are tiny, so segments take
+    both routes; ~2M elements per case also exercise the bf16 rounding-midpoint fallback."""
+    from llmcompressorsharp_b200 import RtnConfig, rtn_quantize
+
+    m = 512
+    w = outlier_weight(m, n, 1000 + n + bits, torch.float32)
+    w[0:8] += 3.0
+    w[8:16] *= 1e-3
+    w = w.to(dtype)
+    cfg = RtnConfig(num_bits=bits, symmetric=sym, strategy=strategy, group_size=gs or 128)
+    deq, codes, scales, zps = rtn_quantize(w.to(DEV), cfg)
+    rdeq, rcodes, rs, rz = o_rtn.rtn_quantize(w, o_rtn.RtnConfig(bits, sym, strategy, group_size=gs or 128))
+    assert torch.equal(deq.cpu(), rdeq)
+    assert np.array_equal(scales.cpu().numpy().reshape(-1), np.asarray(rs, np.float32).reshape(-1))
+    assert np.array_equal(zps.cpu().numpy().reshape(-1), np.asarray(rz).reshape(-1))
+    if bits <= 4:
+        zp_e = torch.from_numpy(np.asarray(rz))
+        zp_e = zp_e[:, torch.arange(n) // gs] if strategy == "group" else zp_e.expand(m, n)
+        ref_codes = o_fq.pack_int4_rows(rcodes, zp_e)
+    else:
+        ref_codes = rcodes.to(torch.uint8)
+    assert torch.equal(codes.cpu(), ref_codes)
+
+
+@pytest.mark.parametrize("strategy,gs", [("tensor", 0), ("channel", 0), ("group", 128)])
+def test_observer_multi_segment_path_exact(strategy, gs):
+    """Observer shapes on the multi-segment kernel (equal-length segments): exact min / max."""
+    import ctypes as C
+
+    from llmcompressorsharp_b200 import _lib
+
+    w = outlier_weight(1000, 4096, 77, torch.bfloat16).to(DEV)
+    cnt = {"tensor": 1, "channel": 1000, "group": 1000 * 32}[strategy]
+    mn = torch.empty(cnt, device=DEV)
+    mx = torch.empty(cnt, device=DEV)
+    _lib.call("llmc_observer_minmax", C.c_void_p(_lib.ctx_for(0)), _lib.ptr(w), _lib.DTYPE_BF16, C.c_int64(1000),
+              C.c_int64(4096), C.c_int64(4096), _lib.STRATEGY[strategy], C.c_int64(gs or 4096), _lib.ptr(mn),
+              _lib.ptr(mx), 0)
+    wf = w.float()
+    if strategy == "tensor":
+        ref_mn, ref_mx = wf.min().reshape(1), wf.max().reshape(1)
+    elif strategy == "channel":
+        ref_mn, ref_mx = wf.amin(1), wf.amax(1)
+    else:
+        ref_mn, ref_mx = wf.view(1000, 32, 128).amin(2).reshape(-1), wf.view(1000, 32, 128).amax(2).reshape(-1)
+    assert torch.equal(mn, ref_mn) and torch.equal(mx, ref_mx)
+
+
 def test_rtn_kats():  # RtnModifierTests.cs
     from llmcompressorsharp_b200 import RtnConfig, RtnModifier, CompressionState
 
