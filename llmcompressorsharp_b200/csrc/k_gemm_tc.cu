@@ -46,6 +46,7 @@ struct TcGemmArgs {
     int a_tri, b_tri, c_mode;
     int* err;
     uint32_t idesc;
+    int tiles_m, tiles_n, group;  // 1-D grid: tiles visited in column strips of `group` M-tiles
 };
 
 // Loads one operand part (128 rows of the MN dimension x 32 K-elements, K contiguous) for a
@@ -71,7 +72,14 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+    // Tile of this CTA: consecutive CTAs walk a strip of `group` M-tiles column by column, so
+    // the CTAs resident at one time share few A and B panels and those stay in L2.
+    const int per_group = a.group * a.tiles_n;
+    const int gidx = (int)blockIdx.x / per_group;
+    const int first_m = gidx * a.group;
+    const int gm = min(a.group, a.tiles_m - first_m);
+    const int local = (int)blockIdx.x - gidx * per_group;
+    const int64_t m0 = (int64_t)(first_m + local % gm) * BM, n0 = (int64_t)(local / gm) * BN;
     if (a.c_mode == 1 && m0 + BM - 1 < n0) return;  // tile entirely above the diagonal
     if (a.c_mode == 2 && m0 > n0 + BN - 1) return;  // tile entirely below the diagonal
 
@@ -346,6 +354,7 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
     if (g.a_dtype != LLMC_DTYPE_F32 || g.b_dtype != LLMC_DTYPE_F32) return LLMC_ERR_UNSUPPORTED;
     if (g.split_k > 1 || g.M < 128 || g.N < 128 || g.K < 64) return LLMC_ERR_UNSUPPORTED;
     if (g.M > (int64_t)INT32_MAX || g.N > (int64_t)INT32_MAX || g.K > (int64_t)INT32_MAX) return LLMC_ERR_UNSUPPORTED;
+    if (((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN) > (int64_t)INT32_MAX) return LLMC_ERR_UNSUPPORTED;
     // Operands as stored: A is [M, K] (a_trans = 0) or [K, M] (a_trans = 1); B is [K, N]
     // (b_trans = 0) or [N, K] (b_trans = 1).  The split copies are K-major [M, K] and [N, K].
     const int64_t ldk = (g.K + 3) / 4 * 4;
@@ -391,9 +400,10 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
         LLMC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         attr = true;
     }
-    dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM));
-    if (grid.y > 65535) return LLMC_ERR_UNSUPPORTED;
-    gemm_tc_kernel<<<grid, NT, SMEM_BYTES, ctx->stream>>>(mah, mal, mbh, mbl, t);
+    t.tiles_m = (int)((g.M + BM - 1) / BM);
+    t.tiles_n = (int)((g.N + BN - 1) / BN);
+    t.group = 12;  // ~sqrt(SM count)
+    gemm_tc_kernel<<<(unsigned)(t.tiles_m * t.tiles_n), NT, SMEM_BYTES, ctx->stream>>>(mah, mal, mbh, mbl, t);
     return check_launch(ctx, "gemm_tc");
 }
 

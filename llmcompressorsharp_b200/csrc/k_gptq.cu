@@ -44,7 +44,8 @@ struct BlockArgs {
 
 template <int MODE>
 constexpr size_t block_smem_bytes() {
-    return (size_t)BW * BW * 4 + (size_t)BW * WLD * 4 + (size_t)BW * ROWS + (MODE == 1 ? (size_t)BW * WLD * 4 : 0);
+    return (size_t)BW * BW * 4 + (size_t)BW * WLD * 4 + (size_t)BW * ROWS + (MODE == 1 ? (size_t)BW * WLD * 4 : 0) +
+           (size_t)BW * 4;
 }
 
 // Keep mask of one row's block (SparseGPT): per-row top-k (unstructured) or N:M, ties to
@@ -89,6 +90,10 @@ __device__ void select_keep(const float* sal, int cnt, float sparsity, int mask_
     }
 }
 
+__device__ __forceinline__ uint32_t smem_u32_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 template <int MODE>  // 0 = GPTQ quantise, 1 = SparseGPT prune
 __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -96,19 +101,68 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
     float* Wt = Us + BW * BW;                                    // [BW][WLD] column-major tile
     uint8_t* Ct = reinterpret_cast<uint8_t*>(Wt + BW * WLD);     // [BW][ROWS] codes / mask bytes
     float* Sal = reinterpret_cast<float*>(Ct + BW * ROWS);       // MODE 1: [BW][WLD] saliencies
+    float* Rp = Sal + (MODE == 1 ? BW * WLD : 0);                // [BW] reciprocals of U's diagonal
     const int tid = threadIdx.x;
     const int64_t r0 = (int64_t)blockIdx.x * ROWS;
     const int cnt = a.cnt;
 
-    for (int t = tid; t < BW * BW; t += ROWS) {
-        const int j = t / BW, c = t % BW;
-        Us[t] = (j < cnt && c < cnt) ? a.U[(a.i1 + j) * a.ldu + a.i1 + c] : 0.f;
+    // U block: 16-byte asynchronous copies, all in flight at once (zero-filled past cnt).
+    // W tile: 16-byte loads eight at a time, scattered into the column-major tile.
+    const bool vec = ((reinterpret_cast<uintptr_t>(a.U) | reinterpret_cast<uintptr_t>(a.W)) % 16 == 0) &&
+                     a.ldu % 4 == 0 && a.ldw % 4 == 0 && a.i1 % 4 == 0;
+    if (vec) {
+        for (int t = tid; t < BW * BW / 4; t += ROWS) {
+            const int j = t / (BW / 4), c = (t % (BW / 4)) * 4;
+            const int valid = (j < cnt) ? max(0, min(4, cnt - c)) : 0;
+            const float* src = valid ? a.U + (a.i1 + j) * a.ldu + a.i1 + c : a.U;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32_addr(&Us[j * BW + c])),
+                         "l"(src), "r"(valid * 4)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        constexpr int PER = ROWS * BW / 4 / ROWS;  // float4 per thread (32)
+        constexpr int BATCH = 8;
+#pragma unroll 1
+        for (int b0 = 0; b0 < PER; b0 += BATCH) {
+            float4 v[BATCH];
+#pragma unroll
+            for (int k = 0; k < BATCH; k++) {
+                const int t = tid + (b0 + k) * ROWS;
+                const int rr = t / (BW / 4), c = (t % (BW / 4)) * 4;
+                const int64_t R = r0 + rr;
+                if (R < a.m && c + 3 < cnt) {
+                    v[k] = *reinterpret_cast<const float4*>(a.W + R * a.ldw + a.i1 + c);
+                } else {
+                    float e[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) e[i] = (R < a.m && c + i < cnt) ? a.W[R * a.ldw + a.i1 + c + i] : 0.f;
+                    v[k] = make_float4(e[0], e[1], e[2], e[3]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < BATCH; k++) {
+                const int t = tid + (b0 + k) * ROWS;
+                const int rr = t / (BW / 4), c = (t % (BW / 4)) * 4;
+                Wt[(c + 0) * WLD + rr] = v[k].x;
+                Wt[(c + 1) * WLD + rr] = v[k].y;
+                Wt[(c + 2) * WLD + rr] = v[k].z;
+                Wt[(c + 3) * WLD + rr] = v[k].w;
+            }
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else {
+        for (int t = tid; t < BW * BW; t += ROWS) {
+            const int j = t / BW, c = t % BW;
+            Us[t] = (j < cnt && c < cnt) ? a.U[(a.i1 + j) * a.ldu + a.i1 + c] : 0.f;
+        }
+        for (int t = tid; t < ROWS * BW; t += ROWS) {
+            const int rr = t / BW, c = t % BW;
+            const int64_t R = r0 + rr;
+            Wt[c * WLD + rr] = (R < a.m && c < cnt) ? a.W[R * a.ldw + a.i1 + c] : 0.f;
+        }
     }
-    for (int t = tid; t < ROWS * BW; t += ROWS) {
-        const int rr = t / BW, c = t % BW;
-        const int64_t R = r0 + rr;
-        Wt[c * WLD + rr] = (R < a.m && c < cnt) ? a.W[R * a.ldw + a.i1 + c] : 0.f;
-    }
+    __syncthreads();
+    for (int c = tid; c < BW; c += ROWS) Rp[c] = __frcp_rn(Us[c * BW + c]);
     __syncthreads();
 
     const int64_t R = r0 + tid;
@@ -130,13 +184,19 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
     // Scale entry of the current column: reloaded when the column crosses a group edge.
     int64_t g = a.i1 / a.gs;
     int64_t next_edge = (g + 1) * a.gs - a.i1;  // block-relative column where g changes
-    float s = 1.f, zf = 0.f;
+    // rs = rcp(s): x * rs stands in for x / s except within a few units in the last place of
+    // a half-integer (where rint could differ) or when rs is not finite; those take the exact
+    // op-by-op chain, so the code and the value equal the chain's.
+    float s = 1.f, zf = 0.f, rs = 1.f;
+    bool rs_ok = true;
     int zi = 0;
     if constexpr (MODE == 0) {
         const int64_t si = row_ok ? R * a.srow + g : 0;
         s = a.scales[si];
         zi = a.zps[si];
         zf = (float)zi;
+        rs = __frcp_rn(s);
+        rs_ok = fabsf(rs) <= 3.0e38f && rs != 0.f;
     }
 
     for (int c0 = 0; c0 < cnt; c0 += SB) {
@@ -158,9 +218,21 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
                         s = a.scales[si];
                         zi = a.zps[si];
                         zf = (float)zi;
+                        rs = __frcp_rn(s);
+                        rs_ok = fabsf(rs) <= 3.0e38f && rs != 0.f;
                     }
                     int code;
-                    q = fq_chain<float>(w[j], s, zf, qmin, qmax, &code);
+                    const float f = __fmul_rn(w[j], rs);
+                    const float fr = rintf(f);
+                    const float dd = fabsf(__fsub_rn(f, fr));
+                    if (!rs_ok || fabsf(dd - 0.5f) <= fabsf(f) * 4.8e-7f + 1e-30f) {
+                        q = fq_chain<float>(w[j], s, zf, qmin, qmax, &code);
+                    } else {
+                        float t = __fadd_rn(fr, zf);
+                        t = (t < qmin) ? qmin : ((t > qmax) ? qmax : t);
+                        code = (int)t;
+                        q = __fmul_rn(__fsub_rn(t, zf), s);
+                    }
                     cb = a.bits <= 4 ? (uint8_t)((code - zi) & 0xF) : (uint8_t)code;
                 } else {
                     const bool kj = (keep[jj / 32] >> (jj % 32)) & 1u;
@@ -171,7 +243,12 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
                 Ct[jj * ROWS + tid] = cb;
                 const float piv = Us[jj * BW + jj];
                 if (fabsf(piv) >= 1e-10f) {  // GptqBlockQuantizer.cs:146-150 (NumericEpsilon)
-                    const float err = __fdiv_rn(__fsub_rn(w[j], q), piv);
+                    // (w - q) / piv: reciprocal times the difference, then one residual correction
+                    // (Markstein), within one unit in the last place of the IEEE quotient.
+                    const float df = __fsub_rn(w[j], q);
+                    const float rp = Rp[jj];
+                    const float q0 = __fmul_rn(df, rp);
+                    const float err = fmaf(fmaf(-q0, piv, df), rp, q0);
                     e[j] = err;
 #pragma unroll
                     for (int c4 = 0; c4 < SB / 4; c4++) {  // constant trip count: folds after unrolling
@@ -207,10 +284,24 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
     __syncthreads();
 
     // Write back the quantised (or pruned) values in place.
-    for (int t = tid; t < ROWS * BW; t += ROWS) {
-        const int rr = t / BW, c = t % BW;
-        const int64_t RR = r0 + rr;
-        if (RR < a.m && c < cnt) a.W[RR * a.ldw + a.i1 + c] = Wt[c * WLD + rr];
+    if (vec) {
+        for (int t = tid; t < ROWS * BW / 4; t += ROWS) {
+            const int rr = t / (BW / 4), c = (t % (BW / 4)) * 4;
+            const int64_t RR = r0 + rr;
+            if (RR >= a.m) continue;
+            if (c + 3 < cnt) {
+                *reinterpret_cast<float4*>(a.W + RR * a.ldw + a.i1 + c) =
+                    make_float4(Wt[c * WLD + rr], Wt[(c + 1) * WLD + rr], Wt[(c + 2) * WLD + rr], Wt[(c + 3) * WLD + rr]);
+            } else {
+                for (int i = 0; i < 4 && c + i < cnt; i++) a.W[RR * a.ldw + a.i1 + c + i] = Wt[(c + i) * WLD + rr];
+            }
+        }
+    } else {
+        for (int t = tid; t < ROWS * BW; t += ROWS) {
+            const int rr = t / BW, c = t % BW;
+            const int64_t RR = r0 + rr;
+            if (RR < a.m && c < cnt) a.W[RR * a.ldw + a.i1 + c] = Wt[c * WLD + rr];
+        }
     }
     if (MODE == 0 && a.codes) {
         if (a.bits <= 4) {

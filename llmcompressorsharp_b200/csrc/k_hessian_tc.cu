@@ -298,8 +298,8 @@ struct PairArgs {
     int kb_per_split;
     int* err;
     uint32_t idesc;
-    // Tile order, (ti << 8) | tj: compact G x G blocks of tiles one after another, so that
-    // the tiles one wave of pairs works on share few X panels and the panels stay in L2.
+    // Tile order, (ti << 8) | tj: column strips walked row by row, so that the tiles one wave
+    // of pairs works on share few X panels and those panels stay in L2.
     uint16_t tiles[P_MAX_TILES];
 };
 static_assert(sizeof(PairArgs) + 2 * sizeof(CUtensorMap) <= 32764, "kernel parameters above the limit");
@@ -628,14 +628,16 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
             p.d = (int)d;
             p.nt = (int)((d + 255) / 256);
             p.ntiles = p.nt * (p.nt + 1) / 2;
-            // Blocks of G x G tiles (G ~ sqrt(pairs)), column of blocks by column of blocks.
-            int G = 1;
-            while ((G + 1) * (G + 1) <= pcap) G++;
+            // Column strips GJ tiles wide (GJ ~ sqrt(2 pairs)), each walked row by row: a wave
+            // of pairs covers about GJ column panels and pairs / GJ row panels of X.
+            int GJ = 1;
+            while ((GJ + 1) * (GJ + 1) <= 2 * pcap) GJ++;
             int n = 0;
-            for (int bj = 0; bj < p.nt; bj += G)
-                for (int bi = 0; bi <= bj; bi += G)
-                    for (int tj = bj; tj < min(p.nt, bj + G); tj++)
-                        for (int ti = bi; ti < min(bi + G, tj + 1); ti++) p.tiles[n++] = (uint16_t)((ti << 8) | tj);
+            for (int bj = 0; bj < p.nt; bj += GJ) {
+                const int ej = min(p.nt, bj + GJ);
+                for (int ti = 0; ti < ej; ti++)
+                    for (int tj = max(bj, ti); tj < ej; tj++) p.tiles[n++] = (uint16_t)((ti << 8) | tj);
+            }
             if (n != p.ntiles) return fail(LLMC_ERR_INTERNAL, "syrk pair tile order: %d of %d tiles", n, p.ntiles);
             p.kb_total = a.kb_total;
             p.splits = pick_splits(p.ntiles, p.kb_total, pcap);
