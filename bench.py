@@ -15,9 +15,10 @@ are far larger than L2, so every timed step streams them from HBM.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 (torchrun): calibration tokens are split across ranks, each rank accumulates partial
-Hessians for every layer, the partials are summed onto each layer's owner over NCCL, and the
-owners (layers dealt round-robin) solve their layers: total work fixed ("strong").
+N > 1 (torchrun): calibration tokens are split across ranks; each rank accumulates partial
+Hessians for every layer, layer by layer, and sums them onto the layer's owner over NCCL while
+the next layer accumulates; owners (layers dealt round-robin) solve their layers on a second
+stream: total work fixed ("strong").
 """
 
 from __future__ import annotations
@@ -177,11 +178,12 @@ def run_ours(args):
                 g.manual_seed(10_000 + 97 * l + 7 * si + wi)
                 weights[l][wname] = _randn_bf16(m, s.d, dev, g, std=0.02)
     pipe = GptqPipeline(sites, cfg, dev, chunk_rows=args.chunk)
-    if world == 1 and args.reserve_sms > 0:
+    if args.reserve_sms > 0:
         pipe.enable_overlap(args.reserve_sms)
+    pipelined_dist = world > 1 and args.reserve_sms > 0
     outputs = {l: pipe.alloc_outputs(weights[l]) for l in mine}
     hbufs = None
-    if world > 1:
+    if world > 1 and not pipelined_dist:
         hbufs = {l: {s.name: torch.empty(s.d, s.d, dtype=torch.float32, device=dev) for s in sites} for l in range(L)}
     torch.cuda.synchronize()
 
@@ -191,6 +193,10 @@ def run_ours(args):
         """One full job; returns nothing (work is enqueued on the current stream)."""
         if world == 1:
             pipe.run(range(L), acts, weights, outputs, hess_events=hess_events if record else None)
+            return
+        if pipelined_dist:
+            pipe.run_distributed(range(L), acts, weights, outputs, world, rank,
+                                 hess_events=hess_events if record else None)
             return
         # phase 1: partial Hessians of every layer over this rank's tokens
         for l in range(L):
@@ -266,9 +272,9 @@ def run_ours(args):
                                    f"{args.tokens} calibration tokens (512 x 2048), bf16",
                        "layers": args.layers, "tokens": args.tokens, "update_rows": args.chunk,
                        "parallelism": f"tokens split over {world} GPU(s), layers dealt round-robin",
-                       "overlap": (f"solve of layer l on a second stream while layer l+1 accumulates; Hessian "
-                                   f"kernel capped at {args.reserve_sms} SMs fewer") if (world == 1 and args.reserve_sms > 0)
-                                  else "none",
+                       "overlap": (f"solve of layer l on a second stream while later layers accumulate (and, "
+                                   f"on N > 1, while their NCCL reductions run); Hessian kernel capped at "
+                                   f"{args.reserve_sms} SMs fewer") if args.reserve_sms > 0 else "none",
                        "activations": "one seeded bf16 [tokens, d] set per input site, shared by all layers",
                        "l2": "inputs larger than L2 (52 GiB of activations streamed per step)"},
             "hessian_tflops": round(hess_flops_full / (tot_hess_ms * 1e-3) / 1e12 if tot_hess_ms else 0, 1),
@@ -370,6 +376,19 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
 
             pipe.run(mine, acts, weights, outputs, before_solve=load_weights, after_solve=store_outputs,
                      acts_ready=ready)
+            return
+        if hbufs is None:  # pipelined multi-GPU job
+            def load_weights_d(l):
+                for k in weights[l]:
+                    weights[l][k].copy_(h_w[l][k], non_blocking=True)
+
+            def store_outputs_d(l):
+                for k, o in stacked[l].items():
+                    for f, t in o.items():
+                        h_out[l][k][f].copy_(t, non_blocking=True)
+
+            pipe.run_distributed(range(args.layers), acts, weights, outputs, world, rank,
+                                 before_solve=load_weights_d, after_solve=store_outputs_d, acts_ready=ready)
             return
         for l in range(args.layers):
             for s in sites:

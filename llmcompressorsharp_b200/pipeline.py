@@ -29,6 +29,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
+from .errors import InvalidOperationError
 from .gptq import GPTQConfig, param_shape
 
 
@@ -186,6 +187,17 @@ class GptqPipeline:
             self.accumulate(s, acts[s.name])
             self.solve_site(s, self.hessian_ptr(s.name), weights, outputs)
 
+    def run_distributed(self, layers, acts, weights, outputs, world: int, rank: int, group=None, before_solve=None,
+                        after_solve=None, hess_events=None, acts_ready=None):
+        """``run`` for one process per GPU (NCCL process group initialised by the caller):
+        ``acts`` are this rank's token shard; ``weights`` / ``outputs`` are needed for the
+        layers this rank owns (``distributed.owned_layers``).  Requires overlap enabled."""
+        if self.overlap is None:
+            raise InvalidOperationError("run_distributed needs enable_overlap() first")
+        acts_for = acts if callable(acts) else (lambda _l: acts)
+        return self.overlap.run_dist(list(layers), acts_for, weights, outputs, world, rank, group, before_solve,
+                                     after_solve, hess_events, dict(acts_ready or {}))
+
     def run(self, layers, acts, weights, outputs, before_solve=None, after_solve=None, hess_events=None,
             acts_ready=None):
         """The whole job over ``layers``: per layer, every site's Hessian, factor and stacked
@@ -261,6 +273,7 @@ class _Overlap:
 
     def close(self):
         torch.cuda.synchronize(self.pipe.device)
+        self.close_dist()
         for b in range(2):
             for p in self.h[b].values():
                 _lib.call("llmc_hessian_destroy", C.c_void_p(p))
@@ -321,6 +334,103 @@ class _Overlap:
             solve(pending)
         cur.wait_stream(self.sh)
         cur.wait_stream(self.ss)
+
+    # ---- one process per GPU ------------------------------------------------------------------
+    DIST_SETS = 6  # Hessian handle sets in flight per rank
+    DIST_LAG = 3   # an owned layer is solved once this many later layers are queued behind it
+
+    def _dist_sets(self):
+        if not getattr(self, "hd", None):
+            self.hd = []
+            for _ in range(self.DIST_SETS):
+                hs = {}
+                for s in self.pipe.sites:
+                    p = C.c_void_p()
+                    _lib.call("llmc_hessian_create", C.c_void_p(self.ch), C.c_int64(s.d), C.byref(p))
+                    hs[s.name] = p.value
+                self.hd.append(hs)
+            self.sc = torch.cuda.Stream(self.pipe.device)
+        return self.hd
+
+    def close_dist(self):
+        for hs in getattr(self, "hd", []):
+            for p in hs.values():
+                _lib.call("llmc_hessian_destroy", C.c_void_p(p))
+        self.hd = []
+
+    def run_dist(self, layers, acts_for, weights, outputs, world, rank, group, before_solve, after_solve,
+                 hess_events, acts_ready):
+        """Token-sharded job on `world` ranks: every rank accumulates its partial Hessians of
+        every layer on the Hessian stream and reduces them onto the layer's owner with NCCL
+        (issued from the Hessian stream, so the transfer of layer l overlaps the accumulation of
+        layer l+1); owners solve on the solve stream once the reduction is done."""
+        import torch.distributed as dist
+
+        from .distributed import layer_owner
+
+        pipe = self.pipe
+        sets = self._dist_sets()
+        cur = torch.cuda.current_stream(pipe.device)
+        for st in (self.sh, self.ss, self.sc):
+            st.wait_stream(cur)
+        released = [None] * len(sets)  # event after which set b may be overwritten
+        queue = []                      # owned layers waiting to be solved: (index, layer, set, reduce event)
+
+        def solve(item):
+            _, l, b, rd = item
+            with torch.cuda.stream(self.ss):
+                self.ss.wait_event(rd)
+                if before_solve is not None:
+                    before_solve(l)
+                for s in pipe.sites:
+                    p = C.c_void_p()
+                    _lib.call("llmc_hessian_data", C.c_void_p(sets[b][s.name]), C.byref(p))
+                    pipe.solve_site(s, p.value, weights[l], outputs[l], ctx=C.c_void_p(self.cs))
+                if after_solve is not None:
+                    after_solve(l)
+                done = torch.cuda.Event()
+                done.record(self.ss)
+                released[b] = done
+
+        layers = list(layers)
+        for i, l in enumerate(layers):
+            b = i % len(sets)
+            a = acts_for(l)
+            with torch.cuda.stream(self.sh):
+                if released[b] is not None:
+                    self.sh.wait_event(released[b])
+                for s in pipe.sites:
+                    if s.name in acts_ready:
+                        self.sh.wait_event(acts_ready.pop(s.name))
+                    ev = _events() if hess_events is not None else None
+                    if ev:
+                        ev[0].record(self.sh)
+                    pipe._accumulate_into(sets[b][s.name], a[s.name])
+                    if ev:
+                        ev[1].record(self.sh)
+                        hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
+                works = []
+                for s in pipe.sites:
+                    p = C.c_void_p()
+                    _lib.call("llmc_hessian_data", C.c_void_p(sets[b][s.name]), C.byref(p))
+                    h = torch.as_tensor(_HView(p.value, s.d), device=pipe.device)
+                    works.append(dist.reduce(h, dst=layer_owner(l, world), op=dist.ReduceOp.SUM, group=group,
+                                             async_op=True))
+            with torch.cuda.stream(self.sc):
+                for w in works:
+                    w.wait()
+                rd = torch.cuda.Event()
+                rd.record(self.sc)
+            if layer_owner(l, world) == rank:
+                queue.append((i, l, b, rd))
+            else:
+                released[b] = rd
+            while queue and queue[0][0] + self.DIST_LAG <= i:
+                solve(queue.pop(0))
+        while queue:
+            solve(queue.pop(0))
+        for st in (self.sh, self.ss, self.sc):
+            cur.wait_stream(st)
 
 
 def _stack_key(site: SiteSpec) -> str:
