@@ -37,6 +37,7 @@ sys.path.insert(0, ROOT)
 
 MODEL = {"name": "llama3-8b", "hidden": 4096, "intermediate": 14336, "heads": 32, "kv_heads": 8, "layers": 32}
 METRIC = "GPTQ W4A16 wall-clock s (Llama-3-8B shape)"
+SPARSE_METRIC = "SparseGPT 2:4 wall-clock s (Llama-3-8B shape)"
 UNIT = "s"
 
 
@@ -46,9 +47,11 @@ def parse():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["gptq", "rtn"], default="gptq",
-                   help="gptq: the GPTQ W4A16 job (default); rtn: RTN W4A16 g128 + min-max observer passes "
-                        "over the Llama-3-8B Linear weights (HBM-bound kernels)")
+    p.add_argument("--workload", choices=["gptq", "sparsegpt", "rtn", "smoothquant", "awq"], default="gptq",
+                   help="gptq: the GPTQ W4A16 job (default); sparsegpt: the same job pruning 2:4 with SparseGPT; "
+                        "rtn: RTN W4A16 g128 + min-max observer passes over the Llama-3-8B Linear weights; "
+                        "smoothquant: SmoothQuant (alpha 0.5) + W8A8 weights on a Llama-2-7B shape; awq: AWQ "
+                        "20-point grid search + scale apply on Llama-3-8B layers")
     p.add_argument("--layers", type=int, default=MODEL["layers"])
     p.add_argument("--tokens", type=int, default=512 * 2048)
     p.add_argument("--chunk", type=int, default=65536, help="calibration rows per Hessian update call")
@@ -160,8 +163,14 @@ def run_ours(args):
     L = args.layers
     r0, r1 = token_shard(args.tokens, world, rank)
     T_local = r1 - r0
-    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128,
-                     dampening_frac=0.01)
+    sparse = args.workload == "sparsegpt"
+    if sparse:
+        from llmcompressorsharp_b200.sparsegpt import SparseGPTConfig
+
+        cfg = SparseGPTConfig(sparsity=0.5, mask_structure="2:4", block_size=128, dampening_frac=0.01)
+    else:
+        cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128,
+                         dampening_frac=0.01)
     mine = owned_layers(range(L), world, rank)
 
     # ---- synthetic inputs, resident in HBM
@@ -177,7 +186,7 @@ def run_ours(args):
             for wi, (wname, m) in enumerate(s.weights):
                 g.manual_seed(10_000 + 97 * l + 7 * si + wi)
                 weights[l][wname] = _randn_bf16(m, s.d, dev, g, std=0.02)
-    pipe = GptqPipeline(sites, cfg, dev, chunk_rows=args.chunk)
+    pipe = GptqPipeline(sites, cfg, dev, chunk_rows=args.chunk, solver="sparsegpt" if sparse else "gptq")
     if args.reserve_sms > 0:
         pipe.enable_overlap(args.reserve_sms)
     pipelined_dist = world > 1 and args.reserve_sms > 0
@@ -264,10 +273,12 @@ def run_ours(args):
         achieved = per_launch_flops / (per_launch_ms * 1e-3) / 1e12
         cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(args)
         line = {
-            "metric": METRIC, "value": round(ms / 1e3, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": SPARSE_METRIC if sparse else METRIC, "value": round(ms / 1e3, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "GPTQ W4A16 asym g128 damp 0.01 block 128, Llama-3-8B shape "
+            "config": {"workload": ("SparseGPT 2:4 (50 %) damp 0.01 block 128, Llama-3-8B shape " if sparse else
+                                    "GPTQ W4A16 asym g128 damp 0.01 block 128, Llama-3-8B shape ") +
                                    f"({args.layers} layers x 7 Linear, hidden 4096, intermediate 14336, 32/8 heads), "
                                    f"{args.tokens} calibration tokens (512 x 2048), bf16",
                        "layers": args.layers, "tokens": args.tokens, "update_rows": args.chunk,
@@ -670,6 +681,125 @@ def run_rtn(args):
         dist.destroy_process_group()
 
 
+def run_smooth_awq(args):
+    """--workload smoothquant: per layer of a Llama-2-7B shape (hidden 4096, intermediate 11008,
+    32 layers, 256 x 2048 = 524,288 calibration tokens), the activation absmax of the attention
+    and MLP inputs, SmoothQuant (alpha 0.5) of input_layernorm -> q/k/v and post_attention_layernorm
+    -> gate/up, and W8A8's int8 per-channel weight quantisation of all seven weights.
+    --workload awq: per layer of a Llama-3-8B shape (128 x 2048 = 262,144 tokens), the activation
+    absmax of the same two inputs, the AWQ 20-point grid search (RTN asym int4 g128) and the
+    scale apply for q/k/v and gate/up.  Both are HBM-bound: throughput = algorithmic bytes /
+    device time; one GPU."""
+    import ctypes as C
+
+    import torch
+
+    from llmcompressorsharp_b200 import _lib
+    from llmcompressorsharp_b200.rtn import RtnConfig
+
+    world, rank, local = dist_env()
+    if world > 1:
+        raise SystemExit("--workload smoothquant / awq run on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    awq = args.workload == "awq"
+    hid = 4096
+    inter = 14336 if awq else 11008
+    kv = 1024 if awq else 4096
+    T = 128 * 2048 if awq else 256 * 2048
+    L = args.layers
+    g = torch.Generator(dev).manual_seed(5)
+    acts = []
+    for _ in range(2):
+        x = _randn_bf16(T, hid, dev, g)
+        hot = torch.randperm(hid, device=dev, generator=g)[: hid // 100]  # 1 % heavy-tailed channels x50
+        x[:, hot] = (x[:, hot].float() * 50 * torch.rand(T, hot.numel(), device=dev, generator=g).pow(-0.5)).to(x.dtype)
+        acts.append(x)
+    shapes = {"qkv": (hid + 2 * kv, hid), "o": (hid, hid), "gu": (2 * inter, hid), "down": (hid, inter)}
+    layers = []
+    for l in range(L):
+        g.manual_seed(20_000 + l)
+        w = {k: _randn_bf16(m, n, dev, g, std=0.02) for k, (m, n) in shapes.items()}
+        w["ln1"] = (1 + 0.1 * torch.randn(hid, device=dev, generator=g)).to(torch.bfloat16)
+        w["ln2"] = (1 + 0.1 * torch.randn(hid, device=dev, generator=g)).to(torch.bfloat16)
+        layers.append(w)
+    amax = [torch.empty(hid, device=dev) for _ in range(2)]
+    s_out = torch.empty(hid, device=dev)
+    n_grid = 20
+    mse = torch.empty(n_grid, dtype=torch.float64, device=dev)
+    best_k = C.c_int32()
+    q8 = RtnConfig(num_bits=8, symmetric=True, strategy="channel").to_c()
+    q4 = RtnConfig(num_bits=4, symmetric=False, strategy="group", group_size=128).to_c()
+    codes = {k: torch.empty(m, n, dtype=torch.uint8, device=dev) for k, (m, n) in shapes.items()}
+    scales = {k: torch.empty(m, 1, dtype=torch.float32, device=dev) for k, (m, n) in shapes.items()}
+    zps = {k: torch.empty(m, 1, dtype=torch.int32, device=dev) for k, (m, n) in shapes.items()}
+
+    def step():
+        c = C.c_void_p(_lib.ctx_for(0))
+        for w in layers:
+            for x, am in zip(acts, amax):
+                _lib.call("llmc_act_absmax", c, _lib.ptr(x), _lib.DTYPE_BF16, C.c_int64(T), C.c_int64(hid),
+                          C.c_int64(hid), _lib.ptr(am), 0)
+            for am, ln, key in ((amax[0], "ln1", "qkv"), (amax[1], "ln2", "gu")):
+                m = shapes[key][0]
+                if awq:
+                    _lib.call("llmc_awq_search", c, _lib.ptr(w[key]), _lib.DTYPE_BF16, C.c_int64(m), C.c_int64(hid),
+                              C.c_int64(hid), _lib.ptr(am), C.c_int32(n_grid), C.byref(q4), _lib.ptr(s_out),
+                              _lib.ptr(mse), C.byref(best_k))
+                    _lib.call("llmc_scale_apply", c, _lib.ptr(s_out), _lib.ptr(w[ln]), _lib.DTYPE_BF16,
+                              _lib.ptr(w[key]), _lib.DTYPE_BF16, C.c_int64(m), C.c_int64(hid))
+                else:
+                    _lib.call("llmc_smooth_apply", c, _lib.ptr(am), _lib.ptr(w[ln]), _lib.DTYPE_BF16,
+                              _lib.ptr(w[key]), _lib.DTYPE_BF16, C.c_int64(m), C.c_int64(hid), C.c_float(0.5),
+                              _lib.ptr(s_out))
+            if not awq:
+                for key, (m, n) in shapes.items():
+                    _lib.call("llmc_rtn_quantize", c, _lib.ptr(w[key]), _lib.DTYPE_BF16, C.c_int64(m), C.c_int64(n),
+                              C.c_int64(n), C.byref(q8), _lib.ptr(codes[key]), _lib.ptr(scales[key]),
+                              _lib.ptr(zps[key]), C.c_void_p(0))
+
+    # algorithmic bytes of one step
+    absmax_b = 2 * T * hid * 2
+    bal = (shapes["qkv"][0] + shapes["gu"][0]) * hid * 2
+    if awq:
+        per_layer = absmax_b + (n_grid + 1) * bal + 2 * bal + 4 * hid * 2
+    else:
+        params = sum(m * n for m, n in shapes.values())
+        per_layer = absmax_b + 3 * bal + 4 * hid * 2 + params * 3 + sum(m for m, _ in shapes.values()) * 8
+    step_bytes = per_layer * L
+    launches0 = _lib.launch_count(0)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    warm_launches = (_lib.launch_count(0) - launches0) // max(1, args.warmup)
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    _, _, hbm, src = peaks()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    name = ("AWQ grid search (20 points, int4 g128) + scale apply throughput (Llama-3-8B shape)" if awq else
+            "SmoothQuant (alpha 0.5) + W8A8 int8 per-channel weights throughput (Llama-2-7B shape)")
+    line = {"metric": name, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{L} layers, {T} calibration tokens, hidden {hid}, intermediate {inter}",
+                       "bytes_per_step": int(step_bytes),
+                       "activations": "two [tokens, 4096] bf16 inputs, 1 % of channels heavy-tailed x50",
+                       "l2": "inputs larger than L2"},
+            "roofline": {"kernel": "awq_err_kernel" if awq else "col_absmax_kernel", "bound": "hbm",
+                         "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 3),
+                         "peak_note": f"{src} HBM copy bandwidth; whole-step bytes over step time", "traffic": None},
+            "gpu_launches": warm_launches * args.steps, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -677,6 +807,9 @@ def main():
         return
     if args.workload == "rtn":
         run_rtn(args)
+        return
+    if args.workload in ("smoothquant", "awq"):
+        run_smooth_awq(args)
         return
     run_ours(args)
 

@@ -55,7 +55,14 @@ class GptqPipeline:
     """Device-resident GPTQ over layers.  ``weights[l][name]`` are [out, in] device tensors,
     ``acts[site]`` are [T, d] device tensors (this rank's calibration tokens)."""
 
-    def __init__(self, sites, cfg: GPTQConfig, device: torch.device, chunk_rows: int = 65536, keep_wq: bool = False):
+    def __init__(self, sites, cfg, device: torch.device, chunk_rows: int = 65536, keep_wq: bool = False,
+                 solver: str = "gptq"):
+        """``cfg`` is a GPTQConfig (``solver="gptq"``) or a SparseGPTConfig (``solver="sparsegpt"``:
+        every weight is pruned against the site's factor, outputs are the keep masks and the
+        pruned fp32 weights)."""
+        if solver not in ("gptq", "sparsegpt"):
+            raise ValueError(f"unknown solver {solver}")
+        self.solver = solver
         self.sites = sites
         self.cfg = cfg
         self.device = device
@@ -141,6 +148,20 @@ class GptqPipeline:
         names = [w for w, _ in site.weights]
         ms = [m for _, m in site.weights]
         k = len(names)
+        if self.solver == "sparsegpt":
+            st = outputs[_stack_key(site)]
+            wq = st.get("wq")
+            if wq is None:
+                wq = self.work[: sum(ms) * d].view(sum(ms), d)
+            r0 = 0
+            for name, m in zip(names, ms):
+                w = weights[name]
+                _lib.call("llmc_sparsegpt_prune", ctx, _lib.ptr(w), _lib.dtype_code(w.dtype), C.c_int64(m),
+                          C.c_int64(d), C.c_int64(w.stride(0)), _lib.ptr(self.u), C.c_int64(d), C.byref(self.qc),
+                          C.c_void_p(wq.data_ptr() + r0 * d * 4), C.c_int64(d),
+                          C.c_void_p(st["mask"].data_ptr() + r0 * d))
+                r0 += m
+            return
         wp = (C.c_void_p * k)(*[weights[w].data_ptr() for w in names])
         mp = (C.c_int64 * k)(*ms)
         lp = (C.c_int64 * k)(*[weights[w].stride(0) for w in names])
@@ -158,6 +179,16 @@ class GptqPipeline:
         for s in self.sites:
             n = s.d
             M = sum(m for _, m in s.weights)
+            if self.solver == "sparsegpt":
+                stacked = {"mask": torch.empty(M, n, dtype=torch.uint8, device=self.device)}
+                if self.keep_wq:
+                    stacked["wq"] = torch.empty(M, n, dtype=torch.float32, device=self.device)
+                outs[_stack_key(s)] = stacked
+                r0 = 0
+                for wname, m in s.weights:
+                    outs[wname] = {f: t[r0:r0 + m] for f, t in stacked.items()}
+                    r0 += m
+                continue
             stacked = {
                 "codes": torch.empty(M, (n + 1) // 2 if self.cfg.num_bits <= 4 else n, dtype=torch.uint8,
                                      device=self.device),

@@ -766,6 +766,58 @@ def test_sparsegpt_matches_oracle(structure):
     assert torch.count_nonzero(out.cpu()[mask.cpu() == 0]) == 0
 
 
+@pytest.mark.parametrize("m,n,structure,sparsity,dtype", [
+    (64, 300, "unstructured", 0.3, torch.float32),
+    (64, 304, "4:8", 0.5, torch.float32),
+    (256, 2048, "2:4", 0.5, torch.float32),
+    (256, 2048, "unstructured", 0.7, torch.float32),
+    (128, 1536, "2:4", 0.5, torch.bfloat16),
+])
+def test_sparsegpt_shapes_match_oracle(m, n, structure, sparsity, dtype):
+    """Ragged widths, N:M and unstructured sparsities, tails long enough for the tensor-core
+    GEMM (n >= 1536), bf16 weights."""
+    from llmcompressorsharp_b200 import SparseGPTConfig, sparsegpt_prune_u
+
+    w, h = gptq_case(m, n, m + n, dtype)
+    u = o_hess.upper_factor(o_hess.hessian_inverse(h, 0.01))
+    cfg = SparseGPTConfig(sparsity=sparsity, mask_structure=structure)
+    out, mask = sparsegpt_prune_u(w.to(DEV), u.to(DEV), cfg)
+    n_, m_ = cfg.nm()
+    rout, rmask = o_sp.sparsegpt_prune_u(w, u, 128, sparsity, n_, m_)
+    assert (mask.cpu().bool() == rmask).float().mean() >= 0.999
+    assert rel_fro(out, rout) < 1e-3
+    assert torch.count_nonzero(out.cpu()[mask.cpu() == 0]) == 0
+    if m_:
+        full = (n // m_) * m_
+        assert (mask.cpu()[:, :full].reshape(m, -1, m_).sum(-1) == n_).all()
+
+
+def test_pipeline_sparsegpt_matches_oracle():
+    """GptqPipeline with solver="sparsegpt" (stacked sites, overlapped schedule) against the
+    oracle's SparseGPT on the oracle Hessian."""
+    from llmcompressorsharp_b200 import SparseGPTConfig
+    from llmcompressorsharp_b200.pipeline import GptqPipeline
+
+    sites, acts, weights = _pipeline_case(seed=51, layers=2)
+    cfg = SparseGPTConfig(sparsity=0.5, mask_structure="2:4")
+    pipe = GptqPipeline(sites, cfg, torch.device(DEV), chunk_rows=4096, keep_wq=True, solver="sparsegpt")
+    pipe.enable_overlap(100)
+    outs = {l: pipe.alloc_outputs(weights[l]) for l in weights}
+    pipe.run(range(len(weights)), acts, weights, outs)
+    torch.cuda.synchronize()
+    pipe.close()
+    for s in sites:
+        h = o_hess.HessianAccumulator(s.d)
+        h.update(acts[s.name].cpu())
+        u = o_hess.upper_factor(o_hess.hessian_inverse(h.get_hessian(), 0.01))
+        for l in weights:
+            for w, _ in s.weights:
+                rout, rmask = o_sp.sparsegpt_prune_u(weights[l][w].cpu(), u, 128, 0.5, 2, 4)
+                got = outs[l][w]
+                assert (got["mask"].cpu().bool() == rmask).float().mean() >= 0.999
+                assert rel_fro(got["wq"], rout) < 1e-3
+
+
 def test_awq_search_matches_oracle():
     from llmcompressorsharp_b200 import RtnConfig, awq_search
 
