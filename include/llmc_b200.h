@@ -86,9 +86,12 @@ llmc_status llmc_destroy(llmc_ctx* ctx);
  * (non-blocking) stream.  To run on the legacy default stream pass cudaStreamLegacy
  * ((void*)0x1), not NULL. */
 llmc_status llmc_set_stream(llmc_ctx* ctx, void* stream);
-/* Cap the number of SMs that this context's persistent Hessian kernel occupies (0 = all).
- * No reference counterpart: it lets a second context on the same device (one solving the
- * previous layer on another stream) run on the SMs left free while this one accumulates. */
+/* Share the device with another context (0 = this context has it to itself).  sms > 0 caps
+ * the persistent Hessian kernel at `sms` SMs, and makes the tensor-core GEMMs of the factor and
+ * the GPTQ tail launch one CTA per tile (instead of one persistent CTA per SM) so that they
+ * start wherever SMs free up.  No reference counterpart: two contexts on one device, one
+ * accumulating the next layer's Hessians while the other solves the previous layer on another
+ * stream. */
 llmc_status llmc_set_sm_limit(llmc_ctx* ctx, int32_t sms);
 llmc_status llmc_sync(llmc_ctx* ctx);
 /* Number of kernels this context has launched since creation (diagnostics / bench). */

@@ -37,7 +37,7 @@ llmc_status fail(llmc_status st, const char* fmt, ...);
 struct llmc_ctx {
     int device = 0;
     int sm_count = 148;
-    // SMs the persistent Hessian kernel may occupy (0 = all); see llmc_set_sm_limit.
+    // SMs this context's persistent kernels may occupy (0 = all); see llmc_set_sm_limit.
     int sm_limit = 0;
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;

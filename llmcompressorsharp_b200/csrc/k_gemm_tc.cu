@@ -72,25 +72,6 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    // Tile of this CTA: consecutive CTAs walk a strip of `group` M-tiles column by column, so
-    // the CTAs resident at one time share few A and B panels and those stay in L2.
-    const int per_group = a.group * a.tiles_n;
-    const int gidx = (int)blockIdx.x / per_group;
-    const int first_m = gidx * a.group;
-    const int gm = min(a.group, a.tiles_m - first_m);
-    const int local = (int)blockIdx.x - gidx * per_group;
-    const int64_t m0 = (int64_t)(first_m + local % gm) * BM, n0 = (int64_t)(local / gm) * BN;
-    if (a.c_mode == 1 && m0 + BM - 1 < n0) return;  // tile entirely above the diagonal
-    if (a.c_mode == 2 && m0 > n0 + BN - 1) return;  // tile entirely below the diagonal
-
-    int64_t kb_lo = 0, kb_hi = a.K;
-    if (a.a_tri == TRI_KLE) kb_hi = min(kb_hi, m0 + BM);
-    if (a.a_tri == TRI_KGE) kb_lo = max(kb_lo, m0);
-    if (a.b_tri == TRI_KLE) kb_hi = min(kb_hi, n0 + BN);
-    if (a.b_tri == TRI_KGE) kb_lo = max(kb_lo, n0);
-    const int kb0 = (int)(kb_lo / BK);
-    const int kb1 = kb_hi > kb_lo ? (int)((kb_hi + BK - 1) / BK) : kb0;
-    const int nchunks = (kb1 - kb0 + KF - 1) / KF;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -118,115 +99,147 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
 #pragma unroll
     for (int s = 0; s < STAGES; s++) pend_par[s] = -1;
     int commit_par[2] = {-1, -1};
+    // Counters that run on across this CTA's tiles: stages filled (producer) and consumed
+    // (MMA issuer); accumulation chunks (MMA issuer and epilogue: TMEM buffer cc & 1).
+    uint32_t prod_it = 0, mma_it = 0, cc = 0;
 
-    if (warp == 0) {
-        if (lane == 0) {
-            uint32_t it = 0;
-            for (int kb = kb0; kb < kb1; kb++, it++) {
-                const int s = it % STAGES;
-                const uint32_t ph = (it / STAGES) & 1u;
-                if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
-                unsigned char* st = smem + s * STAGE_BYTES;
-                mbar_expect_tx(&full[s], STAGE_BYTES);
-                const int k0 = kb * BK;
-                load_part(st + 0 * TILE_BYTES, &ahi, (int)m0, k0, &full[s]);
-                load_part(st + 1 * TILE_BYTES, &alo, (int)m0, k0, &full[s]);
-                load_part(st + 2 * TILE_BYTES, &bhi, (int)n0, k0, &full[s]);
-                load_part(st + 3 * TILE_BYTES, &blo, (int)n0, k0, &full[s]);
-                pend_par[s] = (int)ph;
-            }
-        }
-        __syncwarp();
-    } else if (warp == 1) {
-        if (lane == 0) {
-            uint32_t it = 0;
-            for (int c = 0; c < nchunks && !*abort_flag; c++) {
-                const int b = c & 1;
-                if (!mbar_wait(&tempty[b], ((uint32_t)(c >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
-                tc_fence_after();
-                const uint32_t dst = tmem + (uint32_t)(b * BN);
-                const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
-                bool ok = true;
-                for (int kb = k0; kb < k1; kb++, it++) {
-                    const int s = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1u;
-                    if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 8; kk++) {
-                        const uint64_t dah = part_desc(base + 0 * TILE_BYTES, kk);
-                        const uint64_t dal = part_desc(base + 1 * TILE_BYTES, kk);
-                        const uint64_t dbh = part_desc(base + 2 * TILE_BYTES, kk);
-                        const uint64_t dbl = part_desc(base + 3 * TILE_BYTES, kk);
-                        const uint32_t first = (kb == k0 && kk == 0) ? 0u : 1u;
-                        umma_tf32(dst, dah, dbh, a.idesc, first);
-                        umma_tf32(dst, dah, dbl, a.idesc, 1u);
-                        umma_tf32(dst, dal, dbh, a.idesc, 1u);
-                    }
-                    umma_commit(&empty[s]);
+    // Persistent CTAs: tile t = blockIdx.x, +gridDim.x, ...  Consecutive tiles walk a strip of
+    // `group` M-tiles column by column, so the tiles in flight share few A and B panels.
+    const int total_tiles = a.tiles_m * a.tiles_n;
+    const int per_group = a.group * a.tiles_n;
+    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+        const int gidx = t / per_group;
+        const int first_m = gidx * a.group;
+        const int gm = min(a.group, a.tiles_m - first_m);
+        const int local = t - gidx * per_group;
+        const int64_t m0 = (int64_t)(first_m + local % gm) * BM, n0 = (int64_t)(local / gm) * BN;
+        if (a.c_mode == 1 && m0 + BM - 1 < n0) continue;  // tile entirely above the diagonal
+        if (a.c_mode == 2 && m0 > n0 + BN - 1) continue;  // tile entirely below the diagonal
+
+        int64_t kb_lo = 0, kb_hi = a.K;
+        if (a.a_tri == TRI_KLE) kb_hi = min(kb_hi, m0 + BM);
+        if (a.a_tri == TRI_KGE) kb_lo = max(kb_lo, m0);
+        if (a.b_tri == TRI_KLE) kb_hi = min(kb_hi, n0 + BN);
+        if (a.b_tri == TRI_KGE) kb_lo = max(kb_lo, n0);
+        const int kb0 = (int)(kb_lo / BK);
+        const int kb1 = kb_hi > kb_lo ? (int)((kb_hi + BK - 1) / BK) : kb0;
+        const int nchunks = (kb1 - kb0 + KF - 1) / KF;
+
+        if (warp == 0) {
+            if (lane == 0) {
+                for (int kb = kb0; kb < kb1; kb++, prod_it++) {
+                    const int s = prod_it % STAGES;
+                    const uint32_t ph = (prod_it / STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    unsigned char* st = smem + s * STAGE_BYTES;
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    const int k0 = kb * BK;
+                    load_part(st + 0 * TILE_BYTES, &ahi, (int)m0, k0, &full[s]);
+                    load_part(st + 1 * TILE_BYTES, &alo, (int)m0, k0, &full[s]);
+                    load_part(st + 2 * TILE_BYTES, &bhi, (int)n0, k0, &full[s]);
+                    load_part(st + 3 * TILE_BYTES, &blo, (int)n0, k0, &full[s]);
+                    pend_par[s] = (int)ph;
                 }
-                umma_commit(&tfull[b]);
-                commit_par[b] = (c >> 1) & 1;
-                if (!ok) break;
             }
-        }
-        __syncwarp();
-    } else {
-        // epilogue warps: TMEM lane quadrant q = warp % 4 = rows [32q, 32q + 32) of the tile
-        const int q = warp % 4;
-        float acc[BN];
-#pragma unroll
-        for (int i = 0; i < BN; i++) acc[i] = 0.f;
-        for (int c = 0; c < nchunks; c++) {
-            const int b = c & 1;
-            const bool have = mbar_wait(&tfull[b], (uint32_t)(c >> 1) & 1u, abort_flag, a.err);
-            if (!__all_sync(0xffffffffu, have ? 1 : 0)) break;
-            tc_fence_after();
-#pragma unroll
-            for (int part = 0; part < BN / 32; part++) {
-                uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + part * 32), v);
-#pragma unroll
-                for (int i = 0; i < 32; i++) acc[part * 32 + i] = __fadd_rn(acc[part * 32 + i], __uint_as_float(v[i]));
-            }
-            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
-        }
-        const int64_t r = m0 + q * 32 + lane;
-        if (r < a.M && !*abort_flag) {
-            float* crow = a.C + r * a.ldc + n0;
-            const bool vec = ((reinterpret_cast<uintptr_t>(crow) & 15u) == 0) && n0 + BN <= a.N &&
-                             !(a.c_mode == 1 && r < n0 + BN - 1);
-            if (vec) {
+        } else if (warp == 1) {
+            if (lane == 0) {
+                uint32_t c_it = cc;
+                for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
+                    const int b = (int)(c_it & 1u);
+                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    tc_fence_after();
+                    const uint32_t dst = tmem + (uint32_t)(b * BN);
+                    const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
+                    bool ok = true;
+                    for (int kb = k0; kb < k1; kb++, mma_it++) {
+                        const int s = mma_it % STAGES;
+                        const uint32_t ph = (mma_it / STAGES) & 1u;
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-                for (int i = 0; i < BN; i += 4) {
-                    float4 o = make_float4(a.alpha * acc[i], a.alpha * acc[i + 1], a.alpha * acc[i + 2],
-                                           a.alpha * acc[i + 3]);
-                    if (a.beta != 0.f) {
-                        const float4 c = *reinterpret_cast<const float4*>(crow + i);
-                        o.x = fmaf(a.beta, c.x, o.x);
-                        o.y = fmaf(a.beta, c.y, o.y);
-                        o.z = fmaf(a.beta, c.z, o.z);
-                        o.w = fmaf(a.beta, c.w, o.w);
+                        for (int kk = 0; kk < BK / 8; kk++) {
+                            const uint64_t dah = part_desc(base + 0 * TILE_BYTES, kk);
+                            const uint64_t dal = part_desc(base + 1 * TILE_BYTES, kk);
+                            const uint64_t dbh = part_desc(base + 2 * TILE_BYTES, kk);
+                            const uint64_t dbl = part_desc(base + 3 * TILE_BYTES, kk);
+                            const uint32_t first = (kb == k0 && kk == 0) ? 0u : 1u;
+                            umma_tf32(dst, dah, dbh, a.idesc, first);
+                            umma_tf32(dst, dah, dbl, a.idesc, 1u);
+                            umma_tf32(dst, dal, dbh, a.idesc, 1u);
+                        }
+                        umma_commit(&empty[s]);
                     }
-                    *reinterpret_cast<float4*>(crow + i) = o;
+                    umma_commit(&tfull[b]);
+                    commit_par[b] = (int)((c_it >> 1) & 1u);
+                    if (!ok) break;
                 }
-            } else {
+            }
+            __syncwarp();
+        } else {
+            // epilogue warps: TMEM lane quadrant q = warp % 4 = rows [32q, 32q + 32) of the tile
+            const int q = warp % 4;
+            float acc[BN];
 #pragma unroll
-                for (int i = 0; i < BN; i++) {
-                    const int64_t col = n0 + i;
-                    if (col < a.N && !(a.c_mode == 1 && r < col)) {
-                        const float v = a.alpha * acc[i];
-                        crow[i] = (a.beta == 0.f) ? v : fmaf(a.beta, crow[i], v);
+            for (int i = 0; i < BN; i++) acc[i] = 0.f;
+            uint32_t c_it = cc;
+            bool ok = true;
+            for (int c = 0; c < nchunks; c++, c_it++) {
+                const int b = (int)(c_it & 1u);
+                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
+                if (!__all_sync(0xffffffffu, have ? 1 : 0)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int part = 0; part < BN / 32; part++) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + part * 32), v);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) acc[part * 32 + i] = __fadd_rn(acc[part * 32 + i], __uint_as_float(v[i]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[b]);
+            }
+            // Write-out of this tile; the MMA issuer meanwhile fills TMEM for the next tile.
+            const int64_t r = m0 + q * 32 + lane;
+            if (ok && r < a.M && !*abort_flag) {
+                float* crow = a.C + r * a.ldc + n0;
+                const bool vec = ((reinterpret_cast<uintptr_t>(crow) & 15u) == 0) && n0 + BN <= a.N &&
+                                 !(a.c_mode == 1 && r < n0 + BN - 1);
+                if (vec) {
+#pragma unroll
+                    for (int i = 0; i < BN; i += 4) {
+                        float4 o = make_float4(a.alpha * acc[i], a.alpha * acc[i + 1], a.alpha * acc[i + 2],
+                                               a.alpha * acc[i + 3]);
+                        if (a.beta != 0.f) {
+                            const float4 c = *reinterpret_cast<const float4*>(crow + i);
+                            o.x = fmaf(a.beta, c.x, o.x);
+                            o.y = fmaf(a.beta, c.y, o.y);
+                            o.z = fmaf(a.beta, c.z, o.z);
+                            o.w = fmaf(a.beta, c.w, o.w);
+                        }
+                        *reinterpret_cast<float4*>(crow + i) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < BN; i++) {
+                        const int64_t col = n0 + i;
+                        if (col < a.N && !(a.c_mode == 1 && r < col)) {
+                            const float v = a.alpha * acc[i];
+                            crow[i] = (a.beta == 0.f) ? v : fmaf(a.beta, crow[i], v);
+                        }
                     }
                 }
             }
         }
+        cc += (uint32_t)nchunks;
     }
 
     if (*abort_flag) {
@@ -403,7 +416,12 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
     t.tiles_m = (int)((g.M + BM - 1) / BM);
     t.tiles_n = (int)((g.N + BN - 1) / BN);
     t.group = 12;  // ~sqrt(SM count)
-    gemm_tc_kernel<<<(unsigned)(t.tiles_m * t.tiles_n), NT, SMEM_BYTES, ctx->stream>>>(mah, mal, mbh, mbl, t);
+    const int tiles = t.tiles_m * t.tiles_n;
+    // Persistent CTAs (one per SM) when the context has the GPU to itself; one CTA per tile when
+    // it shares the SMs with another context (llmc_set_sm_limit), so that its CTAs start on any
+    // SM the other context's kernels leave free instead of queueing behind them.
+    const int grid = (ctx->sm_limit > 0 || tiles < ctx->sm_count) ? tiles : ctx->sm_count;
+    gemm_tc_kernel<<<(unsigned)grid, NT, SMEM_BYTES, ctx->stream>>>(mah, mal, mbh, mbl, t);
     return check_launch(ctx, "gemm_tc");
 }
 

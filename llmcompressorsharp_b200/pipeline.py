@@ -288,6 +288,9 @@ class _Overlap:
         limit = max(1, sm - int(reserve_sms))
         self.hessian_sms = limit
         _lib.call("llmc_set_sm_limit", C.c_void_p(self.ch), C.c_int32(limit))
+        # The solve context shares the GPU: its tensor-core GEMMs launch one CTA per tile, which
+        # start on the reserved SMs and on any SM a finishing Hessian launch frees.
+        _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(max(1, int(reserve_sms))))
         self.h = [{}, {}]
         for b in range(2):
             for s in pipe.sites:
