@@ -1,0 +1,436 @@
+/*
+ * llmc_b200.hpp — C++ host mirror of LLMCompressorSharp's one-shot compression primitives,
+ * over the C ABI of include/llmc_b200.h (header-only, C++17, links libllmc_b200 and cudart).
+ *
+ * The reference exposes these as C# classes on TorchSharp tensors
+ * (src/LLMCompressorSharp.TorchExtensions, src/LLMCompressorSharp.Core/Algorithms/Gptq).  This
+ * header keeps their names, argument meaning and exception behaviour:
+ *   HessianAccumulator        HessianAccumulator.cs:16-99
+ *   HessianInverseSolver      HessianInverseSolver.cs:44-108
+ *   GptqBlockQuantizer        GptqBlockQuantizer.cs:71-274 (+ GPTQConfig, Configs/GPTQConfig.cs:22-59)
+ *   MinMaxObserver            MinMaxObserver.cs:14-71
+ *   PerChannelMinMaxObserver  PerChannelMinMaxObserver.cs:15-112
+ *   FakeQuantize              FakeQuantize.cs:22-38
+ *   Int4PackedTensor          Int4PackedTensor.cs:47-161
+ * Tensors are DeviceTensor: a device buffer owned by the host code (the role TorchSharp's
+ * CUDA tensors play for the C# primitives), row-major, float32 / bfloat16 / float16.
+ * Exceptions mirror .NET's: ArgumentNullException, ArgumentException,
+ * ArgumentOutOfRangeException, NotSupportedException, InvalidOperationException; CUDA and
+ * timeout failures raise LlmcException.
+ */
+#ifndef LLMC_B200_HPP
+#define LLMC_B200_HPP
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "llmc_b200.h"
+
+namespace llmcs {
+
+// ---- exceptions ------------------------------------------------------------------------------
+struct LlmcException : std::runtime_error {
+    llmc_status status;
+    LlmcException(llmc_status st, const std::string& m) : std::runtime_error(m), status(st) {}
+};
+struct ArgumentException : std::invalid_argument {
+    explicit ArgumentException(const std::string& m) : std::invalid_argument(m) {}
+};
+struct ArgumentNullException : ArgumentException {
+    explicit ArgumentNullException(const std::string& m) : ArgumentException(m) {}
+};
+struct ArgumentOutOfRangeException : ArgumentException {
+    explicit ArgumentOutOfRangeException(const std::string& m) : ArgumentException(m) {}
+};
+struct NotSupportedException : std::logic_error {
+    explicit NotSupportedException(const std::string& m) : std::logic_error(m) {}
+};
+struct InvalidOperationException : std::logic_error {
+    explicit InvalidOperationException(const std::string& m) : std::logic_error(m) {}
+};
+
+// Maps a status of the C ABI (and the calling thread's message) to the reference's exception.
+inline void Check(llmc_status st) {
+    if (st == LLMC_OK) return;
+    const char* e = llmc_last_error();
+    const std::string m = e ? e : "llmc error";
+    switch (st) {
+        case LLMC_ERR_INVALID_ARG:
+            if (m.find("must not be null") != std::string::npos) throw ArgumentNullException(m);
+            throw ArgumentException(m);
+        case LLMC_ERR_SHAPE: throw ArgumentException(m);
+        case LLMC_ERR_OUT_OF_RANGE: throw ArgumentOutOfRangeException(m);
+        case LLMC_ERR_UNSUPPORTED: throw NotSupportedException(m);
+        case LLMC_ERR_NO_SAMPLES: throw InvalidOperationException(m);
+        default: throw LlmcException(st, m);
+    }
+}
+
+inline void CheckCuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw LlmcException(LLMC_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ---- device context ---------------------------------------------------------------------------
+class Context {
+   public:
+    explicit Context(int device = 0) {
+        Check(llmc_init(device, &ctx_));
+        device_ = device;
+    }
+    ~Context() {
+        if (ctx_) llmc_destroy(ctx_);
+    }
+    Context(const Context&) = delete;
+    Context& operator=(const Context&) = delete;
+    llmc_ctx* get() const { return ctx_; }
+    int device() const { return device_; }
+    void Synchronize() const { Check(llmc_sync(ctx_)); }
+
+   private:
+    llmc_ctx* ctx_ = nullptr;
+    int device_ = 0;
+};
+
+// ---- tensors ---------------------------------------------------------------------------------
+enum class DType : int32_t { Float32 = LLMC_DTYPE_F32, BFloat16 = LLMC_DTYPE_BF16, Float16 = LLMC_DTYPE_F16 };
+
+inline size_t ElementSize(DType t) { return t == DType::Float32 ? 4 : 2; }
+
+class DeviceTensor {
+   public:
+    DeviceTensor() = default;
+    DeviceTensor(std::vector<int64_t> shape, DType dtype) : shape_(std::move(shape)), dtype_(dtype) {
+        if (bytes()) CheckCuda(cudaMalloc(&data_, bytes()), "cudaMalloc");
+    }
+    // Host values converted to `dtype` (round to nearest even).
+    static DeviceTensor FromHost(const std::vector<float>& values, std::vector<int64_t> shape, DType dtype = DType::Float32) {
+        DeviceTensor t(std::move(shape), dtype);
+        if ((int64_t)values.size() != t.numel()) throw ArgumentException("value count does not match the shape");
+        std::vector<unsigned char> raw(t.bytes());
+        for (size_t i = 0; i < values.size(); i++) {
+            if (dtype == DType::Float32) std::memcpy(&raw[4 * i], &values[i], 4);
+            else if (dtype == DType::BFloat16) {
+                const __nv_bfloat16 h = __float2bfloat16_rn(values[i]);
+                std::memcpy(&raw[2 * i], &h, 2);
+            } else {
+                const __half h = __float2half_rn(values[i]);
+                std::memcpy(&raw[2 * i], &h, 2);
+            }
+        }
+        if (t.bytes()) CheckCuda(cudaMemcpy(t.data_, raw.data(), t.bytes(), cudaMemcpyHostToDevice), "cudaMemcpy");
+        return t;
+    }
+    std::vector<float> ToHost() const {
+        std::vector<unsigned char> raw(bytes());
+        if (bytes()) CheckCuda(cudaMemcpy(raw.data(), data_, bytes(), cudaMemcpyDeviceToHost), "cudaMemcpy");
+        std::vector<float> out((size_t)numel());
+        for (size_t i = 0; i < out.size(); i++) {
+            if (dtype_ == DType::Float32) std::memcpy(&out[i], &raw[4 * i], 4);
+            else if (dtype_ == DType::BFloat16) {
+                __nv_bfloat16 h;
+                std::memcpy(&h, &raw[2 * i], 2);
+                out[i] = __bfloat162float(h);
+            } else {
+                __half h;
+                std::memcpy(&h, &raw[2 * i], 2);
+                out[i] = __half2float(h);
+            }
+        }
+        return out;
+    }
+    ~DeviceTensor() {
+        if (data_) cudaFree(data_);
+    }
+    DeviceTensor(DeviceTensor&& o) noexcept { *this = std::move(o); }
+    DeviceTensor& operator=(DeviceTensor&& o) noexcept {
+        if (this != &o) {
+            if (data_) cudaFree(data_);
+            data_ = o.data_;
+            shape_ = std::move(o.shape_);
+            dtype_ = o.dtype_;
+            o.data_ = nullptr;
+        }
+        return *this;
+    }
+    DeviceTensor(const DeviceTensor&) = delete;
+    DeviceTensor& operator=(const DeviceTensor&) = delete;
+
+    void* data() const { return data_; }
+    DType dtype() const { return dtype_; }
+    const std::vector<int64_t>& shape() const { return shape_; }
+    int64_t dim() const { return (int64_t)shape_.size(); }
+    int64_t numel() const {
+        int64_t n = 1;
+        for (int64_t s : shape_) n *= s;
+        return n;
+    }
+    int64_t last() const { return shape_.empty() ? 1 : shape_.back(); }
+    size_t bytes() const { return (size_t)numel() * ElementSize(dtype_); }
+
+   private:
+    void* data_ = nullptr;
+    std::vector<int64_t> shape_;
+    DType dtype_ = DType::Float32;
+};
+
+// ---- HessianAccumulator ------------------------------------------------------------------------
+class HessianAccumulator {
+   public:
+    HessianAccumulator(Context& ctx, int inFeatures) : ctx_(&ctx), d_(inFeatures) {
+        Check(llmc_hessian_create(ctx.get(), inFeatures, &h_));
+    }
+    ~HessianAccumulator() {
+        if (h_) llmc_hessian_destroy(h_);
+    }
+    HessianAccumulator(const HessianAccumulator&) = delete;
+    HessianAccumulator& operator=(const HessianAccumulator&) = delete;
+
+    // H += X^T X over x viewed as [-1, inFeatures] (HessianAccumulator.cs:47-67).
+    void Update(const DeviceTensor& x) {
+        if (x.dim() == 0 || x.last() != d_)
+            throw ArgumentException("Input last dim (" + std::to_string(x.last()) + ") must equal inFeatures (" +
+                                    std::to_string(d_) + ").");
+        Check(llmc_hessian_update(h_, x.data(), (int32_t)x.dtype(), x.numel() / d_, d_));
+    }
+    DeviceTensor GetHessian() const {
+        DeviceTensor out({d_, d_}, DType::Float32);
+        Check(llmc_hessian_get(h_, static_cast<float*>(out.data())));
+        return out;
+    }
+    void Reset() { Check(llmc_hessian_reset(h_)); }
+    int64_t SampleCount() const {
+        int64_t n = 0;
+        Check(llmc_hessian_sample_count(h_, &n));
+        return n;
+    }
+    int InFeatures() const { return d_; }
+
+   private:
+    Context* ctx_;
+    int d_;
+    llmc_hessian* h_ = nullptr;
+};
+
+// ---- HessianInverseSolver ----------------------------------------------------------------------
+struct HessianInverseSolver {
+    // Damped inverse L^-T L^-1 of H + damp * mean(diag H) * I (HessianInverseSolver.cs:44-92).
+    static DeviceTensor Compute(Context& ctx, const DeviceTensor& hessian, float dampingFrac) {
+        if (hessian.dim() != 2 || hessian.shape()[0] != hessian.shape()[1])
+            throw ArgumentException("Hessian must be a square 2-D tensor.");
+        if (hessian.dtype() != DType::Float32) throw ArgumentException("Hessian must be float32.");
+        const int64_t d = hessian.shape()[0];
+        DeviceTensor out({d, d}, DType::Float32);
+        Check(llmc_chol_inverse(ctx.get(), static_cast<const float*>(hessian.data()), d, d, dampingFrac, 0,
+                                static_cast<float*>(out.data()), d, 0));
+        return out;
+    }
+};
+
+// ---- GPTQ -------------------------------------------------------------------------------------
+enum class QuantizationStrategy : int32_t {
+    PerTensor = LLMC_STRATEGY_TENSOR,
+    PerChannel = LLMC_STRATEGY_CHANNEL,
+    PerToken = LLMC_STRATEGY_TOKEN,
+    Group = LLMC_STRATEGY_GROUP,  // the group-size extension
+};
+
+// Defaults of GPTQConfig.cs:22-59, plus GroupSize for the group strategy.
+struct GPTQConfig {
+    int NumBits = 4;
+    bool Symmetric = true;
+    QuantizationStrategy Strategy = QuantizationStrategy::PerChannel;
+    int ChannelAxis = 0;
+    int BlockSize = 128;
+    float DampeningFrac = 0.01f;
+    bool ActOrder = false;
+    int GroupSize = 128;
+
+    llmc_qconfig ToC() const {
+        llmc_qconfig c{};
+        c.num_bits = NumBits;
+        c.symmetric = Symmetric ? 1 : 0;
+        c.strategy = (int32_t)Strategy;
+        c.channel_axis = ChannelAxis;
+        c.group_size = GroupSize;
+        c.block_size = BlockSize;
+        c.damp = DampeningFrac;
+        c.act_order = ActOrder ? 1 : 0;
+        return c;
+    }
+};
+
+struct GptqBlockQuantizer {
+    // The fp32 fake-quantised weight (GptqBlockQuantizer.cs:71-190): U = chol(Hinv)^T with the
+    // U = Hinv fallback, then the column-block solve.
+    static DeviceTensor Quantize(Context& ctx, const DeviceTensor& weight, const DeviceTensor& hinv,
+                                 const GPTQConfig& config) {
+        if (weight.dim() != 2) throw ArgumentException("weight must be 2-D");
+        const int64_t m = weight.shape()[0], n = weight.shape()[1];
+        if (hinv.dim() != 2 || hinv.shape()[0] != n || hinv.shape()[1] != n)
+            throw ArgumentException("hinv must be [in_features, in_features]");
+        const llmc_qconfig c = config.ToC();
+        DeviceTensor u({n, n}, DType::Float32);
+        Check(llmc_upper_factor(ctx.get(), static_cast<const float*>(hinv.data()), n, n, static_cast<float*>(u.data()), n));
+        const int64_t per_row = config.Strategy == QuantizationStrategy::Group ? (n + config.GroupSize - 1) / config.GroupSize : 1;
+        const int64_t nparams = config.Strategy == QuantizationStrategy::PerTensor ? 1 : m * per_row;
+        DeviceTensor scales({nparams}, DType::Float32), zps({nparams}, DType::Float32);  // int32 payload, 4-byte slots
+        DeviceTensor out({m, n}, DType::Float32);
+        Check(llmc_gptq_quantize(ctx.get(), weight.data(), (int32_t)weight.dtype(), m, n, n,
+                                 static_cast<const float*>(u.data()), n, &c, static_cast<float*>(out.data()), n, nullptr,
+                                 static_cast<float*>(scales.data()), static_cast<int32_t*>(zps.data())));
+        return out;
+    }
+};
+
+// ---- observers ----------------------------------------------------------------------------------
+// Host copy of QuantizationParameters (QuantizationParameters.cs:21-25).
+struct QuantizationParameters {
+    std::vector<float> Scale;
+    std::vector<int64_t> ZeroPoint;
+    QuantizationStrategy Strategy;
+};
+
+namespace detail {
+inline QuantizationParameters Affine(Context& ctx, const DeviceTensor& mins, const DeviceTensor& maxs, int64_t count,
+                                     int numBits, bool symmetric, QuantizationStrategy st) {
+    DeviceTensor s({count}, DType::Float32), z({count}, DType::Float32);
+    Check(llmc_affine_params(ctx.get(), static_cast<const float*>(mins.data()), static_cast<const float*>(maxs.data()),
+                             count, numBits, symmetric ? 1 : 0, static_cast<float*>(s.data()),
+                             static_cast<int32_t*>(z.data())));
+    QuantizationParameters p{s.ToHost(), {}, st};
+    std::vector<int32_t> zi((size_t)count);
+    CheckCuda(cudaMemcpy(zi.data(), z.data(), (size_t)count * 4, cudaMemcpyDeviceToHost), "cudaMemcpy");
+    p.ZeroPoint.assign(zi.begin(), zi.end());
+    return p;
+}
+}  // namespace detail
+
+class MinMaxObserver {
+   public:
+    explicit MinMaxObserver(Context& ctx) : ctx_(&ctx), mn_({1}, DType::Float32), mx_({1}, DType::Float32) {}
+    // Running global min / max (MinMaxObserver.cs:24-45).
+    void Update(const DeviceTensor& x) {
+        if (x.numel() == 0) return;
+        Check(llmc_observer_minmax(ctx_->get(), x.data(), (int32_t)x.dtype(), x.numel() / x.last(), x.last(), x.last(),
+                                   LLMC_STRATEGY_TENSOR, x.last(), static_cast<float*>(mn_.data()),
+                                   static_cast<float*>(mx_.data()), has_ ? 1 : 0));
+        has_ = true;
+    }
+    QuantizationParameters GetQuantParams(int numBits, bool symmetric) {
+        if (!has_) throw InvalidOperationException("MinMaxObserver has no calibration samples; call Update first.");
+        return detail::Affine(*ctx_, mn_, mx_, 1, numBits, symmetric, QuantizationStrategy::PerTensor);
+    }
+    void Reset() { has_ = false; }
+
+   private:
+    Context* ctx_;
+    DeviceTensor mn_, mx_;
+    bool has_ = false;
+};
+
+class PerChannelMinMaxObserver {
+   public:
+    explicit PerChannelMinMaxObserver(Context& ctx, int channelAxis = 0) : ctx_(&ctx), axis_(channelAxis) {}
+    // Running per-channel min / max over a 2-D tensor (PerChannelMinMaxObserver.cs:38-76).
+    void Update(const DeviceTensor& x) {
+        if (axis_ < 0 || axis_ >= x.dim())
+            throw ArgumentOutOfRangeException("channelAxis " + std::to_string(axis_) + " is out of range for a " +
+                                              std::to_string(x.dim()) + "-D tensor");
+        if (axis_ != 0 || x.dim() != 2) throw NotSupportedException("per-channel statistics of axis 0 of a 2-D tensor");
+        const int64_t rows = x.shape()[0], cols = x.shape()[1];
+        if (has_ && rows != channels_) throw ArgumentException("channel count changed between updates");
+        if (!has_) {
+            mn_ = DeviceTensor({rows}, DType::Float32);
+            mx_ = DeviceTensor({rows}, DType::Float32);
+            channels_ = rows;
+        }
+        Check(llmc_observer_minmax(ctx_->get(), x.data(), (int32_t)x.dtype(), rows, cols, cols, LLMC_STRATEGY_CHANNEL, cols,
+                                   static_cast<float*>(mn_.data()), static_cast<float*>(mx_.data()), has_ ? 1 : 0));
+        has_ = true;
+    }
+    QuantizationParameters GetQuantParams(int numBits, bool symmetric) {
+        if (!has_) throw InvalidOperationException("PerChannelMinMaxObserver has no calibration samples.");
+        return detail::Affine(*ctx_, mn_, mx_, channels_, numBits, symmetric, QuantizationStrategy::PerChannel);
+    }
+    void Reset() { has_ = false; }
+
+   private:
+    Context* ctx_;
+    int axis_;
+    DeviceTensor mn_, mx_;
+    int64_t channels_ = 0;
+    bool has_ = false;
+};
+
+// ---- FakeQuantize / Int4PackedTensor --------------------------------------------------------------
+struct FakeQuantize {
+    // x.div(s).round().add(zp).clamp(qmin, qmax).sub(zp).mul(s) in x's dtype (FakeQuantize.cs:22-38).
+    static DeviceTensor Apply(Context& ctx, const DeviceTensor& x, float scale, int64_t zeroPoint, int numBits,
+                              bool symmetric) {
+        DeviceTensor out(x.shape(), x.dtype());
+        Check(llmc_fake_quantize(ctx.get(), x.data(), (int32_t)x.dtype(), x.numel(), scale, (int32_t)zeroPoint, numBits,
+                                 symmetric ? 1 : 0, out.data(), nullptr));
+        return out;
+    }
+};
+
+class Int4PackedTensor {
+   public:
+    // Codes q = clamp(round(x / s) + zp) packed two per byte, even index in the high nibble
+    // (Int4PackedTensor.cs:79-100, 47-69).
+    static Int4PackedTensor FromFloat(Context& ctx, const DeviceTensor& x, float scale, int64_t zeroPoint, bool symmetric) {
+        const int64_t n = x.numel();
+        DeviceTensor codes({n}, DType::Float32);  // int32 payload
+        Check(llmc_fake_quantize(ctx.get(), x.data(), (int32_t)x.dtype(), n, scale, (int32_t)zeroPoint, 4,
+                                 symmetric ? 1 : 0, nullptr, static_cast<int32_t*>(codes.data())));
+        Int4PackedTensor t(&ctx, n, scale, zeroPoint, symmetric);
+        Check(llmc_int4_pack(ctx.get(), static_cast<const int32_t*>(codes.data()), n, (int32_t)zeroPoint,
+                             static_cast<uint8_t*>(t.packed_.data())));
+        return t;
+    }
+    // Int4PackedTensor.cs:111-149: (elementCount + 1) / 2 bytes, else ArgumentException.
+    static Int4PackedTensor FromPackedBytes(Context& ctx, const std::vector<uint8_t>& packed, int64_t elementCount,
+                                            float scale, int64_t zeroPoint, bool symmetric) {
+        if ((int64_t)packed.size() != (elementCount + 1) / 2)
+            throw ArgumentException("packed length must be (elementCount + 1) / 2");
+        Int4PackedTensor t(&ctx, elementCount, scale, zeroPoint, symmetric);
+        if (!packed.empty())
+            CheckCuda(cudaMemcpy(t.packed_.data(), packed.data(), packed.size(), cudaMemcpyHostToDevice), "cudaMemcpy");
+        return t;
+    }
+    std::vector<uint8_t> PackedBytes() const {
+        std::vector<uint8_t> b((size_t)((n_ + 1) / 2));
+        if (!b.empty()) CheckCuda(cudaMemcpy(b.data(), packed_.data(), b.size(), cudaMemcpyDeviceToHost), "cudaMemcpy");
+        return b;
+    }
+    int64_t ElementCount() const { return n_; }
+    // stored nibble (sign-extended only when symmetric) * scale (Int4PackedTensor.cs:152-161).
+    DeviceTensor Dequantize() const {
+        DeviceTensor out({n_}, DType::Float32);
+        Check(llmc_int4_unpack_dequant(ctx_->get(), static_cast<const uint8_t*>(packed_.data()), n_, scale_,
+                                       (int32_t)zp_, sym_ ? 1 : 0, static_cast<float*>(out.data())));
+        return out;
+    }
+
+   private:
+    Int4PackedTensor(Context* ctx, int64_t n, float s, int64_t zp, bool sym)
+        : ctx_(ctx), n_(n), scale_(s), zp_(zp), sym_(sym), packed_({((n + 1) / 2 + 1) / 2}, DType::Float16) {}
+    Context* ctx_;
+    int64_t n_;
+    float scale_;
+    int64_t zp_;
+    bool sym_;
+    DeviceTensor packed_;  // (n + 1) / 2 bytes (allocated as 2-byte elements)
+};
+
+}  // namespace llmcs
+
+#endif  // LLMC_B200_HPP

@@ -1,0 +1,282 @@
+// Known-answer tests of the C++ host mirror (include/llmc_b200.hpp), one per case of the
+// reference's xUnit tests (tests/LLMCompressorSharp.Tests/...), run on the GPU through the C ABI.
+// Exit status 0 when every test passes.  Build and run: tests/test_cpp_host.py.
+#include <cmath>
+#include <cstdio>
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "llmc_b200.hpp"
+
+using namespace llmcs;
+
+namespace {
+
+struct Failure {
+    std::string what;
+};
+
+void Assert(bool ok, const std::string& what) {
+    if (!ok) throw Failure{what};
+}
+
+void Near(float got, float want, float tol, const std::string& what) {
+    Assert(std::fabs(got - want) <= tol, what + ": got " + std::to_string(got) + ", want " + std::to_string(want));
+}
+
+template <typename E, typename F>
+void Throws(F f, const std::string& what) {
+    try {
+        f();
+    } catch (const E&) {
+        return;
+    } catch (const std::exception& e) {
+        throw Failure{what + ": wrong exception: " + e.what()};
+    }
+    throw Failure{what + ": nothing thrown"};
+}
+
+std::vector<std::pair<std::string, std::function<void(Context&)>>> tests() {
+    std::vector<std::pair<std::string, std::function<void(Context&)>>> t;
+
+    // ---- HessianAccumulatorTests.cs
+    t.push_back({"HessianAccumulator.InitialIsZero", [](Context& c) {  // :16-25
+                     HessianAccumulator acc(c, 4);
+                     Assert(acc.SampleCount() == 0, "sample count");
+                     for (float v : acc.GetHessian().ToHost()) Assert(v == 0.f, "zero H");
+                 }});
+    t.push_back({"HessianAccumulator.OneBatchIsOuterProduct", [](Context& c) {  // :27-43
+                     HessianAccumulator acc(c, 3);
+                     acc.Update(DeviceTensor::FromHost({1, 2, 3}, {1, 3}));
+                     Assert(acc.SampleCount() == 1, "sample count");
+                     const std::vector<float> want = {1, 2, 3, 2, 4, 6, 3, 6, 9};
+                     Assert(acc.GetHessian().ToHost() == want, "H = x^T x");
+                 }});
+    t.push_back({"HessianAccumulator.BatchesAreAdditive", [](Context& c) {  // :45-58
+                     HessianAccumulator acc(c, 2);
+                     acc.Update(DeviceTensor::FromHost({1, 0}, {1, 2}));
+                     acc.Update(DeviceTensor::FromHost({0, 1}, {1, 2}));
+                     Assert(acc.SampleCount() == 2, "sample count");
+                     Assert(acc.GetHessian().ToHost() == std::vector<float>({1, 0, 0, 1}), "H");
+                 }});
+    t.push_back({"HessianAccumulator.HighRankInputIsFlattened", [](Context& c) {  // :60-83
+                     HessianAccumulator acc(c, 2);
+                     acc.Update(DeviceTensor::FromHost({1, 0, 0, 1, 1, 1, 1, 0, 0, 1, 1, 1}, {2, 3, 2}));
+                     Assert(acc.SampleCount() == 6, "sample count");
+                     Assert(acc.GetHessian().ToHost() == std::vector<float>({4, 2, 2, 4}), "H");
+                 }});
+    t.push_back({"HessianAccumulator.WrongLastDimThrows", [](Context& c) {  // :85-92
+                     HessianAccumulator acc(c, 3);
+                     Throws<ArgumentException>([&] { acc.Update(DeviceTensor::FromHost({1, 2}, {1, 2})); }, "last dim");
+                 }});
+    t.push_back({"HessianAccumulator.HalfInputAccumulatesInFloat32", [](Context& c) {  // :94-103
+                     HessianAccumulator acc(c, 2);
+                     acc.Update(DeviceTensor::FromHost({1, 2}, {1, 2}, DType::Float16));
+                     const DeviceTensor h = acc.GetHessian();
+                     Assert(h.dtype() == DType::Float32, "fp32 H");
+                     Assert(h.ToHost() == std::vector<float>({1, 2, 2, 4}), "H");
+                 }});
+    t.push_back({"HessianAccumulator.Reset", [](Context& c) {  // :105-116
+                     HessianAccumulator acc(c, 2);
+                     acc.Update(DeviceTensor::FromHost({1, 2}, {1, 2}));
+                     acc.Reset();
+                     Assert(acc.SampleCount() == 0, "sample count");
+                     for (float v : acc.GetHessian().ToHost()) Assert(v == 0.f, "zero H");
+                 }});
+    t.push_back({"HessianAccumulator.NonPositiveInFeaturesThrows", [](Context& c) {  // :118-123
+                     Throws<ArgumentOutOfRangeException>([&] { HessianAccumulator acc(c, 0); }, "inFeatures 0");
+                 }});
+
+    // ---- HessianInverseSolverTests.cs
+    t.push_back({"HessianInverseSolver.Identity", [](Context& c) {  // :17-27
+                     std::vector<float> eye(16, 0.f);
+                     for (int i = 0; i < 4; i++) eye[5 * i] = 1.f;
+                     const auto h = HessianInverseSolver::Compute(c, DeviceTensor::FromHost(eye, {4, 4}), 0.f).ToHost();
+                     for (int i = 0; i < 16; i++) Near(h[i], eye[i], 1e-5f, "I^-1");
+                 }});
+    t.push_back({"HessianInverseSolver.ScaledIdentity", [](Context& c) {  // :29-39
+                     std::vector<float> two(9, 0.f);
+                     for (int i = 0; i < 3; i++) two[4 * i] = 2.f;
+                     const auto h = HessianInverseSolver::Compute(c, DeviceTensor::FromHost(two, {3, 3}), 0.f).ToHost();
+                     for (int i = 0; i < 9; i++) Near(h[i], i % 4 == 0 ? 0.5f : 0.f, 1e-5f, "(2I)^-1");
+                 }});
+    t.push_back({"HessianInverseSolver.RankDeficientDampedIsFinite", [](Context& c) {  // :41-51
+                     const auto h = HessianInverseSolver::Compute(c, DeviceTensor::FromHost({1, 1, 1, 1}, {2, 2}), 0.01f).ToHost();
+                     for (float v : h) Assert(std::isfinite(v), "finite");
+                 }});
+    t.push_back({"HessianInverseSolver.ZeroMatrixFallsBackToPinvZero", [](Context& c) {  // :85-91 (pinv(0) = 0)
+                     const auto h = HessianInverseSolver::Compute(c, DeviceTensor::FromHost(std::vector<float>(25, 0.f), {5, 5}),
+                                                                   0.01f).ToHost();
+                     for (float v : h) Assert(v == 0.f, "zero");
+                 }});
+    t.push_back({"HessianInverseSolver.NonSquareThrows", [](Context& c) {  // :72-78
+                     Throws<ArgumentException>(
+                         [&] { HessianInverseSolver::Compute(c, DeviceTensor::FromHost(std::vector<float>(12, 1.f), {3, 4}), 0.01f); },
+                         "square");
+                 }});
+
+    // ---- MinMaxObserverTests.cs
+    t.push_back({"MinMaxObserver.AccumulatesAsymmetric", [](Context& c) {  // :22-42
+                     MinMaxObserver obs(c);
+                     for (const auto& b : {std::vector<float>{-2, 0, 3}, std::vector<float>{-5, 1, 2}, std::vector<float>{-1, 7, 0}})
+                         obs.Update(DeviceTensor::FromHost(b, {3}));
+                     const auto p = obs.GetQuantParams(8, false);
+                     Near(p.Scale[0], 12.f / 255.f, 1e-5f, "scale");
+                     Assert(p.ZeroPoint[0] == 106, "zero-point 106");
+                 }});
+    t.push_back({"MinMaxObserver.Symmetric", [](Context& c) {  // :44-58
+                     MinMaxObserver obs(c);
+                     obs.Update(DeviceTensor::FromHost({-3, 0, 5}, {3}));
+                     const auto p = obs.GetQuantParams(8, true);
+                     Near(p.Scale[0], 5.f / 127.f, 1e-5f, "scale");
+                     Assert(p.ZeroPoint[0] == 0, "zero-point");
+                 }});
+    t.push_back({"MinMaxObserver.Reset", [](Context& c) {  // :60-74
+                     MinMaxObserver obs(c);
+                     obs.Update(DeviceTensor::FromHost({-10, 10}, {2}));
+                     obs.Reset();
+                     obs.Update(DeviceTensor::FromHost({-1, 1}, {2}));
+                     Near(obs.GetQuantParams(8, true).Scale[0], 1.f / 127.f, 1e-5f, "scale");
+                 }});
+    t.push_back({"MinMaxObserver.NoSamplesThrows", [](Context& c) {  // :76-83
+                     MinMaxObserver obs(c);
+                     Throws<InvalidOperationException>([&] { obs.GetQuantParams(8, true); }, "no samples");
+                 }});
+    t.push_back({"MinMaxObserver.AllZerosGiveScaleOne", [](Context& c) {  // :85-95
+                     MinMaxObserver obs(c);
+                     obs.Update(DeviceTensor::FromHost({0, 0, 0}, {3}));
+                     const auto p = obs.GetQuantParams(8, true);
+                     Assert(p.Scale[0] == 1.f && p.ZeroPoint[0] == 0, "(1, 0)");
+                 }});
+    t.push_back({"Observer.BitsOutOfRangeThrow", [](Context& c) {  // Observer.cs:53-56
+                     MinMaxObserver obs(c);
+                     obs.Update(DeviceTensor::FromHost({-1, 1}, {2}));
+                     Throws<ArgumentOutOfRangeException>([&] { obs.GetQuantParams(1, true); }, "bits 1");
+                 }});
+
+    // ---- PerChannelMinMaxObserverTests.cs
+    t.push_back({"PerChannelMinMaxObserver.OneScalePerRow", [](Context& c) {  // :118-143
+                     PerChannelMinMaxObserver obs(c, 0);
+                     obs.Update(DeviceTensor::FromHost({-2, 0, 4, -10, 5, 10}, {2, 3}));
+                     const auto p = obs.GetQuantParams(8, true);
+                     Assert(p.Scale.size() == 2, "two scales");
+                     Near(p.Scale[0], 4.f / 127.f, 1e-5f, "scale 0");
+                     Near(p.Scale[1], 10.f / 127.f, 1e-5f, "scale 1");
+                 }});
+    t.push_back({"PerChannelMinMaxObserver.Accumulates", [](Context& c) {  // :145-171
+                     PerChannelMinMaxObserver obs(c, 0);
+                     obs.Update(DeviceTensor::FromHost({-1, 2, -3, 5}, {2, 2}));
+                     obs.Update(DeviceTensor::FromHost({-5, 1, -2, 8}, {2, 2}));
+                     const auto p = obs.GetQuantParams(8, true);
+                     Near(p.Scale[0], 5.f / 127.f, 1e-5f, "scale 0");
+                     Near(p.Scale[1], 8.f / 127.f, 1e-5f, "scale 1");
+                 }});
+    t.push_back({"PerChannelMinMaxObserver.ResetAndErrors", [](Context& c) {  // :173-219
+                     PerChannelMinMaxObserver obs(c, 0);
+                     Throws<InvalidOperationException>([&] { obs.GetQuantParams(8, true); }, "no samples");
+                     obs.Update(DeviceTensor::FromHost({-10, 10, -20, 20}, {2, 2}));
+                     obs.Reset();
+                     obs.Update(DeviceTensor::FromHost({-1, 1, -2, 2}, {2, 2}));
+                     const auto p = obs.GetQuantParams(8, true);
+                     Near(p.Scale[0], 1.f / 127.f, 1e-5f, "scale 0");
+                     Near(p.Scale[1], 2.f / 127.f, 1e-5f, "scale 1");
+                     PerChannelMinMaxObserver bad(c, 5);
+                     Throws<ArgumentOutOfRangeException>([&] { bad.Update(DeviceTensor::FromHost({1, 1, 1, 1}, {2, 2})); },
+                                                         "axis 5");
+                 }});
+
+    // ---- FakeQuantizeFunctionTests.cs
+    t.push_back({"FakeQuantize.Symmetric8", [](Context& c) {  // :16-30
+                     const auto y = FakeQuantize::Apply(c, DeviceTensor::FromHost({-127.4f, -127.6f, 0.4f, 0.6f, 127.4f, 127.6f}, {6}),
+                                                        1.f, 0, 8, true).ToHost();
+                     Assert(y == std::vector<float>({-127, -127, 0, 1, 127, 127}), "grid");
+                 }});
+    t.push_back({"FakeQuantize.Symmetric4Scale", [](Context& c) {  // :32-43
+                     const auto y = FakeQuantize::Apply(c, DeviceTensor::FromHost({-3.6f, 0.f, 3.6f}, {3}), 0.5f, 0, 4, true).ToHost();
+                     Assert(y == std::vector<float>({-3.5f, 0.f, 3.5f}), "grid");
+                 }});
+    t.push_back({"FakeQuantize.AsymmetricZeroPoint", [](Context& c) {  // :60-73
+                     const auto y = FakeQuantize::Apply(c, DeviceTensor::FromHost({-8.f, 0.f, 7.f}, {3}), 1.f, 8, 4, false).ToHost();
+                     Assert(y == std::vector<float>({-8.f, 0.f, 7.f}), "grid");
+                 }});
+    t.push_back({"FakeQuantize.InvalidBitsThrow", [](Context& c) {  // :75-81
+                     Throws<ArgumentOutOfRangeException>(
+                         [&] { FakeQuantize::Apply(c, DeviceTensor::FromHost({1.f, 2.f}, {2}), 1.f, 0, 1, true); }, "bits 1");
+                 }});
+
+    // ---- Int4PackedTensorTests.cs
+    t.push_back({"Int4PackedTensor.ClampsSymmetric", [](Context& c) {  // :16-31
+                     auto p = Int4PackedTensor::FromFloat(c, DeviceTensor::FromHost({-8.5f, -7.f, 0.f, 7.f, 9.f}, {5}), 1.f, 0, true);
+                     Assert(p.Dequantize().ToHost() == std::vector<float>({-7, -7, 0, 7, 7}), "clamped");
+                 }});
+    t.push_back({"Int4PackedTensor.HalvesStorage", [](Context& c) {  // :33-41
+                     auto p = Int4PackedTensor::FromFloat(c, DeviceTensor::FromHost({1, 2, 3, 4, 5, 6, 7, 8}, {8}), 1.f, 0, true);
+                     Assert(p.PackedBytes().size() == 4, "4 bytes");
+                 }});
+    t.push_back({"Int4PackedTensor.RoundTrip", [](Context& c) {  // :43-59
+                     const std::vector<float> vals = {-7, -3, 0, 4, 7, -2};
+                     auto p = Int4PackedTensor::FromFloat(c, DeviceTensor::FromHost(vals, {6}), 1.f, 0, true);
+                     auto r = Int4PackedTensor::FromPackedBytes(c, p.PackedBytes(), 6, 1.f, 0, true);
+                     Assert(r.Dequantize().ToHost() == vals, "round trip");
+                 }});
+    t.push_back({"Int4PackedTensor.NibbleOrder", [](Context& c) {  // Int4PackedTensor.cs:52-64
+                     auto p = Int4PackedTensor::FromFloat(c, DeviceTensor::FromHost({1.f, 2.f, -1.f}, {3}), 1.f, 0, true);
+                     Assert(p.PackedBytes() == std::vector<uint8_t>({0x12, 0xF0}), "even index in the high nibble");
+                     Throws<ArgumentException>([&] { Int4PackedTensor::FromPackedBytes(c, {0x12}, 3, 1.f, 0, true); }, "length");
+                 }});
+
+    // ---- GptqBlockQuantizerTests.cs / GPTQModifierTests.cs
+    t.push_back({"GptqBlockQuantizer.ZeroWeightStaysZero", [](Context& c) {  // GptqBlockQuantizerTests.cs:18-30
+                     std::vector<float> eye(16, 0.f);
+                     for (int i = 0; i < 4; i++) eye[5 * i] = 1.f;
+                     GPTQConfig cfg;
+                     cfg.NumBits = 8;
+                     cfg.Strategy = QuantizationStrategy::PerTensor;
+                     const auto q = GptqBlockQuantizer::Quantize(c, DeviceTensor::FromHost(std::vector<float>(8, 0.f), {2, 4}),
+                                                                 DeviceTensor::FromHost(eye, {4, 4}), cfg).ToHost();
+                     for (float v : q) Near(v, 0.f, 1e-6f, "zero");
+                 }});
+    t.push_back({"GptqBlockQuantizer.SixteenBitIsNearIdentity", [](Context& c) {  // :115-138
+                     GPTQConfig cfg;
+                     cfg.NumBits = 16;
+                     cfg.Strategy = QuantizationStrategy::PerTensor;
+                     cfg.BlockSize = 1;
+                     const auto q = GptqBlockQuantizer::Quantize(c, DeviceTensor::FromHost({1, 2, 3, 4}, {2, 2}),
+                                                                 DeviceTensor::FromHost({1, 0, 0, 1}, {2, 2}), cfg).ToHost();
+                     const std::vector<float> w = {1, 2, 3, 4};
+                     for (int i = 0; i < 4; i++) Near(q[i], w[i], 0.01f, "identity");
+                 }});
+    t.push_back({"GptqBlockQuantizer.ActOrderThrows", [](Context& c) {  // GPTQModifierTests.cs:130-141
+                     GPTQConfig cfg;
+                     cfg.ActOrder = true;
+                     Throws<NotSupportedException>(
+                         [&] {
+                             GptqBlockQuantizer::Quantize(c, DeviceTensor::FromHost({1, 1, 1, 1}, {2, 2}),
+                                                          DeviceTensor::FromHost({1, 0, 0, 1}, {2, 2}), cfg);
+                         },
+                         "ActOrder");
+                 }});
+    return t;
+}
+
+}  // namespace
+
+int main() {
+    Context ctx(0);
+    int failed = 0, passed = 0;
+    for (auto& [name, fn] : tests()) {
+        try {
+            fn(ctx);
+            passed++;
+        } catch (const Failure& f) {
+            failed++;
+            std::printf("FAIL %s: %s\n", name.c_str(), f.what.c_str());
+        } catch (const std::exception& e) {
+            failed++;
+            std::printf("FAIL %s: unexpected exception: %s\n", name.c_str(), e.what());
+        }
+    }
+    std::printf("%d passed, %d failed\n", passed, failed);
+    return failed == 0 ? 0 : 1;
+}
