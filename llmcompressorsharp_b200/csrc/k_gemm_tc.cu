@@ -24,6 +24,8 @@
 
 #include <cuda.h>
 
+#include <mutex>
+
 namespace llmc {
 namespace {
 
@@ -259,6 +261,291 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
     }
 }
 
+// ---- CTA-pair variant (large products) -----------------------------------------------------------
+// A cluster of two CTAs computes 256 x 256 output tiles with tcgen05.mma.cta_group::2.kind::tf32
+// (M = 256, N = 256, K = 8): CTA r stages A hi / lo for rows 128 r .. of the tile and B hi / lo
+// for columns 128 r .., so each SM moves 64 KB per 32-K step for twice the MMA work of the
+// 128 x 128 kernel and the tensor cores read each B half once for both SMs.  Barrier protocol
+// as in the Hessian pair kernel: the leader (rank 0) arms full[s] with both CTAs' bytes and
+// issues the MMAs; its commits are multicast to both CTAs' empty / tfull barriers; epilogue
+// warps of both CTAs arrive on the leader's tempty; producers wait for their last stages to be
+// released before the cluster exits.
+constexpr int P_EPI = 8, P_NT = 32 * (2 + P_EPI);
+constexpr int P_BN = 256;                       // columns per pair tile (128 per CTA's B half)
+constexpr int P_STAGE_BYTES = 4 * TILE_BYTES;   // A hi, A lo (128 rows), B hi, B lo (128 columns)
+constexpr int P_SMEM_MAIN = STAGES * P_STAGE_BYTES;
+constexpr int P_OUT_BYTES = 32 * 32 * 4;         // epilogue box per warp: 32 rows x 32 fp32
+constexpr int P_SMEM_BYTES = P_SMEM_MAIN + P_EPI * P_OUT_BYTES + 1024 + 256;
+static_assert(P_SMEM_BYTES <= 232448, "shared memory above the per-block limit");
+constexpr int P_TMEM_COLS = 2 * P_BN;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap ahi, const __grid_constant__ CUtensorMap alo,
+                    const __grid_constant__ CUtensorMap bhi, const __grid_constant__ CUtensorMap blo,
+                    const __grid_constant__ CUtensorMap cmap, const TcGemmArgs a, const int tma_out) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* outbufs = smem + P_SMEM_MAIN;  // P_EPI x 4 KB, 1024-byte aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(outbufs + P_EPI * P_OUT_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_ctarank();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * P_EPI);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(P_TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int pend_par[STAGES];
+#pragma unroll
+    for (int s = 0; s < STAGES; s++) pend_par[s] = -1;
+    int commit_par[2] = {-1, -1};
+    uint32_t prod_it = 0, mma_it = 0, cc = 0;
+
+    const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+    const int total_tiles = a.tiles_m * a.tiles_n;  // 256 x 256 pair tiles
+    const int per_group = a.group * a.tiles_n;
+    for (int t = pair; t < total_tiles && !*abort_flag; t += npairs) {
+        const int gidx = t / per_group;
+        const int first_m = gidx * a.group;
+        const int gm = min(a.group, a.tiles_m - first_m);
+        const int local = t - gidx * per_group;
+        const int64_t pm0 = (int64_t)(first_m + local % gm) * 256, n0 = (int64_t)(local / gm) * P_BN;
+        if (a.c_mode == 1 && pm0 + 255 < n0) continue;
+        if (a.c_mode == 2 && pm0 > n0 + P_BN - 1) continue;
+        int64_t kb_lo = 0, kb_hi = a.K;
+        if (a.a_tri == TRI_KLE) kb_hi = min(kb_hi, pm0 + 256);
+        if (a.a_tri == TRI_KGE) kb_lo = max(kb_lo, pm0);
+        if (a.b_tri == TRI_KLE) kb_hi = min(kb_hi, n0 + P_BN);
+        if (a.b_tri == TRI_KGE) kb_lo = max(kb_lo, n0);
+        const int kb0 = (int)(kb_lo / BK);
+        const int kb1 = kb_hi > kb_lo ? (int)((kb_hi + BK - 1) / BK) : kb0;
+        const int nchunks = (kb1 - kb0 + KF - 1) / KF;
+        const int64_t m0 = pm0 + (int64_t)rank * 128;   // this CTA's rows
+        const int64_t nb = n0 + (int64_t)rank * 128;    // this CTA's half of the B panel
+
+        if (warp == 0) {
+            if (lane == 0) {
+                for (int kb = kb0; kb < kb1; kb++, prod_it++) {
+                    const int s = prod_it % STAGES;
+                    const uint32_t ph = (prod_it / STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    unsigned char* st = smem + s * P_STAGE_BYTES;
+                    if (rank == 0) mbar_expect_tx(&full[s], 2 * P_STAGE_BYTES);
+                    const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
+                    const int k0 = kb * BK;
+                    tma_load_2d_pair(st + 0 * TILE_BYTES, &ahi, k0, (int)m0, fbar);
+                    tma_load_2d_pair(st + 1 * TILE_BYTES, &alo, k0, (int)m0, fbar);
+                    tma_load_2d_pair(st + 2 * TILE_BYTES, &bhi, k0, (int)nb, fbar);
+                    tma_load_2d_pair(st + 3 * TILE_BYTES, &blo, k0, (int)nb, fbar);
+                    pend_par[s] = (int)ph;
+                }
+            }
+            __syncwarp();
+        } else if (warp == 1) {
+            if (lane == 0 && rank == 0) {
+                uint32_t c_it = cc;
+                for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
+                    const int b = (int)(c_it & 1u);
+                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    tc_fence_after();
+                    const uint32_t dst = tmem + (uint32_t)(b * P_BN);
+                    const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
+                    bool ok = true;
+                    for (int kb = k0; kb < k1; kb++, mma_it++) {
+                        const int s = mma_it % STAGES;
+                        const uint32_t ph = (mma_it / STAGES) & 1u;
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t base = smem_u32(smem + s * P_STAGE_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; kk++) {
+                            const uint64_t dah = part_desc(base + 0 * TILE_BYTES, kk);
+                            const uint64_t dal = part_desc(base + 1 * TILE_BYTES, kk);
+                            const uint64_t dbh = part_desc(base + 2 * TILE_BYTES, kk);
+                            const uint64_t dbl = part_desc(base + 3 * TILE_BYTES, kk);
+                            const uint32_t first = (kb == k0 && kk == 0) ? 0u : 1u;
+                            umma2_tf32(dst, dah, dbh, a.idesc, first);
+                            umma2_tf32(dst, dah, dbl, a.idesc, 1u);
+                            umma2_tf32(dst, dal, dbh, a.idesc, 1u);
+                        }
+                        umma2_commit_mc(&empty[s], 0x3);
+                    }
+                    umma2_commit_mc(&tfull[b], 0x3);
+                    commit_par[b] = (int)((c_it >> 1) & 1u);
+                    if (!ok) break;
+                }
+            }
+            __syncwarp();
+        } else {
+            // epilogue warps: TMEM lane quadrant q (rows 32 q ..), column half h of the 256
+            const int e = warp - 2, q = warp % 4, h = e / 4;
+            float acc[128];
+#pragma unroll
+            for (int i = 0; i < 128; i++) acc[i] = 0.f;
+            uint32_t c_it = cc;
+            bool ok = true;
+            for (int c = 0; c < nchunks; c++, c_it++) {
+                const int b = (int)(c_it & 1u);
+                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
+                if (!__all_sync(0xffffffffu, have ? 1 : 0)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int part = 0; part < 4; part++) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * P_BN + h * 128 + part * 32), v);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) acc[part * 32 + i] = __fadd_rn(acc[part * 32 + i], __uint_as_float(v[i]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+            }
+            const int64_t r = m0 + q * 32 + lane;
+            const int64_t c0 = n0 + h * 128;
+            // TMA epilogue (tma_out: beta is 0 or 1, C 16-byte aligned with ldc % 4 == 0): the
+            // warp's 32 x 128 block leaves in four 32 x 32 boxes through its shared buffer, as a
+            // tensor store (beta 0) or reduce-add (beta 1), so no thread reads C.  Tiles crossing
+            // the diagonal of a lower-triangle output take the register path below.
+            const bool tri_cross = a.c_mode == 1 && (m0 + q * 32 < c0 + 127);
+            if (ok && tma_out && !tri_cross && !*abort_flag && m0 + q * 32 < a.M && c0 < a.N) {
+                unsigned char* ob = outbufs + e * P_OUT_BYTES;
+                const uint32_t ob_s = smem_u32(ob);
+#pragma unroll
+                for (int round = 0; round < 4; round++) {
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const int i = round * 32 + c * 4;
+                        *reinterpret_cast<float4*>(ob + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                            make_float4(a.alpha * acc[i], a.alpha * acc[i + 1], a.alpha * acc[i + 2], a.alpha * acc[i + 3]);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (tma_out == 2) tma_reduce_add_2d(&cmap, ob_s, (int)(c0 + round * 32), (int)(m0 + q * 32));
+                        else tma_store_2d(&cmap, ob_s, (int)(c0 + round * 32), (int)(m0 + q * 32));
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                }
+            } else if (ok && r < a.M && c0 < a.N && !*abort_flag) {
+                float* crow = a.C + r * a.ldc + c0;
+                const bool vec = ((reinterpret_cast<uintptr_t>(crow) & 15u) == 0) && c0 + 128 <= a.N &&
+                                 !(a.c_mode == 1 && r < c0 + 127) && !(a.c_mode == 2 && r > c0);
+                if (vec) {
+#pragma unroll
+                    for (int i = 0; i < 128; i += 4) {
+                        float4 o = make_float4(a.alpha * acc[i], a.alpha * acc[i + 1], a.alpha * acc[i + 2],
+                                               a.alpha * acc[i + 3]);
+                        if (a.beta != 0.f) {
+                            const float4 cv = *reinterpret_cast<const float4*>(crow + i);
+                            o.x = fmaf(a.beta, cv.x, o.x);
+                            o.y = fmaf(a.beta, cv.y, o.y);
+                            o.z = fmaf(a.beta, cv.z, o.z);
+                            o.w = fmaf(a.beta, cv.w, o.w);
+                        }
+                        *reinterpret_cast<float4*>(crow + i) = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 128; i++) {
+                        const int64_t col = c0 + i;
+                        if (col < a.N && !(a.c_mode == 1 && r < col) && !(a.c_mode == 2 && r > col)) {
+                            const float v = a.alpha * acc[i];
+                            crow[i] = (a.beta == 0.f) ? v : fmaf(a.beta, crow[i], v);
+                        }
+                    }
+                }
+            }
+        }
+        cc += (uint32_t)nchunks;
+    }
+
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (warp == 0 && lane == 0)
+        for (int s = 0; s < STAGES; s++)
+            if (pend_par[s] >= 0) mbar_wait_drain(&empty[s], (uint32_t)pend_par[s]);
+    if (*abort_flag && warp == 1 && lane == 0 && rank == 0)
+        for (int b = 0; b < 2; b++)
+            if (commit_par[b] >= 0) mbar_wait_drain(&tfull[b], (uint32_t)commit_par[b]);
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P_TMEM_COLS));
+    }
+}
+
+// Pairs of gemm_tc2_kernel that can be resident at once on the context's device (0: unusable).
+int max_pairs_gemm(llmc_ctx* ctx) {
+    static std::mutex mu;
+    static int cache[64];
+    static bool known[64];
+    const int dev = ctx->device;
+    if (dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!known[dev]) {
+        known[dev] = true;
+        cache[dev] = 0;
+        if (cudaFuncSetAttribute(gemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (unsigned)ctx->sm_count, 1, 1);
+        cfg.blockDim = dim3(P_NT, 1, 1);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_tc2_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            cfg.numAttrs = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_tc2_kernel, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+        }
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
 // hi = x rounded to TF32 (round to nearest, ties away), lo = x - hi (exact in fp32).
 __device__ __forceinline__ void tf32_split(float x, float* h, float* l) {
     uint32_t u = __float_as_uint(x);
@@ -408,6 +695,44 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
     d |= (uint32_t)(BM >> 4) << 24;
     t.idesc = d;
 
+    // Large products: CTA pairs on 256 x 256 tiles.
+    if (g.M >= 512 && g.N >= 512) {
+        const int pcap = max_pairs_gemm(ctx);
+        if (pcap >= 1) {
+            TcGemmArgs p = t;
+            p.tiles_m = (int)((g.M + 255) / 256);
+            p.tiles_n = (int)((g.N + P_BN - 1) / P_BN);
+            p.group = 8;
+            uint32_t d2 = 0;
+            d2 |= 1u << 4;
+            d2 |= 2u << 7;
+            d2 |= 2u << 10;
+            d2 |= (uint32_t)(P_BN >> 3) << 17;
+            d2 |= (uint32_t)(256 >> 4) << 24;
+            p.idesc = d2;
+            const int tiles = p.tiles_m * p.tiles_n;
+            // Persistent pairs when the context has the GPU to itself; one pair per tile when it
+            // shares the SMs (its CTAs then start wherever SMs free up).
+            const int pairs = (ctx->sm_limit > 0 || tiles < pcap) ? tiles : pcap;
+            // C through TMA when beta is 0 (store) or 1 (reduce-add) and C's layout allows a map.
+            int tma_out = 0;
+            CUtensorMap mc;
+            if ((g.beta == 0.f || g.beta == 1.f) && (reinterpret_cast<uintptr_t>(g.C) % 16) == 0 && g.ldc % 4 == 0) {
+                EncodeTiledFn enc = encode_fn();
+                const cuuint64_t cdim[2] = {(cuuint64_t)g.N, (cuuint64_t)g.M};
+                const cuuint64_t cstride[1] = {(cuuint64_t)g.ldc * 4};
+                const cuuint32_t cbox[2] = {32, 32};
+                const cuuint32_t est[2] = {1, 1};
+                if (enc && enc(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, g.C, cdim, cstride, cbox, est,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+                    tma_out = g.beta == 0.f ? 1 : 2;
+            }
+            if (!tma_out) mc = mah;  // unused placeholder
+            gemm_tc2_kernel<<<(unsigned)(2 * pairs), P_NT, P_SMEM_BYTES, ctx->stream>>>(mah, mal, mbh, mbl, mc, p, tma_out);
+            return check_launch(ctx, "gemm_tc2");
+        }
+    }
     static bool attr = false;
     if (!attr) {
         LLMC_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));

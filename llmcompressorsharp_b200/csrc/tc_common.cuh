@@ -120,6 +120,13 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
                  : "memory");
 }
 
+// Tiled TMA store of a shared-memory box to global memory (same rules as the reduce above).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t smem_src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_src)
+                 : "memory");
+}
+
 // UMMA shared-memory descriptor for a K-major, 128-byte-swizzled operand: rows of 128 bytes
 // along K, 8-row swizzle atoms 1024 bytes apart (leading byte offset unused).
 __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t addr) {
@@ -177,6 +184,16 @@ __device__ __forceinline__ void umma2_f16(uint32_t tmem_d, uint64_t da, uint64_t
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+        ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
+
+// Pair MMA with TF32 operands (both K-major).
+__device__ __forceinline__ void umma2_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
         ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u)
         : "memory");
 }
