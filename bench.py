@@ -47,8 +47,9 @@ def parse():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["gptq", "sparsegpt", "rtn", "smoothquant", "awq"], default="gptq",
+    p.add_argument("--workload", choices=["gptq", "sparsegpt", "solve", "rtn", "smoothquant", "awq"], default="gptq",
                    help="gptq: the GPTQ W4A16 job (default); sparsegpt: the same job pruning 2:4 with SparseGPT; "
+                        "solve: the job's factor + GPTQ solve alone, Hessians given; "
                         "rtn: RTN W4A16 g128 + min-max observer passes over the Llama-3-8B Linear weights; "
                         "smoothquant: SmoothQuant (alpha 0.5) + W8A8 weights on a Llama-2-7B shape; awq: AWQ "
                         "20-point grid search + scale apply on Llama-3-8B layers")
@@ -362,15 +363,20 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
     copy_stream = torch.cuda.Stream(dev)
 
     def copy_acts():
-        """Host->device copy of each site's activations on a copy stream, one event per site,
-        so accumulation starts as soon as its own site has arrived."""
+        """Host->device copy of each site's activations on a copy stream, in update-call
+        chunks with one event per chunk, so accumulation follows the copy chunk by chunk."""
         copy_stream.wait_stream(torch.cuda.current_stream(dev))
         ready = {}
         with torch.cuda.stream(copy_stream):
             for k in acts:
-                acts[k].copy_(h_acts[k], non_blocking=True)
-                ready[k] = torch.cuda.Event()
-                ready[k].record(copy_stream)
+                T = acts[k].shape[0]
+                ready[k] = []
+                for r0 in range(0, T, args.chunk):
+                    r1 = min(T, r0 + args.chunk)
+                    acts[k][r0:r1].copy_(h_acts[k][r0:r1], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(copy_stream)
+                    ready[k].append((r1, ev))
         return ready
 
     def e2e_step():
@@ -404,7 +410,7 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
         for l in range(args.layers):
             for s in sites:
                 if s.name in ready:
-                    torch.cuda.current_stream(dev).wait_event(ready.pop(s.name))
+                    torch.cuda.current_stream(dev).wait_event(ready.pop(s.name)[-1][1])
                 pipe.accumulate(s, acts[s.name], out_h=hbufs[l][s.name])
         reduce_hessians(hbufs, sites, range(args.layers), world)
         for l in mine:
@@ -514,6 +520,87 @@ def run_reference(args):
             "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc},
             "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def run_solve(args):
+    """--workload solve: the solve half of the GPTQ W4A16 job alone, on one GPU that it has to
+    itself.  Every site's Hessian is accumulated once, before the timed region, from 2d seeded
+    bf16 rows; a step then runs, for each of the layers and each site, the damped inverse factor
+    U and the stacked GPTQ solve to packed codes, scales and zero-points (the same calls as the
+    job's solve stream).  Algorithmic work per site: (2/3)d^3 for the factor (Cholesky and
+    triangular inverse) + M d^2 for the solve's rank updates (M stacked rows), all in fp32."""
+    import torch
+
+    from llmcompressorsharp_b200.gptq import GPTQConfig
+    from llmcompressorsharp_b200.pipeline import GptqPipeline
+
+    world, rank, local = dist_env()
+    if world > 1:
+        raise SystemExit("--workload solve runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    sites = sites_for(MODEL)
+    L = args.layers
+    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128,
+                     dampening_frac=0.01)
+    pipe = GptqPipeline(sites, cfg, dev, chunk_rows=args.chunk)
+    g = torch.Generator(dev)
+    for i, st in enumerate(sites):
+        g.manual_seed(3000 + i)
+        x = _randn_bf16(2 * st.d, st.d, dev, g)
+        pipe.accumulate(st, x)
+        del x
+    weights = {}
+    for l in range(L):
+        weights[l] = {}
+        for si, st in enumerate(sites):
+            for wi, (wname, m) in enumerate(st.weights):
+                g.manual_seed(10_000 + 97 * l + 7 * si + wi)
+                weights[l][wname] = _randn_bf16(m, st.d, dev, g, std=0.02)
+    outputs = {l: pipe.alloc_outputs(weights[l]) for l in range(L)}
+    hptr = {st.name: pipe.hessian_ptr(st.name) for st in sites}
+    torch.cuda.synchronize()
+
+    def step():
+        for l in range(L):
+            for st in sites:
+                pipe.solve_site(st, hptr[st.name], weights[l], outputs[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches0 = pipe.launch_count()
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = pipe.launch_count() - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    flops = L * sum(2 * st.d ** 3 / 3 + sum(m for _, m in st.weights) * st.d ** 2 for st in sites)
+    achieved = flops / (ms * 1e-3) / 1e12
+    _, sustained, _, src = peaks()
+    # 3xTF32: three tf32 MMAs per fp32 product, tf32 at half the bf16 rate
+    peak = sustained / 2 / 3
+    line = {"metric": "GPTQ W4A16 solve wall-clock s, Hessians given (Llama-3-8B shape)", "value": round(ms / 1e3, 4),
+            "unit": "s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"damped inverse factor + stacked GPTQ W4A16 asym g128 solve of {L} Llama-3-8B "
+                                   f"layers x 4 sites (d 4096 x 3, 14336), Hessians from 2d seeded bf16 rows",
+                       "layers": L, "l2": "inputs larger than L2 (each layer's weights 0.44 GB, U up to 0.82 GB)"},
+            "solve_tflops": round(achieved, 1),
+            "roofline": {"kernel": "whole solve (3xTF32 gemm_tc2 / gemm_tc GEMMs, Cholesky base blocks, GPTQ block "
+                                   "kernel)", "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 3),
+                         "peak_note": f"{src} sustained bf16 / 2 (tf32 rate) / 3 (3xTF32 MMAs per fp32 product)",
+                         "algorithmic": "(2/3) d^3 + M d^2 fp32 FLOP per site and layer", "traffic": None},
+            "gpu_launches": launches, "clocks": clk}
+    print(json.dumps(line), flush=True)
+    pipe.close()
 
 
 def run_rtn(args):
@@ -810,6 +897,9 @@ def main():
         return
     if args.workload in ("smoothquant", "awq"):
         run_smooth_awq(args)
+        return
+    if args.workload == "solve":
+        run_solve(args)
         return
     run_ours(args)
 

@@ -125,13 +125,25 @@ class GptqPipeline:
         if out_h is not None:
             out_h.copy_(torch.as_tensor(_HView(self.hessian_ptr(site.name), site.d), device=self.device))
 
-    def _accumulate_into(self, handle: int, x: torch.Tensor):
-        """Reset one Hessian handle and add X^T X over X in row chunks (on the handle's stream)."""
+    def _accumulate_into(self, handle: int, x: torch.Tensor, ready=None):
+        """Reset one Hessian handle and add X^T X over X in row chunks (on the handle's stream).
+        ``ready`` marks rows of X that are still arriving on another stream: a CUDA event (all
+        of X), or a list of (rows, event) in row order, the event completing once rows [0, rows)
+        have arrived.  Each chunk [r0, r1) first waits for the first event with rows >= r1 (the
+        last event when none covers r1), so accumulation follows the copy chunk by chunk."""
+        stream = torch.cuda.current_stream(self.device)
+        if isinstance(ready, torch.cuda.Event):
+            stream.wait_event(ready)
+            ready = None
+        marks = list(ready or [])
+        T = x.shape[0]
+        waits = chunk_waits([r for r, _ in marks], T, self.chunk)
         h = C.c_void_p(handle)
         _lib.call("llmc_hessian_reset", h)
-        T = x.shape[0]
-        for r0 in range(0, T, self.chunk):
+        for i, r0 in enumerate(range(0, T, self.chunk)):
             r1 = min(T, r0 + self.chunk)
+            if waits[i] >= 0:
+                stream.wait_event(marks[waits[i]][1])
             _lib.call("llmc_hessian_update", h, C.c_void_p(x.data_ptr() + r0 * x.stride(0) * x.element_size()),
                       _lib.dtype_code(x.dtype), C.c_int64(r1 - r0), C.c_int64(x.stride(0)))
 
@@ -237,9 +249,10 @@ class GptqPipeline:
         and ``after_solve(l)`` run on the stream that solves layer l, just before / after it
         (e.g. host->device weight copies and device->host result copies).  With
         ``hess_events`` (a list), CUDA event pairs bracketing each site's accumulation are
-        appended as (start, end, d, rows).  ``acts_ready`` ({site: CUDA event}) makes the first
-        accumulation of each site wait for that event (activations still being copied in on
-        another stream).  Work is enqueued on the current stream (or, with overlap enabled,
+        appended as (start, end, d, rows).  ``acts_ready`` ({site: CUDA event, or a list of
+        (rows, event) per copied row range}) makes the first accumulation of each site wait for
+        its activations, still being copied in on another stream (chunk by chunk with the list
+        form).  Work is enqueued on the current stream (or, with overlap enabled,
         on the two pipeline streams joined back into it)."""
         acts_for = acts if callable(acts) else (lambda _l: acts)
         pending = dict(acts_ready or {})
@@ -249,12 +262,11 @@ class GptqPipeline:
         for l in layers:
             a = acts_for(l)
             for s in self.sites:
-                if s.name in pending:
-                    torch.cuda.current_stream(self.device).wait_event(pending.pop(s.name))
                 ev = _events() if hess_events is not None else None
                 if ev:
                     ev[0].record()
-                self.accumulate(s, a[s.name])
+                _lib.ctx_for(self.device.index)
+                self._accumulate_into(self.h[s.name], a[s.name], ready=pending.pop(s.name, None))
                 if ev:
                     ev[1].record()
                     hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
@@ -263,6 +275,24 @@ class GptqPipeline:
                 self.solve_site(s, self.hessian_ptr(s.name), weights[l], outputs[l])
             if after_solve is not None:
                 after_solve(l)
+
+
+def chunk_waits(mark_rows: list, T: int, chunk: int) -> list:
+    """For each update chunk [r0, r1) of T rows, the index of the copy mark to wait for
+    before it, or -1 when an earlier wait already covers it.  ``mark_rows`` are the row
+    counts after which each mark's event completes, in order; a chunk waits for the first
+    mark with rows >= r1, or the last mark when none reaches r1."""
+    out, k, waited = [], 0, -1
+    for r0 in range(0, T, chunk):
+        r1 = min(T, r0 + chunk)
+        if not mark_rows:
+            out.append(-1)
+            continue
+        while k < len(mark_rows) - 1 and mark_rows[k] < r1:
+            k += 1
+        out.append(k if k != waited else -1)
+        waited = k
+    return out
 
 
 def _events():
@@ -350,12 +380,10 @@ class _Overlap:
                 if solved[b] is not None:
                     self.sh.wait_event(solved[b])
                 for s in pipe.sites:
-                    if s.name in acts_ready:
-                        self.sh.wait_event(acts_ready.pop(s.name))
                     ev = _events() if hess_events is not None else None
                     if ev:
                         ev[0].record(self.sh)
-                    pipe._accumulate_into(self.h[b][s.name], a[s.name])
+                    pipe._accumulate_into(self.h[b][s.name], a[s.name], ready=acts_ready.pop(s.name, None))
                     if ev:
                         ev[1].record(self.sh)
                         hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
@@ -434,12 +462,10 @@ class _Overlap:
                 if released[b] is not None:
                     self.sh.wait_event(released[b])
                 for s in pipe.sites:
-                    if s.name in acts_ready:
-                        self.sh.wait_event(acts_ready.pop(s.name))
                     ev = _events() if hess_events is not None else None
                     if ev:
                         ev[0].record(self.sh)
-                    pipe._accumulate_into(sets[b][s.name], a[s.name])
+                    pipe._accumulate_into(sets[b][s.name], a[s.name], ready=acts_ready.pop(s.name, None))
                     if ev:
                         ev[1].record(self.sh)
                         hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))

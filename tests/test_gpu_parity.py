@@ -597,6 +597,53 @@ def test_pipeline_overlap_matches_oracle(reserve):
                            dict(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128), got)
 
 
+@pytest.mark.parametrize("reserve", [0, 100])
+def test_pipeline_chunked_copy_matches_resident(reserve):
+    """Activations copied in from pinned host memory on another stream, with one event per
+    copied row range (acts_ready in its list form), give the same outputs as the same job on
+    resident activations: scales and zero-points (from W alone) equal, codes equal up to the
+    order of the Hessian's split-K additions."""
+    from llmcompressorsharp_b200 import GPTQConfig
+    from llmcompressorsharp_b200.pipeline import GptqPipeline
+
+    sites, acts, weights = _pipeline_case(seed=52, layers=2, tokens=10000)
+    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128)
+    outs = []
+    for mode in ("resident", "copied"):
+        pipe = GptqPipeline(sites, cfg, torch.device(DEV), chunk_rows=4096)
+        if reserve:
+            pipe.enable_overlap(reserve)
+        out = {l: pipe.alloc_outputs(weights[l]) for l in weights}
+        ready = None
+        a = acts
+        if mode == "copied":
+            a = {k: torch.empty_like(v) for k, v in acts.items()}
+            host = {k: v.cpu().pin_memory() for k, v in acts.items()}
+            cs = torch.cuda.Stream(torch.device(DEV))
+            cs.wait_stream(torch.cuda.current_stream())
+            ready = {}
+            with torch.cuda.stream(cs):
+                for k in a:
+                    ready[k] = []
+                    for r0 in range(0, a[k].shape[0], 3000):  # marks not aligned with the 4096-row chunks
+                        r1 = min(a[k].shape[0], r0 + 3000)
+                        a[k][r0:r1].copy_(host[k][r0:r1], non_blocking=True)
+                        ev = torch.cuda.Event()
+                        ev.record(cs)
+                        ready[k].append((r1, ev))
+        pipe.run(range(len(weights)), a, weights, out, acts_ready=ready)
+        torch.cuda.synchronize()
+        pipe.close()
+        outs.append(out)
+    for l in weights:
+        for s in sites:
+            for w, _ in s.weights:
+                for f in ("scales", "zero_points"):
+                    assert torch.equal(outs[0][l][w][f], outs[1][l][w][f]), (l, w, f)
+                same = (outs[0][l][w]["codes"] == outs[1][l][w]["codes"]).float().mean().item()
+                assert same >= 0.999, (l, w, same)
+
+
 def test_gptq_kats():  # GptqBlockQuantizerTests.cs
     from llmcompressorsharp_b200 import GPTQConfig, GptqBlockQuantizer
     from llmcompressorsharp_b200.errors import NotSupportedError

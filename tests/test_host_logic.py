@@ -97,3 +97,16 @@ def test_gptq_config_defaults():  # GPTQConfig.cs:22-59
     assert abs(c.dampening_frac - 0.01) < 1e-9
     q = c.to_c()
     assert q.num_bits == 4 and q.strategy == 1 and q.block_size == 128
+
+
+def test_chunk_waits():
+    """Which copy mark each Hessian update chunk waits for (pipeline.chunk_waits)."""
+    from llmcompressorsharp_b200.pipeline import chunk_waits
+
+    assert chunk_waits([], 10, 4) == [-1, -1, -1]
+    assert chunk_waits([4, 8, 10], 10, 4) == [0, 1, 2]
+    assert chunk_waits([10], 10, 4) == [0, -1, -1]
+    # marks every 3000 rows, chunks of 4096 rows: chunk 0 needs rows 4096 -> mark 1 (6000)
+    assert chunk_waits([3000, 6000, 9000, 10000], 10000, 4096) == [1, 2, 3]
+    # marks finer than chunks and one mark short of the end: the last mark covers the rest
+    assert chunk_waits([1, 2, 3, 4, 5], 12, 4) == [3, 4, -1]
