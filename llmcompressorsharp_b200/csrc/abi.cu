@@ -230,6 +230,20 @@ llmc_status llmc_hessian_update(llmc_hessian* h, const void* x, int32_t dtype, i
     if (rows > 0) {
         llmc_status st = LLMC_ERR_UNSUPPORTED;
         if (dtype != LLMC_DTYPE_F32) st = syrk_tc(ctx, x, dtype, rows, h->d, ld, h->h, h->d);
+        if (dtype == LLMC_DTYPE_F32 && h->d >= 512 && rows >= 1024) {
+            // fp32 input: 3xTF32 on the tensor cores (hi/lo split of X once, CTA pairs on 256 x 256
+            // upper tiles), the token range split so that the units fill the pairs, with at least
+            // 1024 tokens per split.
+            const int64_t t = (h->d + 255) / 256;
+            const int64_t upper = t * (t + 1) / 2;
+            int64_t split = ((int64_t)persistent_sms(ctx) / 2 + upper - 1) / upper;
+            if (split > rows / 1024) split = rows / 1024;
+            if (split < 1) split = 1;
+            GemmArgs g{h->d, h->d, rows, x, ld, 1, dtype, x, ld, 0, dtype, h->h, h->d, 1.f, 1.f};
+            g.c_mode = 2;
+            g.split_k = (int)split;
+            st = gemm_tc(ctx, g);
+        }
         if (st == LLMC_ERR_UNSUPPORTED) {
             // fp32 input (or a shape outside the tensor-core kernel's contract): fp32 SIMT.
             const int64_t tiles = (h->d + 127) / 128;

@@ -49,6 +49,7 @@ struct TcGemmArgs {
     int* err;
     uint32_t idesc;
     int tiles_m, tiles_n, group;  // 1-D grid: tiles visited in column strips of `group` M-tiles
+    int splits;                   // K splits per tile (pair kernel; > 1 needs beta == 1)
 };
 
 // Loads one operand part (128 rows of the MN dimension x 32 K-elements, K contiguous) for a
@@ -326,7 +327,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
     const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
     const int total_tiles = a.tiles_m * a.tiles_n;  // 256 x 256 pair tiles
     const int per_group = a.group * a.tiles_n;
-    for (int t = pair; t < total_tiles && !*abort_flag; t += npairs) {
+    // A unit is a tile x a K split; consecutive units are tiles of one split, which read the
+    // same K range of the operands.
+    const int total_units = total_tiles * a.splits;
+    for (int u = pair; u < total_units && !*abort_flag; u += npairs) {
+        const int t = u % total_tiles, sp = u / total_tiles;
         const int gidx = t / per_group;
         const int first_m = gidx * a.group;
         const int gm = min(a.group, a.tiles_m - first_m);
@@ -339,8 +344,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
         if (a.a_tri == TRI_KGE) kb_lo = max(kb_lo, pm0);
         if (a.b_tri == TRI_KLE) kb_hi = min(kb_hi, n0 + P_BN);
         if (a.b_tri == TRI_KGE) kb_lo = max(kb_lo, n0);
-        const int kb0 = (int)(kb_lo / BK);
-        const int kb1 = kb_hi > kb_lo ? (int)((kb_hi + BK - 1) / BK) : kb0;
+        int kb0 = (int)(kb_lo / BK);
+        int kb1 = kb_hi > kb_lo ? (int)((kb_hi + BK - 1) / BK) : kb0;
+        if (a.splits > 1) {
+            const int per = (kb1 - kb0 + a.splits - 1) / a.splits;
+            const int s0 = kb0 + sp * per, s1 = min(kb1, s0 + per);
+            if (s0 >= s1) continue;  // nothing to add for this split
+            kb0 = s0;
+            kb1 = s1;
+        }
         const int nchunks = (kb1 - kb0 + KF - 1) / KF;
         const int64_t m0 = pm0 + (int64_t)rank * 128;   // this CTA's rows
         const int64_t nb = n0 + (int64_t)rank * 128;    // this CTA's half of the B panel
@@ -432,9 +444,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
             const int64_t c0 = n0 + h * 128;
             // TMA epilogue (tma_out: beta is 0 or 1, C 16-byte aligned with ldc % 4 == 0): the
             // warp's 32 x 128 block leaves in four 32 x 32 boxes through its shared buffer, as a
-            // tensor store (beta 0) or reduce-add (beta 1), so no thread reads C.  Tiles crossing
-            // the diagonal of a lower-triangle output take the register path below.
-            const bool tri_cross = a.c_mode == 1 && (m0 + q * 32 < c0 + 127);
+            // tensor store (beta 0) or reduce-add (beta 1), so no thread reads C.  Blocks not
+            // wholly inside a triangle-only output's triangle take the register path below.
+            const bool tri_cross = (a.c_mode == 1 && m0 + q * 32 < c0 + 127) ||
+                                   (a.c_mode == 2 && m0 + q * 32 + 31 > c0);
             if (ok && tma_out && !tri_cross && !*abort_flag && m0 + q * 32 < a.M && c0 < a.N) {
                 unsigned char* ob = outbufs + e * P_OUT_BYTES;
                 const uint32_t ob_s = smem_u32(ob);
@@ -455,6 +468,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
                         else tma_store_2d(&cmap, ob_s, (int)(c0 + round * 32), (int)(m0 + q * 32));
                         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                     }
+                }
+            } else if (ok && r < a.M && c0 < a.N && !*abort_flag && a.splits > 1) {
+                // K split: other units add into the same C elements (beta is 1).
+                float* crow = a.C + r * a.ldc + c0;
+#pragma unroll
+                for (int i = 0; i < 128; i++) {
+                    const int64_t col = c0 + i;
+                    if (col < a.N && !(a.c_mode == 1 && r < col) && !(a.c_mode == 2 && r > col))
+                        atomicAdd(crow + i, a.alpha * acc[i]);
                 }
             } else if (ok && r < a.M && c0 < a.N && !*abort_flag) {
                 float* crow = a.C + r * a.ldc + c0;
@@ -652,22 +674,27 @@ llmc_status split_operand(llmc_ctx* ctx, const float* src, int64_t mn, int64_t k
 // is too small to pay for the split (the caller then runs the SIMT kernel).
 llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
     if (g.a_dtype != LLMC_DTYPE_F32 || g.b_dtype != LLMC_DTYPE_F32) return LLMC_ERR_UNSUPPORTED;
-    if (g.split_k > 1 || g.M < 128 || g.N < 128 || g.K < 64) return LLMC_ERR_UNSUPPORTED;
+    if (g.M < 128 || g.N < 128 || g.K < 64) return LLMC_ERR_UNSUPPORTED;
+    // K splits run on the pair kernel only (its epilogue adds atomically); beta must be 1.
+    if (g.split_k > 1 && (g.M < 512 || g.N < 512 || g.beta != 1.f || max_pairs_gemm(ctx) < 1))
+        return LLMC_ERR_UNSUPPORTED;
     if (g.M > (int64_t)INT32_MAX || g.N > (int64_t)INT32_MAX || g.K > (int64_t)INT32_MAX) return LLMC_ERR_UNSUPPORTED;
     if (((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN) > (int64_t)INT32_MAX) return LLMC_ERR_UNSUPPORTED;
     // Operands as stored: A is [M, K] (a_trans = 0) or [K, M] (a_trans = 1); B is [K, N]
     // (b_trans = 0) or [N, K] (b_trans = 1).  The split copies are K-major [M, K] and [N, K].
     const int64_t ldk = (g.K + 3) / 4 * 4;
-    const size_t need = (size_t)(2 * g.M * ldk + 2 * g.N * ldk) * 4 + 4096;
+    // A product of an operand with its own transpose (X^T X) splits the operand once.
+    const bool same = g.A == g.B && g.M == g.N && g.lda == g.ldb && g.a_trans == !g.b_trans;
+    const size_t need = (size_t)(2 * g.M * ldk + (same ? 0 : 2 * g.N * ldk)) * 4 + 4096;
     void* sp;
     LLMC_TRY(workspace2(ctx, need, &sp));
     Carver cv{(char*)sp};
     float* ah = cv.take<float>((size_t)g.M * ldk);
     float* al = cv.take<float>((size_t)g.M * ldk);
-    float* bh = cv.take<float>((size_t)g.N * ldk);
-    float* bl = cv.take<float>((size_t)g.N * ldk);
+    float* bh = same ? ah : cv.take<float>((size_t)g.N * ldk);
+    float* bl = same ? al : cv.take<float>((size_t)g.N * ldk);
     LLMC_TRY(split_operand(ctx, (const float*)g.A, g.M, g.K, g.lda, g.a_trans, ah, al, ldk));
-    LLMC_TRY(split_operand(ctx, (const float*)g.B, g.N, g.K, g.ldb, !g.b_trans, bh, bl, ldk));
+    if (!same) LLMC_TRY(split_operand(ctx, (const float*)g.B, g.N, g.K, g.ldb, !g.b_trans, bh, bl, ldk));
     CUtensorMap mah, mal, mbh, mbl;
     LLMC_TRY(make_map(&mah, ah, g.M, g.K, ldk));
     LLMC_TRY(make_map(&mal, al, g.M, g.K, ldk));
@@ -685,6 +712,7 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
     t.a_tri = g.a_tri;
     t.b_tri = g.b_tri;
     t.c_mode = g.c_mode;
+    t.splits = 1;
     t.err = ctx->dflags + 2;
     uint32_t d = 0;
     d |= 1u << 4;          // D: F32
@@ -710,10 +738,13 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
             d2 |= (uint32_t)(P_BN >> 3) << 17;
             d2 |= (uint32_t)(256 >> 4) << 24;
             p.idesc = d2;
-            const int tiles = p.tiles_m * p.tiles_n;
-            // Persistent pairs when the context has the GPU to itself; one pair per tile when it
+            p.splits = g.split_k > 1 ? g.split_k : 1;
+            const int64_t units64 = (int64_t)p.tiles_m * p.tiles_n * p.splits;
+            if (units64 > (int64_t)INT32_MAX / 2) return LLMC_ERR_UNSUPPORTED;
+            const int units = (int)units64;
+            // Persistent pairs when the context has the GPU to itself; one pair per unit when it
             // shares the SMs (its CTAs then start wherever SMs free up).
-            const int pairs = (ctx->sm_limit > 0 || tiles < pcap) ? tiles : pcap;
+            const int pairs = (ctx->sm_limit > 0 || units < pcap) ? units : pcap;
             // C through TMA when beta is 0 (store) or 1 (reduce-add) and C's layout allows a map.
             int tma_out = 0;
             CUtensorMap mc;

@@ -135,6 +135,37 @@ def test_hessian_tensor_cores_match_fp64(dtype, d, rows):
         assert rel_fro(h_tc, ref.get_hessian()) < HESSIAN_TC_TOL
 
 
+@pytest.mark.parametrize("d,rows", [(576, 65536), (1536, 65536), (1024, 3000), (600, 1024), (4096, 8192)])
+def test_hessian_fp32_tensor_cores_match_fp64(d, rows):
+    """fp32 activations take the 3xTF32 path (X split once into tf32 hi + lo, CTA pairs on
+    256 x 256 upper tiles, token range split across pairs with atomic adds): against the
+    fp64 product, within fp32 accumulation error; only the upper triangle of the stored
+    matrix is written."""
+    import ctypes as C
+    from llmcompressorsharp_b200 import HessianAccumulator, _lib
+    from llmcompressorsharp_b200.pipeline import _HView
+
+    g = torch.Generator(DEV).manual_seed(d * 3 + rows)
+    x = torch.randn(rows, d, device=DEV, generator=g)
+    acc = HessianAccumulator(d, DEV)
+    acc.update(x)
+    acc.update(x[: rows // 3])
+    h = acc.get_hessian()
+    xd = x.double()
+    h64 = xd.t() @ xd + xd[: rows // 3].t() @ xd[: rows // 3]
+    assert torch.equal(h, h.t())
+    assert rel_fro(h, h64) < 1e-6
+    p = C.c_void_p()
+    _lib.call("llmc_hessian_data", C.c_void_p(acc._h), C.byref(p))
+    raw = torch.as_tensor(_HView(p.value, d), device=DEV)
+    assert torch.count_nonzero(torch.tril(raw, -1)) == 0
+    if d <= 1024 and rows <= 4096:
+        ref = o_hess.HessianAccumulator(d)
+        ref.update(x.cpu())
+        ref.update(x[: rows // 3].cpu())
+        assert rel_fro(h, ref.get_hessian()) < 1e-6
+
+
 def test_hessian_tensor_cores_accumulate_across_calls():
     from llmcompressorsharp_b200 import HessianAccumulator
 
