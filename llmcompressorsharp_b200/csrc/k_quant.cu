@@ -623,12 +623,14 @@ llmc_status launch_rtn(llmc_ctx* ctx, const void* x, int64_t m, int64_t n, int64
     // Vector path also needs whole code bytes per lane (even column starts) and aligned output.
     const bool deq_ok = deq == nullptr || ((uintptr_t)deq % 16 == 0);
     const bool codes_ok = codes == nullptr || bits > 4 || (n % 2 == 0);
+    // The vector paths store a vector's packed codes with one 4-byte store.
+    const bool codes_al = codes == nullptr || (uintptr_t)codes % 4 == 0;
     const int64_t seglen = gs < n ? gs : n;
     const int64_t lanes = seglen / (RV * V);
     const bool reg_ok = seglen % (RV * V) == 0 && lanes >= 1 && lanes <= 32 && (lanes & (lanes - 1)) == 0 &&
                         n % seglen == 0 && total < (int64_t(1) << 31) && g.nseg < (int64_t(1) << 31);
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && reg_ok) {
+        if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && codes_al && reg_ok) {
             g.L = (int)lanes;
             const FastDiv fd = make_fastdiv((uint32_t)g.nseg);
             if (deq)
@@ -641,12 +643,12 @@ llmc_status launch_rtn(llmc_ctx* ctx, const void* x, int64_t m, int64_t n, int64
             return check_launch(ctx, "rtn_bf16");
         }
     }
-    if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && reg_ok) {
+    if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && codes_al && reg_ok) {
         g.L = (int)lanes;
         rtn_reg_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
             reinterpret_cast<const T*>(x), g, make_fastdiv((uint32_t)g.nseg), bits, sym, tensor_mode, scales, zps, codes,
             reinterpret_cast<T*>(deq), n);
-    } else if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok) {
+    } else if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && codes_al) {
         g.L = lanes_for(gs < n ? gs : n, V);
         rtn_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
             reinterpret_cast<const T*>(x), g, bits, sym, tensor_mode, scales, zps, codes, reinterpret_cast<T*>(deq), n);
