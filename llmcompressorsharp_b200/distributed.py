@@ -8,6 +8,12 @@ unquantised model, src/LLMCompressorSharp.Core/Algorithms/Gptq/GPTQModifier.cs:1
 each layer is solved by one owner rank, dealt round-robin.  The only exchange is the sum of
 the partial Hessians onto each owner (``torch.distributed.reduce``; NCCL on GPUs, gloo in the
 CPU tests).
+
+Row sharding is the other partition: GPTQ and SparseGPT rows are independent given the factor U
+(every step of GptqBlockQuantizer.Quantize except U itself is row-wise,
+src/LLMCompressorSharp.Core/Algorithms/Gptq/GptqBlockQuantizer.cs:124-180).  Every rank then
+receives the full H with one all-reduce, factors it, and solves its own rows of the site's
+stacked weights (``row_shard`` / ``stack_slices``).
 """
 
 from __future__ import annotations
@@ -48,3 +54,26 @@ def reduce_hessians(hbufs: dict, sites, layers, world: int, group=None) -> None:
                                     async_op=True))
     for r in reqs:
         r.wait()
+
+
+def row_shard(rows: int, world: int, rank: int, align: int = 64) -> tuple[int, int]:
+    """Rows [r0, r1) of a stacked weight that `rank` solves: contiguous, in whole blocks of
+    `align` rows (the solve kernel's CTA height) except at the end; ranks past the last block
+    get an empty range."""
+    if align < 1:
+        raise ValueError("align must be positive")
+    blocks = (rows + align - 1) // align
+    b0, b1 = token_shard(blocks, world, rank)
+    return min(rows, b0 * align), min(rows, b1 * align)
+
+
+def stack_slices(ms, r0: int, r1: int) -> list:
+    """The parts of stacked rows [r0, r1) that fall in each weight of a stack of weights with
+    row counts `ms` (stacked in order): [(index, first row in the weight, row count)]."""
+    out, off = [], 0
+    for i, m in enumerate(ms):
+        lo, hi = max(r0, off), min(r1, off + m)
+        if hi > lo:
+            out.append((i, lo - off, hi - lo))
+        off += m
+    return out

@@ -18,7 +18,8 @@ the buffer set they share.
 Multi-GPU: calibration tokens are split across ranks; each rank accumulates its partial
 H for every site, the partial Hessians are summed onto the layer's owner rank
 (``torch.distributed.reduce`` over NCCL), and owners solve their layers (layers are dealt
-round-robin).
+round-robin).  In the row-sharded mode every Hessian is all-reduced instead and each rank
+solves its own rows of every layer.
 """
 
 from __future__ import annotations
@@ -147,43 +148,60 @@ class GptqPipeline:
             _lib.call("llmc_hessian_update", h, C.c_void_p(x.data_ptr() + r0 * x.stride(0) * x.element_size()),
                       _lib.dtype_code(x.dtype), C.c_int64(r1 - r0), C.c_int64(x.stride(0)))
 
-    def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict, ctx=None):
+    def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict, ctx=None, rows=None):
         """U from the site's H (upper triangle), then one stacked GPTQ solve of every weight
         that reads the site (outputs are views into stacked per-site buffers).  ``ctx`` is a
-        library context bound to the stream to run on (default: torch's current stream)."""
+        library context bound to the stream to run on (default: torch's current stream).
+        ``rows`` = (r0, r1) solves only those rows of the site's stack (rows are independent
+        given U); the stacked outputs are written at the same rows.  Row ranges need a
+        per-row strategy (channel or group)."""
+        from .distributed import stack_slices
+
         d = site.d
         if ctx is None:
             _lib.ctx_for(self.device.index)
             ctx = self.c
-        _lib.call("llmc_chol_inverse", ctx, C.c_void_p(h_ptr), C.c_int64(d), C.c_int64(d),
-                  C.c_float(self.cfg.dampening_frac), 1, _lib.ptr(self.u), C.c_int64(d), 1)
         names = [w for w, _ in site.weights]
         ms = [m for _, m in site.weights]
-        k = len(names)
-        if self.solver == "sparsegpt":
-            st = outputs[_stack_key(site)]
-            wq = st.get("wq")
-            if wq is None:
-                wq = self.work[: sum(ms) * d].view(sum(ms), d)
-            r0 = 0
-            for name, m in zip(names, ms):
-                w = weights[name]
-                _lib.call("llmc_sparsegpt_prune", ctx, _lib.ptr(w), _lib.dtype_code(w.dtype), C.c_int64(m),
-                          C.c_int64(d), C.c_int64(w.stride(0)), _lib.ptr(self.u), C.c_int64(d), C.byref(self.qc),
-                          C.c_void_p(wq.data_ptr() + r0 * d * 4), C.c_int64(d),
-                          C.c_void_p(st["mask"].data_ptr() + r0 * d))
-                r0 += m
+        M = sum(ms)
+        r0, r1 = (0, M) if rows is None else (int(rows[0]), int(rows[1]))
+        if not 0 <= r0 <= r1 <= M:
+            raise ValueError(f"row range [{r0}, {r1}) outside the stack of {M} rows")
+        if rows is not None and self.solver == "gptq" and self.cfg.strategy == "tensor":
+            raise ValueError("row-sharded solves need a per-row strategy (channel or group)")
+        _lib.call("llmc_chol_inverse", ctx, C.c_void_p(h_ptr), C.c_int64(d), C.c_int64(d),
+                  C.c_float(self.cfg.dampening_frac), 1, _lib.ptr(self.u), C.c_int64(d), 1)
+        if r1 == r0:
             return
-        wp = (C.c_void_p * k)(*[weights[w].data_ptr() for w in names])
-        mp = (C.c_int64 * k)(*ms)
-        lp = (C.c_int64 * k)(*[weights[w].stride(0) for w in names])
+        parts = stack_slices(ms, r0, r1)  # [(weight index, first row, rows)]
         st = outputs[_stack_key(site)]
         wq = st.get("wq")
         if wq is None:
-            wq = self.work[: sum(ms) * d].view(sum(ms), d)
-        _lib.call("llmc_gptq_quantize_batch", ctx, C.c_int32(k), wp, mp, lp, _lib.dtype_code(weights[names[0]].dtype),
+            wq = self.work[: (r1 - r0) * d].view(r1 - r0, d)
+        else:
+            wq = wq[r0:r1]
+        if self.solver == "sparsegpt":
+            q0 = 0
+            for i, a, m in parts:
+                w = weights[names[i]]
+                _lib.call("llmc_sparsegpt_prune", ctx,
+                          C.c_void_p(w.data_ptr() + a * w.stride(0) * w.element_size()), _lib.dtype_code(w.dtype),
+                          C.c_int64(m), C.c_int64(d), C.c_int64(w.stride(0)), _lib.ptr(self.u), C.c_int64(d),
+                          C.byref(self.qc), C.c_void_p(wq.data_ptr() + q0 * d * 4), C.c_int64(d),
+                          C.c_void_p(st["mask"].data_ptr() + (r0 + q0) * d))
+                q0 += m
+            return
+        k = len(parts)
+        ws = [weights[names[i]] for i, _, _ in parts]
+        wp = (C.c_void_p * k)(*[w.data_ptr() + a * w.stride(0) * w.element_size() for w, (_, a, _) in zip(ws, parts)])
+        mp = (C.c_int64 * k)(*[m for _, _, m in parts])
+        lp = (C.c_int64 * k)(*[w.stride(0) for w in ws])
+        codes, scales, zps = st["codes"], st["scales"], st["zero_points"]
+        _lib.call("llmc_gptq_quantize_batch", ctx, C.c_int32(k), wp, mp, lp, _lib.dtype_code(ws[0].dtype),
                   C.c_int64(d), _lib.ptr(self.u), C.c_int64(d), C.byref(self.qc), _lib.ptr(wq), C.c_int64(d),
-                  _lib.ptr(st["codes"]), _lib.ptr(st["scales"]), _lib.ptr(st["zero_points"]))
+                  C.c_void_p(codes.data_ptr() + r0 * codes.stride(0) * codes.element_size()),
+                  C.c_void_p(scales.data_ptr() + r0 * (scales.stride(0) if scales.dim() > 1 else 1) * 4),
+                  C.c_void_p(zps.data_ptr() + r0 * (zps.stride(0) if zps.dim() > 1 else 1) * 4))
 
     def alloc_outputs(self, layer_weights: dict):
         """Stacked per-site output buffers plus per-weight views into them."""
@@ -231,15 +249,22 @@ class GptqPipeline:
             self.solve_site(s, self.hessian_ptr(s.name), weights, outputs)
 
     def run_distributed(self, layers, acts, weights, outputs, world: int, rank: int, group=None, before_solve=None,
-                        after_solve=None, hess_events=None, acts_ready=None):
+                        after_solve=None, hess_events=None, acts_ready=None, shard: str = "layers"):
         """``run`` for one process per GPU (NCCL process group initialised by the caller):
-        ``acts`` are this rank's token shard; ``weights`` / ``outputs`` are needed for the
-        layers this rank owns (``distributed.owned_layers``).  Requires overlap enabled."""
+        ``acts`` are this rank's token shard.  ``shard="layers"``: partial Hessians are reduced
+        onto each layer's owner, which solves the whole layer; ``weights`` / ``outputs`` are
+        needed for the layers this rank owns (``distributed.owned_layers``).  ``shard="rows"``:
+        each Hessian is all-reduced, every rank factors it and solves its rows of every site's
+        stack (``distributed.row_shard``, 64-row blocks); ``weights`` / ``outputs`` are needed for
+        every layer and only this rank's rows of the stacked outputs are written.  Requires
+        overlap enabled."""
         if self.overlap is None:
             raise InvalidOperationError("run_distributed needs enable_overlap() first")
+        if shard not in ("layers", "rows"):
+            raise ValueError(f"unknown shard mode {shard}")
         acts_for = acts if callable(acts) else (lambda _l: acts)
         return self.overlap.run_dist(list(layers), acts_for, weights, outputs, world, rank, group, before_solve,
-                                     after_solve, hess_events, dict(acts_ready or {}))
+                                     after_solve, hess_events, dict(acts_ready or {}), rows=shard == "rows")
 
     def run(self, layers, acts, weights, outputs, before_solve=None, after_solve=None, hess_events=None,
             acts_ready=None):
@@ -421,14 +446,15 @@ class _Overlap:
         self.hd = []
 
     def run_dist(self, layers, acts_for, weights, outputs, world, rank, group, before_solve, after_solve,
-                 hess_events, acts_ready):
+                 hess_events, acts_ready, rows=False):
         """Token-sharded job on `world` ranks: every rank accumulates its partial Hessians of
         every layer on the Hessian stream and reduces them onto the layer's owner with NCCL
         (issued from the Hessian stream, so the transfer of layer l overlaps the accumulation of
-        layer l+1); owners solve on the solve stream once the reduction is done."""
+        layer l+1); owners solve on the solve stream once the reduction is done.  With ``rows``
+        the reduction is an all-reduce and every rank solves its row shard of every layer."""
         import torch.distributed as dist
 
-        from .distributed import layer_owner
+        from .distributed import layer_owner, row_shard
 
         pipe = self.pipe
         sets = self._dist_sets()
@@ -447,7 +473,8 @@ class _Overlap:
                 for s in pipe.sites:
                     p = C.c_void_p()
                     _lib.call("llmc_hessian_data", C.c_void_p(sets[b][s.name]), C.byref(p))
-                    pipe.solve_site(s, p.value, weights[l], outputs[l], ctx=C.c_void_p(self.cs))
+                    shard = row_shard(sum(m for _, m in s.weights), world, rank) if rows else None
+                    pipe.solve_site(s, p.value, weights[l], outputs[l], ctx=C.c_void_p(self.cs), rows=shard)
                 if after_solve is not None:
                     after_solve(l)
                 done = torch.cuda.Event()
@@ -474,14 +501,17 @@ class _Overlap:
                     p = C.c_void_p()
                     _lib.call("llmc_hessian_data", C.c_void_p(sets[b][s.name]), C.byref(p))
                     h = torch.as_tensor(_HView(p.value, s.d), device=pipe.device)
-                    works.append(dist.reduce(h, dst=layer_owner(l, world), op=dist.ReduceOp.SUM, group=group,
-                                             async_op=True))
+                    if rows:
+                        works.append(dist.all_reduce(h, op=dist.ReduceOp.SUM, group=group, async_op=True))
+                    else:
+                        works.append(dist.reduce(h, dst=layer_owner(l, world), op=dist.ReduceOp.SUM, group=group,
+                                                 async_op=True))
             with torch.cuda.stream(self.sc):
                 for w in works:
                     w.wait()
                 rd = torch.cuda.Event()
                 rd.record(self.sc)
-            if layer_owner(l, world) == rank:
+            if rows or layer_owner(l, world) == rank:
                 queue.append((i, l, b, rd))
             else:
                 released[b] = rd
