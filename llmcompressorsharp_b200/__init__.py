@@ -20,5 +20,6 @@ from .sparsegpt import SparseGPTConfig, SparseGPTModifier, sparsegpt_prune_u
 from .awq import AWQConfig, AWQModifier, awq_search, scale_apply
 from .session import (CompressionSession, CompressionState, ModifierBase, ModifierLifecycleError, SessionStatus,
                       TargetMatcher)
+from .output import CompressedTensorsWriter, SafetensorsWriter
 
 __all__ = [n for n in dir() if not n.startswith("_")]
