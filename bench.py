@@ -47,9 +47,11 @@ def parse():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["gptq", "sparsegpt", "solve", "rtn", "smoothquant", "awq"], default="gptq",
+    p.add_argument("--workload", choices=["gptq", "sparsegpt", "solve", "smollm", "rtn", "smoothquant", "awq"],
+                   default="gptq",
                    help="gptq: the GPTQ W4A16 job (default); sparsegpt: the same job pruning 2:4 with SparseGPT; "
-                        "solve: the job's factor + GPTQ solve alone, Hessians given; "
+                        "solve: the job's factor + GPTQ solve alone, Hessians given; smollm: GPTQ W4A16 of a "
+                        "SmolLM2-135M-shaped fp32 model driven by its calibration forward (128 x 512 tokens); "
                         "rtn: RTN W4A16 g128 + min-max observer passes over the Llama-3-8B Linear weights; "
                         "smoothquant: SmoothQuant (alpha 0.5) + W8A8 weights on a Llama-2-7B shape; awq: AWQ "
                         "20-point grid search + scale apply on Llama-3-8B layers")
@@ -603,6 +605,165 @@ def run_solve(args):
     pipe.close()
 
 
+SMOL = {"seqs": 128, "seq_len": 512, "batch": 16}
+
+
+def _smol_layer_flops(shape) -> float:
+    """fp32 algorithmic FLOP of one SmolLM2 layer's GPTQ job: Hessians d(d+1)T of the four
+    distinct inputs, the damped factor (2/3)d^3 per input, the GPTQ rank updates m d^2 per weight."""
+    T = SMOL["seqs"] * SMOL["seq_len"]
+    h, i = shape.hidden, shape.intermediate
+    kv = shape.kv_heads * shape.head_dim
+    hess = (3 * h * (h + 1) + i * (i + 1)) * T
+    factor = (3 * h ** 3 + i ** 3) * 2 / 3
+    solve = (h + 2 * kv + h + 2 * i) * h * h + h * i * i
+    return hess + factor + solve
+
+
+def smol_cpu_sample(threads: int):
+    """The oracle (and the torch CPU forward) on one decoder layer of the SmolLM2 job: the
+    layer's forward and its four Hessians over 8,192 of the 65,536 tokens (scaled x8), the
+    four factorisations and the seven GPTQ solves in full; x30 layers.  Returns (seconds for
+    the whole job, description)."""
+    import torch
+
+    from llmcompressorsharp_b200.calibration import SHAPES, LlamaForCalibration
+    from oracle import gptq as o_gptq, hessian as o_hess
+
+    torch.set_num_threads(threads)
+    shape = SHAPES["smollm2-135m"]
+    one = type(shape)(**{**shape.__dict__, "layers": 1})
+    model = LlamaForCalibration(one, dtype=torch.float32, seed=0)
+    layer = model.model.layers[0]
+    sample = 8192
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(sample // 512, 512, shape.hidden, generator=g)
+    acts = {}
+    def keep(name):
+        def hook(mod, inp, out):
+            acts.setdefault(name, inp[0])
+        return hook
+
+    hooks = [m.register_forward_hook(keep(n)) for n, m in layer.named_modules() if isinstance(m, torch.nn.Linear)]
+    cos, sin = model.rope_tables(512, torch.float32)
+    t = time.perf_counter()
+    with torch.no_grad():
+        layer(x, cos, sin)
+    t_fwd = time.perf_counter() - t
+    for hk in hooks:
+        hk.remove()
+    sites = {"self_attn.q_proj": ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"],
+             "self_attn.o_proj": ["self_attn.o_proj"], "mlp.gate_proj": ["mlp.gate_proj", "mlp.up_proj"],
+             "mlp.down_proj": ["mlp.down_proj"]}
+    cfg = o_gptq.GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128)
+    weights = dict(layer.named_modules())
+    t_h = t_f = t_q = 0.0
+    for site, names in sites.items():
+        a = acts[site].reshape(-1, acts[site].shape[-1])
+        acc = o_hess.HessianAccumulator(a.shape[1])
+        t = time.perf_counter()
+        acc.update(a)
+        t_h += time.perf_counter() - t
+        t = time.perf_counter()
+        u = o_hess.upper_factor(o_hess.hessian_inverse(acc.get_hessian(), 0.01))
+        t_f += time.perf_counter() - t
+        for n in names:
+            t = time.perf_counter()
+            o_gptq.gptq_quantize_u(weights[n].weight.detach(), u, cfg)
+            t_q += time.perf_counter() - t
+    scale = SMOL["seqs"] * SMOL["seq_len"] / sample
+    per_layer = (t_fwd + t_h) * scale + t_f + t_q
+    desc = (f"oracle + torch CPU forward on {threads} host threads, one SmolLM2 layer: forward {t_fwd:.2f} s and "
+            f"Hessians {t_h:.2f} s over 8,192 tokens (x8), 4 factorisations {t_f:.2f} s, 7 GPTQ solves {t_q:.2f} s; "
+            "x30 layers")
+    return per_layer * shape.layers, desc
+
+
+def run_smollm(args):
+    """--workload smollm: GPTQ W4A16 (asym int4 g128, damp 0.01, block 128) of a random-init
+    SmolLM2-135M-shaped LLaMA (30 layers, hidden 576, intermediate 1536, 9 / 3 heads, vocab
+    49152) with fp32 weights ~N(0, 0.02), calibrated on 128 x 512 uniform-random token ids run
+    through the model: the reference's own CPU-runnable configuration.  A step is one
+    CompressionSession with GPTQModifier (shared inputs deduplicated) driven by the calibration
+    forward (``calibration.drive``): every Hessian update is the fp32 3xTF32 path, then the
+    factor and the GPTQ solve of all 210 weights.  The forward is torch (cuBLAS); it is also
+    timed alone."""
+    import torch
+
+    from llmcompressorsharp_b200 import _lib
+    from llmcompressorsharp_b200.calibration import SHAPES, LlamaForCalibration, calibration_batches, drive
+    from llmcompressorsharp_b200.gptq import GPTQConfig, GPTQModifier
+    from llmcompressorsharp_b200.session import CompressionSession, CompressionState, SessionStatus
+
+    world, _, _ = dist_env()
+    if world > 1:
+        raise SystemExit("--workload smollm runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    shape = SHAPES["smollm2-135m"]
+    model = LlamaForCalibration(shape, dtype=torch.float32, device=dev, seed=0)
+    batches = list(calibration_batches(shape.vocab, SMOL["seqs"], SMOL["seq_len"], SMOL["batch"], seed=1, device=dev))
+    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128,
+                     dampening_frac=0.01)
+
+    def step():
+        state = CompressionState(model.linear_weights())
+        state.named_modules = model.linear_modules()
+        session = CompressionSession([GPTQModifier(cfg, share_inputs=True)])
+        if session.run(state, drive(model, batches)) != SessionStatus.COMPLETED:
+            raise RuntimeError(f"GPTQ session failed: {session.failure!r}")
+        return state
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for b in batches:
+        model(b)
+    f1.record()
+    torch.cuda.synchronize()
+    fwd_ms = f0.elapsed_time(f1)
+    launches0 = _lib.launch_count(0)
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        state = step()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = _lib.launch_count(0) - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    codes = sum(1 for e in state.compressed.values() if e.get("codes") is not None)
+    flops = _smol_layer_flops(shape) * shape.layers
+    _, sustained, _, src = peaks()
+    peak = sustained / 2 / 3
+    achieved = flops / ((ms - fwd_ms) * 1e-3) / 1e12
+    cpu = None
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        total, desc = smol_cpu_sample(threads)
+        cpu = {"value": round(total, 1), "unit": "s", "cores": threads, "kind": "port", "sample": desc}
+    line = {"metric": "GPTQ W4A16 wall-clock s (SmolLM2-135M shape, fp32, calibration forward included)",
+            "value": round(ms / 1e3, 4), "unit": "s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "GPTQ W4A16 asym g128 damp 0.01 block 128 of a random-init SmolLM2-135M-shaped "
+                                   "LLaMA (30 layers, hidden 576, intermediate 1536, 9/3 heads), fp32 weights "
+                                   "N(0, 0.02), 128 x 512 uniform-random token ids through the model in batches of 16",
+                       "weights_quantised": codes, "l2": "weights (0.5 GB fp32) and activations larger than L2"},
+            "forward_ms": round(fwd_ms, 2),
+            "roofline": {"kernel": "whole step less the forward: fp32 Hessians (3xTF32 gemm_tc2 with token splits), "
+                                   "factorisations, GPTQ solves", "bound": "tensor", "achieved": round(achieved, 1),
+                         "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 3),
+                         "peak_note": f"{src} sustained bf16 / 2 (tf32 rate) / 3 (3xTF32 MMAs per fp32 product)",
+                         "algorithmic": "Hessians d(d+1)T + factors (2/3)d^3 + GPTQ m d^2, fp32", "traffic": None},
+            "cpu_baseline": cpu, "e2e": None, "gpu_launches": launches, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def run_rtn(args):
     """RTN W4A16 (asym int4, group 128) quantise+pack and a group-128 min-max observer pass
     over every Linear weight of a Llama-3-8B-shaped model (224 bf16 weights, 7.0 G params),
@@ -900,6 +1061,9 @@ def main():
         return
     if args.workload == "solve":
         run_solve(args)
+        return
+    if args.workload == "smollm":
+        run_smollm(args)
         return
     run_ours(args)
 

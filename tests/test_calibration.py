@@ -1,0 +1,101 @@
+"""The calibration forward on CPU: a small random-initialised LLaMA, its module names, and
+``drive`` feeding hooks inside a CompressionSession (a recording accumulator stands in for
+the device Hessian)."""
+
+import torch
+
+from llmcompressorsharp_b200.calibration import SHAPES, LlamaForCalibration, LlamaShape, calibration_batches, drive
+from llmcompressorsharp_b200.hessian import ActivationHookManager
+from llmcompressorsharp_b200.session import CompressionSession, CompressionState, ModifierBase
+
+TINY = LlamaShape(hidden=64, intermediate=96, heads=4, kv_heads=2, layers=2, vocab=101)
+
+
+def test_presets_match_the_job_shapes():
+    s = SHAPES["llama-3-8b"]
+    assert (s.hidden, s.intermediate, s.heads, s.kv_heads, s.layers) == (4096, 14336, 32, 8, 32)
+    s = SHAPES["smollm2-135m"]
+    assert (s.hidden, s.intermediate, s.heads, s.kv_heads, s.layers, s.vocab) == (576, 1536, 9, 3, 30, 49152)
+    assert SHAPES["llama-3-70b"].intermediate == 28672
+
+
+def test_model_names_shapes_and_seed():
+    m = LlamaForCalibration(TINY, dtype=torch.float32, seed=3)
+    names = sorted(m.linear_modules())
+    assert "model.layers.0.self_attn.q_proj" in names and "model.layers.1.mlp.down_proj" in names
+    assert len(names) == 7 * TINY.layers
+    w = m.linear_weights()
+    assert w["model.layers.0.self_attn.k_proj.weight"].shape == (TINY.kv_heads * TINY.head_dim, TINY.hidden)
+    assert w["model.layers.1.mlp.down_proj.weight"].shape == (TINY.hidden, TINY.intermediate)
+    again = LlamaForCalibration(TINY, dtype=torch.float32, seed=3)
+    assert all(torch.equal(a, b) for a, b in zip(w.values(), again.linear_weights().values()))
+    assert abs(float(w["model.layers.0.mlp.up_proj.weight"].std()) - 0.02) < 0.005
+
+
+def test_forward_is_causal():
+    m = LlamaForCalibration(TINY, dtype=torch.float32, seed=4)
+    ids = next(calibration_batches(TINY.vocab, 2, 12, 2, seed=5))
+    y = m(ids)
+    assert y.shape == (2, 12, TINY.hidden) and torch.isfinite(y).all()
+    ids2 = ids.clone()
+    ids2[:, 8:] = (ids2[:, 8:] + 1) % TINY.vocab
+    y2 = m(ids2)
+    assert torch.allclose(y[:, :8], y2[:, :8], atol=1e-5)
+    assert not torch.allclose(y[:, 8:], y2[:, 8:])
+
+
+def test_calibration_batches_are_seeded_and_sized():
+    a = list(calibration_batches(50, 7, 5, 3, seed=9))
+    b = list(calibration_batches(50, 7, 5, 3, seed=9))
+    assert [t.shape for t in a] == [(3, 5), (3, 5), (1, 5)]
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    assert all(int(t.min()) >= 0 and int(t.max()) < 50 for t in a)
+
+
+class _Recorder:
+    def __init__(self):
+        self.rows = 0
+        self.d = None
+
+    def update(self, x):
+        self.d = x.shape[-1]
+        self.rows += x.reshape(-1, x.shape[-1]).shape[0]
+
+
+class _RecordingModifier(ModifierBase):
+    """Attaches hooks in OnStart like GPTQModifier and checks in OnBatch that the caller's
+    forward has already fired them for the current batch."""
+
+    def __init__(self):
+        super().__init__("record")
+        self.acc = {}
+        self.seen = []
+
+    def on_start_core(self, state):
+        self.hooks = ActivationHookManager()
+        for name, mod in state.named_modules.items():
+            self.acc[name] = _Recorder()
+            self.hooks.register_for(mod, self.acc[name])
+
+    def on_batch_core(self, state):
+        self.seen.append(self.acc["model.layers.0.self_attn.q_proj"].rows)
+
+    def on_end_core(self, state):
+        self.hooks.dispose()
+
+
+def test_drive_fires_the_hooks_before_each_batch_reaches_the_session():
+    m = LlamaForCalibration(TINY, dtype=torch.float32, seed=6)
+    batches = list(calibration_batches(TINY.vocab, 5, 8, 2, seed=7))
+    state = CompressionState(m.linear_weights())
+    state.named_modules = m.linear_modules()
+    mod = _RecordingModifier()
+    session = CompressionSession([mod])
+    status = session.run(state, drive(m, batches))
+    assert status.name == "COMPLETED", session.failure
+    assert mod.seen == [16, 32, 40]  # rows seen by the time each batch reaches OnBatch (2, 2, 1 sequences of 8)
+    tokens = 5 * 8
+    for name, acc in mod.acc.items():
+        assert acc.rows == tokens, name
+        want = TINY.intermediate if name.endswith("down_proj") else TINY.hidden
+        assert acc.d == want, name
