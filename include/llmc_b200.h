@@ -105,7 +105,8 @@ llmc_status llmc_launch_count(llmc_ctx* ctx, int64_t* out);
 llmc_status llmc_hessian_create(llmc_ctx* ctx, int64_t in_features, llmc_hessian** out);
 /* Update(x), HessianAccumulator.cs:47-67: H += X^T X for X = [rows, in_features] with row
  * stride ld (elements); dtype F32/BF16/F16.  bf16/f16 run on tcgen05 tensor cores with
- * fp32 accumulation (products are exact); f32 runs an fp32 SIMT kernel. */
+ * fp32 accumulation (products are exact); f32 runs 3xTF32 on the tensor cores (in_features
+ * >= 512 and rows >= 1024) or an fp32 SIMT kernel (smaller calls). */
 llmc_status llmc_hessian_update(llmc_hessian* h, const void* x, int32_t dtype, int64_t rows, int64_t ld);
 /* GetHessian(), HessianAccumulator.cs:71-75: writes the full symmetric [d,d] fp32 to out. */
 llmc_status llmc_hessian_get(llmc_hessian* h, float* out);
@@ -120,6 +121,27 @@ llmc_status llmc_hessian_sample_count(llmc_hessian* h, int64_t* out);
 llmc_status llmc_hessian_add_samples(llmc_hessian* h, int64_t rows);
 /* Dispose(), HessianAccumulator.cs:86-93 */
 llmc_status llmc_hessian_destroy(llmc_hessian* h);
+
+/* ---- Hessian collectives over NCCL (multi-GPU: one process or thread per GPU) -------------
+ * Calibration tokens are split across ranks; the partial Hessians sum exactly
+ * (HessianAccumulator.cs:59-64 is a sum over rows).  NCCL is loaded from libnccl.so.2 at the
+ * first call (the library does not link it; a process that already loaded it shares that
+ * copy); without it these calls return LLMC_ERR_UNSUPPORTED.  `comm` is an ncclComm_t: the
+ * caller's own, or one made by llmc_nccl_comm_init.  Every rank must make the same calls in
+ * the same order. */
+#define LLMC_NCCL_UNIQUE_ID_BYTES 128
+/* ncclGetUniqueId on the root rank; the caller sends the bytes to the other ranks. */
+llmc_status llmc_nccl_unique_id(uint8_t* out, int64_t size);
+/* ncclCommInitRank on the context's device. */
+llmc_status llmc_nccl_comm_init(llmc_ctx* ctx, int32_t world, int32_t rank, const uint8_t* unique_id, int64_t size,
+                                void** comm_out);
+llmc_status llmc_nccl_comm_destroy(void* comm);
+/* H and the sample count summed over all ranks, in place on every rank (ncclAllReduce of the
+ * [d,d] fp32 matrix on the context's stream).  Synchronises the stream (the count is read back). */
+llmc_status llmc_hessian_allreduce(llmc_hessian* h, void* comm);
+/* H and the sample count summed onto `root` only (ncclReduce); other ranks keep their partial
+ * H and count.  Synchronises the stream. */
+llmc_status llmc_hessian_reduce(llmc_hessian* h, void* comm, int32_t root);
 
 /* ---- damped Cholesky inverse: HessianInverseSolver.Compute ------------------------------
  * src/LLMCompressorSharp.TorchExtensions/Hessian/HessianInverseSolver.cs:44-92 and the U

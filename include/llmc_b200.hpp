@@ -212,6 +212,10 @@ class HessianAccumulator {
         return n;
     }
     int InFeatures() const { return d_; }
+    // Multi-GPU: sum the partial H and sample counts of a token-sharded calibration set over
+    // an NCCL communicator (an ncclComm_t), on every rank or onto `root`.
+    void AllReduce(void* ncclComm) { Check(llmc_hessian_allreduce(h_, ncclComm)); }
+    void Reduce(void* ncclComm, int root) { Check(llmc_hessian_reduce(h_, ncclComm, root)); }
 
    private:
     Context* ctx_;

@@ -44,6 +44,8 @@ P = C.c_void_p
 I32, I64, F32 = C.c_int32, C.c_int64, C.c_float
 
 # name -> argtypes (every function returns llmc_status as int32)
+NCCL_UNIQUE_ID_BYTES = 128  # LLMC_NCCL_UNIQUE_ID_BYTES
+
 _SIGS = {
     "llmc_abi_version": [],
     "llmc_init": [I32, C.POINTER(P)],
@@ -60,6 +62,11 @@ _SIGS = {
     "llmc_hessian_sample_count": [P, C.POINTER(I64)],
     "llmc_hessian_add_samples": [P, I64],
     "llmc_hessian_destroy": [P],
+    "llmc_nccl_unique_id": [P, I64],
+    "llmc_nccl_comm_init": [P, I32, I32, P, I64, C.POINTER(P)],
+    "llmc_nccl_comm_destroy": [P],
+    "llmc_hessian_allreduce": [P, P],
+    "llmc_hessian_reduce": [P, P, I32],
     "llmc_chol_inverse": [P, P, I64, I64, F32, I32, P, I64, I32],
     "llmc_upper_factor": [P, P, I64, I64, P, I64],
     "llmc_gptq_quantize": [P, P, I32, I64, I64, I64, P, I64, C.POINTER(QConfig), P, I64, P, P, P],

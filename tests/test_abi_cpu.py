@@ -96,3 +96,23 @@ def test_error_mapping():
         errors.raise_for_status(10, "x")
     with pytest.raises(errors.NotPositiveDefiniteError):
         errors.raise_for_status(4, "x")
+
+
+def test_nccl_unique_id_through_the_abi():
+    """NCCL is opened at the first collective call (no link dependency); a unique id needs no
+    GPU, and a short buffer is rejected before NCCL is touched."""
+    import ctypes as C
+
+    from llmcompressorsharp_b200 import _lib
+
+    lib = _lib.load()
+    short = (C.c_uint8 * 64)()
+    assert lib.llmc_nccl_unique_id(C.cast(short, C.c_void_p), 64) == 2  # LLMC_ERR_SHAPE
+    assert "need 128" in _lib.last_error()
+    buf = (C.c_uint8 * _lib.NCCL_UNIQUE_ID_BYTES)()
+    st = lib.llmc_nccl_unique_id(C.cast(buf, C.c_void_p), len(buf))
+    if st == 3:  # LLMC_ERR_UNSUPPORTED: no libnccl.so.2 on this host
+        pytest.skip(_lib.last_error())
+    assert st == 0, _lib.last_error()
+    assert any(bytes(buf))
+    assert lib.llmc_nccl_comm_destroy(None) == 0

@@ -1,6 +1,7 @@
-"""Multi-GPU pipeline on two GPUs (skipped when fewer are visible): the layer-owner and the
-row-sharded partitions of ``GptqPipeline.run_distributed`` against a single-GPU solve of the
-same job, each rank run by torchrun (tests/mgpu_pipeline_job.py)."""
+"""Multi-GPU on two GPUs (skipped when fewer are visible), each rank run by torchrun: the
+layer-owner and the row-sharded partitions of ``GptqPipeline.run_distributed`` against a
+single-GPU solve of the same job (tests/mgpu_pipeline_job.py), and the C-ABI Hessian
+reductions over NCCL (tests/mgpu_hessian_job.py)."""
 
 import os
 import socket
@@ -28,5 +29,17 @@ def test_two_rank_pipeline_matches_single_gpu(mode):
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "tests", "mgpu_pipeline_job.py"), mode]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+
+
+@pytest.mark.gpu
+def test_two_rank_hessian_reductions_through_the_c_abi():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "mgpu_hessian_job.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
