@@ -4,8 +4,15 @@
 // header); each maps to an llmc_status and a thread-local message.
 #include "ops.h"
 
+#include <nvtx3/nvToolsExt.h>
+
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <new>
+#include <string>
+#include <vector>
 
 namespace llmc {
 
@@ -28,6 +35,59 @@ llmc_status fail(llmc_status st, const char* fmt, ...) {
     va_end(ap);
     g_err = buf;
     return st;
+}
+
+NvtxScope::NvtxScope(const char* name) { nvtxRangePushA(name); }
+NvtxScope::~NvtxScope() { nvtxRangePop(); }
+
+namespace {
+
+struct Fault {
+    std::string fn;
+    llmc_status status;
+    long long nth;  // 0: every call
+    std::atomic<long long> calls{0};
+};
+
+std::vector<Fault*>& faults() {
+    static std::vector<Fault*> list;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* env = std::getenv("LLMC_FAULT");
+        if (!env) return;
+        std::string spec(env);
+        size_t pos = 0;
+        while (pos <= spec.size()) {
+            size_t end = spec.find(',', pos);
+            if (end == std::string::npos) end = spec.size();
+            std::string item = spec.substr(pos, end - pos);
+            pos = end + 1;
+            size_t c1 = item.find(':');
+            if (c1 == std::string::npos || c1 == 0) continue;
+            size_t c2 = item.find(':', c1 + 1);
+            const long st = std::strtol(item.substr(c1 + 1, c2 == std::string::npos ? std::string::npos : c2 - c1 - 1).c_str(),
+                                        nullptr, 10);
+            const long long k = c2 == std::string::npos ? 0 : std::strtoll(item.substr(c2 + 1).c_str(), nullptr, 10);
+            if (st <= 0 || st > LLMC_ERR_OUT_OF_RANGE || k < 0) continue;
+            Fault* f = new Fault();
+            f->fn = item.substr(0, c1);
+            f->status = (llmc_status)st;
+            f->nth = k;
+            list.push_back(f);
+        }
+    });
+    return list;
+}
+
+}  // namespace
+
+llmc_status injected_fault(const char* fn) {
+    for (Fault* f : faults()) {
+        if (f->fn != fn) continue;
+        const long long n = ++f->calls;
+        if (f->nth == 0 || n == f->nth) return fail(f->status, "injected fault in %s (call %lld)", fn, n);
+    }
+    return LLMC_OK;
 }
 
 // Synchronises the stream and reports a bounded device wait that gave up (error word 2,
@@ -129,6 +189,7 @@ const char* llmc_last_error(void) { return g_err.c_str(); }
 int32_t llmc_abi_version(void) { return LLMC_ABI_VERSION; }
 
 llmc_status llmc_init(int32_t device, llmc_ctx** out) {
+    LLMC_ENTRY();
     NULL_CHECK(out, "out");
     *out = nullptr;
     int n = 0;
@@ -159,6 +220,7 @@ llmc_status llmc_init(int32_t device, llmc_ctx** out) {
 }
 
 llmc_status llmc_destroy(llmc_ctx* ctx) {
+    LLMC_ENTRY();
     if (!ctx) return LLMC_OK;
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
@@ -172,12 +234,14 @@ llmc_status llmc_destroy(llmc_ctx* ctx) {
 }
 
 llmc_status llmc_set_stream(llmc_ctx* ctx, void* stream) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
     return LLMC_OK;
 }
 
 llmc_status llmc_set_sm_limit(llmc_ctx* ctx, int32_t sms) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     if (sms < 0) return fail(LLMC_ERR_INVALID_ARG, "sm limit must be >= 0 (0 = no limit)");
     ctx->sm_limit = sms;
@@ -185,11 +249,13 @@ llmc_status llmc_set_sm_limit(llmc_ctx* ctx, int32_t sms) {
 }
 
 llmc_status llmc_sync(llmc_ctx* ctx) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     return device_error_check(ctx);
 }
 
 llmc_status llmc_launch_count(llmc_ctx* ctx, int64_t* out) {
+    LLMC_ENTRY();
     NULL_CHECK(ctx, "ctx");
     NULL_CHECK(out, "out");
     *out = ctx->launches;
@@ -198,6 +264,7 @@ llmc_status llmc_launch_count(llmc_ctx* ctx, int64_t* out) {
 
 // ---- Hessian ------------------------------------------------------------------------------
 llmc_status llmc_hessian_create(llmc_ctx* ctx, int64_t in_features, llmc_hessian** out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(out, "out");
     *out = nullptr;
@@ -219,6 +286,7 @@ llmc_status llmc_hessian_create(llmc_ctx* ctx, int64_t in_features, llmc_hessian
 }
 
 llmc_status llmc_hessian_update(llmc_hessian* h, const void* x, int32_t dtype, int64_t rows, int64_t ld) {
+    LLMC_ENTRY();
     NULL_CHECK(h, "hessian");
     llmc_ctx* ctx = h->ctx;
     CTX_CHECK(ctx);
@@ -268,6 +336,7 @@ llmc_status llmc_hessian_update(llmc_hessian* h, const void* x, int32_t dtype, i
 }
 
 llmc_status llmc_hessian_get(llmc_hessian* h, float* out) {
+    LLMC_ENTRY();
     NULL_CHECK(h, "hessian");
     CTX_CHECK(h->ctx);
     NULL_CHECK(out, "out");
@@ -276,6 +345,7 @@ llmc_status llmc_hessian_get(llmc_hessian* h, float* out) {
 }
 
 llmc_status llmc_hessian_data(llmc_hessian* h, float** out) {
+    LLMC_ENTRY();
     NULL_CHECK(h, "hessian");
     NULL_CHECK(out, "out");
     *out = h->h;
@@ -283,6 +353,7 @@ llmc_status llmc_hessian_data(llmc_hessian* h, float** out) {
 }
 
 llmc_status llmc_hessian_reset(llmc_hessian* h) {
+    LLMC_ENTRY();
     NULL_CHECK(h, "hessian");
     CTX_CHECK(h->ctx);
     LLMC_CUDA_TRY(cudaMemsetAsync(h->h, 0, (size_t)h->d * h->d * sizeof(float), h->ctx->stream));
@@ -291,6 +362,7 @@ llmc_status llmc_hessian_reset(llmc_hessian* h) {
 }
 
 llmc_status llmc_hessian_sample_count(llmc_hessian* h, int64_t* out) {
+    LLMC_ENTRY();
     NULL_CHECK(h, "hessian");
     NULL_CHECK(out, "out");
     *out = h->samples;
@@ -298,12 +370,14 @@ llmc_status llmc_hessian_sample_count(llmc_hessian* h, int64_t* out) {
 }
 
 llmc_status llmc_hessian_add_samples(llmc_hessian* h, int64_t rows) {
+    LLMC_ENTRY();
     NULL_CHECK(h, "hessian");
     h->samples += rows;
     return LLMC_OK;
 }
 
 llmc_status llmc_hessian_destroy(llmc_hessian* h) {
+    LLMC_ENTRY();
     if (!h) return LLMC_OK;
     cudaSetDevice(h->ctx->device);
     cudaStreamSynchronize(h->ctx->stream);
@@ -315,6 +389,7 @@ llmc_status llmc_hessian_destroy(llmc_hessian* h) {
 // ---- inverse ----------------------------------------------------------------------------------
 llmc_status llmc_chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, float damp, int32_t upper_only,
                               float* out, int64_t ldo, int32_t want_upper) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(H, "hessian");
     NULL_CHECK(out, "out");
@@ -323,6 +398,7 @@ llmc_status llmc_chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t 
 }
 
 llmc_status llmc_upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ldh, float* out, int64_t ldo) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(hinv, "hinv");
     NULL_CHECK(out, "out");
@@ -334,6 +410,7 @@ llmc_status llmc_upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64
 llmc_status llmc_gptq_quantize(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t m, int64_t n, int64_t ldw,
                                const float* U, int64_t ldu, const llmc_qconfig* cfg, float* wq_out, int64_t ldq,
                                uint8_t* codes_out, float* scales_out, int32_t* zps_out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(W, "weight");
     NULL_CHECK(U, "hinv");
@@ -351,6 +428,7 @@ llmc_status llmc_gptq_quantize_batch(llmc_ctx* ctx, int32_t count, const void* c
                                      const int64_t* ldw, int32_t dtype, int64_t n, const float* U, int64_t ldu,
                                      const llmc_qconfig* cfg, float* wq_out, int64_t ldq, uint8_t* codes_out,
                                      float* scales_out, int32_t* zps_out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(W, "weights");
     NULL_CHECK(m, "m");
@@ -375,6 +453,7 @@ llmc_status llmc_gptq_quantize_batch(llmc_ctx* ctx, int32_t count, const void* c
 llmc_status llmc_sparsegpt_prune(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t m, int64_t n, int64_t ldw,
                                  const float* U, int64_t ldu, const llmc_qconfig* cfg, float* out, int64_t ldo,
                                  uint8_t* mask_out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(W, "weight");
     NULL_CHECK(U, "hinv");
@@ -395,6 +474,7 @@ llmc_status llmc_sparsegpt_prune(llmc_ctx* ctx, const void* W, int32_t dtype, in
 // ---- observers ------------------------------------------------------------------------------
 llmc_status llmc_observer_minmax(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows, int64_t cols, int64_t ld,
                                  int32_t strategy, int64_t group_size, float* min_io, float* max_io, int32_t accumulate) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(x, "x");
     NULL_CHECK(min_io, "min");
@@ -415,6 +495,7 @@ llmc_status llmc_observer_minmax(llmc_ctx* ctx, const void* x, int32_t dtype, in
 
 llmc_status llmc_affine_params(llmc_ctx* ctx, const float* mins, const float* maxs, int64_t count, int32_t num_bits,
                                int32_t symmetric, float* scale_out, int32_t* zp_out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     LLMC_TRY(check_bits(num_bits));
     NULL_CHECK(mins, "mins");
@@ -428,6 +509,7 @@ llmc_status llmc_affine_params(llmc_ctx* ctx, const float* mins, const float* ma
 // ---- fake quant / RTN / packing ---------------------------------------------------------------
 llmc_status llmc_fake_quantize(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t count, float scale, int32_t zp,
                                int32_t num_bits, int32_t symmetric, void* out, int32_t* codes_out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(x, "x");
     if (!out && !codes_out) return fail(LLMC_ERR_INVALID_ARG, "out and codes_out must not both be null");
@@ -440,6 +522,7 @@ llmc_status llmc_fake_quantize(llmc_ctx* ctx, const void* x, int32_t dtype, int6
 llmc_status llmc_rtn_quantize(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t m, int64_t n, int64_t ldw,
                               const llmc_qconfig* cfg, uint8_t* codes_out, float* scales_out, int32_t* zps_out,
                               void* deq_out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(W, "weight");
     LLMC_TRY(check_qconfig(cfg, 0));
@@ -460,6 +543,7 @@ llmc_status llmc_rtn_quantize(llmc_ctx* ctx, const void* W, int32_t dtype, int64
 }
 
 llmc_status llmc_int4_pack(llmc_ctx* ctx, const int32_t* q, int64_t count, int32_t zero_point, uint8_t* packed) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(q, "q");
     NULL_CHECK(packed, "packed");
@@ -469,6 +553,7 @@ llmc_status llmc_int4_pack(llmc_ctx* ctx, const int32_t* q, int64_t count, int32
 
 llmc_status llmc_int4_unpack_dequant(llmc_ctx* ctx, const uint8_t* packed, int64_t count, float scale, int32_t zero_point,
                                      int32_t symmetric, float* out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(packed, "packed");
     NULL_CHECK(out, "out");
@@ -480,6 +565,7 @@ llmc_status llmc_int4_unpack_dequant(llmc_ctx* ctx, const uint8_t* packed, int64
 // ---- SmoothQuant / AWQ --------------------------------------------------------------------------
 llmc_status llmc_act_absmax(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows, int64_t cols, int64_t ld,
                             float* running_max, int32_t accumulate) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(x, "x");
     NULL_CHECK(running_max, "running_max");
@@ -490,6 +576,7 @@ llmc_status llmc_act_absmax(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t
 
 llmc_status llmc_smooth_apply(llmc_ctx* ctx, const float* act_max, void* smooth_w, int32_t smooth_dtype, void* balance_w,
                               int32_t balance_dtype, int64_t m, int64_t hidden, float alpha, float* s_out) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(act_max, "act_max");
     NULL_CHECK(smooth_w, "smooth weight");
@@ -501,6 +588,7 @@ llmc_status llmc_smooth_apply(llmc_ctx* ctx, const float* act_max, void* smooth_
 
 llmc_status llmc_scale_apply(llmc_ctx* ctx, const float* s, void* smooth_w, int32_t smooth_dtype, void* balance_w,
                              int32_t balance_dtype, int64_t m, int64_t hidden) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(s, "s");
     NULL_CHECK(balance_w, "balance weight");
@@ -511,6 +599,7 @@ llmc_status llmc_scale_apply(llmc_ctx* ctx, const float* s, void* smooth_w, int3
 llmc_status llmc_awq_search(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t m, int64_t n, int64_t ldw,
                             const float* act_max, int32_t n_grid, const llmc_qconfig* cfg, float* best_s,
                             double* mse_out, int32_t* best_k) {
+    LLMC_ENTRY();
     CTX_CHECK(ctx);
     NULL_CHECK(W, "weight");
     NULL_CHECK(act_max, "act_max");

@@ -31,6 +31,27 @@ llmc_status fail(llmc_status st, const char* fmt, ...);
         if (_s != LLMC_OK) return _s;                                                          \
     } while (0)
 
+// ---- entry-point guard ----------------------------------------------------------------
+// Every llmc_status entry point opens with LLMC_ENTRY():
+//  - an NVTX range named after the function (seen by nsys / ncu --nvtx, a no-op without a
+//    tool attached);
+//  - host-side fault injection for failure-path tests, read once from the environment:
+//    LLMC_FAULT="<function>:<status>[:<k>][,...]" makes <function> return <status> with the
+//    message "injected fault in <function>" on every call, or on its k-th call only (k >= 1).
+//    An injected call touches neither its arguments nor the GPU.
+struct NvtxScope {
+    explicit NvtxScope(const char* name);
+    ~NvtxScope();
+};
+llmc_status injected_fault(const char* fn);
+
+#define LLMC_ENTRY()                                        \
+    ::llmc::NvtxScope _llmc_nvtx(__func__);                 \
+    do {                                                    \
+        llmc_status _f = ::llmc::injected_fault(__func__);  \
+        if (_f != LLMC_OK) return _f;                       \
+    } while (0)
+
 }  // namespace llmc
 
 // ---- context ---------------------------------------------------------------------------

@@ -107,6 +107,7 @@ using namespace llmc;
 extern "C" {
 
 llmc_status llmc_nccl_unique_id(uint8_t* out, int64_t size) {
+    LLMC_ENTRY();
     if (!out) return fail(LLMC_ERR_INVALID_ARG, "out must not be null");
     if (size < (int64_t)sizeof(ncclUniqueId))
         return fail(LLMC_ERR_SHAPE, "unique id buffer of %lld bytes, need %zu", (long long)size, sizeof(ncclUniqueId));
@@ -120,6 +121,7 @@ llmc_status llmc_nccl_unique_id(uint8_t* out, int64_t size) {
 
 llmc_status llmc_nccl_comm_init(llmc_ctx* ctx, int32_t world, int32_t rank, const uint8_t* unique_id, int64_t size,
                                 void** comm_out) {
+    LLMC_ENTRY();
     if (!ctx || !unique_id || !comm_out) return fail(LLMC_ERR_INVALID_ARG, "ctx, unique_id and comm_out must not be null");
     *comm_out = nullptr;
     if (world < 1 || rank < 0 || rank >= world)
@@ -138,15 +140,20 @@ llmc_status llmc_nccl_comm_init(llmc_ctx* ctx, int32_t world, int32_t rank, cons
 }
 
 llmc_status llmc_nccl_comm_destroy(void* comm) {
+    LLMC_ENTRY();
     if (!comm) return LLMC_OK;
     const NcclApi* api;
     LLMC_TRY(need_nccl(&api));
     return nccl_check(api, api->comm_destroy(static_cast<ncclComm_t>(comm)), "ncclCommDestroy");
 }
 
-llmc_status llmc_hessian_allreduce(llmc_hessian* h, void* comm) { return hessian_collective(h, comm, -1); }
+llmc_status llmc_hessian_allreduce(llmc_hessian* h, void* comm) {
+    LLMC_ENTRY();
+    return hessian_collective(h, comm, -1);
+}
 
 llmc_status llmc_hessian_reduce(llmc_hessian* h, void* comm, int32_t root) {
+    LLMC_ENTRY();
     if (root < 0) return fail(LLMC_ERR_OUT_OF_RANGE, "root must be a rank (got %d)", root);
     return hessian_collective(h, comm, root);
 }

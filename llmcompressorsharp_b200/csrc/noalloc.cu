@@ -64,6 +64,7 @@ using namespace llmc;
 extern "C" llmc_status llmc_observer_minmax_tensor_noalloc(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows,
                                                           int64_t cols, int64_t ld, float* min_io, float* max_io,
                                                           int32_t accumulate) {
+    LLMC_ENTRY();
     if (!ctx) return fail(LLMC_ERR_INVALID_ARG, "context must not be null");
     if (!x) return fail(LLMC_ERR_INVALID_ARG, "x must not be null");
     if (!min_io) return fail(LLMC_ERR_INVALID_ARG, "min must not be null");
