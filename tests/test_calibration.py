@@ -99,3 +99,23 @@ def test_drive_fires_the_hooks_before_each_batch_reaches_the_session():
         assert acc.rows == tokens, name
         want = TINY.intermediate if name.endswith("down_proj") else TINY.hidden
         assert acc.d == want, name
+
+
+def test_forward_matches_the_transformers_llama():
+    """With the same weights, the calibration model's output equals transformers' LlamaModel
+    (last hidden state after the final norm), so the activations reaching the hooks are a
+    standard LLaMA's."""
+    tr = __import__("pytest").importorskip("transformers")
+    s = LlamaShape(hidden=64, intermediate=96, heads=4, kv_heads=2, layers=2, vocab=101, rope_theta=10000.0)
+    ours = LlamaForCalibration(s, dtype=torch.float32, seed=3)
+    cfg = tr.LlamaConfig(hidden_size=64, intermediate_size=96, num_attention_heads=4, num_key_value_heads=2,
+                         num_hidden_layers=2, vocab_size=101, rope_theta=10000.0, rms_norm_eps=1e-5,
+                         max_position_embeddings=128, attention_bias=False, mlp_bias=False)
+    hf = tr.LlamaModel(cfg).eval()
+    sd = {k[len("model."):]: v for k, v in ours.state_dict().items() if k.startswith("model.")}
+    hf.load_state_dict(sd, strict=True)
+    ids = next(calibration_batches(s.vocab, 2, 12, 2, seed=8))
+    with torch.no_grad():
+        a = ours(ids)
+        b = hf(input_ids=ids).last_hidden_state
+    assert torch.allclose(a, b, atol=1e-5, rtol=1e-5), float((a - b).abs().max())
