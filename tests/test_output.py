@@ -157,3 +157,24 @@ def test_entries_from_pipeline_outputs():
     assert list(e) == ["model.layers.3.mlp.gate_proj.weight"]
     assert e["model.layers.3.mlp.gate_proj.weight"]["num_bits"] == 4
     assert e["model.layers.3.mlp.gate_proj.weight"]["strategy"] == "group"
+
+
+def test_vllm_reads_the_quantization_config():
+    """vLLM's compressed-tensors config parser maps each written target to the W4A16 group
+    scheme in pack-quantized format (config only: loading weights needs a GPU)."""
+    pytest.importorskip("vllm")
+    try:
+        from vllm.model_executor.layers.quantization.compressed_tensors.compressed_tensors import (
+            CompressedTensorsConfig)
+    except Exception as e:  # noqa: BLE001 — vLLM's import can fail on hosts without its native parts
+        pytest.skip(f"vLLM compressed-tensors config unavailable: {e}")
+    entries = {f"model.layers.{i}.mlp.down_proj.weight": {"codes": torch.zeros(1), "num_bits": 4, "symmetric": False,
+                                                          "strategy": "group", "group_size": 128} for i in range(2)}
+    qc = CompressedTensorsWriter.quantization_config(entries, ignore=["lm_head"])
+    cfg = CompressedTensorsConfig.from_config(qc)
+    assert sorted(cfg.target_scheme_map) == ["model.layers.0.mlp.down_proj", "model.layers.1.mlp.down_proj"]
+    args = cfg.target_scheme_map["model.layers.0.mlp.down_proj"]["weights"]
+    strategy = getattr(args.strategy, "value", args.strategy)
+    assert (args.num_bits, args.symmetric, args.group_size, strategy) == (4, False, 128, "group")
+    assert cfg.target_scheme_map["model.layers.0.mlp.down_proj"]["format"] == "pack-quantized"
+    assert cfg.ignore == ["lm_head"]
