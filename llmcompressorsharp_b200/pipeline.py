@@ -345,7 +345,8 @@ class _Overlap:
         _lib.call("llmc_set_sm_limit", C.c_void_p(self.ch), C.c_int32(limit))
         # The solve context shares the GPU: its tensor-core GEMMs launch one CTA per tile, which
         # start on the reserved SMs and on any SM a finishing Hessian launch frees.
-        _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(max(1, int(reserve_sms))))
+        self.solve_sms = max(1, int(reserve_sms))
+        _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(self.solve_sms))
         self.h = [{}, {}]
         for b in range(2):
             for s in pipe.sites:
@@ -418,7 +419,13 @@ class _Overlap:
                 solve(pending)  # may block the host (factor flags) while the Hessian stream runs on
             pending = (l, b, acc_done)
         if pending is not None:
-            solve(pending)
+            # The last layer's solve waits for the last accumulation, so nothing else runs beside
+            # it: lift the solve context's SM limit (persistent grids over the whole GPU) for it.
+            _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(0))
+            try:
+                solve(pending)
+            finally:
+                _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(self.solve_sms))
         cur.wait_stream(self.sh)
         cur.wait_stream(self.ss)
 
