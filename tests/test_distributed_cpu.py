@@ -179,3 +179,35 @@ def test_row_sharded_solve_matches_whole_solve(tmp_path):
             assert (codes == full[i][1][a:a + m]).float().mean() >= 0.999
             assert np.array_equal(scales.numpy(), np.asarray(full[i][2])[a:a + m])
     assert all(bool((c == 1).all()) for c in covered)
+
+
+def _dropout_worker(rank, world, port, out_dir):
+    """Rank 1 leaves between steps (before the reduction); rank 0 must get an error from its
+    next collective instead of waiting for ever."""
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    dist.barrier()
+    if rank == 1:
+        return  # leaves without joining the reduction (no collective in flight)
+    hbufs = {0: {"attn_in": torch.ones(8, 8)}}
+    t = time.monotonic()
+    try:
+        reduce_hessians(hbufs, ["attn_in"], [0], world)
+        outcome = "completed"
+    except Exception as e:  # noqa: BLE001 — any error from the collective is the expected outcome
+        outcome = f"error {type(e).__name__}"
+    with open(os.path.join(out_dir, "dropout.txt"), "w") as f:
+        f.write(f"{outcome} {time.monotonic() - t:.1f}")
+
+
+def test_a_rank_that_leaves_fails_the_next_reduction_within_the_timeout(tmp_path):
+    """Failure detection on the host: with a short process-group timeout, the surviving rank's
+    Hessian reduction ends with an error (gloo ranks on CPU; nothing runs on a GPU)."""
+    world = 2
+    mp.spawn(_dropout_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    outcome, secs = (tmp_path / "dropout.txt").read_text().rsplit(" ", 1)
+    assert outcome.startswith("error"), outcome
+    assert float(secs) < 60
