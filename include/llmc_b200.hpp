@@ -435,6 +435,179 @@ class Int4PackedTensor {
     DeviceTensor packed_;  // (n + 1) / 2 bytes (allocated as 2-byte elements)
 };
 
+// ---- raw device bytes (codes, masks) ------------------------------------------------------------
+class DeviceBytes {
+   public:
+    explicit DeviceBytes(size_t n) : n_(n) {
+        if (n_) CheckCuda(cudaMalloc(&data_, n_), "cudaMalloc");
+    }
+    ~DeviceBytes() {
+        if (data_) cudaFree(data_);
+    }
+    DeviceBytes(const DeviceBytes&) = delete;
+    DeviceBytes& operator=(const DeviceBytes&) = delete;
+    void* data() const { return data_; }
+    size_t size() const { return n_; }
+    template <typename T>
+    std::vector<T> ToHost() const {
+        std::vector<T> out(n_ / sizeof(T));
+        if (n_) CheckCuda(cudaMemcpy(out.data(), data_, out.size() * sizeof(T), cudaMemcpyDeviceToHost), "cudaMemcpy");
+        return out;
+    }
+
+   private:
+    void* data_ = nullptr;
+    size_t n_;
+};
+
+// ---- RTN (RtnModifier.cs:44-122 for one weight) -----------------------------------------------
+struct RtnConfig {
+    int NumBits = 4;
+    bool Symmetric = true;
+    QuantizationStrategy Strategy = QuantizationStrategy::PerChannel;
+    int GroupSize = 128;
+
+    llmc_qconfig ToC() const {
+        llmc_qconfig c{};
+        c.num_bits = NumBits;
+        c.symmetric = Symmetric ? 1 : 0;
+        c.strategy = (int32_t)Strategy;
+        c.group_size = GroupSize;
+        c.block_size = 128;
+        return c;
+    }
+};
+
+struct RtnResult {
+    DeviceTensor Dequantized;           // the weight's dtype, like the reference's replacement weight
+    std::vector<uint8_t> Codes;         // bits <= 4: (q - zp) & 0xF, two per byte, even column high
+    std::vector<float> Scales;          // TENSOR: 1, CHANNEL: m, GROUP: m * ceil(n / GroupSize)
+    std::vector<int32_t> ZeroPoints;
+};
+
+struct Rtn {
+    static RtnResult Quantize(Context& ctx, const DeviceTensor& weight, const RtnConfig& config) {
+        if (weight.dim() != 2) throw ArgumentException("weight must be 2-D");
+        const int64_t m = weight.shape()[0], n = weight.shape()[1];
+        const llmc_qconfig c = config.ToC();
+        const int64_t per_row =
+            config.Strategy == QuantizationStrategy::Group ? (n + config.GroupSize - 1) / config.GroupSize : 1;
+        const int64_t nparams = config.Strategy == QuantizationStrategy::PerTensor ? 1 : m * per_row;
+        const int64_t row_bytes = config.NumBits <= 4 ? (n + 1) / 2 : n;
+        DeviceBytes codes((size_t)(m * row_bytes)), scales((size_t)nparams * 4), zps((size_t)nparams * 4);
+        RtnResult r{DeviceTensor(weight.shape(), weight.dtype()), {}, {}, {}};
+        Check(llmc_rtn_quantize(ctx.get(), weight.data(), (int32_t)weight.dtype(), m, n, n, &c,
+                                static_cast<uint8_t*>(codes.data()), static_cast<float*>(scales.data()),
+                                static_cast<int32_t*>(zps.data()), r.Dequantized.data()));
+        r.Codes = codes.ToHost<uint8_t>();
+        r.Scales = scales.ToHost<float>();
+        r.ZeroPoints = zps.ToHost<int32_t>();
+        return r;
+    }
+};
+
+// ---- SmoothQuant (SmoothQuantModifier.cs:71-182) -----------------------------------------------
+struct SmoothQuant {
+    // UpdateActivationMax: runningMax[cols] = max(runningMax, max over rows |x|) (accumulate = false
+    // overwrites); x is [-1, cols].
+    static void UpdateActivationMax(Context& ctx, const DeviceTensor& x, DeviceTensor& runningMax, bool accumulate) {
+        const int64_t cols = x.last();
+        if (runningMax.numel() != cols || runningMax.dtype() != DType::Float32)
+            throw ArgumentException("running max must be fp32 [cols]");
+        Check(llmc_act_absmax(ctx.get(), x.data(), (int32_t)x.dtype(), x.numel() / cols, cols, cols,
+                              static_cast<float*>(runningMax.data()), accumulate ? 1 : 0));
+    }
+    // ApplyMapping: smooth /= s, balance *= s in place; returns s.
+    static std::vector<float> ApplyMapping(Context& ctx, const DeviceTensor& actMax, DeviceTensor& smooth,
+                                           DeviceTensor& balance, float alpha) {
+        if (balance.dim() != 2 || smooth.dim() != 1 || smooth.numel() != balance.last() || actMax.numel() != balance.last())
+            throw ArgumentException("smooth must be 1-D and balance 2-D with matching last dims");
+        DeviceTensor s({balance.last()}, DType::Float32);
+        Check(llmc_smooth_apply(ctx.get(), static_cast<const float*>(actMax.data()), smooth.data(),
+                                (int32_t)smooth.dtype(), balance.data(), (int32_t)balance.dtype(), balance.shape()[0],
+                                balance.last(), alpha, static_cast<float*>(s.data())));
+        return s.ToHost();
+    }
+};
+
+// ---- SparseGPT (plan phase-4c-sparsegpt.md, in GPTQ's U-factor form) --------------------------
+struct SparseGPTResult {
+    DeviceTensor Pruned;            // fp32 [m, n]
+    std::vector<uint8_t> Mask;      // 1 = kept
+};
+
+struct SparseGPT {
+    // maskN:maskM = 0:0 for unstructured pruning at `sparsity`, e.g. 2:4 for the N:M structure.
+    static SparseGPTResult Prune(Context& ctx, const DeviceTensor& weight, const DeviceTensor& upper, float sparsity,
+                                 int maskN, int maskM, int blockSize = 128) {
+        if (weight.dim() != 2) throw ArgumentException("weight must be 2-D");
+        const int64_t m = weight.shape()[0], n = weight.shape()[1];
+        llmc_qconfig c{};
+        c.num_bits = 8;
+        c.symmetric = 1;
+        c.block_size = blockSize;
+        c.sparsity = sparsity;
+        c.mask_n = maskN;
+        c.mask_m = maskM;
+        SparseGPTResult r{DeviceTensor({m, n}, DType::Float32), {}};
+        DeviceBytes mask((size_t)(m * n));
+        Check(llmc_sparsegpt_prune(ctx.get(), weight.data(), (int32_t)weight.dtype(), m, n, n,
+                                   static_cast<const float*>(upper.data()), n, &c, static_cast<float*>(r.Pruned.data()), n,
+                                   static_cast<uint8_t*>(mask.data())));
+        r.Mask = mask.ToHost<uint8_t>();
+        return r;
+    }
+};
+
+// ---- AWQ grid search (algorithm-mapping.md:214-249) --------------------------------------------
+struct AwqResult {
+    std::vector<float> BestScale;   // per input channel
+    std::vector<double> Mse;        // per grid point
+    int BestK = 0;                  // 1-based grid index
+};
+
+struct AWQ {
+    static AwqResult Search(Context& ctx, const DeviceTensor& weight, const DeviceTensor& actMax, int nGrid,
+                            const RtnConfig& quant) {
+        if (weight.dim() != 2) throw ArgumentException("weight must be 2-D");
+        const int64_t m = weight.shape()[0], n = weight.shape()[1];
+        const llmc_qconfig c = quant.ToC();
+        DeviceBytes s((size_t)n * 4), mse((size_t)nGrid * 8);
+        AwqResult r;
+        int32_t k = 0;
+        Check(llmc_awq_search(ctx.get(), weight.data(), (int32_t)weight.dtype(), m, n, n,
+                              static_cast<const float*>(actMax.data()), nGrid, &c, static_cast<float*>(s.data()),
+                              static_cast<double*>(mse.data()), &k));
+        r.BestScale = s.ToHost<float>();
+        r.Mse = mse.ToHost<double>();
+        r.BestK = k;
+        return r;
+    }
+};
+
+// ---- NCCL communicator for the Hessian collectives ---------------------------------------------
+class NcclCommunicator {
+   public:
+    // Rank 0 makes the id and sends it to the other ranks by the host's own channel.
+    static std::vector<uint8_t> UniqueId() {
+        std::vector<uint8_t> id(LLMC_NCCL_UNIQUE_ID_BYTES);
+        Check(llmc_nccl_unique_id(id.data(), (int64_t)id.size()));
+        return id;
+    }
+    NcclCommunicator(Context& ctx, int world, int rank, const std::vector<uint8_t>& id) {
+        Check(llmc_nccl_comm_init(ctx.get(), world, rank, id.data(), (int64_t)id.size(), &comm_));
+    }
+    ~NcclCommunicator() {
+        if (comm_) llmc_nccl_comm_destroy(comm_);
+    }
+    NcclCommunicator(const NcclCommunicator&) = delete;
+    NcclCommunicator& operator=(const NcclCommunicator&) = delete;
+    void* get() const { return comm_; }
+
+   private:
+    void* comm_ = nullptr;
+};
+
 }  // namespace llmcs
 
 #endif  // LLMC_B200_HPP
