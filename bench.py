@@ -448,48 +448,61 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
 
 
 # ------------------------------------------------------------------------------ CPU side
-def cpu_sample_seconds(threads: int, sample_tokens: int = 4096):
+def cpu_sample_seconds(threads: int, scale: float = 1.0):
     """Times the oracle (a PyTorch-CPU restatement of the reference's TorchSharp path) on a
-    bounded sample of the job and extrapolates to the full job linearly in tokens, layers
-    and weights.  Returns (seconds for the full job, description)."""
+    bounded sample of the job and extrapolates to the whole job as the reference runs it:
+    GPTQModifier keeps one accumulator, one HessianInverseSolver.Compute and one
+    GptqBlockQuantizer.Quantize per targeted weight (GPTQModifier.cs:73-94,119-136), so a
+    Llama-3-8B layer costs 6 Hessians and factorisations at d = hidden, 1 at d = intermediate,
+    and 7 solves.  Hessian time is linear in tokens (timed on a token sample at both widths);
+    the factorisation is timed at d = hidden and scaled by d^3; each solve is fitted as
+    a + b*m per width from two row counts (the column loop has a per-column cost that does not
+    grow with m).  ``scale`` < 1 shrinks the samples (warm-up).  Returns (seconds, description)."""
     import torch
 
     from oracle import gptq as o_gptq, hessian as o_hess
 
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(0)
-    d = MODEL["hidden"]
-    x = torch.randn(sample_tokens, d, generator=g).to(torch.bfloat16)
-    acc = o_hess.HessianAccumulator(d)
-    t = time.perf_counter()
-    acc.update(x)
-    t_h = time.perf_counter() - t  # d=4096 site, sample_tokens rows
-    h = acc.get_hessian()
-    t = time.perf_counter()
-    hinv = o_hess.hessian_inverse(h, 0.01)
-    u = o_hess.upper_factor(hinv)
-    t_chol = time.perf_counter() - t  # d = 4096
-    m_s = 256
-    w = (torch.randn(m_s, d, generator=g) * 0.02).to(torch.bfloat16)
-    cfg = o_gptq.GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128)
-    t = time.perf_counter()
-    o_gptq.gptq_quantize_u(w, u, cfg)
-    t_gptq = time.perf_counter() - t  # 256 x 4096
     hid, inter, L, T = MODEL["hidden"], MODEL["intermediate"], MODEL["layers"], 512 * 2048
-    # Hessian: 3 sites of width hidden + 1 of width intermediate, time ~ d^2 T
-    hess = t_h * (T / sample_tokens) * (3 + (inter / hid) ** 2) * L
-    chol = t_chol * (3 + (inter / hid) ** 3) * L
-    # GPTQ column loop: per-column vector ops over m rows; time ~ n * (c0 + c1 * m) ~ m * n for
-    # large m; tail GEMMs ~ m n^2.  Scale by m*n (lower bound for the n^2 tail).
     kv = MODEL["kv_heads"] * (hid // MODEL["heads"])
-    mn = (2 * hid * hid + 2 * kv * hid + 2 * inter * hid) + inter * hid * (inter / hid)
-    gptq_t = t_gptq * (mn / (m_s * d)) * L
-    total = hess + chol + gptq_t
-    desc = (f"oracle on {threads} host threads: Hessian of {sample_tokens} tokens at d={d} ({t_h:.2f} s), damped "
-            f"Cholesky inverse + U at d={d} ({t_chol:.2f} s), GPTQ of a {m_s}x{d} weight ({t_gptq:.2f} s); "
-            "extrapolated to 32 layers x 4 sites x 1,048,576 tokens (d^2 T), 128 factorisations (d^3) and 224 "
-            "weights (m n^2 tail at n=14336 scaled from m n) — a lower bound on the reference, whose per-row "
-            "P/Invoke loops this vectorised restatement does not pay")
+
+    def hess_per_token(d, tokens):
+        x = torch.randn(tokens, d, generator=g).to(torch.bfloat16)
+        acc = o_hess.HessianAccumulator(d)
+        t = time.perf_counter()
+        acc.update(x)
+        return (time.perf_counter() - t) / tokens, acc.get_hessian()
+
+    tok_h, tok_i = max(256, int(8192 * scale)), max(256, int(2048 * scale))
+    ph_h, h = hess_per_token(hid, tok_h)
+    ph_i, _ = hess_per_token(inter, tok_i)
+    t = time.perf_counter()
+    u = o_hess.upper_factor(o_hess.hessian_inverse(h, 0.01))
+    t_f = time.perf_counter() - t  # HessianInverseSolver.Compute + U at d = hidden
+    cfg = o_gptq.GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128, block_size=128)
+
+    def solve_fit(n, upper, m0, m1):
+        ts = []
+        for m in (m0, m1):
+            w = (torch.randn(m, n, generator=g) * 0.02).to(torch.bfloat16)
+            t = time.perf_counter()
+            o_gptq.gptq_quantize_u(w, upper, cfg)
+            ts.append(time.perf_counter() - t)
+        b = max(0.0, (ts[1] - ts[0]) / (m1 - m0))
+        return max(0.0, ts[0] - b * m0), b, ts
+
+    a_h, b_h, ts_h = solve_fit(hid, u, 64, 256)
+    a_i, b_i, ts_i = solve_fit(inter, torch.eye(inter), 32, 128)  # timing does not depend on U's values
+    solves = sum(a_h + b_h * m for m in (hid, kv, kv, hid, inter, inter)) + a_i + b_i * hid
+    per_layer = T * (6 * ph_h + ph_i) + t_f * (6 + (inter / hid) ** 3) + solves
+    total = per_layer * L
+    desc = (f"oracle on {threads} host threads, as the reference runs it (one accumulator, factorisation and "
+            f"solve per weight, 7 per layer): Hessians timed on {tok_h} tokens at d={hid} and {tok_i} at "
+            f"d={inter}, Hessian inverse + U at d={hid} ({t_f:.2f} s, d^3 for d={inter}), GPTQ fitted a + b*m "
+            f"from m=64/256 at n={hid} ({ts_h[0]:.2f}/{ts_h[1]:.2f} s) and m=32/128 at n={inter} "
+            f"({ts_i[0]:.2f}/{ts_i[1]:.2f} s); x32 layers, 1,048,576 tokens. A lower bound on the reference, whose "
+            "per-row P/Invoke loops this vectorised restatement does not pay")
     return total, desc
 
 
@@ -509,7 +522,7 @@ def run_reference(args):
     desc = ""
     threads = os.cpu_count() or 1
     if args.warmup > 0:
-        cpu_sample_seconds(threads, 1024)  # warm the CPU kernels once; a step is already seconds long
+        cpu_sample_seconds(threads, 0.125)  # warm the CPU kernels once; a step is already seconds long
     for _ in range(args.steps):
         total, desc = cpu_sample_seconds(threads)
         steps.append(total)
