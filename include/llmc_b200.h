@@ -228,6 +228,14 @@ llmc_status llmc_affine_params(llmc_ctx* ctx, const float* mins, const float* ma
  * (Int4PackedTensor.FromFloat, Int4PackedTensor.cs:79-100, before the zero-point shift). */
 llmc_status llmc_fake_quantize(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t count, float scale, int32_t zp,
                                int32_t num_bits, int32_t symmetric, void* out, int32_t* codes_out);
+/* MSEObserver.GetQuantParams (MSEObserver.cs:50-93) over `count` elements of x: absMax = max|x|;
+ * for i = 1..grid_points the symmetric range +-absMax*i/grid_points gives (scale, zp) through
+ * ComputeAffineParams, and mse_i = mean((x - FQ(x))^2) with the FakeQuantize op chain in x's dtype;
+ * the first minimum wins (absMax == 0: scale 1, zp 0).  scale_out, zp_out and mse_out (optional,
+ * [grid_points], NaN for a skipped candidate) are HOST pointers; synchronises the stream.
+ * grid_points < 2 -> OUT_OF_RANGE; count == 0 -> NO_SAMPLES. */
+llmc_status llmc_observer_mse(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t count, int32_t grid_points,
+                              int32_t num_bits, int32_t symmetric, float* scale_out, int32_t* zp_out, double* mse_out);
 /* RtnModifier.OnEndCore (RtnModifier.cs:44-122) for one weight [m,n]: observer -> params ->
  * fake-quant, one pass over W for CHANNEL/GROUP (TENSOR adds one reduction pass).  Outputs as
  * llmc_gptq_quantize; deq_out (optional) has W's dtype like the reference's result. */

@@ -12,7 +12,7 @@ from .errors import (ArgumentError, ArgumentOutOfRangeError, CudaError, InvalidO
                      NotPositiveDefiniteError, NotSupportedError, ShapeError)
 from .hessian import ActivationHookManager, HessianAccumulator, HessianInverseSolver, upper_factor
 from .quantization import (FakeQuantize, GroupMinMaxObserver, Int4PackedTensor, MinMaxObserver,
-                           MovingAverageMinMaxObserver, PerChannelMinMaxObserver, affine_params)
+                           MovingAverageMinMaxObserver, MSEObserver, PerChannelMinMaxObserver, affine_params)
 from .gptq import GPTQConfig, GPTQModifier, GptqBlockQuantizer, GptqResult, gptq_quantize_u
 from .rtn import RtnConfig, RtnModifier, rtn_quantize
 from .smoothquant import SmoothQuantConfig, SmoothQuantMapping, SmoothQuantModifier, act_absmax, smooth_apply

@@ -75,6 +75,7 @@ _SIGS = {
     "llmc_observer_minmax": [P, P, I32, I64, I64, I64, I32, I64, P, P, I32],
     "llmc_observer_minmax_tensor_noalloc": [P, P, I32, I64, I64, I64, P, P, I32],
     "llmc_affine_params": [P, P, P, I64, I32, I32, P, P],
+    "llmc_observer_mse": [P, P, I32, I64, I32, I32, I32, C.POINTER(F32), C.POINTER(I32), P],
     "llmc_fake_quantize": [P, P, I32, I64, F32, I32, I32, I32, P, P],
     "llmc_rtn_quantize": [P, P, I32, I64, I64, I64, C.POINTER(QConfig), P, P, P, P],
     "llmc_int4_pack": [P, P, I64, I32, P],

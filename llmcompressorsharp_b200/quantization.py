@@ -236,6 +236,47 @@ class MovingAverageMinMaxObserver(Observer):
         self._has = False
 
 
+class MSEObserver(Observer):
+    """MSEObserver.cs:17-124: keeps the calibration samples (device copies) and, in
+    get_quant_params, grid-searches the symmetric ranges +-absMax*i/G for the (scale, zero-point)
+    with the lowest fake-quantisation MSE (llmc_observer_mse: one device pass adds the squared
+    errors of every candidate; the candidates and the choice are the reference's scalar math)."""
+
+    strategy = "tensor"
+
+    def __init__(self, grid_points: int = 100, device=None):
+        if grid_points < 2:
+            raise ArgumentOutOfRangeError("gridPoints must be >= 2.")
+        self.grid_points = grid_points
+        self.device = torch.device(device) if device is not None else None
+        self._samples: list[torch.Tensor] = []
+        self.last_mse = None
+
+    def update(self, x: torch.Tensor) -> None:
+        if x is None:
+            raise ArgumentError("x must not be null")
+        if self.device is None:
+            self.device = target_device(x)
+        self._samples.append(to_device(supported_dtype(x.detach()), self.device).flatten().clone())
+
+    def get_quant_params(self, num_bits: int, symmetric: bool):
+        if not self._samples:
+            raise InvalidOperationError("MSEObserver has no calibration samples. Call Update before GetQuantParams.")
+        _check_bits(num_bits)
+        flat = torch.cat(self._samples) if len(self._samples) > 1 else self._samples[0]
+        scale, zp = C.c_float(), C.c_int32()
+        mse = np.empty(self.grid_points, dtype=np.float64)
+        _lib.call("llmc_observer_mse", C.c_void_p(ctx(self.device)), _lib.ptr(flat), _lib.dtype_code(flat.dtype),
+                  C.c_int64(flat.numel()), C.c_int32(self.grid_points), C.c_int32(num_bits), C.c_int32(int(symmetric)),
+                  C.byref(scale), C.byref(zp), C.c_void_p(mse.ctypes.data))
+        self.last_mse = mse
+        return float(scale.value), int(zp.value)
+
+    def reset(self) -> None:
+        self._samples.clear()
+        self.last_mse = None
+
+
 class Int4PackedTensor:
     """Int4PackedTensor.cs:17-162: codes q - zp stored two per byte, even index in the high
     nibble.  The bytes live on the device."""

@@ -453,6 +453,54 @@ def test_fake_quantize_kats_and_ste():  # FakeQuantizeFunctionTests.cs
         FakeQuantize.apply(torch.ones(2, device=DEV), 1.0, 0, 1, True)
 
 
+def test_mse_observer_kats():  # MSEObserverTests.cs:38-66
+    from llmcompressorsharp_b200 import MinMaxObserver, MSEObserver
+    from llmcompressorsharp_b200.errors import ArgumentOutOfRangeError, InvalidOperationError
+
+    o = MSEObserver(80)
+    o.update(torch.tensor([-3.0, -2.5, -1.0, 0.0, 1.0, 2.5, 3.0], device=DEV))
+    s, z = o.get_quant_params(8, True)
+    assert 0.001 <= s <= 0.5 and z == 0
+    vals = torch.tensor([i / 98 for i in range(99)] + [1.5], device=DEV)
+    mse, mm = MSEObserver(100), MinMaxObserver()
+    mse.update(vals)
+    mm.update(vals)
+    assert mse.get_quant_params(4, True)[0] < mm.get_quant_params(4, True)[0]
+    o = MSEObserver()
+    o.update(torch.zeros(5, device=DEV))
+    assert o.get_quant_params(8, True) == (1.0, 0)
+    with pytest.raises(InvalidOperationError):
+        MSEObserver().get_quant_params(8, True)
+    with pytest.raises(ArgumentOutOfRangeError):
+        MSEObserver(1)
+
+
+@pytest.mark.parametrize("n", [1000, 100003])
+@pytest.mark.parametrize("bits,sym", [(8, True), (4, True), (4, False)])
+def test_mse_observer_matches_oracle(n, bits, sym):
+    """fp32 samples (two update calls): the grid search picks the oracle's (scale, zero-point)
+    and the per-candidate MSEs agree with the oracle's to fp32 rounding."""
+    from llmcompressorsharp_b200 import MSEObserver
+
+    g = gen(n + 7 * bits + int(sym))
+    x = torch.randn(n, generator=g) * 0.02
+    x[torch.rand(n, generator=g) < 0.002] *= 20
+    half = n // 3
+    dev_obs, ref = MSEObserver(100), o_aff.MSEObserver(100)
+    for part in (x[:half], x[half:]):
+        dev_obs.update(part.to(DEV))
+        ref.update(part)
+    got = dev_obs.get_quant_params(bits, sym)
+    want = ref.get_quant_params(bits, sym)
+    assert np.float32(got[0]) == np.float32(want[0]) and got[1] == want[1], (got, want)
+    # the MSE of the chosen candidate, recomputed in fp64 from the oracle's fake-quant chain
+    s, z = want
+    qmin, qmax = o_fq.qrange(bits, sym)
+    fq = ((x / s).round() + z).clamp(qmin, qmax).sub(z).mul(s)
+    best = float(((x - fq) ** 2).double().mean())
+    assert abs(np.nanmin(dev_obs.last_mse) - best) <= 1e-5 * best
+
+
 def test_observer_kats():  # MinMaxObserverTests.cs, PerChannelMinMaxObserverTests.cs, MovingAverage...
     from llmcompressorsharp_b200 import MinMaxObserver, MovingAverageMinMaxObserver, PerChannelMinMaxObserver
     from llmcompressorsharp_b200.errors import ArgumentOutOfRangeError, InvalidOperationError
