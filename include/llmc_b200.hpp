@@ -340,6 +340,53 @@ class MinMaxObserver {
     bool has_ = false;
 };
 
+// MSEObserver (MSEObserver.cs:17-124): samples kept on the device; the grid search over the
+// symmetric ranges +-absMax*i/G runs in llmc_observer_mse.
+class MSEObserver {
+   public:
+    MSEObserver(Context& ctx, int gridPoints = 100) : ctx_(&ctx), grid_(gridPoints) {
+        if (gridPoints < 2) throw ArgumentOutOfRangeException("gridPoints must be >= 2.");
+    }
+    void Update(const DeviceTensor& x) {
+        DeviceTensor copy({x.numel()}, x.dtype());
+        if (x.bytes()) CheckCuda(cudaMemcpy(copy.data(), x.data(), x.bytes(), cudaMemcpyDeviceToDevice), "cudaMemcpy");
+        samples_.push_back(std::move(copy));
+    }
+    QuantizationParameters GetQuantParams(int numBits, bool symmetric) {
+        if (samples_.empty())
+            throw InvalidOperationException("MSEObserver has no calibration samples. Call Update before GetQuantParams.");
+        const DeviceTensor* flat = &samples_[0];
+        DeviceTensor joined;
+        if (samples_.size() > 1) {
+            int64_t n = 0;
+            for (const auto& t : samples_) {
+                if (t.dtype() != samples_[0].dtype()) throw ArgumentException("samples must share one dtype");
+                n += t.numel();
+            }
+            joined = DeviceTensor({n}, samples_[0].dtype());
+            size_t off = 0;
+            for (const auto& t : samples_) {
+                if (t.bytes())
+                    CheckCuda(cudaMemcpy(static_cast<char*>(joined.data()) + off, t.data(), t.bytes(),
+                                         cudaMemcpyDeviceToDevice), "cudaMemcpy");
+                off += t.bytes();
+            }
+            flat = &joined;
+        }
+        float scale = 1.f;
+        int32_t zp = 0;
+        Check(llmc_observer_mse(ctx_->get(), flat->data(), (int32_t)flat->dtype(), flat->numel(), grid_, numBits,
+                                symmetric ? 1 : 0, &scale, &zp, nullptr));
+        return QuantizationParameters{{scale}, {(int64_t)zp}, QuantizationStrategy::PerTensor};
+    }
+    void Reset() { samples_.clear(); }
+
+   private:
+    Context* ctx_;
+    int grid_;
+    std::vector<DeviceTensor> samples_;
+};
+
 class PerChannelMinMaxObserver {
    public:
     explicit PerChannelMinMaxObserver(Context& ctx, int channelAxis = 0) : ctx_(&ctx), axis_(channelAxis) {}
