@@ -24,6 +24,11 @@ column in the high nibble (Int4PackedTensor.cs:47-69).  compressed-tensors keeps
 codes for both, so asymmetric codes and zero-points move down by 2^(b-1); (q' - zp') * s is
 unchanged, so the dequantised weight is the same.
 
+A weight whose in_features is not a multiple of the group size keeps its ragged last group:
+``weight_scale`` has ceil(in / group) columns.  Readers that infer the group size from the
+shapes (compressed-tensors' argument-free ``dequantize``) need in_features divisible by the
+group size; the ``quantization_config`` states the group size for the others.
+
 SparseGPT masks are recorded as a ``sparsity_config`` (dense format, the pruned weights are
 written as they are).  Nothing here runs on the GPU: the writer packs on the host after the
 results are copied back.

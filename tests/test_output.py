@@ -178,3 +178,15 @@ def test_vllm_reads_the_quantization_config():
     assert (args.num_bits, args.symmetric, args.group_size, strategy) == (4, False, 128, "group")
     assert cfg.target_scheme_map["model.layers.0.mlp.down_proj"]["format"] == "pack-quantized"
     assert cfg.ignore == ["lm_head"]
+
+
+def test_ragged_last_group_keeps_ceil_groups():
+    w = torch.randn(16, 320, generator=torch.Generator().manual_seed(3)) * 0.02
+    entry, q, _ = _rtn_entry(w, 4, False, "group", 128)
+    out = CompressedTensorsWriter.module_tensors("fc.weight", entry, w.shape, torch.float32)
+    assert out["fc.weight_scale"].shape == (16, 3)
+    assert out["fc.weight_packed"].shape == (16, 40)
+    assert out["fc.weight_zero_point"].shape == (2, 3)
+    assert out["fc.weight_shape"].tolist() == [16, 320]
+    qs, _ = signed_codes(entry["codes"], entry["zero_points"], 4, False, 320, "group", 128)
+    assert np.array_equal(qs.astype(np.int64), q.numpy().astype(np.int64) - 8)
