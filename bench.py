@@ -204,11 +204,11 @@ def run_ours(args):
     def step(record=False):
         """One full job; returns nothing (work is enqueued on the current stream)."""
         if world == 1:
-            pipe.run(range(L), acts, weights, outputs, hess_events=hess_events if record else None)
+            pipe.run(range(L), acts, weights, outputs, hess_events=hess_events if record else None, sync=False)
             return
         if pipelined_dist:
             pipe.run_distributed(range(L), acts, weights, outputs, world, rank,
-                                 hess_events=hess_events if record else None)
+                                 hess_events=hess_events if record else None, sync=False)
             return
         # phase 1: partial Hessians of every layer over this rank's tokens
         for l in range(L):
@@ -247,6 +247,7 @@ def run_ours(args):
     t1.record()
     barrier()
     clk = clocks.stop()
+    pipe.check()  # deferred device errors of the timed steps (a non-PD Hessian, a wait that gave up)
     launches = pipe.launch_count() - launches0
     ms = t0.elapsed_time(t1) / args.steps
     hess_ms = sum(a.elapsed_time(b) for a, b, _, _ in hess_events) / args.steps

@@ -93,6 +93,23 @@ llmc_status llmc_set_stream(llmc_ctx* ctx, void* stream);
  * accumulating the next layer's Hessians while the other solves the previous layer on another
  * stream. */
 llmc_status llmc_set_sm_limit(llmc_ctx* ctx, int32_t sms);
+/* Bound of every wait inside this context's tensor-core kernels (the Hessian and the 3xTF32
+ * GEMMs), in try_wait attempts; tries < 0 restores the default (2^26).  A wait that runs out
+ * stops its kernel: the kernel raises an error word, waits (bounded) for the copies and MMAs
+ * it issued, frees its tensor memory and returns; the next llmc_sync (or any call that reads
+ * results) reports LLMC_ERR_TIMEOUT, clears the word, and the context stays usable.  tries = 0
+ * makes the first wait of the next such kernel give up at once, before it has issued any copy.
+ * No reference counterpart (the reference has no device waits). */
+llmc_status llmc_set_wait_limit(llmc_ctx* ctx, int64_t tries);
+/* on = 1: llmc_chol_inverse with want_upper = 1 and llmc_upper_factor no longer wait for the
+ * factorisation.  A non-positive-definite input is then decided on the device: the all-zero
+ * matrix still gives the zero factor (pinv(0) = 0, HessianInverseSolver.cs:85-91) and
+ * llmc_upper_factor still falls back to U = Hinv (GptqBlockQuantizer.cs:112-118), while any
+ * other non-PD input gets a zero factor and LLMC_ERR_NOT_PD from the next llmc_sync (or from
+ * any call that reads results back) instead of from the call itself.  on = 0 (the default)
+ * restores the synchronous reporting.  No reference counterpart: it lets one host thread
+ * enqueue a layer's solve while other streams keep running. */
+llmc_status llmc_set_deferred_errors(llmc_ctx* ctx, int32_t on);
 llmc_status llmc_sync(llmc_ctx* ctx);
 /* Number of kernels this context has launched since creation (diagnostics / bench). */
 llmc_status llmc_launch_count(llmc_ctx* ctx, int64_t* out);
@@ -210,9 +227,11 @@ llmc_status llmc_observer_minmax(llmc_ctx* ctx, const void* x, int32_t dtype, in
  * would stall the forward; a host whose caching allocator owns a fixed memory budget).
  * Its row buffer is a fixed array in the library, so rows <= LLMC_NOALLOC_MINMAX_MAX_ROWS
  * (larger: LLMC_ERR_SHAPE, nothing launched).  The first call on a device looks up that
- * array's address; make it before any stream capture.  All calls on a device share the
- * array, so calls that can overlap (two streams, two threads) race: order them on one
- * stream.  Arguments as llmc_observer_minmax with strategy TENSOR; output count 1. */
+ * array's address; make it before any stream capture.  llmc_init drops the looked-up address
+ * of its device, so after a device reset create a new context before calling again.  All
+ * calls on a device share the array, so calls that can overlap (two streams, two threads)
+ * race: order them on one stream.  The calling thread's current device is the same after the
+ * call as before it.  Arguments as llmc_observer_minmax with strategy TENSOR; output count 1. */
 #define LLMC_NOALLOC_MINMAX_MAX_ROWS 65536
 llmc_status llmc_observer_minmax_tensor_noalloc(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows,
                                                 int64_t cols, int64_t ld, float* min_io, float* max_io,

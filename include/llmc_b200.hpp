@@ -30,6 +30,7 @@
 #include <stdexcept>
 #include <string>
 #include <utility>
+#include <limits>
 #include <vector>
 
 #include "llmc_b200.h"
@@ -320,12 +321,18 @@ inline QuantizationParameters Affine(Context& ctx, const DeviceTensor& mins, con
 class MinMaxObserver {
    public:
     explicit MinMaxObserver(Context& ctx) : ctx_(&ctx), mn_({1}, DType::Float32), mx_({1}, DType::Float32) {}
-    // Running global min / max (MinMaxObserver.cs:24-45).
+    // Running global min / max (MinMaxObserver.cs:24-45): starts at +inf / -inf and folds each
+    // batch in by the observer's strict-less rule, so a batch holding a NaN changes nothing.
     void Update(const DeviceTensor& x) {
         if (x.numel() == 0) return;
+        if (!has_) {
+            const float init[2] = {std::numeric_limits<float>::infinity(), -std::numeric_limits<float>::infinity()};
+            CheckCuda(cudaMemcpy(mn_.data(), &init[0], 4, cudaMemcpyHostToDevice), "cudaMemcpy");
+            CheckCuda(cudaMemcpy(mx_.data(), &init[1], 4, cudaMemcpyHostToDevice), "cudaMemcpy");
+        }
         Check(llmc_observer_minmax(ctx_->get(), x.data(), (int32_t)x.dtype(), x.numel() / x.last(), x.last(), x.last(),
                                    LLMC_STRATEGY_TENSOR, x.last(), static_cast<float*>(mn_.data()),
-                                   static_cast<float*>(mx_.data()), has_ ? 1 : 0));
+                                   static_cast<float*>(mx_.data()), 1));
         has_ = true;
     }
     QuantizationParameters GetQuantParams(int numBits, bool symmetric) {

@@ -52,6 +52,8 @@ _SIGS = {
     "llmc_destroy": [P],
     "llmc_set_stream": [P, P],
     "llmc_set_sm_limit": [P, I32],
+    "llmc_set_wait_limit": [P, I64],
+    "llmc_set_deferred_errors": [P, I32],
     "llmc_sync": [P],
     "llmc_launch_count": [P, C.POINTER(I64)],
     "llmc_hessian_create": [P, I64, C.POINTER(P)],

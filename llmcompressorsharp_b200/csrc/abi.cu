@@ -90,17 +90,25 @@ llmc_status injected_fault(const char* fn) {
     return LLMC_OK;
 }
 
-// Synchronises the stream and reports a bounded device wait that gave up (error word 2,
-// written by the tensor-core kernels) as LLMC_ERR_TIMEOUT, clearing the word.
+// Synchronises the stream and reports the device error words, clearing them: word 2, a bounded
+// device wait that gave up (written by the tensor-core kernels), as LLMC_ERR_TIMEOUT; word 3, a
+// Hessian that was not positive definite in a factorisation run with deferred errors, as
+// LLMC_ERR_NOT_PD.
 llmc_status device_error_check(llmc_ctx* ctx) {
-    LLMC_CUDA_TRY(cudaMemcpyAsync(ctx->hflags + 2, ctx->dflags + 2, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    LLMC_CUDA_TRY(cudaMemcpyAsync(ctx->hflags + 2, ctx->dflags + 2, 2 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
     LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-    if (ctx->hflags[2] != 0) {
-        ctx->hflags[2] = 0;
-        LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags + 2, 0, sizeof(int), ctx->stream));
+    const int timeout = ctx->hflags[2], not_pd = ctx->hflags[3];
+    if (timeout || not_pd) {
+        ctx->hflags[2] = ctx->hflags[3] = 0;
+        LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags + 2, 0, 2 * sizeof(int), ctx->stream));
+    }
+    if (timeout)
         return fail(LLMC_ERR_TIMEOUT, "a bounded wait inside a tensor-core kernel gave up; results of the "
                     "affected calls are incomplete");
-    }
+    if (not_pd)
+        return fail(LLMC_ERR_NOT_PD, "a damped Hessian factorised with deferred errors was not positive definite "
+                    "(its factor was written as zeros); pseudo-inverse fallback is only available for the "
+                    "all-zero matrix");
     return LLMC_OK;
 }
 
@@ -215,6 +223,7 @@ llmc_status llmc_init(int32_t device, llmc_ctx** out) {
         return fail(LLMC_ERR_CUDA, "context setup failed: %s", cudaGetErrorString(e));
     }
     c->stream = c->own_stream;
+    noalloc_forget(device);
     *out = c;
     return LLMC_OK;
 }
@@ -245,6 +254,21 @@ llmc_status llmc_set_sm_limit(llmc_ctx* ctx, int32_t sms) {
     CTX_CHECK(ctx);
     if (sms < 0) return fail(LLMC_ERR_INVALID_ARG, "sm limit must be >= 0 (0 = no limit)");
     ctx->sm_limit = sms;
+    return LLMC_OK;
+}
+
+llmc_status llmc_set_wait_limit(llmc_ctx* ctx, int64_t tries) {
+    LLMC_ENTRY();
+    CTX_CHECK(ctx);
+    if (tries > (int64_t)UINT32_MAX) return fail(LLMC_ERR_OUT_OF_RANGE, "wait limit above 2^32 - 1");
+    ctx->wait_limit = tries < 0 ? (uint32_t)(1u << 26) : (uint32_t)tries;
+    return LLMC_OK;
+}
+
+llmc_status llmc_set_deferred_errors(llmc_ctx* ctx, int32_t on) {
+    LLMC_ENTRY();
+    CTX_CHECK(ctx);
+    ctx->deferred_errors = on ? 1 : 0;
     return LLMC_OK;
 }
 

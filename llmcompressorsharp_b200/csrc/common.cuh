@@ -72,6 +72,12 @@ struct llmc_ctx {
     // Device status words (flags written by kernels, e.g. a non-positive pivot).
     int* dflags = nullptr;
     int* hflags = nullptr;  // pinned mirror
+    // try_wait attempts each bounded wait of the tensor-core kernels makes before it gives up
+    // (llmc_set_wait_limit); 0 gives up at the first wait.
+    uint32_t wait_limit = 1u << 26;
+    // llmc_set_deferred_errors: decide device-side failures (a non-PD Hessian) without a host
+    // wait and report them at the next llmc_sync.
+    int deferred_errors = 0;
 };
 
 struct llmc_hessian {
@@ -148,11 +154,47 @@ __device__ __forceinline__ float fq_chain(float x, float s, float zpf, float qmi
     return rnd<T>(__fmul_rn(t, s));
 }
 
+// min / max that return NaN when either operand is NaN (torch.amin / amax / minimum /
+// maximum, .NET MathF.Min / MathF.Max); fminf / fmaxf would drop the NaN instead.
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// How a segment's min / max is folded into the stored value (k_quant.cu's observer kernels):
+//   FOLD_NONE      store the batch value (torch x.min(): NaN when any element is NaN);
+//   FOLD_MINIMUM   torch.minimum / maximum with the stored value, NaN propagating
+//                  (PerChannelMinMaxObserver.cs:64-74);
+//   FOLD_OBSERVER  MinMaxObserver's `if (bMin < _min) _min = bMin` (MinMaxObserver.cs:34-42):
+//                  the stored value changes only where the batch value is strictly beyond it,
+//                  so a NaN batch changes nothing;
+//   FOLD_FRESH     FOLD_OBSERVER against a new observer's +inf / -inf.
+enum { FOLD_NONE = 0, FOLD_MINIMUM = 1, FOLD_OBSERVER = 2, FOLD_FRESH = 3 };
+__device__ __forceinline__ float fold_min(float b, const float* stored, int mode) {
+    if (mode == FOLD_NONE) return b;
+    if (mode == FOLD_MINIMUM) return fmin_nan(b, *stored);
+    const float o = mode == FOLD_OBSERVER ? *stored : INFINITY;
+    return b < o ? b : o;
+}
+__device__ __forceinline__ float fold_max(float b, const float* stored, int mode) {
+    if (mode == FOLD_NONE) return b;
+    if (mode == FOLD_MINIMUM) return fmax_nan(b, *stored);
+    const float o = mode == FOLD_OBSERVER ? *stored : -INFINITY;
+    return b > o ? b : o;
+}
+
 // Observer.ComputeAffineParams (Observer.cs:47-75) with IEEE single ops; the zero-point
-// conversion saturates like .NET's (long) cast before Math.Clamp.
+// conversion saturates like .NET's (long) cast before Math.Clamp.  MathF.Max returns NaN for a
+// NaN operand, so a NaN min or max gives a NaN scale (and zero-point 0) as in the reference.
 __device__ __forceinline__ void affine_params(float mn, float mx, int bits, int sym, float* scale, int* zp) {
     if (sym) {
-        float am = fmaxf(fabsf(mn), fabsf(mx));
+        float am = fmax_nan(fabsf(mn), fabsf(mx));
         float qmax = (float)((1 << (bits - 1)) - 1);
         *scale = (am == 0.f) ? 1.f : __fdiv_rn(am, qmax);
         *zp = 0;

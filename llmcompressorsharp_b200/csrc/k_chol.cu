@@ -276,15 +276,43 @@ __global__ void copy2d_kernel(const float* src, int64_t rows, int64_t cols, int6
     }
 }
 
-// flags[1] = 1 when any element of the (symmetric) input is nonzero.
-__global__ void nonzero_kernel(const float* H, int64_t d, int64_t ldh, int* flags) {
+// flags[1] = 1 when any element of the (symmetric) input is nonzero.  With only_if_failed
+// the kernel does nothing unless flags[0] (a non-positive pivot) is set.
+__global__ void nonzero_kernel(const float* H, int64_t d, int64_t ldh, int upper_only, int* flags, int only_if_failed) {
+    if (only_if_failed && *(volatile int*)flags == 0) return;
     const int64_t total = d * d;
     int any = 0;
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = t / d, j = t % d;
-        if (H[i * ldh + j] != 0.f) any = 1;
+        if ((!upper_only || i <= j) && H[i * ldh + j] != 0.f) any = 1;
     }
     if (__syncthreads_or(any) && threadIdx.x == 0) atomicOr(flags + 1, 1);
+}
+
+// Deferred end of llmc_chol_inverse(want_upper = 1): the flipped factor (as remap_kernel mode 0)
+// when the factorisation succeeded; otherwise zeros (pinv of the all-zero matrix, the
+// reference's fallback, HessianInverseSolver.cs:85-91), and for a nonzero matrix also the
+// deferred NOT_PD word flags[3], reported by the next llmc_sync.
+__global__ void finish_upper_kernel(const float* src, int64_t d, int64_t lds, float* out, int64_t ldo, int* flags) {
+    const int failed = *(volatile int*)flags;
+    if (failed && blockIdx.x == 0 && threadIdx.x == 0 && *(volatile int*)(flags + 1)) atomicOr(flags + 3, 1);
+    const int64_t total = d * d;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / d, j = t % d;
+        out[i * ldo + j] = failed ? 0.f : src[(d - 1 - i) * lds + (d - 1 - j)];
+    }
+}
+
+// Deferred end of llmc_upper_factor: U = L^T (remap_kernel mode 1) when chol(Hinv) succeeded,
+// else Hinv itself (GptqBlockQuantizer.cs:112-118).
+__global__ void finish_factor_kernel(const float* L, const float* hinv, int64_t d, int64_t ldl, int64_t ldh, float* out,
+                                     int64_t ldo, const int* flags) {
+    const int failed = *(volatile const int*)flags;
+    const int64_t total = d * d;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / d, j = t % d;
+        out[i * ldo + j] = failed ? hinv[i * ldh + j] : ((j >= i) ? L[j * ldl + i] : 0.f);
+    }
 }
 
 int grid_for(llmc_ctx* ctx, int64_t items) {
@@ -358,16 +386,19 @@ llmc_status read_flags(llmc_ctx* ctx, int* f0, int* f1) {
     return LLMC_OK;
 }
 
-// Factor the prepared lower matrix in w.A; on a non-positive pivot decide between the
-// all-zero case (pinv(0) = 0) and a genuine failure.
-llmc_status factor(llmc_ctx* ctx, const CholWs& w, int64_t d, int keep_L, int* not_pd, int* all_zero) {
+// Factor the prepared lower matrix in w.A.  Unless the context defers errors, wait for it and
+// report a non-positive pivot in *not_pd (the caller then decides between the all-zero case,
+// pinv(0) = 0, and a genuine failure); with deferred errors *not_pd is 0 and the decision is
+// left to the device (flags[0]).
+llmc_status factor(llmc_ctx* ctx, const CholWs& w, int64_t d, int keep_L, int* not_pd) {
     LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags, 0, 2 * sizeof(int), ctx->stream));
     LLMC_CUDA_TRY(cudaMemsetAsync(w.I, 0, (size_t)d * w.ld * sizeof(float), ctx->stream));
     LLMC_TRY(rec(ctx, w, 0, d, keep_L));
+    *not_pd = 0;
+    if (ctx->deferred_errors) return LLMC_OK;
     int f0, f1;
     LLMC_TRY(read_flags(ctx, &f0, &f1));
     *not_pd = f0 != 0;
-    *all_zero = 0;
     return LLMC_OK;
 }
 
@@ -385,15 +416,28 @@ llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, 
     LLMC_TRY(check_launch(ctx, "diag_lambda"));
     prep_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(H, d, ldh, upper_only, want_upper ? 1 : 0, lam, w.A, d);
     LLMC_TRY(check_launch(ctx, "prep"));
-    int not_pd = 0, all_zero = 0;
-    LLMC_TRY(factor(ctx, w, d, 0, &not_pd, &all_zero));
+    int not_pd = 0;
+    LLMC_TRY(factor(ctx, w, d, 0, &not_pd));
+    if (ctx->deferred_errors && want_upper) {
+        // No host wait: the zero test and the output choice run on the device.
+        nonzero_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(H, d, ldh, upper_only, ctx->dflags, 1);
+        LLMC_TRY(check_launch(ctx, "nonzero"));
+        finish_upper_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.I, d, d, out, ldo, ctx->dflags);
+        return check_launch(ctx, "finish_upper");
+    }
+    if (ctx->deferred_errors) {
+        // Hinv needs the host's decision below; take it synchronously.
+        int f0, f1;
+        LLMC_TRY(read_flags(ctx, &f0, &f1));
+        not_pd = f0 != 0;
+    }
     if (not_pd) {
         // HessianInverseSolver.cs:85-91 falls back to pinv(H').  pinv of the zero matrix is
         // zero (the no-calibration-data case); anything else is reported.
         LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags, 0, 2 * sizeof(int), ctx->stream));
         prep_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(H, d, ldh, upper_only, 0, lam, w.A, d);
         LLMC_TRY(check_launch(ctx, "prep"));
-        nonzero_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.A, d, d, ctx->dflags);
+        nonzero_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.A, d, d, 0, ctx->dflags, 0);
         LLMC_TRY(check_launch(ctx, "nonzero"));
         int f0, f1;
         LLMC_TRY(read_flags(ctx, &f0, &f1));
@@ -427,8 +471,12 @@ llmc_status upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ld
     LLMC_TRY(check_launch(ctx, "diag_lambda"));
     prep_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(hinv, d, ldh, 0, 0, lam, w.A, d);
     LLMC_TRY(check_launch(ctx, "prep"));
-    int not_pd = 0, all_zero = 0;
-    LLMC_TRY(factor(ctx, w, d, 1, &not_pd, &all_zero));
+    int not_pd = 0;
+    LLMC_TRY(factor(ctx, w, d, 1, &not_pd));
+    if (ctx->deferred_errors) {
+        finish_factor_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.A, hinv, d, d, ldh, out, ldo, ctx->dflags);
+        return check_launch(ctx, "finish_factor");
+    }
     if (not_pd) {
         // GptqBlockQuantizer.cs:112-118: fall back to Hinv itself.
         copy2d_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(hinv, d, d, ldh, out, ldo);

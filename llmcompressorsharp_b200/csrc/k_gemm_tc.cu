@@ -47,6 +47,7 @@ struct TcGemmArgs {
     float alpha, beta;
     int a_tri, b_tri, c_mode;
     int* err;
+    uint32_t wait_limit;  // try_wait attempts per bounded wait (llmc_set_wait_limit)
     uint32_t idesc;
     int tiles_m, tiles_n, group;  // 1-D grid: tiles visited in column strips of `group` M-tiles
     int splits;                   // K splits per tile (pair kernel; > 1 needs beta == 1)
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 for (int kb = kb0; kb < kb1; kb++, prod_it++) {
                     const int s = prod_it % STAGES;
                     const uint32_t ph = (prod_it / STAGES) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     unsigned char* st = smem + s * STAGE_BYTES;
                     mbar_expect_tx(&full[s], STAGE_BYTES);
                     const int k0 = kb * BK;
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                 uint32_t c_it = cc;
                 for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
                     const int b = (int)(c_it & 1u);
-                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     tc_fence_after();
                     const uint32_t dst = tmem + (uint32_t)(b * BN);
                     const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
                     for (int kb = k0; kb < k1; kb++, mma_it++) {
                         const int s = mma_it % STAGES;
                         const uint32_t ph = (mma_it / STAGES) & 1u;
-                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err, a.wait_limit)) {
                             ok = false;
                             break;
                         }
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_tc_kernel(const __grid_constant__ 
             bool ok = true;
             for (int c = 0; c < nchunks; c++, c_it++) {
                 const int b = (int)(c_it & 1u);
-                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
+                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err, a.wait_limit);
                 if (!__all_sync(0xffffffffu, have ? 1 : 0)) {
                     ok = false;
                     break;
@@ -362,7 +363,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
                 for (int kb = kb0; kb < kb1; kb++, prod_it++) {
                     const int s = prod_it % STAGES;
                     const uint32_t ph = (prod_it / STAGES) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     unsigned char* st = smem + s * P_STAGE_BYTES;
                     if (rank == 0) mbar_expect_tx(&full[s], 2 * P_STAGE_BYTES);
                     const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
@@ -380,7 +381,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
                 uint32_t c_it = cc;
                 for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
                     const int b = (int)(c_it & 1u);
-                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     tc_fence_after();
                     const uint32_t dst = tmem + (uint32_t)(b * P_BN);
                     const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
@@ -388,7 +389,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
                     for (int kb = k0; kb < k1; kb++, mma_it++) {
                         const int s = mma_it % STAGES;
                         const uint32_t ph = (mma_it / STAGES) & 1u;
-                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err, a.wait_limit)) {
                             ok = false;
                             break;
                         }
@@ -423,7 +424,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
             bool ok = true;
             for (int c = 0; c < nchunks; c++, c_it++) {
                 const int b = (int)(c_it & 1u);
-                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
+                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err, a.wait_limit);
                 if (!__all_sync(0xffffffffu, have ? 1 : 0)) {
                     ok = false;
                     break;
@@ -714,6 +715,7 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g) {
     t.c_mode = g.c_mode;
     t.splits = 1;
     t.err = ctx->dflags + 2;
+    t.wait_limit = ctx->wait_limit;
     uint32_t d = 0;
     d |= 1u << 4;          // D: F32
     d |= 2u << 7;          // A: TF32

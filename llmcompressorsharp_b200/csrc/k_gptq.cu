@@ -452,12 +452,13 @@ llmc_status gptq_batch(llmc_ctx* ctx, int count, const void* const* Ws, const in
     a.err1t = err1t;
     if (mode == 0) {
         // ComputeScaleZeroPoint from the ORIGINAL weight (GptqBlockQuantizer.cs:97, :196-234);
-        // the fp32 copy holds exactly the original values.
+        // the fp32 copy holds exactly the original values.  Accumulate mode 2 is a new
+        // MinMaxObserver per scale entry, as the reference creates one per tensor or row.
         if (tensor) {
             off = 0;
             for (int k = 0; k < count; k++) {
                 LLMC_TRY(minmax(ctx, work + off * ldwork, LLMC_DTYPE_F32, ms[k], n, ldwork, LLMC_STRATEGY_TENSOR, n,
-                                mins + k, maxs + k, 0, red));
+                                mins + k, maxs + k, 2, red));
                 off += ms[k];
             }
             LLMC_TRY(affine(ctx, mins, maxs, count, cfg->num_bits, cfg->symmetric, ts, tz));
@@ -471,7 +472,8 @@ llmc_status gptq_batch(llmc_ctx* ctx, int count, const void* const* Ws, const in
             a.srow = 1;
             a.gs = n;
         } else {
-            LLMC_TRY(minmax(ctx, work, LLMC_DTYPE_F32, M, n, ldwork, strategy, gs, mins, maxs, 0, red));
+            // One fresh MinMaxObserver per row (or per row and group): a NaN row gets +inf / -inf.
+            LLMC_TRY(minmax(ctx, work, LLMC_DTYPE_F32, M, n, ldwork, strategy, gs, mins, maxs, 2, red));
             LLMC_TRY(affine(ctx, mins, maxs, M * G, cfg->num_bits, cfg->symmetric, krs, krz));
             a.srow = G;
             a.gs = strategy == LLMC_STRATEGY_GROUP ? gs : n;

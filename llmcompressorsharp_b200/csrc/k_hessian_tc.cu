@@ -68,6 +68,7 @@ struct SyrkArgs {
     int kb_per_split;
     int tile_off[MAX_TJ + 1];  // first tile index of column-panel tj
     int* err;         // device error word (bit 0: a wait timed out)
+    uint32_t wait_limit;
     uint32_t idesc;
 };
 
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ 
                 for (int kb = kb0; kb < kb1; kb++, prod_it++) {
                     const int s = prod_it % STAGES;
                     const uint32_t ph = (prod_it / STAGES) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     unsigned char* st = smem + s * STAGE_BYTES;
                     mbar_expect_tx(&full[s], STAGE_BYTES);
                     const int y = kb * BK;
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ 
                 uint32_t c_it = cc;
                 for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
                     const int b = (int)(c_it & 1u);
-                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     tc_fence_after();
                     const uint32_t dst = tmem + (uint32_t)(b * BN);
                     const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
@@ -166,7 +167,7 @@ __global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ 
                     for (int kb = k0; kb < k1; kb++, mma_it++) {
                         const int s = mma_it % STAGES;
                         const uint32_t ph = (mma_it / STAGES) & 1u;
-                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err, a.wait_limit)) {
                             ok = false;
                             break;
                         }
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ 
             uint32_t c_it = cc;
             for (int c = 0; c < nchunks; c++, c_it++) {
                 const int b = (int)(c_it & 1u);
-                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
+                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err, a.wait_limit);
                 if (!__all_sync(0xffffffffu, have ? 1 : 0)) break;
                 tc_fence_after();
 #pragma unroll
@@ -277,12 +278,27 @@ __global__ void __launch_bounds__(NT, 1) syrk_tc_kernel(const __grid_constant__ 
 // TMEM is allocated for the pair (same 512 columns in both SMs); each CTA's epilogue reads
 // its own 128 rows.  Before exit each producer waits until every stage it filled has been
 // released, so no arrive or load targets a CTA that has left.
+//
+// Work units are (token split, tile), split-major, tiles in the order of PairArgs::tiles.
+// Dynamic order (DYN): the leader's producer takes the next unit from a device counter and
+// hands it to every role of both CTAs through a ring of UR slots:
+//   * uring[k % UR] (each CTA) holds the unit (-1 when the work is exhausted);
+//   * ufull[k % UR] (each CTA): one arrive (release, cluster scope) from the leader's producer
+//     after it has written the slot in both CTAs;
+//   * uempty[k % UR] (leader): one arrive from each reader of the slot: the MMA issuer, the
+//     other CTA's producer and the 16 epilogue warps.
+// The units in flight are then always a contiguous stretch of the unit order, whose tiles
+// share X panels and whose token range is one split, so their X reads meet in L2 however
+// unevenly the pairs progress.  Static order: pair p runs units p, p + pairs, ...
 constexpr int P_STAGES = 6;
 constexpr int P_HALF_BYTES = 128 * BK * 2;         // 16 KB: 128 features x 64 tokens
 constexpr int P_STAGE_BYTES = 2 * P_HALF_BYTES;    // A half + B half
 constexpr int P_SMEM_MAIN = P_STAGES * P_STAGE_BYTES;  // 192 KB
 constexpr int P_SMEM_BYTES = P_SMEM_MAIN + EPI_WARPS * OUT_BYTES + 1024 + 256;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory above the per-block limit");
+constexpr int UR = 4;                             // unit ring slots
+constexpr int UR_READERS = 2 + 2 * EPI_WARPS;     // leader's MMA issuer, rank 1's producer, 16 epilogue warps
+static_assert((2 * P_STAGES + 4 + 2 * UR) * 8 + 8 + UR * 4 <= 256, "barrier area");
 
 constexpr int P_MAX_NT = 160;                                // d <= 40960
 constexpr int P_MAX_TILES = P_MAX_NT * (P_MAX_NT + 1) / 2;   // 12,880
@@ -297,6 +313,8 @@ struct PairArgs {
     int splits;
     int kb_per_split;
     int* err;
+    int* next_unit;  // DYN: unit counter, zero at launch
+    uint32_t wait_limit;
     uint32_t idesc;
     // Tile order, (ti << 8) | tj: column strips walked row by row, so that the tiles one wave
     // of pairs works on share few X panels and those panels stay in L2.
@@ -304,6 +322,23 @@ struct PairArgs {
 };
 static_assert(sizeof(PairArgs) + 2 * sizeof(CUtensorMap) <= 32764, "kernel parameters above the limit");
 
+// Unit u of PairArgs: this CTA's rows i0, the pair's columns j0 and the k-block range.
+struct PairUnit {
+    int i0, j0, kb0, kb1, nchunks;
+};
+__device__ __forceinline__ PairUnit pair_unit(const PairArgs& a, int u, uint32_t rank) {
+    const int split = u / a.ntiles, tile = u % a.ntiles;
+    const int ti = a.tiles[tile] >> 8, tj = a.tiles[tile] & 0xFF;
+    PairUnit p;
+    p.kb0 = split * a.kb_per_split;
+    p.kb1 = min(a.kb_total, p.kb0 + a.kb_per_split);
+    p.nchunks = (p.kb1 - p.kb0 + KF - 1) / KF;
+    p.i0 = ti * 256 + (int)rank * 128;
+    p.j0 = tj * 256;
+    return p;
+}
+
+template <bool DYN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
     syrk_tc2_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap hmap, const PairArgs a) {
     extern __shared__ unsigned char smem_raw[];
@@ -313,8 +348,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
     uint64_t* empty = full + P_STAGES;
     uint64_t* tfull = empty + P_STAGES;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* ufull = tempty + 2;
+    uint64_t* uempty = ufull + UR;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(uempty + UR);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* uring = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t rank = cluster_ctarank();
@@ -327,6 +365,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
         for (int b = 0; b < 2; b++) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 2 * EPI_WARPS);
+        }
+        for (int k = 0; k < UR; k++) {
+            mbar_init(&ufull[k], 1);
+            mbar_init(&uempty[k], UR_READERS);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -342,54 +384,85 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
     const uint32_t tmem = *tmem_slot;
 
     const int total_units = a.ntiles * a.splits;
+    // k-th unit of this pair, for a role that reads the ring (DYN) or walks the static order;
+    // -1 when there is no further unit or the wait gave up.
+    auto take = [&](uint32_t k) -> int {
+        if constexpr (DYN) {
+            const int slot = (int)(k % UR);
+            if (!mbar_wait_cluster(&ufull[slot], (k / UR) & 1u, abort_flag, a.err, a.wait_limit)) return -1;
+            const int u = uring[slot];
+            mbar_arrive_cluster(mapa_shared(smem_u32(&uempty[slot]), 0));
+            return u;
+        } else {
+            const int u = pair + (int)k * npairs;
+            return u < total_units ? u : -1;
+        }
+    };
+    // Leader producer (DYN): claim the k-th unit and publish it to both CTAs.
+    auto publish = [&](uint32_t k) -> int {
+        const int slot = (int)(k % UR);
+        if (!mbar_wait_cluster(&uempty[slot], ((k / UR) & 1u) ^ 1u, abort_flag, a.err, a.wait_limit)) return -1;
+        int u = atomicAdd(a.next_unit, 1);
+        if (u >= total_units) u = -1;
+        uring[slot] = u;
+        st_cluster_u32(mapa_shared(smem_u32((const void*)&uring[slot]), 1), (uint32_t)u);
+        mbar_arrive_cluster(mapa_shared(smem_u32(&ufull[slot]), 0));
+        mbar_arrive_cluster(mapa_shared(smem_u32(&ufull[slot]), 1));
+        return u;
+    };
+
     uint32_t prod_it = 0, mma_it = 0, cc = 0;
     int pend_par[P_STAGES];
 #pragma unroll
     for (int s = 0; s < P_STAGES; s++) pend_par[s] = -1;
     int commit_par[2] = {-1, -1};
 
-    for (int u = pair; u < total_units && !*abort_flag; u += npairs) {
-        const int split = u / a.ntiles, tile = u % a.ntiles;
-        const int ti = a.tiles[tile] >> 8, tj = a.tiles[tile] & 0xFF;
-        const int kb0 = split * a.kb_per_split;
-        const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
-        const int nchunks = (kb1 - kb0 + KF - 1) / KF;
-        const int i0 = ti * 256 + (int)rank * 128;  // this CTA's rows of H
-        const int j0 = tj * 256;                    // the pair's columns
-        const int jb = j0 + (int)rank * 128;        // this CTA's half of the B panel
-
-        if (warp == 0) {
-            if (lane == 0) {
-                for (int kb = kb0; kb < kb1; kb++, prod_it++) {
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer (this CTA's halves of the A and B panels)
+            for (uint32_t k = 0; !*abort_flag; k++) {
+                const int u = (DYN && rank == 0) ? publish(k) : take(k);
+                if (u < 0) break;
+                const PairUnit pu = pair_unit(a, u, rank);
+                const int jb = pu.j0 + (int)rank * 128;  // this CTA's half of the B panel
+                for (int kb = pu.kb0; kb < pu.kb1; kb++, prod_it++) {
                     const int s = prod_it % P_STAGES;
                     const uint32_t ph = (prod_it / P_STAGES) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     unsigned char* st = smem + s * P_STAGE_BYTES;
                     if (rank == 0) mbar_expect_tx(&full[s], 2 * P_STAGE_BYTES);
                     const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
                     const int y = kb * BK;
-                    tma_load_2d_pair(st, &xmap, i0, y, fbar);
-                    tma_load_2d_pair(st + BOX_BYTES, &xmap, i0 + 64, y, fbar);
+                    tma_load_2d_pair(st, &xmap, pu.i0, y, fbar);
+                    tma_load_2d_pair(st + BOX_BYTES, &xmap, pu.i0 + 64, y, fbar);
                     tma_load_2d_pair(st + P_HALF_BYTES, &xmap, jb, y, fbar);
                     tma_load_2d_pair(st + P_HALF_BYTES + BOX_BYTES, &xmap, jb + 64, y, fbar);
                     pend_par[s] = (int)ph;
                 }
             }
-            __syncwarp();
-        } else if (warp == 1) {
-            if (lane == 0 && rank == 0) {
-                uint32_t c_it = cc;
-                for (int c = 0; c < nchunks && !*abort_flag; c++, c_it++) {
-                    const int b = (int)(c_it & 1u);
-                    if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err)) break;
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ---- MMA issuer: chunk c accumulates into TMEM buffer (cc & 1)
+            for (uint32_t k = 0; !*abort_flag; k++) {
+                const int u = take(k);
+                if (u < 0) break;
+                const PairUnit pu = pair_unit(a, u, rank);
+                bool ok = true;
+                for (int c = 0; c < pu.nchunks && ok; c++, cc++) {
+                    const int b = (int)(cc & 1u);
+                    if (!mbar_wait(&tempty[b], ((cc >> 1) & 1u) ^ 1u, abort_flag, a.err, a.wait_limit)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t dst = tmem + (uint32_t)(b * BN);
-                    const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
-                    bool ok = true;
+                    const int k0 = pu.kb0 + c * KF, k1 = min(pu.kb1, k0 + KF);
                     for (int kb = k0; kb < k1; kb++, mma_it++) {
                         const int s = mma_it % P_STAGES;
                         const uint32_t ph = (mma_it / P_STAGES) & 1u;
-                        if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+                        if (!mbar_wait(&full[s], ph, abort_flag, a.err, a.wait_limit)) {
                             ok = false;
                             break;
                         }
@@ -404,22 +477,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
                         }
                         umma2_commit_mc(&empty[s], 0x3);
                     }
-                    umma2_commit_mc(&tfull[b], 0x3);
-                    commit_par[b] = (int)((c_it >> 1) & 1u);
-                    if (!ok) break;
+                    umma2_commit_mc(&tfull[b], 0x3);  // chunk complete (fires even if the loop broke early)
+                    commit_par[b] = (int)((cc >> 1) & 1u);
                 }
+                if (!ok) break;
             }
-            __syncwarp();
-        } else {
-            const int e = warp - 2, q = warp % 4, h = e / 4;
+        }
+        __syncwarp();
+    } else {
+        // ---- epilogue warps: TMEM lane quadrant q, column half h
+        const int e = warp - 2, q = warp % 4, h = e / 4;
+        for (uint32_t k = 0; !*abort_flag; k++) {
+            int u = 0;
+            if (lane == 0) u = take(k);
+            u = __shfl_sync(0xffffffffu, u, 0);
+            if (u < 0) break;
+            const PairUnit pu = pair_unit(a, u, rank);
             float acc[BN / 2];
 #pragma unroll
             for (int i = 0; i < BN / 2; i++) acc[i] = 0.f;
-            uint32_t c_it = cc;
-            for (int c = 0; c < nchunks; c++, c_it++) {
-                const int b = (int)(c_it & 1u);
-                const bool have = mbar_wait(&tfull[b], (c_it >> 1) & 1u, abort_flag, a.err);
-                if (!__all_sync(0xffffffffu, have ? 1 : 0)) break;
+            bool ok = true;
+            for (int c = 0; c < pu.nchunks; c++, cc++) {
+                const int b = (int)(cc & 1u);
+                const bool have = mbar_wait(&tfull[b], (cc >> 1) & 1u, abort_flag, a.err, a.wait_limit);
+                if (!__all_sync(0xffffffffu, have ? 1 : 0)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
 #pragma unroll
                 for (int part = 0; part < 4; part++) {
@@ -432,29 +516,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NT, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
             }
-            if (!*abort_flag) {
-                unsigned char* ob = outbufs + e * OUT_BYTES;
-                const uint32_t ob_s = smem_u32(ob);
+            if (!ok || *abort_flag) break;
+            // Write-out: rounds of one 32 x 32 box (rows of quadrant q, columns j0 + 128 h +
+            // 32 round ..) through this warp's buffer, reused only after the previous reduce has
+            // read it; TMA clips rows / columns beyond d.
+            unsigned char* ob = outbufs + e * OUT_BYTES;
+            const uint32_t ob_s = smem_u32(ob);
 #pragma unroll
-                for (int round = 0; round < 4; round++) {
-                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-                    __syncwarp();
+            for (int round = 0; round < 4; round++) {
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
 #pragma unroll
-                    for (int c = 0; c < 8; c++) {
-                        const int i = round * 32 + c * 4;
-                        *reinterpret_cast<float4*>(ob + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-                            make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-                    }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_reduce_add_2d(&hmap, ob_s, j0 + h * 128 + round * 32, i0 + q * 32);
-                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                    }
+                for (int c = 0; c < 8; c++) {
+                    const int i = round * 32 + c * 4;
+                    *reinterpret_cast<float4*>(ob + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                        make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    tma_reduce_add_2d(&hmap, ob_s, pu.j0 + h * 128 + round * 32, pu.i0 + q * 32);
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
             }
         }
-        cc += (uint32_t)nchunks;
     }
 
     // Tail: the producer waits until the MMAs have released every stage it filled (so no
@@ -505,6 +590,23 @@ uint32_t make_idesc(int dtype, int m = BM, int n = BN) {
     return d;
 }
 
+// Unit order of the pair kernel: dynamic (a device counter deals units in order) or static.
+constexpr bool SYRK_DYNAMIC = true;
+// Dynamic order: token splits sized to about this many k-blocks per unit, so that the X rows
+// of the units in flight (one split's token range) stay in L2.
+constexpr int SYRK_UNIT_KB = 128;
+// Index of the unit counter in the context's device flag words.
+constexpr int SYRK_COUNTER_WORD = 8;
+
+// Token splits for the dynamic order: about SYRK_UNIT_KB k-blocks per unit, at most 16 splits,
+// and >= 32 k-blocks per unit when split.
+int unit_splits(int kb_total) {
+    int s = (kb_total + SYRK_UNIT_KB / 2) / SYRK_UNIT_KB;
+    if (s > 16) s = 16;
+    while (s > 1 && (kb_total + s - 1) / s < 32) s--;
+    return s < 1 ? 1 : s;
+}
+
 // Token splits: balance the last wave over `cap` workers while keeping >= 32 k-blocks (2048
 // tokens) per unit.
 int pick_splits(int ntiles, int kb_total, int cap) {
@@ -536,7 +638,7 @@ int max_pairs(llmc_ctx* ctx) {
     if (!known[dev]) {
         known[dev] = true;
         cache[dev] = 0;
-        if (cudaFuncSetAttribute(syrk_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES) !=
+        if (cudaFuncSetAttribute(syrk_tc2_kernel<SYRK_DYNAMIC>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES) !=
             cudaSuccess) {
             cudaGetLastError();
             return 0;
@@ -553,10 +655,10 @@ int max_pairs(llmc_ctx* ctx) {
         cfg.attrs = at;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, (const void*)syrk_tc2_kernel, &cfg) != cudaSuccess) {
+        if (cudaOccupancyMaxActiveClusters(&n, (const void*)syrk_tc2_kernel<SYRK_DYNAMIC>, &cfg) != cudaSuccess) {
             cudaGetLastError();
             cfg.numAttrs = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, (const void*)syrk_tc2_kernel, &cfg) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&n, (const void*)syrk_tc2_kernel<SYRK_DYNAMIC>, &cfg) != cudaSuccess) {
                 cudaGetLastError();
                 n = 0;
             }
@@ -599,6 +701,7 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
     a.splits = pick_splits(a.ntiles, a.kb_total, grid_cap);
     a.kb_per_split = (a.kb_total + a.splits - 1) / a.splits;
     a.err = ctx->dflags + 2;
+    a.wait_limit = ctx->wait_limit;
     a.idesc = make_idesc(dtype);
 
     CUtensorMap map;
@@ -640,20 +743,24 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
             }
             if (n != p.ntiles) return fail(LLMC_ERR_INTERNAL, "syrk pair tile order: %d of %d tiles", n, p.ntiles);
             p.kb_total = a.kb_total;
-            p.splits = pick_splits(p.ntiles, p.kb_total, pcap);
+            p.splits = SYRK_DYNAMIC ? unit_splits(p.kb_total) : pick_splits(p.ntiles, p.kb_total, pcap);
             p.kb_per_split = (p.kb_total + p.splits - 1) / p.splits;
             p.err = ctx->dflags + 2;
+            p.next_unit = ctx->dflags + SYRK_COUNTER_WORD;
+            p.wait_limit = ctx->wait_limit;
             p.idesc = make_idesc(dtype, 256, 256);
             const int punits = p.ntiles * p.splits;
             const int pairs = punits < pcap ? punits : pcap;
-            syrk_tc2_kernel<<<2 * pairs, NT, P_SMEM_BYTES, ctx->stream>>>(map, hmap, p);
+            if (SYRK_DYNAMIC) LLMC_CUDA_TRY(cudaMemsetAsync(p.next_unit, 0, sizeof(int), ctx->stream));
+            syrk_tc2_kernel<SYRK_DYNAMIC><<<2 * pairs, NT, P_SMEM_BYTES, ctx->stream>>>(map, hmap, p);
             return check_launch(ctx, "syrk_tc2");
         }
     }
-    static bool attr = false;
-    if (!attr) {
+    static bool attr[64];  // per device
+    if (ctx->device < 0 || ctx->device >= 64) return LLMC_ERR_UNSUPPORTED;
+    if (!attr[ctx->device]) {
         LLMC_CUDA_TRY(cudaFuncSetAttribute(syrk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        attr = true;
+        attr[ctx->device] = true;
     }
     const int units = a.ntiles * a.splits;
     const int grid = units < grid_cap ? units : grid_cap;

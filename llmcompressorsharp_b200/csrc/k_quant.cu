@@ -62,25 +62,25 @@ __device__ __forceinline__ void seg_reduce(const T* x, const SegGeom& g, int64_t
             v.load(row + c);
 #pragma unroll
             for (int i = 0; i < VEC; i++) {
-                mn = fminf(mn, v.v[i]);
-                mx = fmaxf(mx, v.v[i]);
+                mn = fmin_nan(mn, v.v[i]);
+                mx = fmax_nan(mx, v.v[i]);
             }
         } else {
             for (int64_t i = c; i < c1; i++) {
                 float f = to_f<T>(row[i]);
-                mn = fminf(mn, f);
-                mx = fmaxf(mx, f);
+                mn = fmin_nan(mn, f);
+                mx = fmax_nan(mx, f);
             }
         }
     }
     for (int off = g.L / 2; off > 0; off >>= 1) {
-        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+        mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     }
 }
 
 template <typename T, int VEC>
-__global__ void __launch_bounds__(NT) seg_minmax_kernel(const T* x, SegGeom g, float* mins, float* maxs, int accumulate) {
+__global__ void __launch_bounds__(NT) seg_minmax_kernel(const T* x, SegGeom g, float* mins, float* maxs, int fold) {
     const int64_t groups_per_block = NT / g.L;
     const int64_t total = g.rows * g.nseg;
     const int64_t lg = threadIdx.x / g.L;
@@ -92,10 +92,8 @@ __global__ void __launch_bounds__(NT) seg_minmax_kernel(const T* x, SegGeom g, f
         float mn, mx;
         seg_reduce<T, VEC>(x, g, seg, active, mn, mx);
         if (active && (lane_id() % g.L) == 0) {
-            if (accumulate) {
-                mn = fminf(mn, mins[seg]);
-                mx = fmaxf(mx, maxs[seg]);
-            }
+            mn = fold_min(mn, mins + seg, fold);
+            mx = fold_max(mx, maxs + seg, fold);
             mins[seg] = mn;
             maxs[seg] = mx;
         }
@@ -126,7 +124,7 @@ constexpr int RV = 4;
 
 template <typename T, int VEC>
 __global__ void __launch_bounds__(NT) seg_minmax_reg_kernel(const T* x, SegGeom g, FastDiv fd, float* mins,
-                                                            float* maxs, int accumulate) {
+                                                            float* maxs, int fold) {
     const int L = g.L;
     const uint32_t gpb = NT / L;
     const uint32_t total = (uint32_t)(g.rows * g.nseg);
@@ -154,24 +152,20 @@ __global__ void __launch_bounds__(NT) seg_minmax_reg_kernel(const T* x, SegGeom 
                 for (int j = 0; j < RV; j++)
 #pragma unroll
                     for (int i = 0; i < VEC; i++) {
-                        mn[j] = fminf(mn[j], v[j].v[i]);
-                        mx[j] = fmaxf(mx[j], v[j].v[i]);
+                        mn[j] = fmin_nan(mn[j], v[j].v[i]);
+                        mx[j] = fmax_nan(mx[j], v[j].v[i]);
                     }
             }
         }
-        float a = fminf(fminf(mn[0], mn[1]), fminf(mn[2], mn[3]));
-        float b = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        float a = fmin_nan(fmin_nan(mn[0], mn[1]), fmin_nan(mn[2], mn[3]));
+        float b = fmax_nan(fmax_nan(mx[0], mx[1]), fmax_nan(mx[2], mx[3]));
         for (int off = L / 2; off > 0; off >>= 1) {
-            a = fminf(a, __shfl_xor_sync(0xffffffffu, a, off));
-            b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, off));
+            a = fmin_nan(a, __shfl_xor_sync(0xffffffffu, a, off));
+            b = fmax_nan(b, __shfl_xor_sync(0xffffffffu, b, off));
         }
         if (active && sub == 0) {
-            if (accumulate) {
-                a = fminf(a, mins[seg]);
-                b = fmaxf(b, maxs[seg]);
-            }
-            mins[seg] = a;
-            maxs[seg] = b;
+            mins[seg] = fold_min(a, mins + seg, fold);
+            maxs[seg] = fold_max(b, maxs + seg, fold);
         }
     }
 }
@@ -346,15 +340,15 @@ __global__ void __launch_bounds__(NT) rtn_reg_kernel(const T* x, SegGeom g, Fast
             for (int j = 0; j < RV; j++)
 #pragma unroll
                 for (int i = 0; i < VEC; i++) {
-                    mn[j] = fminf(mn[j], v[j].v[i]);
-                    mx[j] = fmaxf(mx[j], v[j].v[i]);
+                    mn[j] = fmin_nan(mn[j], v[j].v[i]);
+                    mx[j] = fmax_nan(mx[j], v[j].v[i]);
                 }
         }
-        float smin = fminf(fminf(mn[0], mn[1]), fminf(mn[2], mn[3]));
-        float smax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        float smin = fmin_nan(fmin_nan(mn[0], mn[1]), fmin_nan(mn[2], mn[3]));
+        float smax = fmax_nan(fmax_nan(mx[0], mx[1]), fmax_nan(mx[2], mx[3]));
         for (int off = L / 2; off > 0; off >>= 1) {
-            smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, off));
-            smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+            smin = fmin_nan(smin, __shfl_xor_sync(0xffffffffu, smin, off));
+            smax = fmax_nan(smax, __shfl_xor_sync(0xffffffffu, smax, off));
         }
         if (!active) continue;
         float s;
@@ -436,17 +430,17 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
                     const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(&ww[k]);
-                    mn2[k & 1] = __hmin2(mn2[k & 1], p);
-                    mx2[k & 1] = __hmax2(mx2[k & 1], p);
+                    mn2[k & 1] = __hmin2_nan(mn2[k & 1], p);
+                    mx2[k & 1] = __hmax2_nan(mx2[k & 1], p);
                 }
             }
         }
-        const __nv_bfloat162 mnp = __hmin2(mn2[0], mn2[1]), mxp = __hmax2(mx2[0], mx2[1]);
-        float smin = fminf(__low2float(mnp), __high2float(mnp));
-        float smax = fmaxf(__low2float(mxp), __high2float(mxp));
+        const __nv_bfloat162 mnp = __hmin2_nan(mn2[0], mn2[1]), mxp = __hmax2_nan(mx2[0], mx2[1]);
+        float smin = fmin_nan(__low2float(mnp), __high2float(mnp));
+        float smax = fmax_nan(__low2float(mxp), __high2float(mxp));
         for (int off = L / 2; off > 0; off >>= 1) {
-            smin = fminf(smin, __shfl_xor_sync(0xffffffffu, smin, off));
-            smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+            smin = fmin_nan(smin, __shfl_xor_sync(0xffffffffu, smin, off));
+            smax = fmax_nan(smax, __shfl_xor_sync(0xffffffffu, smax, off));
         }
         if (!active) continue;
         float s;
@@ -580,7 +574,7 @@ bool vec_ok(const void* x, int64_t ld, int64_t gs, int64_t cols) {
 
 template <typename T>
 llmc_status launch_minmax(llmc_ctx* ctx, const void* x, int64_t rows, int64_t cols, int64_t ld, int64_t gs,
-                          float* mins, float* maxs, int accumulate) {
+                          float* mins, float* maxs, int fold) {
     constexpr int V = 16 / sizeof(T);
     SegGeom g{rows, cols, ld, gs, (cols + gs - 1) / gs, 1};
     const int64_t total = rows * g.nseg;
@@ -591,25 +585,25 @@ llmc_status launch_minmax(llmc_ctx* ctx, const void* x, int64_t rows, int64_t co
         if (cols % seglen == 0 && rl > 0 && total < (int64_t(1) << 31) && g.nseg < (int64_t(1) << 31)) {
             g.L = rl;
             seg_minmax_reg_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
-                reinterpret_cast<const T*>(x), g, make_fastdiv((uint32_t)g.nseg), mins, maxs, accumulate);
+                reinterpret_cast<const T*>(x), g, make_fastdiv((uint32_t)g.nseg), mins, maxs, fold);
         } else {
             seg_minmax_kernel<T, V><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
-                reinterpret_cast<const T*>(x), g, mins, maxs, accumulate);
+                reinterpret_cast<const T*>(x), g, mins, maxs, fold);
         }
     } else {
         g.L = lanes_for(gs < cols ? gs : cols, 1);
         seg_minmax_kernel<T, 1><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
-            reinterpret_cast<const T*>(x), g, mins, maxs, accumulate);
+            reinterpret_cast<const T*>(x), g, mins, maxs, fold);
     }
     return check_launch(ctx, "seg_minmax");
 }
 
 llmc_status dispatch_minmax(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, int64_t gs,
-                            float* mins, float* maxs, int accumulate) {
+                            float* mins, float* maxs, int fold) {
     switch (dtype) {
-        case LLMC_DTYPE_F32: return launch_minmax<float>(ctx, x, rows, cols, ld, gs, mins, maxs, accumulate);
-        case LLMC_DTYPE_BF16: return launch_minmax<__nv_bfloat16>(ctx, x, rows, cols, ld, gs, mins, maxs, accumulate);
-        case LLMC_DTYPE_F16: return launch_minmax<__half>(ctx, x, rows, cols, ld, gs, mins, maxs, accumulate);
+        case LLMC_DTYPE_F32: return launch_minmax<float>(ctx, x, rows, cols, ld, gs, mins, maxs, fold);
+        case LLMC_DTYPE_BF16: return launch_minmax<__nv_bfloat16>(ctx, x, rows, cols, ld, gs, mins, maxs, fold);
+        case LLMC_DTYPE_F16: return launch_minmax<__half>(ctx, x, rows, cols, ld, gs, mins, maxs, fold);
     }
     return fail(LLMC_ERR_INVALID_ARG, "bad dtype %d", dtype);
 }
@@ -674,17 +668,21 @@ llmc_status minmax(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_
                    int64_t group_size, float* mins, float* maxs, int accumulate, float* scratch) {
     if (strategy == LLMC_STRATEGY_TENSOR) {
         // Level 1: per-row min/max into scratch; level 2: min over the row minima and max
-        // over the row maxima (each level-2 call also produces one unused value).
+        // over the row maxima (each level-2 call also produces one unused value).  Both levels
+        // propagate NaN, so the batch value is torch's x.min() / x.max(); the fold into the
+        // running value is MinMaxObserver's.
+        const int fold = accumulate == 0 ? FOLD_NONE : (accumulate == 1 ? FOLD_OBSERVER : FOLD_FRESH);
         float* rmin = scratch;
         float* rmax = scratch + rows;
         float* unused = scratch + 2 * rows + 32;
-        LLMC_TRY(dispatch_minmax(ctx, x, dtype, rows, cols, ld, cols, rmin, rmax, 0));
-        LLMC_TRY(dispatch_minmax(ctx, rmin, LLMC_DTYPE_F32, 1, rows, rows, rows, mins, unused, accumulate));
-        LLMC_TRY(dispatch_minmax(ctx, rmax, LLMC_DTYPE_F32, 1, rows, rows, rows, unused, maxs, accumulate));
+        LLMC_TRY(dispatch_minmax(ctx, x, dtype, rows, cols, ld, cols, rmin, rmax, FOLD_NONE));
+        LLMC_TRY(dispatch_minmax(ctx, rmin, LLMC_DTYPE_F32, 1, rows, rows, rows, mins, unused, fold));
+        LLMC_TRY(dispatch_minmax(ctx, rmax, LLMC_DTYPE_F32, 1, rows, rows, rows, unused, maxs, fold));
         return LLMC_OK;
     }
     const int64_t gs = strategy == LLMC_STRATEGY_GROUP ? group_size : cols;
-    return dispatch_minmax(ctx, x, dtype, rows, cols, ld, gs, mins, maxs, accumulate);
+    const int fold = accumulate == 0 ? FOLD_NONE : (accumulate == 1 ? FOLD_MINIMUM : FOLD_FRESH);
+    return dispatch_minmax(ctx, x, dtype, rows, cols, ld, gs, mins, maxs, fold);
 }
 
 llmc_status affine(llmc_ctx* ctx, const float* mins, const float* maxs, int64_t count, int bits, int sym, float* scales,
@@ -702,7 +700,7 @@ llmc_status rtn(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64_t n, i
         // scratch: [2m + 64] for the two-level reduction, then 2 device scalars.
         float* mn = scratch + 2 * m + 64;
         float* mx = mn + 1;
-        LLMC_TRY(minmax(ctx, W, dtype, m, n, ldw, LLMC_STRATEGY_TENSOR, n, mn, mx, 0, scratch));
+        LLMC_TRY(minmax(ctx, W, dtype, m, n, ldw, LLMC_STRATEGY_TENSOR, n, mn, mx, 2, scratch));  // fresh observer
         LLMC_TRY(affine(ctx, mn, mx, 1, bits, sym, scales, zps));
         tensor_mode = 1;
     } else if (cfg->strategy == LLMC_STRATEGY_GROUP) {

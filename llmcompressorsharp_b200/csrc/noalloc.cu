@@ -18,7 +18,11 @@
 //     LLMC_ERR_SHAPE before anything is launched.  cols and ld are not limited.
 //   * The first call on a device does set-up: it looks up the array's device address with
 //     cudaGetSymbolAddress (which may load the module).  Make that first call before any
-//     stream capture begins.
+//     stream capture begins.  llmc_init forgets the looked-up address of its device, so a
+//     host that resets the device (cudaDeviceReset, which unloads the module and may place
+//     the array elsewhere) and then creates a new context gets a fresh lookup.
+//   * The call makes its context's device current for its own work and gives the calling
+//     thread its previous current device back before it returns.
 //   * Every call on one device shares the one array.  Calls whose kernels can overlap
 //     (different streams, or different host threads without ordering) race on it and give
 //     wrong results; order them on one stream.
@@ -57,6 +61,13 @@ llmc_status rows_buffer(int device, float** out) {
 }
 
 }  // namespace
+
+void noalloc_forget(int device) {
+    if (device < 0 || device >= kMaxDevices) return;
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    g_rows_addr[device] = nullptr;
+}
+
 }  // namespace llmc
 
 using namespace llmc;
@@ -76,9 +87,21 @@ extern "C" llmc_status llmc_observer_minmax_tensor_noalloc(llmc_ctx* ctx, const 
                     "rows=%lld exceeds the static row buffer of the no-allocation observer (at most %lld rows); "
                     "use llmc_observer_minmax",
                     (long long)rows, (long long)kMaxRows);
-    cudaError_t e = cudaSetDevice(ctx->device);
-    if (e != cudaSuccess) return fail(LLMC_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    int prev = -1;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return fail(LLMC_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (prev != ctx->device) {
+        e = cudaSetDevice(ctx->device);
+        if (e != cudaSuccess) return fail(LLMC_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    }
     float* scratch = nullptr;
-    LLMC_TRY(rows_buffer(ctx->device, &scratch));
-    return minmax(ctx, x, dtype, rows, cols, ld, LLMC_STRATEGY_TENSOR, cols, min_io, max_io, accumulate, scratch);
+    llmc_status st = rows_buffer(ctx->device, &scratch);
+    if (st == LLMC_OK)
+        st = minmax(ctx, x, dtype, rows, cols, ld, LLMC_STRATEGY_TENSOR, cols, min_io, max_io, accumulate, scratch);
+    if (prev != ctx->device) {
+        e = cudaSetDevice(prev);
+        if (e != cudaSuccess && st == LLMC_OK)
+            return fail(LLMC_ERR_CUDA, "restoring the caller's device: %s", cudaGetErrorString(e));
+    }
+    return st;
 }

@@ -31,7 +31,11 @@ llmc_status gemm_tc(llmc_ctx* ctx, const GemmArgs& g);
 llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t d, int64_t ld, float* H, int64_t ldh);
 
 // ---- observers / quantisation (k_quant.cu) -----------------------------------------------
-// scratch: minmax_scratch_floats(strategy, rows) floats (only the per-tensor reduction uses it)
+// scratch: minmax_scratch_floats(strategy, rows) floats (only the per-tensor reduction uses it).
+// Element reductions propagate NaN (torch.amin / amax).  accumulate: 0 stores the batch values;
+// 1 folds them into mins / maxs (TENSOR: MinMaxObserver's strict-less rule, a NaN batch changes
+// nothing; CHANNEL / GROUP: torch.minimum / maximum); 2 folds them into a new MinMaxObserver
+// (+inf / -inf) per entry.
 llmc_status minmax(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
                    int strategy, int64_t group_size, float* mins, float* maxs, int accumulate, float* scratch);
 size_t minmax_scratch_floats(int strategy, int64_t rows);
@@ -48,6 +52,9 @@ llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, 
 llmc_status upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ldh, float* out, int64_t ldo);
 
 // ---- misc ----------------------------------------------------------------------------------
+// Drops the no-allocation observer's cached device address of its static row buffer on
+// `device` (noalloc.cu); llmc_init calls it so that a reset device gets a fresh lookup.
+void noalloc_forget(int device);
 llmc_status device_error_check(llmc_ctx* ctx);
 llmc_status symmetrize_from_upper(llmc_ctx* ctx, const float* src, int64_t d, int64_t lds, float* dst, int64_t ldd);
 llmc_status convert_to_f32(llmc_ctx* ctx, const void* src, int dtype, int64_t rows, int64_t cols, int64_t lds,

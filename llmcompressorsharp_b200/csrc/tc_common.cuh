@@ -8,7 +8,9 @@
 namespace llmc {
 namespace tc {
 
-constexpr unsigned WAIT_LIMIT = 1u << 26;  // try_wait attempts before giving up
+// try_wait attempts before a wait gives up: the default of llmc_ctx::wait_limit, and the fixed
+// bound of the drain waits that run after an abort.
+constexpr unsigned WAIT_LIMIT = 1u << 26;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -38,10 +40,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait; returns false (and raises the abort flag) when it gives up or when
-// another thread has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
-    for (unsigned i = 0; i < WAIT_LIMIT; i++) {
+// Bounded wait of at most `limit` attempts; returns false (and raises the abort flag) when it
+// gives up or when another thread has already aborted.  limit = 0 gives up at once.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,
+                                          uint32_t limit) {
+    for (unsigned i = 0; i < limit; i++) {
         if (mbar_try_wait(b, parity)) return true;
         if ((i & 255u) == 255u && *abort_flag) return false;
     }
@@ -209,6 +212,37 @@ __device__ __forceinline__ void umma2_commit_mc(uint64_t* bar, uint16_t mask) {
 // Arrive on an mbarrier given as a shared::cluster address (possibly in the other CTA).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// try_wait with cluster-scope acquire: the waiter sees what another CTA of the cluster wrote
+// before its release-cluster arrive on this barrier.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded cluster-scope wait (same contract as mbar_wait).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,
+                                                  uint32_t limit) {
+    for (unsigned i = 0; i < limit; i++) {
+        if (mbar_try_wait_cluster(b, parity)) return true;
+        if ((i & 255u) == 255u && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    atomicOr(err, 1);
+    return false;
+}
+
+// 32-bit store into shared memory given as a shared::cluster address (possibly the other CTA's).
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr_cluster, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr_cluster), "r"(v) : "memory");
 }
 
 }  // namespace tc

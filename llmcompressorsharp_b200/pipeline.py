@@ -109,6 +109,11 @@ class GptqPipeline:
                 n += int(v.value)
         return n
 
+    def check(self):
+        """Waits for the job and raises the first deferred device error (overlap mode)."""
+        if self.overlap is not None:
+            self.overlap.check()
+
     def hessian_sms(self) -> int:
         """SMs the Hessian kernel runs on."""
         sm = torch.cuda.get_device_properties(self.device).multi_processor_count
@@ -249,7 +254,7 @@ class GptqPipeline:
             self.solve_site(s, self.hessian_ptr(s.name), weights, outputs)
 
     def run_distributed(self, layers, acts, weights, outputs, world: int, rank: int, group=None, before_solve=None,
-                        after_solve=None, hess_events=None, acts_ready=None, shard: str = "layers"):
+                        after_solve=None, hess_events=None, acts_ready=None, shard: str = "layers", sync: bool = True):
         """``run`` for one process per GPU (NCCL process group initialised by the caller):
         ``acts`` are this rank's token shard.  ``shard="layers"``: partial Hessians are reduced
         onto each layer's owner, which solves the whole layer; ``weights`` / ``outputs`` are
@@ -264,10 +269,10 @@ class GptqPipeline:
             raise ValueError(f"unknown shard mode {shard}")
         acts_for = acts if callable(acts) else (lambda _l: acts)
         return self.overlap.run_dist(list(layers), acts_for, weights, outputs, world, rank, group, before_solve,
-                                     after_solve, hess_events, dict(acts_ready or {}), rows=shard == "rows")
+                                     after_solve, hess_events, dict(acts_ready or {}), rows=shard == "rows", sync=sync)
 
     def run(self, layers, acts, weights, outputs, before_solve=None, after_solve=None, hess_events=None,
-            acts_ready=None):
+            acts_ready=None, sync: bool = True):
         """The whole job over ``layers``: per layer, every site's Hessian, factor and stacked
         GPTQ solve.  ``acts`` is {site: [T, d]} (shared by the layers) or a callable
         layer -> {site: tensor}; ``weights[l]`` / ``outputs[l]`` per layer.  ``before_solve(l)``
@@ -278,12 +283,14 @@ class GptqPipeline:
         (rows, event) per copied row range}) makes the first accumulation of each site wait for
         its activations, still being copied in on another stream (chunk by chunk with the list
         form).  Work is enqueued on the current stream (or, with overlap enabled,
-        on the two pipeline streams joined back into it)."""
+        on the two pipeline streams joined back into it).  With overlap enabled the solves report a
+        non-PD Hessian on the device; ``sync=True`` waits for the job at the end and raises such an
+        error, ``sync=False`` returns at once and leaves the check to ``check()``."""
         acts_for = acts if callable(acts) else (lambda _l: acts)
         pending = dict(acts_ready or {})
         if self.overlap is not None:
             return self.overlap.run(list(layers), acts_for, weights, outputs, before_solve, after_solve, hess_events,
-                                    pending)
+                                    pending, sync=sync)
         for l in layers:
             a = acts_for(l)
             for s in self.sites:
@@ -347,6 +354,9 @@ class _Overlap:
         # start on the reserved SMs and on any SM a finishing Hessian launch frees.
         self.solve_sms = max(1, int(reserve_sms))
         _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(self.solve_sms))
+        # The factorisation decides a non-PD Hessian on the device, so enqueueing a solve never
+        # waits for the GPU; a failure surfaces at the llmc_sync that ends the job.
+        _lib.call("llmc_set_deferred_errors", C.c_void_p(self.cs), C.c_int32(1))
         self.h = [{}, {}]
         for b in range(2):
             for s in pipe.sites:
@@ -377,7 +387,7 @@ class _Overlap:
         _lib.call("llmc_hessian_data", C.c_void_p(self.h[b][site]), C.byref(p))
         return p.value
 
-    def run(self, layers, acts_for, weights, outputs, before_solve, after_solve, hess_events, acts_ready):
+    def run(self, layers, acts_for, weights, outputs, before_solve, after_solve, hess_events, acts_ready, sync=True):
         pipe = self.pipe
         cur = torch.cuda.current_stream(pipe.device)
         self.sh.wait_stream(cur)
@@ -416,7 +426,7 @@ class _Overlap:
                 acc_done = torch.cuda.Event()
                 acc_done.record(self.sh)
             if pending is not None:
-                solve(pending)  # may block the host (factor flags) while the Hessian stream runs on
+                solve(pending)
             pending = (l, b, acc_done)
         if pending is not None:
             # The last layer's solve waits for the last accumulation, so nothing else runs beside
@@ -428,10 +438,21 @@ class _Overlap:
                 _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(self.solve_sms))
         cur.wait_stream(self.sh)
         cur.wait_stream(self.ss)
+        if sync:
+            self.check()
+
+    def check(self):
+        """Waits for the solve stream and raises the first deferred device error (a Hessian
+        that was not positive definite, a bounded wait that gave up) of either context."""
+        for c in (self.cs, self.ch):
+            _lib.call("llmc_sync", C.c_void_p(c))
 
     # ---- one process per GPU ------------------------------------------------------------------
     DIST_SETS = 6  # Hessian handle sets in flight per rank
-    DIST_LAG = 3   # an owned layer is solved once this many later layers are queued behind it
+    # An owned layer's solve is enqueued once this many later layers are queued behind it.  The
+    # solve stream waits for the layer's reduction on the device, so enqueueing never blocks the
+    # host; one layer of lag keeps the next accumulation ahead of the solve in the launch order.
+    DIST_LAG = 1
 
     def _dist_sets(self):
         if not getattr(self, "hd", None):
@@ -453,7 +474,7 @@ class _Overlap:
         self.hd = []
 
     def run_dist(self, layers, acts_for, weights, outputs, world, rank, group, before_solve, after_solve,
-                 hess_events, acts_ready, rows=False):
+                 hess_events, acts_ready, rows=False, sync=True):
         """Token-sharded job on `world` ranks: every rank accumulates its partial Hessians of
         every layer on the Hessian stream and reduces them onto the layer's owner with NCCL
         (issued from the Hessian stream, so the transfer of layer l overlaps the accumulation of
@@ -528,6 +549,8 @@ class _Overlap:
             solve(queue.pop(0))
         for st in (self.sh, self.ss, self.sc):
             cur.wait_stream(st)
+        if sync:
+            self.check()
 
 
 def _stack_key(site: SiteSpec) -> str:

@@ -107,8 +107,11 @@ class MinMaxObserver(Observer):
         if self.device is None:
             self.device = target_device(x)
         if self._mm is None:
-            self._mm = torch.empty(2, dtype=torch.float32, device=self.device)
-        _minmax(x, 0, 0, self._mm[0:1], self._mm[1:2], self._has)
+            # MinMaxObserver.cs:16-17: the running values start at +inf / -inf, and every batch
+            # is folded in by the observer's strict-less rule (a batch holding a NaN changes
+            # nothing, MinMaxObserver.cs:34-42).
+            self._mm = torch.tensor([float("inf"), float("-inf")], dtype=torch.float32, device=self.device)
+        _minmax(x, 0, 0, self._mm[0:1], self._mm[1:2], True)
         self._has = True
 
     def get_quant_params(self, num_bits: int, symmetric: bool):
@@ -208,13 +211,20 @@ class MovingAverageMinMaxObserver(Observer):
         if not (0.0 < averaging_constant <= 1.0):
             raise ArgumentOutOfRangeError("averagingConstant must be in (0, 1].")
         self._alpha = f32(averaging_constant)
-        self._batch = MinMaxObserver(device)
+        self.device = torch.device(device) if device is not None else None
+        self._mm = None
         self.reset()
 
     def update(self, x: torch.Tensor) -> None:
-        self._batch.reset()
-        self._batch.update(x)
-        bmin, bmax = (f32(v) for v in self._batch.min_max())
+        if x is None:
+            raise ArgumentError("x must not be null")
+        if self.device is None:
+            self.device = target_device(x)
+        if self._mm is None:
+            self._mm = torch.empty(2, dtype=torch.float32, device=self.device)
+        # The batch's own x.min() / x.max() (MovingAverageMinMaxObserver.cs:44-47), NaN included.
+        _minmax(x, 0, 0, self._mm[0:1], self._mm[1:2], False)
+        bmin, bmax = (f32(v) for v in self._mm.tolist())
         if not self._has:
             self._min, self._max, self._has = bmin, bmax, True
         else:
@@ -225,7 +235,7 @@ class MovingAverageMinMaxObserver(Observer):
     def get_quant_params(self, num_bits: int, symmetric: bool):
         if not self._has:
             raise InvalidOperationError("MovingAverageMinMaxObserver has no calibration samples.")
-        dev = self._batch.device
+        dev = self.device
         s, z = affine_params(torch.tensor([self._min], device=dev), torch.tensor([self._max], device=dev), num_bits,
                              symmetric)
         return float(s.item()), int(z.item())

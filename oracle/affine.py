@@ -33,7 +33,9 @@ def compute_affine_params(mn: float, mx: float, num_bits: int, symmetric: bool) 
     mn = f32(mn)
     mx = f32(mx)
     if symmetric:
-        abs_max = max(abs(mn), abs(mx))  # MathF.Max(MathF.Abs(min), MathF.Abs(max)), :60
+        # MathF.Max(MathF.Abs(min), MathF.Abs(max)), :60; MathF.Max returns NaN when either
+        # operand is NaN (Python's max would depend on the argument order).
+        abs_max = f32(np.nan) if (np.isnan(mn) or np.isnan(mx)) else max(abs(mn), abs(mx))
         q_max = (1 << (num_bits - 1)) - 1
         scale = f32(1.0) if abs_max == f32(0) else f32(abs_max / f32(q_max))
         return float(scale), 0
@@ -41,8 +43,11 @@ def compute_affine_params(mn: float, mx: float, num_bits: int, symmetric: bool) 
     q_max = (1 << num_bits) - 1
     rng = f32(mx - mn)  # :69
     scale = f32(1.0) if rng == f32(0) else f32(rng / f32(q_max - q_min))  # :70
-    zp = int(np.rint(f32(f32(q_min) - f32(mn / scale))))  # :71, MathF.Round = half-even
-    zp = min(max(zp, q_min), q_max)  # :72
+    with np.errstate(invalid="ignore", divide="ignore"):
+        zf = np.rint(f32(f32(q_min) - f32(mn / scale)))  # :71, MathF.Round = half-even
+    # (long) of a float saturates in .NET 10 (the reference's target): NaN -> 0, +-inf -> the
+    # long range; Math.Clamp then bounds it (:72).
+    zp = 0 if np.isnan(zf) else int(min(max(zf, q_min), q_max))
     return float(scale), zp
 
 
@@ -63,9 +68,23 @@ def affine_params_array(mins, maxs, num_bits: int, symmetric: bool):
         q_max = (1 << num_bits) - 1
         rng = (maxs - mins).astype(np.float32)
         scale = np.where(rng == 0, f32(1), (rng / f32(q_max)).astype(np.float32)).astype(np.float32)
-        zp = np.rint((f32(0) - (mins / scale).astype(np.float32)).astype(np.float32)).astype(np.int64)
-        zp = np.clip(zp, 0, q_max)
+        zf = np.rint((f32(0) - (mins / scale).astype(np.float32)).astype(np.float32))
+        zp = np.where(np.isnan(zf), 0, np.clip(zf, 0, q_max)).astype(np.int64)  # saturating, NaN -> 0
         return scale, zp
+
+
+def observer_fold(b_min, b_max):
+    """MinMaxObserver.Update on a new observer (MinMaxObserver.cs:16-17,34-42): the running
+    values start at +inf / -inf and take the batch value only when it is strictly beyond them,
+    so a NaN batch minimum (torch's x.min() of a tensor holding a NaN) leaves +inf.  Works on
+    scalars and, element-wise, on arrays (one observer per element, as ComputeScaleZeroPoint
+    creates one per row, GptqBlockQuantizer.cs:212-230)."""
+    b_min = np.asarray(b_min, dtype=np.float32)
+    b_max = np.asarray(b_max, dtype=np.float32)
+    with np.errstate(invalid="ignore"):
+        mn = np.where(b_min < np.float32(np.inf), b_min, np.float32(np.inf)).astype(np.float32)
+        mx = np.where(b_max > np.float32(-np.inf), b_max, np.float32(-np.inf)).astype(np.float32)
+    return mn, mx
 
 
 def _as_f32(x: torch.Tensor) -> torch.Tensor:

@@ -17,7 +17,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .affine import compute_affine_params, affine_params_array, group_minmax
+from .affine import compute_affine_params, affine_params_array, group_minmax, observer_fold
 from .fakequant import fake_quantize_codes
 from .hessian import upper_factor
 
@@ -43,17 +43,21 @@ def compute_scale_zero_point(w: torch.Tensor, cfg: GPTQConfig):
     as [m, G] where G = 1 (tensor/channel) or the group count."""
     m, n = w.shape
     wf = w.detach().to(torch.float32)
+    # One new MinMaxObserver per tensor / row (:200-203, :212-222): observer_fold.
     if cfg.strategy == "tensor":
-        s, z = compute_affine_params(wf.min().item(), wf.max().item(), cfg.num_bits, cfg.symmetric)
+        mn, mx = observer_fold(wf.min().item(), wf.max().item())
+        s, z = compute_affine_params(float(mn), float(mx), cfg.num_bits, cfg.symmetric)
         return (np.full((m, 1), s, dtype=np.float32), np.full((m, 1), z, dtype=np.int64))
     if cfg.strategy == "channel":
         if cfg.channel_axis != 0:
             raise NotImplementedError("per-channel GPTQ uses output channels (axis 0)")
-        s, z = affine_params_array(wf.amin(dim=1).numpy(), wf.amax(dim=1).numpy(), cfg.num_bits, cfg.symmetric)
+        mn, mx = observer_fold(wf.amin(dim=1).numpy(), wf.amax(dim=1).numpy())
+        s, z = affine_params_array(mn, mx, cfg.num_bits, cfg.symmetric)
         return s.reshape(m, 1), z.reshape(m, 1)
     if cfg.strategy == "group":
         mins, maxs = group_minmax(wf, cfg.group_size)
-        s, z = affine_params_array(mins.numpy(), maxs.numpy(), cfg.num_bits, cfg.symmetric)
+        mn, mx = observer_fold(mins.numpy(), maxs.numpy())
+        s, z = affine_params_array(mn, mx, cfg.num_bits, cfg.symmetric)
         return s, z
     raise NotImplementedError(f"Quantization strategy '{cfg.strategy}' is not supported by GptqBlockQuantizer.")
 

@@ -139,7 +139,52 @@ def test_minmax_all_zeros_scale_one():  # :85-95
     assert obs.get_quant_params(8, True) == (1.0, 0)
 
 
+# Derived from the code (no reference test): a batch holding a NaN has x.min() = x.max() = NaN,
+# `NaN < _min` is false, so MinMaxObserver.Update (MinMaxObserver.cs:29-42) leaves both running
+# values as they were; a first NaN batch leaves +inf / -inf.
+def test_minmax_nan_batch_changes_nothing():
+    obs = affine.MinMaxObserver()
+    obs.update(torch.tensor([-2.0, float("nan"), 3.0]))
+    assert obs._min == np.float32(np.inf) and obs._max == np.float32(-np.inf)
+    obs.update(torch.tensor([-1.0, 4.0]))
+    obs.update(torch.tensor([float("nan"), -9.0, 9.0]))
+    assert (obs._min, obs._max) == (np.float32(-1.0), np.float32(4.0))
+    assert obs.get_quant_params(8, True) == pytest.approx((4 / 127, 0))
+
+
+# MathF.Max(MathF.Abs(NaN), x) is NaN, so ComputeAffineParams (Observer.cs:58-75) gives a NaN
+# scale; NaN zero-points saturate to 0.
+def test_affine_params_nan_inputs():
+    s, z = affine.compute_affine_params(float("nan"), 1.0, 8, True)
+    assert np.isnan(s) and z == 0
+    s, z = affine.compute_affine_params(1.0, float("nan"), 8, True)
+    assert np.isnan(s) and z == 0
+    s, z = affine.compute_affine_params(float("nan"), 1.0, 4, False)
+    assert np.isnan(s) and z == 0
+
+
 # --- PerChannelMinMaxObserverTests.cs ------------------------------------------------
+
+# Derived: amin / amax and torch.minimum / maximum propagate NaN
+# (PerChannelMinMaxObserver.cs:55-74), so a channel that ever saw a NaN stays NaN.
+def test_per_channel_nan_propagates():
+    obs = affine.PerChannelMinMaxObserver(0)
+    obs.update(torch.tensor([[-1.0, float("nan")], [-3.0, 5.0]]))
+    obs.update(torch.tensor([[-5.0, 1.0], [-2.0, 8.0]]))
+    assert np.isnan(obs._min[0].item()) and np.isnan(obs._max[0].item())
+    assert obs._min[1].item() == -3.0 and obs._max[1].item() == 8.0
+
+
+# Derived: ComputeScaleZeroPoint builds a new MinMaxObserver per row (GptqBlockQuantizer.cs:212-222),
+# so a weight row holding a NaN is quantised with the parameters of (+inf, -inf).
+def test_gptq_params_of_a_nan_row_follow_the_observer():
+    w = torch.tensor([[1.0, float("nan"), -2.0, 0.5], [0.25, -0.5, 1.0, -1.0]])
+    s, z = gptq.compute_scale_zero_point(w, gptq.GPTQConfig(num_bits=4, symmetric=False, strategy="channel"))
+    ref = affine.compute_affine_params(np.inf, -np.inf, 4, False)
+    assert (np.isnan(s[0, 0]) and np.isnan(ref[0])) or s[0, 0] == ref[0]
+    assert z[0, 0] == ref[1]
+    assert (s[1, 0], z[1, 0]) == affine.compute_affine_params(-1.0, 1.0, 4, False)
+
 
 def test_per_channel_one_scale_per_row():  # PerChannelMinMaxObserverTests.cs:118-143
     obs = affine.PerChannelMinMaxObserver(0)

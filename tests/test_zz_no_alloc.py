@@ -70,6 +70,44 @@ def test_noalloc_running_update_and_strided_view():
 
 
 @pytest.mark.gpu
+def test_noalloc_call_allocates_no_device_memory():
+    """The property the entry exists for.  On a fresh context (empty workspace) the calls after
+    the first one leave the device's free memory unchanged, while the workspace observer on the
+    same context has to grow its workspace (a cudaMalloc that shows in the free memory), which
+    shows that the check would see an allocation."""
+    lib = _lib.load()
+    c = C.c_void_p()
+    assert lib.llmc_init(0, C.byref(c)) == 0, _lib.last_error()
+    try:
+        assert lib.llmc_set_stream(c, C.c_void_p(torch.cuda.current_stream().cuda_stream or 1)) == 0
+        x = torch.randn(8192, 1024, device="cuda")
+        mn = torch.zeros(1, device="cuda")
+        mx = torch.zeros(1, device="cuda")
+        args = (_lib.ptr(x), _lib.dtype_code(x.dtype), C.c_int64(x.shape[0]), C.c_int64(x.shape[1]),
+                C.c_int64(x.stride(0)))
+
+        def noalloc():
+            assert lib.llmc_observer_minmax_tensor_noalloc(c, *args, _lib.ptr(mn), _lib.ptr(mx), 0) == 0, \
+                _lib.last_error()
+
+        noalloc()  # first call on the context's device: address lookup
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        for _ in range(3):
+            noalloc()
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] == free0
+        assert float(mn) == float(x.min()) and float(mx) == float(x.max())
+        st = lib.llmc_observer_minmax(c, *args, _lib.STRATEGY["tensor"], C.c_int64(x.shape[1]), _lib.ptr(mn),
+                                      _lib.ptr(mx), 0)
+        assert st == 0, _lib.last_error()
+        torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] < free0
+    finally:
+        lib.llmc_destroy(c)
+
+
+@pytest.mark.gpu
 def test_noalloc_rejects_rows_over_the_limit():
     x = torch.zeros(MAX_ROWS + 1, 8, device="cuda")
     launches = _lib.launch_count(0)
