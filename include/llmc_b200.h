@@ -205,6 +205,26 @@ llmc_status llmc_gptq_quantize_batch(llmc_ctx* ctx, int32_t count, const void* c
                                      const llmc_qconfig* cfg, float* wq_out, int64_t ldq, uint8_t* codes_out,
                                      float* scales_out, int32_t* zps_out);
 
+/* ---- GPTQ activation order (extension) -----------------------------------------------------
+ * No reference counterpart: the reference rejects GPTQConfig.ActOrder (GPTQModifier.cs:47-56,
+ * GptqBlockQuantizer.cs:77-82; llmc_gptq_quantize keeps that rejection).  Flow: perm from
+ * llmc_gptq_act_order_perm(H); H_p from llmc_permute_hessian(H, perm); U_p from
+ * llmc_chol_inverse(H_p, want_upper = 1); then llmc_gptq_quantize_batch_perm(W, U_p, perm).
+ * Scales / zero-points come from the original weight per original column group (static
+ * groups, as GptqBlockQuantizer.cs:97 computes them before the loop); outputs are in the
+ * original column order. */
+/* perm_out[k] = column with the k-th largest H[k][k] (stable: equal values by index; NaN first). */
+llmc_status llmc_gptq_act_order_perm(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int32_t* perm_out);
+/* out[a][b] = H[perm[a]][perm[b]], full matrix; upper_only reads H's upper triangle. */
+llmc_status llmc_permute_hessian(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int32_t upper_only,
+                                 const int32_t* perm, float* out, int64_t ldo);
+/* llmc_gptq_quantize_batch with U the factor of the permuted Hessian and perm its column order;
+ * cfg->act_order is not checked.  Arguments otherwise as llmc_gptq_quantize_batch. */
+llmc_status llmc_gptq_quantize_batch_perm(llmc_ctx* ctx, int32_t count, const void* const* W, const int64_t* m,
+                                          const int64_t* ldw, int32_t dtype, int64_t n, const float* U, int64_t ldu,
+                                          const int32_t* perm, const llmc_qconfig* cfg, float* wq_out, int64_t ldq,
+                                          uint8_t* codes_out, float* scales_out, int32_t* zps_out);
+
 /* ---- SparseGPT (plan docs/superpowers/plans/2026-05-18-phase-4c-sparsegpt.md:37-59,1584-1656,
  * in the U-factor form of GptqBlockQuantizer.cs:124-181).  out fp32 [m,n] pruned weight,
  * mask_out (optional) one byte per element, 1 = kept. */
@@ -266,6 +286,22 @@ llmc_status llmc_rtn_quantize(llmc_ctx* ctx, const void* W, int32_t dtype, int64
 llmc_status llmc_int4_pack(llmc_ctx* ctx, const int32_t* q, int64_t count, int32_t zero_point, uint8_t* packed);
 llmc_status llmc_int4_unpack_dequant(llmc_ctx* ctx, const uint8_t* packed, int64_t count, float scale,
                                      int32_t zero_point, int32_t symmetric, float* out);
+
+/* ---- per-token activation quantisation (extension) -------------------------------------------
+ * No reference counterpart: QuantizationStrategy.PerToken exists (QuantizationStrategy.cs:9-19)
+ * but RtnModifier.cs:69-70 rejects it for weights and the reference has no activation quantiser.
+ * Dynamic W8A8-style quantisation of activations x [rows = tokens, cols = hidden] (row stride ld):
+ * one min-max observer per token row (PerChannelMinMaxObserver.cs:38-76 on axis 0; NaN propagates
+ * to the row's parameters), Observer.ComputeAffineParams (Observer.cs:47-75), and the
+ * FakeQuantizeFunction op chain in x's dtype (FakeQuantizeFunction.cs:39-44).
+ *   codes_out (optional) [rows, ldc] bytes: q = clamp(round(x / s) + zp), two's complement for a
+ *     symmetric grid (int8 view), unsigned for an asymmetric one; a NaN element's code is 0;
+ *   scales_out [rows] fp32; zps_out (optional) [rows] int32;
+ *   deq_out (optional) [rows, ldd] in x's dtype: the fake-quantised activations.
+ * num_bits in [2, 8]. */
+llmc_status llmc_act_quant_per_token(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows, int64_t cols, int64_t ld,
+                                     int32_t num_bits, int32_t symmetric, uint8_t* codes_out, int64_t ldc,
+                                     float* scales_out, int32_t* zps_out, void* deq_out, int64_t ldd);
 
 /* ---- SmoothQuant / AWQ ------------------------------------------------------------------
  * UpdateActivationMax (SmoothQuantModifier.cs:71-115): running_max[cols] = max(running_max,

@@ -12,8 +12,10 @@ from .errors import (ArgumentError, ArgumentOutOfRangeError, CudaError, InvalidO
                      NotPositiveDefiniteError, NotSupportedError, ShapeError)
 from .hessian import ActivationHookManager, HessianAccumulator, HessianInverseSolver, upper_factor
 from .quantization import (FakeQuantize, GroupMinMaxObserver, Int4PackedTensor, MinMaxObserver,
-                           MovingAverageMinMaxObserver, MSEObserver, PerChannelMinMaxObserver, affine_params)
-from .gptq import GPTQConfig, GPTQModifier, GptqBlockQuantizer, GptqResult, gptq_quantize_u
+                           MovingAverageMinMaxObserver, MSEObserver, PerChannelMinMaxObserver, affine_params,
+                           quantize_per_token)
+from .gptq import (GPTQConfig, GPTQModifier, GptqBlockQuantizer, GptqResult, act_order_perm, gptq_quantize_act_order,
+                   gptq_quantize_u)
 from .rtn import RtnConfig, RtnModifier, rtn_quantize
 from .smoothquant import SmoothQuantConfig, SmoothQuantMapping, SmoothQuantModifier, act_absmax, smooth_apply
 from .sparsegpt import SparseGPTConfig, SparseGPTModifier, sparsegpt_prune_u

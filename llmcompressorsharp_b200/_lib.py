@@ -73,6 +73,9 @@ _SIGS = {
     "llmc_upper_factor": [P, P, I64, I64, P, I64],
     "llmc_gptq_quantize": [P, P, I32, I64, I64, I64, P, I64, C.POINTER(QConfig), P, I64, P, P, P],
     "llmc_gptq_quantize_batch": [P, I32, P, P, P, I32, I64, P, I64, C.POINTER(QConfig), P, I64, P, P, P],
+    "llmc_gptq_act_order_perm": [P, P, I64, I64, P],
+    "llmc_permute_hessian": [P, P, I64, I64, I32, P, P, I64],
+    "llmc_gptq_quantize_batch_perm": [P, I32, P, P, P, I32, I64, P, I64, P, C.POINTER(QConfig), P, I64, P, P, P],
     "llmc_sparsegpt_prune": [P, P, I32, I64, I64, I64, P, I64, C.POINTER(QConfig), P, I64, P],
     "llmc_observer_minmax": [P, P, I32, I64, I64, I64, I32, I64, P, P, I32],
     "llmc_observer_minmax_tensor_noalloc": [P, P, I32, I64, I64, I64, P, P, I32],
@@ -82,6 +85,7 @@ _SIGS = {
     "llmc_rtn_quantize": [P, P, I32, I64, I64, I64, C.POINTER(QConfig), P, P, P, P],
     "llmc_int4_pack": [P, P, I64, I32, P],
     "llmc_int4_unpack_dequant": [P, P, I64, F32, I32, I32, P],
+    "llmc_act_quant_per_token": [P, P, I32, I64, I64, I64, I32, I32, P, I64, P, P, P, I64],
     "llmc_act_absmax": [P, P, I32, I64, I64, I64, P, I32],
     "llmc_smooth_apply": [P, P, P, I32, P, I32, I64, I64, F32, P],
     "llmc_scale_apply": [P, P, P, I32, P, I32, I64, I64],

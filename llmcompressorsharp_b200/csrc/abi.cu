@@ -147,7 +147,8 @@ llmc_status int4_unpack(llmc_ctx*, const uint8_t*, int64_t, float, int, float*);
 llmc_status gptq(llmc_ctx*, const void*, int, int64_t, int64_t, int64_t, const float*, int64_t, const llmc_qconfig*,
                  float*, int64_t, uint8_t*, float*, int32_t*, int, uint8_t*);
 llmc_status gptq_batch(llmc_ctx*, int, const void* const*, const int64_t*, const int64_t*, int, int64_t, const float*,
-                       int64_t, const llmc_qconfig*, float*, int64_t, uint8_t*, float*, int32_t*, int, uint8_t*);
+                       int64_t, const llmc_qconfig*, float*, int64_t, uint8_t*, float*, int32_t*, int, uint8_t*,
+                       const int32_t*);
 llmc_status col_absmax(llmc_ctx*, const void*, int, int64_t, int64_t, int64_t, float*, int);
 llmc_status smooth_apply(llmc_ctx*, const float*, void*, int, void*, int, int64_t, int64_t, float, float*);
 llmc_status scale_apply(llmc_ctx*, const float*, void*, int, void*, int, int64_t, int64_t);
@@ -471,7 +472,55 @@ llmc_status llmc_gptq_quantize_batch(llmc_ctx* ctx, int32_t count, const void* c
     if (codes_out && cfg->num_bits <= 4 && cfg->strategy == LLMC_STRATEGY_GROUP && (cfg->group_size % 2))
         return fail(LLMC_ERR_UNSUPPORTED, "packed int4 codes need an even group size");
     return gptq_batch(ctx, count, W, m, ldw, dtype, n, U, ldu, cfg, wq_out, ldq, codes_out, scales_out, zps_out, 0,
-                      nullptr);
+                      nullptr, nullptr);
+}
+
+// ---- GPTQ activation order (extension) ---------------------------------------------------------
+llmc_status llmc_gptq_act_order_perm(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int32_t* perm_out) {
+    LLMC_ENTRY();
+    CTX_CHECK(ctx);
+    NULL_CHECK(H, "hessian");
+    NULL_CHECK(perm_out, "perm_out");
+    if (d <= 0 || ldh < d || d > (int64_t)INT32_MAX)
+        return fail(LLMC_ERR_SHAPE, "Hessian must be a square 2-D tensor (d=%lld).", (long long)d);
+    return act_order_perm(ctx, H, d, ldh, perm_out);
+}
+
+llmc_status llmc_permute_hessian(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int32_t upper_only,
+                                 const int32_t* perm, float* out, int64_t ldo) {
+    LLMC_ENTRY();
+    CTX_CHECK(ctx);
+    NULL_CHECK(H, "hessian");
+    NULL_CHECK(perm, "perm");
+    NULL_CHECK(out, "out");
+    if (d <= 0 || ldh < d || ldo < d) return fail(LLMC_ERR_SHAPE, "Hessian must be a square 2-D tensor (d=%lld).", (long long)d);
+    if (out == H) return fail(LLMC_ERR_INVALID_ARG, "out must not alias the Hessian");
+    return permute_hessian(ctx, H, d, ldh, upper_only, perm, out, ldo);
+}
+
+llmc_status llmc_gptq_quantize_batch_perm(llmc_ctx* ctx, int32_t count, const void* const* W, const int64_t* m,
+                                          const int64_t* ldw, int32_t dtype, int64_t n, const float* U, int64_t ldu,
+                                          const int32_t* perm, const llmc_qconfig* cfg, float* wq_out, int64_t ldq,
+                                          uint8_t* codes_out, float* scales_out, int32_t* zps_out) {
+    LLMC_ENTRY();
+    CTX_CHECK(ctx);
+    NULL_CHECK(W, "weights");
+    NULL_CHECK(m, "m");
+    NULL_CHECK(ldw, "ldw");
+    NULL_CHECK(U, "hinv");
+    NULL_CHECK(perm, "perm");
+    LLMC_TRY(check_qconfig(cfg, 0));
+    if (count < 1 || count > 64) return fail(LLMC_ERR_INVALID_ARG, "count must be in [1, 64]");
+    if (!dtype_ok(dtype)) return fail(LLMC_ERR_INVALID_ARG, "unsupported dtype %d", dtype);
+    if (n <= 0 || ldu < n || n > (int64_t)INT32_MAX) return fail(LLMC_ERR_SHAPE, "bad U shape");
+    for (int k = 0; k < count; k++) {
+        NULL_CHECK(W[k], "weight");
+        if (m[k] <= 0 || ldw[k] < n) return fail(LLMC_ERR_SHAPE, "bad shape of weight %d", k);
+    }
+    if (wq_out && ldq < n) return fail(LLMC_ERR_SHAPE, "ldq < n");
+    if (codes_out && cfg->num_bits > 8) return fail(LLMC_ERR_UNSUPPORTED, "integer codes are produced for num_bits <= 8");
+    return gptq_batch(ctx, count, W, m, ldw, dtype, n, U, ldu, cfg, wq_out, ldq, codes_out, scales_out, zps_out, 0,
+                      nullptr, perm);
 }
 
 llmc_status llmc_sparsegpt_prune(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t m, int64_t n, int64_t ldw,
@@ -584,6 +633,25 @@ llmc_status llmc_int4_unpack_dequant(llmc_ctx* ctx, const uint8_t* packed, int64
     (void)zero_point;  // Dequantize() multiplies the stored (q - zp) value by the scale.
     if (count <= 0) return LLMC_OK;
     return int4_unpack(ctx, packed, count, scale, symmetric, out);
+}
+
+// ---- per-token activation quantisation (extension) ------------------------------------------------
+llmc_status llmc_act_quant_per_token(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows, int64_t cols, int64_t ld,
+                                     int32_t num_bits, int32_t symmetric, uint8_t* codes_out, int64_t ldc,
+                                     float* scales_out, int32_t* zps_out, void* deq_out, int64_t ldd) {
+    LLMC_ENTRY();
+    CTX_CHECK(ctx);
+    NULL_CHECK(x, "x");
+    NULL_CHECK(scales_out, "scales_out");
+    LLMC_TRY(check_bits(num_bits));
+    if (num_bits > 8) return fail(LLMC_ERR_UNSUPPORTED, "per-token codes are bytes: num_bits must be <= 8");
+    if (!dtype_ok(dtype)) return fail(LLMC_ERR_INVALID_ARG, "unsupported dtype %d", dtype);
+    if (rows < 0 || cols <= 0 || ld < cols) return fail(LLMC_ERR_SHAPE, "bad activation shape");
+    if (codes_out && ldc < cols) return fail(LLMC_ERR_SHAPE, "ldc < cols");
+    if (deq_out && ldd < cols) return fail(LLMC_ERR_SHAPE, "ldd < cols");
+    if (rows == 0) return LLMC_OK;
+    return act_quant_per_token(ctx, x, dtype, rows, cols, ld, num_bits, symmetric, codes_out, ldc, scales_out, zps_out,
+                               deq_out, ldd);
 }
 
 // ---- SmoothQuant / AWQ --------------------------------------------------------------------------

@@ -36,6 +36,8 @@ struct BlockArgs {
     int64_t srow;   // scale entries per row (0 tensor, 1 channel / per-row, G group)
     int64_t gs;     // columns per scale entry along a row (n for tensor/channel)
     uint8_t* codes; int64_t crow;  // packed (bits<=4) or bytes; nullable
+    int codes_bytes;               // 1: one byte per code even for bits <= 4 (act_order scatters them)
+    const int32_t* col_group;      // act_order: scale entry (group) of each column; nullable
     float* err1t;   // [cnt, m] errors of the current block (inside the super-block's buffer)
     // SparseGPT
     float sparsity; int mask_n, mask_m;
@@ -181,8 +183,9 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
 
     float qmin, qmax;
     qrange(a.bits, a.sym, &qmin, &qmax);
-    // Scale entry of the current column: reloaded when the column crosses a group edge.
-    int64_t g = a.i1 / a.gs;
+    // Scale entry of the current column: reloaded when the column crosses a group edge (or,
+    // with a column-group map, when the map changes group).
+    int64_t g = a.col_group ? a.col_group[a.i1] : a.i1 / a.gs;
     int64_t next_edge = (g + 1) * a.gs - a.i1;  // block-relative column where g changes
     // rs = rcp(s): x * rs stands in for x / s except within a few units in the last place of
     // a half-integer (where rint could differ) or when rs is not finite; those take the exact
@@ -211,9 +214,17 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
                 float q;
                 uint8_t cb;
                 if constexpr (MODE == 0) {
-                    if (jj == next_edge) {
+                    bool reload = false;
+                    if (a.col_group) {
+                        const int64_t gc = a.col_group[a.i1 + jj];
+                        reload = gc != g;
+                        g = gc;
+                    } else if (jj == next_edge) {
                         g++;
                         next_edge += a.gs;
+                        reload = true;
+                    }
+                    if (reload) {
                         const int64_t si = row_ok ? R * a.srow + g : 0;
                         s = a.scales[si];
                         zi = a.zps[si];
@@ -304,7 +315,7 @@ __global__ void __launch_bounds__(ROWS) block_kernel(BlockArgs a) {
         }
     }
     if (MODE == 0 && a.codes) {
-        if (a.bits <= 4) {
+        if (a.bits <= 4 && !a.codes_bytes) {
             const int64_t b0 = a.i1 / 2, b1 = (a.i1 + cnt - 1) / 2;
             const int nb = (int)(b1 - b0 + 1);
             for (int t = tid; t < ROWS * nb; t += ROWS) {
@@ -395,7 +406,8 @@ llmc_status run_blocks(llmc_ctx* ctx, BlockArgs a, int block_size) {
 // Per-tensor parameters come out one per weight; channel / group parameters per stacked row.
 llmc_status gptq_batch(llmc_ctx* ctx, int count, const void* const* Ws, const int64_t* ms, const int64_t* ldws, int dtype,
                        int64_t n, const float* U, int64_t ldu, const llmc_qconfig* cfg, float* wq_out, int64_t ldq,
-                       uint8_t* codes, float* scales_out, int32_t* zps_out, int mode, uint8_t* mask_out) {
+                       uint8_t* codes, float* scales_out, int32_t* zps_out, int mode, uint8_t* mask_out,
+                       const int32_t* perm) {
     const int strategy = cfg->strategy;
     int64_t M = 0, mmax = 0;
     for (int k = 0; k < count; k++) {
@@ -415,6 +427,11 @@ llmc_status gptq_batch(llmc_ctx* ctx, int count, const void* const* Ws, const in
     need += (size_t)nrow_params * 8 + 512;                          // per-row params (kernel side)
     need += (size_t)(tensor ? count : 0) * 8 + 512;                 // per-weight params if not returned
     need += (size_t)(2 * mmax + 128) * 4 + 256;                     // per-tensor reduction scratch
+    if (perm) {                                                     // act_order
+        need += (size_t)M * n * 4 + 256;                            // permuted working copy
+        need += (size_t)2 * n * 4 + 512;                            // column-group map, inverse
+        need += codes ? (size_t)M * n + 256 : 0;                    // codes in permuted order
+    }
     void* wsp;
     LLMC_TRY(workspace(ctx, need, &wsp));
     Carver cv{(char*)wsp};
@@ -437,6 +454,10 @@ llmc_status gptq_batch(llmc_ctx* ctx, int count, const void* const* Ws, const in
         krz = zps_out ? zps_out : cv.take<int32_t>(M * G);
     }
     float* red = cv.take<float>(2 * mmax + 128);
+    float* workp = perm ? cv.take<float>((size_t)M * n) : nullptr;
+    int32_t* col_group = perm ? cv.take<int32_t>(n) : nullptr;
+    int32_t* inv = perm ? cv.take<int32_t>(n) : nullptr;
+    uint8_t* codes_p = (perm && codes) ? cv.take<uint8_t>((size_t)M * n) : nullptr;
 
     // Stacked fp32 working copy of the ORIGINAL weights.
     int64_t off = 0;
@@ -481,7 +502,22 @@ llmc_status gptq_batch(llmc_ctx* ctx, int count, const void* const* Ws, const in
         a.scales = krs; a.zps = krz;
         a.codes = codes;
         a.crow = cfg->num_bits <= 4 ? (n + 1) / 2 : n;
-        return run_blocks<0>(ctx, a, cfg->block_size);
+        if (!perm) return run_blocks<0>(ctx, a, cfg->block_size);
+        // act_order: the parameters above come from the original columns; the solve runs on the
+        // permuted columns against the permuted Hessian's factor U, then everything is scattered
+        // back to the original column order.
+        LLMC_TRY(gather_cols(ctx, work, M, n, ldwork, perm, workp, n));
+        LLMC_TRY(perm_maps(ctx, perm, n, a.gs, col_group, inv));
+        a.W = workp;
+        a.ldw = n;
+        a.col_group = strategy == LLMC_STRATEGY_GROUP ? col_group : nullptr;
+        a.codes = codes_p;
+        a.codes_bytes = 1;
+        a.crow = n;
+        LLMC_TRY(run_blocks<0>(ctx, a, cfg->block_size));
+        if (wq_out) LLMC_TRY(scatter_cols(ctx, workp, M, n, n, perm, wq_out, ldq));
+        if (codes) LLMC_TRY(scatter_codes(ctx, codes_p, M, n, inv, cfg->num_bits, codes, cfg->num_bits <= 4 ? (n + 1) / 2 : n));
+        return LLMC_OK;
     }
     a.srow = 0; a.gs = n;
     a.sparsity = cfg->sparsity; a.mask_n = cfg->mask_n; a.mask_m = cfg->mask_m;
@@ -494,7 +530,8 @@ llmc_status gptq(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64_t n, 
                  int32_t* zps_out, int mode, uint8_t* mask_out) {
     const void* ws[1] = {W};
     const int64_t mm[1] = {m}, ll[1] = {ldw};
-    return gptq_batch(ctx, 1, ws, mm, ll, dtype, n, U, ldu, cfg, wq_out, ldq, codes, scales_out, zps_out, mode, mask_out);
+    return gptq_batch(ctx, 1, ws, mm, ll, dtype, n, U, ldu, cfg, wq_out, ldq, codes, scales_out, zps_out, mode, mask_out,
+                      nullptr);
 }
 
 }  // namespace llmc

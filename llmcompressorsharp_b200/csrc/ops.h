@@ -51,6 +51,23 @@ llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, 
                          float* out, int64_t ldo, int want_upper);
 llmc_status upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ldh, float* out, int64_t ldo);
 
+// ---- per-token activation quantisation (k_act.cu) ------------------------------------------
+llmc_status act_quant_per_token(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                int bits, int sym, uint8_t* codes, int64_t ldc, float* scales, int32_t* zps, void* deq,
+                                int64_t ldd);
+
+// ---- GPTQ activation order (k_actorder.cu) --------------------------------------------------
+llmc_status act_order_perm(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int32_t* perm);
+llmc_status permute_hessian(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int upper_only, const int32_t* perm,
+                            float* out, int64_t ldo);
+llmc_status gather_cols(llmc_ctx* ctx, const float* src, int64_t rows, int64_t n, int64_t lds, const int32_t* perm,
+                        float* dst, int64_t ldd);
+llmc_status scatter_cols(llmc_ctx* ctx, const float* src, int64_t rows, int64_t n, int64_t lds, const int32_t* perm,
+                         float* dst, int64_t ldd);
+llmc_status perm_maps(llmc_ctx* ctx, const int32_t* perm, int64_t n, int64_t gs, int32_t* col_group, int32_t* inv);
+llmc_status scatter_codes(llmc_ctx* ctx, const uint8_t* src, int64_t rows, int64_t n, const int32_t* inv, int bits,
+                          uint8_t* dst, int64_t crow);
+
 // ---- misc ----------------------------------------------------------------------------------
 // Drops the no-allocation observer's cached device address of its static row buffer on
 // `device` (noalloc.cu); llmc_init calls it so that a reset device gets a fresh lookup.

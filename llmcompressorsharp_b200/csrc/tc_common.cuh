@@ -214,6 +214,13 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
+// Arrive on an mbarrier given as a shared::cluster address with release at CTA scope only (no
+// cluster-wide fence): for arrivals that publish no memory writes to the other CTA, such as the
+// epilogue handing a TMEM accumulator back after its tcgen05.ld has completed.
+__device__ __forceinline__ void mbar_arrive_cluster_cta(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
 // try_wait with cluster-scope acquire: the waiter sees what another CTA of the cluster wrote
 // before its release-cluster arrive on this barrier.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* b, uint32_t parity) {

@@ -89,6 +89,58 @@ def gptq_quantize_u(weight: torch.Tensor, upper: torch.Tensor, config: GPTQConfi
     return GptqResult(wq, codes, scales, zps)
 
 
+def act_order_perm(h: torch.Tensor, upper_only: bool = False) -> torch.Tensor:
+    """Extension (the reference rejects ActOrder, GPTQModifier.cs:47-56): the GPTQ activation
+    order of a Hessian, columns by decreasing H[k][k] (equal values by index, NaN first), as an
+    int32 device tensor.  ``upper_only`` is accepted for symmetry with the other calls; only the
+    diagonal is read."""
+    dev = target_device(h)
+    hd = to_device(h.detach(), dev, torch.float32)
+    d = hd.shape[0]
+    perm = torch.empty(d, dtype=torch.int32, device=dev)
+    _lib.call("llmc_gptq_act_order_perm", C.c_void_p(ctx(dev)), _lib.ptr(hd), C.c_int64(d), C.c_int64(hd.stride(0)),
+              _lib.ptr(perm))
+    return perm
+
+
+def gptq_quantize_act_order(weight: torch.Tensor, h: torch.Tensor, config: GPTQConfig, want_codes: bool = True,
+                            upper_only: bool = False) -> tuple[GptqResult, torch.Tensor]:
+    """Extension: GPTQ with activation order and static groups, from the Hessian H (not Hinv:
+    the order needs diag(H)).  perm = act_order_perm(H); U_p = the factor of H[perm][:, perm]
+    damped by ``config.dampening_frac`` (HessianInverseSolver.cs:44-92); scales and zero-points
+    from the original weight per original column group (GptqBlockQuantizer.cs:97); the column
+    loop over W[:, perm]; outputs in the original column order.  Returns (result, perm)."""
+    if weight is None or h is None or config is None:
+        raise ArgumentError("weight, hessian and config must not be null")
+    dev = target_device(weight, h)
+    w = to_device(supported_dtype(weight.detach()), dev)
+    hd = to_device(h.detach(), dev, torch.float32)
+    m, n = w.shape
+    if hd.shape != (n, n):
+        raise ArgumentError("Hessian must be a square 2-D tensor matching the weight's in_features.")
+    perm = act_order_perm(hd)
+    c = C.c_void_p(ctx(dev))
+    hp = torch.empty(n, n, dtype=torch.float32, device=dev)
+    _lib.call("llmc_permute_hessian", c, _lib.ptr(hd), C.c_int64(n), C.c_int64(hd.stride(0)), C.c_int32(int(upper_only)),
+              _lib.ptr(perm), _lib.ptr(hp), C.c_int64(n))
+    up = HessianInverseSolver.upper(hp, config.dampening_frac)
+    wq = torch.empty(m, n, dtype=torch.float32, device=dev)
+    codes = None
+    if want_codes and config.num_bits <= 8:
+        codes = torch.empty(m, (n + 1) // 2 if config.num_bits <= 4 else n, dtype=torch.uint8, device=dev)
+    shp = param_shape(config.strategy, m, n, config.group_size)
+    scales = torch.empty(shp, dtype=torch.float32, device=dev)
+    zps = torch.empty(shp, dtype=torch.int32, device=dev)
+    cfg = config.to_c()
+    wp = (C.c_void_p * 1)(w.data_ptr())
+    mp = (C.c_int64 * 1)(m)
+    lp = (C.c_int64 * 1)(w.stride(0))
+    _lib.call("llmc_gptq_quantize_batch_perm", c, C.c_int32(1), wp, mp, lp, _lib.dtype_code(w.dtype), C.c_int64(n),
+              _lib.ptr(up), C.c_int64(n), _lib.ptr(perm), C.byref(cfg), _lib.ptr(wq), C.c_int64(n), _lib.ptr(codes),
+              _lib.ptr(scales), _lib.ptr(zps))
+    return GptqResult(wq, codes, scales, zps), perm
+
+
 class GptqBlockQuantizer:
     """GptqBlockQuantizer (GptqBlockQuantizer.cs:46-275)."""
 

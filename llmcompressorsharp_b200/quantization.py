@@ -334,3 +334,28 @@ class Int4PackedTensor:
                   C.c_int64(self.element_count), C.c_float(self.scale), C.c_int32(self.zero_point),
                   C.c_int32(int(self.symmetric)), _lib.ptr(out))
         return out
+
+
+def quantize_per_token(x: torch.Tensor, num_bits: int = 8, symmetric: bool = True, want_values: bool = False):
+    """Dynamic per-token quantisation of activations x [tokens, hidden] (extension; the reference
+    rejects PerToken for weights, RtnModifier.cs:69-70): one min-max observer per token row,
+    ComputeAffineParams and the FakeQuantize op chain in x's dtype, on the device
+    (llmc_act_quant_per_token).  Returns (codes, scales [tokens] fp32, zero-points [tokens] int32,
+    fake-quantised x or None); codes are int8 for a symmetric grid and uint8 otherwise."""
+    _check_bits(num_bits)
+    if num_bits > 8:
+        raise ArgumentOutOfRangeError("per-token codes are bytes: num_bits must be <= 8")
+    dev = target_device(x)
+    xd = to_device(supported_dtype(x.detach()), dev)
+    x2 = xd.reshape(-1, xd.shape[-1]) if xd.dim() != 2 else xd
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    rows, cols = x2.shape
+    codes = torch.empty(rows, cols, dtype=torch.int8 if symmetric else torch.uint8, device=dev)
+    scales = torch.empty(rows, dtype=torch.float32, device=dev)
+    zps = torch.empty(rows, dtype=torch.int32, device=dev)
+    deq = torch.empty(rows, cols, dtype=x2.dtype, device=dev) if want_values else None
+    _lib.call("llmc_act_quant_per_token", C.c_void_p(ctx(dev)), _lib.ptr(x2), _lib.dtype_code(x2.dtype),
+              C.c_int64(rows), C.c_int64(cols), C.c_int64(x2.stride(0)), C.c_int32(num_bits), C.c_int32(int(symmetric)),
+              _lib.ptr(codes), C.c_int64(cols), _lib.ptr(scales), _lib.ptr(zps), _lib.ptr(deq), C.c_int64(cols))
+    return codes, scales, zps, deq

@@ -19,7 +19,7 @@ import torch
 
 from .affine import compute_affine_params, affine_params_array, group_minmax, observer_fold
 from .fakequant import fake_quantize_codes
-from .hessian import upper_factor
+from .hessian import hessian_inverse, upper_factor
 
 NUMERIC_EPSILON = np.float32(1e-10)  # GptqBlockQuantizer.cs:48
 
@@ -74,12 +74,49 @@ def gptq_quantize_u(weight: torch.Tensor, upper: torch.Tensor, cfg: GPTQConfig):
     Returns (wq fp32 [m,n], codes int32 [m,n], scales [m,G] fp32, zps [m,G] int64)."""
     if cfg.act_order:
         raise NotImplementedError("GPTQConfig.ActOrder=true is not yet implemented.")  # :77-82
-    m, n = weight.shape
+    scales, zps = compute_scale_zero_point(weight, cfg)  # :97
+    return _column_loop(weight.detach().to(torch.float32).clone(), upper, cfg, scales, zps, None)
+
+
+def act_order_perm(h: torch.Tensor) -> torch.Tensor:
+    """Extension (parity unpinned; the reference rejects ActOrder, GPTQModifier.cs:47-56): the
+    GPTQ activation order, columns by decreasing Hessian diagonal.  Stable: equal values keep
+    index order; NaN entries come first."""
+    diag = torch.diagonal(h).to(torch.float32).tolist()
+    order = sorted(range(len(diag)), key=lambda i: (0 if diag[i] != diag[i] else 1,
+                                                    0.0 if diag[i] != diag[i] else -diag[i], i))
+    return torch.tensor(order, dtype=torch.int64)
+
+
+def gptq_quantize_act_order(weight: torch.Tensor, h: torch.Tensor, damping_frac: float, cfg: GPTQConfig):
+    """Extension (parity unpinned): GPTQ with activation order and static groups.
+
+    perm = act_order_perm(H); U_p is the factor of H[perm][:, perm] (hessian_inverse and
+    upper_factor as for any Hessian); scales and zero-points come from the ORIGINAL weight per
+    original column group, before the loop, as ComputeScaleZeroPoint does (:97); the loop of
+    Quantize (:122-181) runs over W[:, perm] against U_p, column a quantised with the parameters
+    of original column perm[a]; results are scattered back to the original columns.
+    Returns (wq fp32 [m,n], codes int32 [m,n], scales, zps, perm)."""
+    perm = act_order_perm(h)
+    hp = h.detach().to(torch.float32)[perm][:, perm].contiguous()
+    up = upper_factor(hessian_inverse(hp, damping_frac))
+    scales, zps = compute_scale_zero_point(weight, cfg)
+    wp = weight.detach().to(torch.float32)[:, perm].clone()
+    wq_p, codes_p, _, _ = _column_loop(wp, up, cfg, scales, zps, perm)
+    wq = torch.empty_like(wq_p)
+    codes = torch.empty_like(codes_p)
+    wq[:, perm] = wq_p
+    codes[:, perm] = codes_p
+    return wq, codes, scales, zps, perm
+
+
+def _column_loop(w_work: torch.Tensor, upper: torch.Tensor, cfg: GPTQConfig, scales, zps, col_of):
+    """The block loop of Quantize, :122-181, on the fp32 working copy w_work (modified in place).
+    Column aj takes the parameters of column col_of[aj] (aj itself when col_of is None)."""
+    m, n = w_work.shape
     bs = cfg.block_size
-    w_work = weight.detach().to(torch.float32).clone()  # :91
     wq = torch.zeros_like(w_work)  # :92
     codes = torch.zeros(m, n, dtype=torch.int32)
-    scales, zps = compute_scale_zero_point(weight, cfg)  # :97
     u = upper.detach().to(torch.float32)
     for i1 in range(0, n, bs):  # :124
         i2 = min(i1 + bs, n)
@@ -88,7 +125,7 @@ def gptq_quantize_u(weight: torch.Tensor, upper: torch.Tensor, cfg: GPTQConfig):
         for j in range(cnt):  # :134
             aj = i1 + j
             w_col = w_work[:, aj].clone()  # :141
-            s, z = _column_params(scales, zps, cfg, aj)
+            s, z = _column_params(scales, zps, cfg, aj if col_of is None else int(col_of[aj]))
             q, c = fake_quantize_codes(w_col, s, z, cfg.num_bits, cfg.symmetric)  # :142
             wq[:, aj] = q  # :143
             codes[:, aj] = c

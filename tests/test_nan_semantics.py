@@ -22,9 +22,16 @@ DEV = "cuda:0"
 NAN = float("nan")
 
 
+def _np(a):
+    if torch.is_tensor(a):  # bf16 / f16 widen to fp32 exactly (NaN stays NaN)
+        a = a.detach().cpu()
+        a = a.float() if a.is_floating_point() else a
+        return a.numpy().astype(np.float64)
+    return np.asarray(a, dtype=np.float64)
+
+
 def same(a, b):
-    a = np.asarray(a.detach().cpu().numpy() if torch.is_tensor(a) else a, dtype=np.float64)
-    b = np.asarray(b.detach().cpu().numpy() if torch.is_tensor(b) else b, dtype=np.float64)
+    a, b = _np(a), _np(b)
     return a.shape == b.shape and np.array_equal(a, b, equal_nan=True)
 
 
