@@ -287,6 +287,21 @@ llmc_status llmc_int4_pack(llmc_ctx* ctx, const int32_t* q, int64_t count, int32
 llmc_status llmc_int4_unpack_dequant(llmc_ctx* ctx, const uint8_t* packed, int64_t count, float scale,
                                      int32_t zero_point, int32_t symmetric, float* out);
 
+/* ---- compressed-tensors "pack-quantized" words --------------------------------------------
+ * SafetensorsWriter.cs:25-35 writes dense fp32 weights only; the checkpoint the reference's
+ * documentation names (docs/llm-compressor/deployment.md:124-132) is compressed-tensors'
+ * pack-quantized layout.  From one weight's codes as the GPTQ / RTN entry points write them
+ * ((q - zp) & 0xF nibbles, even column high, for num_bits <= 4; the byte q otherwise; crow bytes
+ * per row) and its int32 zero-points (one per scale entry of `strategy`):
+ *   packed_out [m, ldp] int32: q' + 2^(bits-1) in bits-wide fields, first column in the low
+ *     bits, q' = q (symmetric) or q - 2^(bits-1) (asymmetric), last word zero-padded;
+ *   zp_packed_out (optional; asymmetric channel / group only) [ceil(m / (32 / bits)), G] int32:
+ *     zp packed the same way along the rows.
+ * num_bits must divide 32. */
+llmc_status llmc_pack_compressed_tensors(llmc_ctx* ctx, const uint8_t* codes, int64_t m, int64_t n, int64_t crow,
+                                         const int32_t* zps, int32_t strategy, int64_t group_size, int32_t num_bits,
+                                         int32_t symmetric, int32_t* packed_out, int64_t ldp, int32_t* zp_packed_out);
+
 /* ---- per-token activation quantisation (extension) -------------------------------------------
  * No reference counterpart: QuantizationStrategy.PerToken exists (QuantizationStrategy.cs:9-19)
  * but RtnModifier.cs:69-70 rejects it for weights and the reference has no activation quantiser.

@@ -85,6 +85,7 @@ _SIGS = {
     "llmc_rtn_quantize": [P, P, I32, I64, I64, I64, C.POINTER(QConfig), P, P, P, P],
     "llmc_int4_pack": [P, P, I64, I32, P],
     "llmc_int4_unpack_dequant": [P, P, I64, F32, I32, I32, P],
+    "llmc_pack_compressed_tensors": [P, P, I64, I64, I64, P, I32, I64, I32, I32, P, I64, P],
     "llmc_act_quant_per_token": [P, P, I32, I64, I64, I64, I32, I32, P, I64, P, P, P, I64],
     "llmc_act_absmax": [P, P, I32, I64, I64, I64, P, I32],
     "llmc_smooth_apply": [P, P, P, I32, P, I32, I64, I64, F32, P],

@@ -635,6 +635,33 @@ llmc_status llmc_int4_unpack_dequant(llmc_ctx* ctx, const uint8_t* packed, int64
     return int4_unpack(ctx, packed, count, scale, symmetric, out);
 }
 
+// ---- compressed-tensors packing ---------------------------------------------------------------------
+llmc_status llmc_pack_compressed_tensors(llmc_ctx* ctx, const uint8_t* codes, int64_t m, int64_t n, int64_t crow,
+                                         const int32_t* zps, int32_t strategy, int64_t group_size, int32_t num_bits,
+                                         int32_t symmetric, int32_t* packed_out, int64_t ldp, int32_t* zp_packed_out) {
+    LLMC_ENTRY();
+    CTX_CHECK(ctx);
+    NULL_CHECK(codes, "codes");
+    NULL_CHECK(packed_out, "packed_out");
+    LLMC_TRY(check_bits(num_bits));
+    if (num_bits > 8) return fail(LLMC_ERR_UNSUPPORTED, "codes are produced for num_bits <= 8");
+    if (32 % num_bits) return fail(LLMC_ERR_UNSUPPORTED, "pack-quantized needs 32 / num_bits fields per word");
+    if (m <= 0 || n <= 0) return fail(LLMC_ERR_SHAPE, "bad weight shape");
+    if (crow < (num_bits <= 4 ? (n + 1) / 2 : n)) return fail(LLMC_ERR_SHAPE, "crow shorter than a row of codes");
+    const int64_t per = 32 / num_bits;
+    if (ldp < (n + per - 1) / per) return fail(LLMC_ERR_SHAPE, "ldp shorter than a row of packed words");
+    if (strategy != LLMC_STRATEGY_TENSOR && strategy != LLMC_STRATEGY_CHANNEL && strategy != LLMC_STRATEGY_GROUP)
+        return fail(LLMC_ERR_UNSUPPORTED, "strategy %d", strategy);
+    if (strategy == LLMC_STRATEGY_GROUP && group_size <= 0) return fail(LLMC_ERR_INVALID_ARG, "group_size must be positive");
+    if (!symmetric && num_bits <= 4) NULL_CHECK(zps, "zero_points");
+    if (zp_packed_out && (symmetric || strategy == LLMC_STRATEGY_TENSOR))
+        return fail(LLMC_ERR_INVALID_ARG, "packed zero-points exist for asymmetric channel / group weights only");
+    if (zp_packed_out) NULL_CHECK(zps, "zero_points");
+    const int64_t gs = strategy == LLMC_STRATEGY_GROUP ? group_size : n;
+    const int64_t zrow = strategy == LLMC_STRATEGY_TENSOR ? 0 : n_groups(strategy, n, gs);
+    return ct_pack(ctx, codes, m, n, crow, zps, zrow, gs, num_bits, symmetric, packed_out, ldp, zp_packed_out);
+}
+
 // ---- per-token activation quantisation (extension) ------------------------------------------------
 llmc_status llmc_act_quant_per_token(llmc_ctx* ctx, const void* x, int32_t dtype, int64_t rows, int64_t cols, int64_t ld,
                                      int32_t num_bits, int32_t symmetric, uint8_t* codes_out, int64_t ldc,

@@ -56,6 +56,12 @@ llmc_status act_quant_per_token(llmc_ctx* ctx, const void* x, int dtype, int64_t
                                 int bits, int sym, uint8_t* codes, int64_t ldc, float* scales, int32_t* zps, void* deq,
                                 int64_t ldd);
 
+// ---- compressed-tensors packing (k_pack.cu) --------------------------------------------------
+// zrow: zero-point entries per row (0: one shared entry, tensor strategy); zp_out (nullable)
+// receives the row-packed zero-points [ceil(m / (32 / bits)), zrow] (zrow >= 1).
+llmc_status ct_pack(llmc_ctx* ctx, const uint8_t* codes, int64_t m, int64_t n, int64_t crow, const int32_t* zps,
+                    int64_t zrow, int64_t gs, int bits, int sym, int32_t* out, int64_t ldo, int32_t* zp_out);
+
 // ---- GPTQ activation order (k_actorder.cu) --------------------------------------------------
 llmc_status act_order_perm(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int32_t* perm);
 llmc_status permute_hessian(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, int upper_only, const int32_t* perm,

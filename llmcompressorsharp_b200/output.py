@@ -30,8 +30,10 @@ shapes (compressed-tensors' argument-free ``dequantize``) need in_features divis
 group size; the ``quantization_config`` states the group size for the others.
 
 SparseGPT masks are recorded as a ``sparsity_config`` (dense format, the pruned weights are
-written as they are).  Nothing here runs on the GPU: the writer packs on the host after the
-results are copied back.
+written as they are).  Codes that are CUDA tensors are packed on the device
+(``llmc_pack_compressed_tensors``, ``pack_on_device``), so only the packed words cross PCIe;
+host codes take the numpy path (``signed_codes`` + ``pack_int32``), which produces the same
+words.
 """
 
 from __future__ import annotations
@@ -171,6 +173,33 @@ def pack_int32(values: np.ndarray, num_bits: int, packed_dim: int = 1) -> np.nda
     return out.T.copy() if packed_dim == 0 else out
 
 
+def pack_on_device(codes: torch.Tensor, zero_points: torch.Tensor, m: int, n: int, num_bits: int, symmetric: bool,
+                   strategy: str, group_size: int):
+    """``weight_packed`` (int32 [m, ceil(n / (32 / bits))]) and, for asymmetric channel / group
+    weights, the row-packed ``weight_zero_point`` of one weight whose codes and zero-points are
+    on a CUDA device; the same words as ``pack_int32(signed_codes(...))``.  Returns (packed,
+    packed zero-points or None), both on the codes' device."""
+    import ctypes as C
+
+    from . import _lib
+    from ._device import ctx
+
+    dev = codes.device
+    c = codes.detach().contiguous()
+    z = zero_points.detach().to(device=dev, dtype=torch.int32).contiguous()
+    per = 32 // num_bits
+    packed = torch.empty(m, -(-n // per), dtype=torch.int32, device=dev)
+    zp_packed = None
+    if not symmetric and strategy in ("group", "channel"):
+        g = -(-n // group_size) if strategy == "group" else 1
+        zp_packed = torch.empty(-(-m // per), g, dtype=torch.int32, device=dev)
+    _lib.call("llmc_pack_compressed_tensors", C.c_void_p(ctx(dev)), _lib.ptr(c), C.c_int64(m), C.c_int64(n),
+              C.c_int64(c.shape[1]), _lib.ptr(z), C.c_int32(_lib.STRATEGY[strategy]), C.c_int64(group_size),
+              C.c_int32(num_bits), C.c_int32(int(symmetric)), _lib.ptr(packed), C.c_int64(packed.shape[1]),
+              _lib.ptr(zp_packed))
+    return packed, zp_packed
+
+
 class CompressedTensorsWriter:
     """compressed-tensors ``pack-quantized`` checkpoint from a CompressionState."""
 
@@ -182,7 +211,15 @@ class CompressedTensorsWriter:
         if bits not in (4, 8):
             raise ArgumentError(f"{name}: pack-quantized needs 4 or 8 bits (got {bits})")
         m, n = int(shape[0]), int(shape[-1])
-        q, zp = signed_codes(entry["codes"], entry["zero_points"], bits, sym, n, strat, gs)
+        codes = entry["codes"]
+        if torch.is_tensor(codes) and codes.is_cuda:
+            packed, zp_words = pack_on_device(codes, entry["zero_points"], m, n, bits, sym, strat, gs)
+            packed, zp_words = packed.cpu(), (zp_words.cpu() if zp_words is not None else None)
+            zp = (entry["zero_points"].detach().cpu().numpy().astype(np.int64) - (1 << (bits - 1))).astype(np.int8)
+        else:
+            q, zp = signed_codes(codes, entry["zero_points"], bits, sym, n, strat, gs)
+            packed = torch.from_numpy(pack_int32(q, bits))
+            zp_words = None
         scales = entry["scales"].detach().cpu().to(torch.float32)
         if strat == "group":
             scales = scales.reshape(m, -1)
@@ -190,12 +227,13 @@ class CompressedTensorsWriter:
             scales = scales.reshape(m, 1)
         else:
             scales = scales.reshape(1)
-        out = {f"{module}.weight_packed": torch.from_numpy(pack_int32(q, bits)),
+        out = {f"{module}.weight_packed": packed,
                f"{module}.weight_scale": scales.to(scale_dtype),
                f"{module}.weight_shape": torch.tensor([m, n], dtype=torch.int64)}
         if not sym:
             if strat in ("group", "channel"):
-                out[f"{module}.weight_zero_point"] = torch.from_numpy(pack_int32(zp.reshape(m, -1), bits, packed_dim=0))
+                out[f"{module}.weight_zero_point"] = (zp_words if zp_words is not None else
+                                                      torch.from_numpy(pack_int32(zp.reshape(m, -1), bits, packed_dim=0)))
             else:
                 out[f"{module}.weight_zero_point"] = torch.from_numpy(zp.reshape(1).astype(np.int8))
         return out
