@@ -124,6 +124,110 @@ __global__ void __launch_bounds__(NT) awq_err_kernel(const T* W, int64_t m, int6
     if (lane == 0) atomicAdd(mse_acc, acc);
 }
 
+// reciprocals of the grid's scales, for the error term FQ(W*s)/s of the one-pass search
+__global__ void recip_kernel(const float* x, int64_t n, float* out) {
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x)
+        out[t] = __frcp_rn(x[t]);
+}
+
+// One pass over W for every grid point (group strategy, group <= 256 columns).  A block owns one
+// column group: it stages that group's columns of every s_k and 1 / s_k in shared memory, and its
+// warps take rows.  A warp holds its (row, group) segment in registers (8 columns per lane) and,
+// per grid point, takes the min / max of W * s_k with shuffles, the affine parameters, the
+// fake-quantised value (x * rcp(scale) where that provably equals the op-by-op chain, the chain
+// itself elsewhere, as in the GPTQ block kernel) and the squared error of FQ(W * s_k) / s_k - W,
+// summed per lane in double in shared memory.  W is read from memory once instead of twice per
+// grid point.  The error divides by multiplying with 1 / s_k (within one unit in the last place of
+// the quotient), so the sums differ from the per-point kernel's by about 1e-7 relative.
+constexpr int AWQ_WARPS = NT / 32;
+constexpr int AWQ_PER = 8;  // columns per lane: groups of up to 256
+
+template <typename T>
+__global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m, int64_t n, int64_t ldw, int gs,
+                                                           const float* sk, const float* rsk, int grid_pts, int bits,
+                                                           int sym, double* sums) {
+    extern __shared__ __align__(16) unsigned char awq_smem[];
+    double* accs = reinterpret_cast<double*>(awq_smem);           // [warps][grid_pts][32]
+    float* ss = reinterpret_cast<float*>(accs + (size_t)AWQ_WARPS * grid_pts * 32);  // [grid_pts][gs]
+    float* rs = ss + (size_t)grid_pts * gs;                        // [grid_pts][gs]
+    const int64_t c0 = (int64_t)blockIdx.x * gs;
+    const int L = (int)min((int64_t)gs, n - c0);
+    for (int t = threadIdx.x; t < grid_pts * gs; t += NT) {
+        const int k = t / gs, i = t % gs;
+        ss[t] = i < L ? sk[(int64_t)k * n + c0 + i] : 1.f;
+        rs[t] = i < L ? rsk[(int64_t)k * n + c0 + i] : 1.f;
+    }
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    double* acc = accs + (size_t)warp * grid_pts * 32 + lane;
+    for (int k = 0; k < grid_pts; k++) acc[k * 32] = 0.0;
+    __syncthreads();
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    for (int64_t r = (int64_t)blockIdx.y * AWQ_WARPS + warp; r < m; r += (int64_t)gridDim.y * AWQ_WARPS) {
+        float w[AWQ_PER];
+#pragma unroll
+        for (int i = 0; i < AWQ_PER; i++) {
+            const int col = lane + 32 * i;
+            w[i] = col < L ? to_f<T>(W[r * ldw + c0 + col]) : 0.f;
+        }
+#pragma unroll 1
+        for (int k = 0; k < grid_pts; k++) {
+            const float* sv = ss + k * gs;
+            const float* rv = rs + k * gs;
+            float v[AWQ_PER];
+            float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < AWQ_PER; i++) {
+                const int col = lane + 32 * i;
+                v[i] = col < L ? __fmul_rn(w[i], sv[col]) : 0.f;
+                if (col < L) {
+                    mn = fmin_nan(mn, v[i]);
+                    mx = fmax_nan(mx, v[i]);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+                mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            }
+            float sc;
+            int z;
+            affine_params(mn, mx, bits, sym, &sc, &z);
+            const float zf = (float)z;
+            const float rsc = __frcp_rn(sc);
+            const bool rs_ok = fabsf(rsc) <= 3.0e38f && rsc != 0.f;
+            double part = 0.0;
+#pragma unroll
+            for (int i = 0; i < AWQ_PER; i++) {
+                const int col = lane + 32 * i;
+                if (col >= L) continue;
+                float fq;
+                int code;
+                const float f = __fmul_rn(v[i], rsc);
+                const float fr = rintf(f);
+                if (!rs_ok || fabsf(fabsf(__fsub_rn(f, fr)) - 0.5f) <= fabsf(f) * 4.8e-7f + 1e-30f) {
+                    fq = fq_chain<float>(v[i], sc, zf, qmin, qmax, &code);
+                } else {
+                    float t = __fadd_rn(fr, zf);
+                    t = (t < qmin) ? qmin : ((t > qmax) ? qmax : t);
+                    fq = __fmul_rn(__fsub_rn(t, zf), sc);
+                }
+                const float e = __fsub_rn(__fmul_rn(fq, rv[col]), w[i]);
+                part = fma((double)e, (double)e, part);
+            }
+            acc[k * 32] += part;
+        }
+    }
+    __syncthreads();
+    // sum over warps and lanes: one thread per grid point
+    for (int k = threadIdx.x; k < grid_pts; k += NT) {
+        double t = 0.0;
+        for (int wq = 0; wq < AWQ_WARPS; wq++)
+            for (int l = 0; l < 32; l++) t += accs[((size_t)wq * grid_pts + k) * 32 + l];
+        atomicAdd(sums + k, t);
+    }
+}
+
 __global__ void awq_pick_kernel(const double* sums, int grid_pts, double denom, const float* sk, int64_t n, double* mse_out,
                                 float* best_s, int* best_k) {
     __shared__ int kbest;
@@ -233,24 +337,62 @@ llmc_status awq_search(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64
     if (nb > (int64_t)ctx->sm_count * 8) nb = (int64_t)ctx->sm_count * 8;
     int blocks = (int)nb;
     if (blocks < 1) blocks = 1;
-    for (int k = 0; k < grid_pts; k++) {
-        const float* s = sk + (int64_t)k * n;
+    const size_t smem = (size_t)AWQ_WARPS * grid_pts * 32 * 8 + (size_t)2 * grid_pts * gs * 4;
+    if (cfg->strategy == LLMC_STRATEGY_GROUP && gs <= 32 * AWQ_PER && smem <= 200 * 1024 && ctx->device >= 0 &&
+        ctx->device < 64) {
+        float* rsk = nullptr;
+        void* wsp2;
+        LLMC_TRY(workspace2(ctx, (size_t)grid_pts * n * 4 + 256, &wsp2));
+        rsk = static_cast<float*>(wsp2);
+        recip_kernel<<<grid_for(ctx, (int64_t)grid_pts * n), NT, 0, ctx->stream>>>(sk, (int64_t)grid_pts * n, rsk);
+        LLMC_TRY(check_launch(ctx, "recip"));
+        const int64_t ngroups = (n + gs - 1) / gs;
+        int64_t ry = ((int64_t)ctx->sm_count * 4 + ngroups - 1) / ngroups;  // ~4 blocks per SM in all
+        const int64_t ry_max = (m + AWQ_WARPS - 1) / AWQ_WARPS;
+        if (ry > ry_max) ry = ry_max;
+        if (ry < 1) ry = 1;
+        if (ry > 65535) ry = 65535;
+        const dim3 grid((unsigned)ngroups, (unsigned)ry);
+        static bool attr[64][3];
+        const int ti = dtype == LLMC_DTYPE_F32 ? 0 : (dtype == LLMC_DTYPE_BF16 ? 1 : 2);
+#define LLMC_AWQ1(T)                                                                                              \
+    do {                                                                                                          \
+        if (!attr[ctx->device][ti]) {                                                                             \
+            LLMC_CUDA_TRY(cudaFuncSetAttribute(awq_err_group_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                               200 * 1024));                                                      \
+            attr[ctx->device][ti] = true;                                                                         \
+        }                                                                                                         \
+        awq_err_group_kernel<T><<<grid, NT, smem, ctx->stream>>>((const T*)W, m, n, ldw, (int)gs, sk, rsk, grid_pts, \
+                                                                 cfg->num_bits, cfg->symmetric, sums);            \
+    } while (0)
         switch (dtype) {
-            case LLMC_DTYPE_F32:
-                awq_err_kernel<float><<<blocks, NT, 0, ctx->stream>>>((const float*)W, m, n, ldw, gs, s, cfg->num_bits,
-                                                                      cfg->symmetric, sums + k);
-                break;
-            case LLMC_DTYPE_BF16:
-                awq_err_kernel<__nv_bfloat16><<<blocks, NT, 0, ctx->stream>>>((const __nv_bfloat16*)W, m, n, ldw, gs, s,
-                                                                              cfg->num_bits, cfg->symmetric, sums + k);
-                break;
-            case LLMC_DTYPE_F16:
-                awq_err_kernel<__half><<<blocks, NT, 0, ctx->stream>>>((const __half*)W, m, n, ldw, gs, s, cfg->num_bits,
-                                                                       cfg->symmetric, sums + k);
-                break;
+            case LLMC_DTYPE_F32: LLMC_AWQ1(float); break;
+            case LLMC_DTYPE_BF16: LLMC_AWQ1(__nv_bfloat16); break;
+            case LLMC_DTYPE_F16: LLMC_AWQ1(__half); break;
             default: return fail(LLMC_ERR_INVALID_ARG, "bad dtype");
         }
-        LLMC_TRY(check_launch(ctx, "awq_err"));
+#undef LLMC_AWQ1
+        LLMC_TRY(check_launch(ctx, "awq_err_group"));
+    } else {
+        for (int k = 0; k < grid_pts; k++) {
+            const float* s = sk + (int64_t)k * n;
+            switch (dtype) {
+                case LLMC_DTYPE_F32:
+                    awq_err_kernel<float><<<blocks, NT, 0, ctx->stream>>>((const float*)W, m, n, ldw, gs, s, cfg->num_bits,
+                                                                          cfg->symmetric, sums + k);
+                    break;
+                case LLMC_DTYPE_BF16:
+                    awq_err_kernel<__nv_bfloat16><<<blocks, NT, 0, ctx->stream>>>((const __nv_bfloat16*)W, m, n, ldw, gs, s,
+                                                                                  cfg->num_bits, cfg->symmetric, sums + k);
+                    break;
+                case LLMC_DTYPE_F16:
+                    awq_err_kernel<__half><<<blocks, NT, 0, ctx->stream>>>((const __half*)W, m, n, ldw, gs, s, cfg->num_bits,
+                                                                           cfg->symmetric, sums + k);
+                    break;
+                default: return fail(LLMC_ERR_INVALID_ARG, "bad dtype");
+            }
+            LLMC_TRY(check_launch(ctx, "awq_err"));
+        }
     }
     awq_pick_kernel<<<1, NT, 0, ctx->stream>>>(sums, grid_pts, (double)m * (double)n, sk, n, mse_out, best_s, kdev);
     LLMC_TRY(check_launch(ctx, "awq_pick"));
