@@ -35,7 +35,13 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-MODEL = {"name": "llama3-8b", "hidden": 4096, "intermediate": 14336, "heads": 32, "kv_heads": 8, "layers": 32}
+MODELS = {
+    "llama3-8b": {"name": "llama3-8b", "label": "Llama-3-8B", "hidden": 4096, "intermediate": 14336, "heads": 32,
+                  "kv_heads": 8, "layers": 32},
+    "llama3-70b": {"name": "llama3-70b", "label": "Llama-3-70B", "hidden": 8192, "intermediate": 28672, "heads": 64,
+                   "kv_heads": 8, "layers": 80},
+}
+MODEL = dict(MODELS["llama3-8b"])
 METRIC = "GPTQ W4A16 wall-clock s (Llama-3-8B shape)"
 SPARSE_METRIC = "SparseGPT 2:4 wall-clock s (Llama-3-8B shape)"
 UNIT = "s"
@@ -55,7 +61,9 @@ def parse():
                         "rtn: RTN W4A16 g128 + min-max observer passes over the Llama-3-8B Linear weights; "
                         "smoothquant: SmoothQuant (alpha 0.5) + W8A8 weights on a Llama-2-7B shape; awq: AWQ "
                         "20-point grid search + scale apply on Llama-3-8B layers")
-    p.add_argument("--layers", type=int, default=MODEL["layers"])
+    p.add_argument("--model", choices=sorted(MODELS), default="llama3-8b",
+                   help="layer shapes of the gptq / sparsegpt / solve workloads (the headline is llama3-8b)")
+    p.add_argument("--layers", type=int, default=None, help="decoder layers (default: the model's)")
     p.add_argument("--tokens", type=int, default=512 * 2048)
     p.add_argument("--chunk", type=int, default=65536, help="calibration rows per Hessian update call")
     p.add_argument("--e2e-steps", type=int, default=2)
@@ -275,23 +283,26 @@ def run_ours(args):
         per_launch_flops = hess_flops_computed / max(1, hess_launches)
         per_launch_ms = tot_hess_ms / max(1, hess_launches)
         achieved = per_launch_flops / (per_launch_ms * 1e-3) / 1e12
-        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(args)
+        # The CPU sample is sized for the headline (Llama-3-8B) shapes.
+        cpu = None if args.no_cpu_baseline or world > 1 or args.model != "llama3-8b" else cpu_baseline(args)
         line = {
             "metric": SPARSE_METRIC if sparse else METRIC, "value": round(ms / 1e3, 4), "unit": UNIT, "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": ("SparseGPT 2:4 (50 %) damp 0.01 block 128, Llama-3-8B shape " if sparse else
-                                    "GPTQ W4A16 asym g128 damp 0.01 block 128, Llama-3-8B shape ") +
-                                   f"({args.layers} layers x 7 Linear, hidden 4096, intermediate 14336, 32/8 heads), "
-                                   f"{args.tokens} calibration tokens (512 x 2048), bf16",
+            "config": {"workload": ("SparseGPT 2:4 (50 %) damp 0.01 block 128, " if sparse else
+                                    "GPTQ W4A16 asym g128 damp 0.01 block 128, ") +
+                                   f"{MODEL['label']} shape ({args.layers} layers x 7 Linear, hidden {MODEL['hidden']}, "
+                                   f"intermediate {MODEL['intermediate']}, {MODEL['heads']}/{MODEL['kv_heads']} heads), "
+                                   f"{args.tokens} calibration tokens ({args.tokens // 2048} x 2048), bf16",
                        "layers": args.layers, "tokens": args.tokens, "update_rows": args.chunk,
                        "parallelism": f"tokens split over {world} GPU(s), layers dealt round-robin",
                        "overlap": (f"solve of layer l on a second stream while later layers accumulate (and, "
                                    f"on N > 1, while their NCCL reductions run); Hessian kernel capped at "
                                    f"{args.reserve_sms} SMs fewer") if args.reserve_sms > 0 else "none",
                        "activations": "one seeded bf16 [tokens, d] set per input site, shared by all layers",
-                       "l2": "inputs larger than L2 (52 GiB of activations streamed per step)"},
+                       "l2": "inputs larger than L2 ({:.0f} GiB of activations streamed per step)".format(
+                           sum(args.tokens * st.d * 2 for st in sites_for(MODEL)) / 2 ** 30)},
             "hessian_tflops": round(hess_flops_full / (tot_hess_ms * 1e-3) / 1e12 if tot_hess_ms else 0, 1),
             "hessian_tflops_note": "Hessian TFLOP/s with the full-GEMM count 2*d^2*T (the metric's definition); "
                                    "the kernel computes the symmetric half",
@@ -1063,7 +1074,14 @@ def run_smooth_awq(args):
 
 
 def main():
+    global METRIC, SPARSE_METRIC
     args = parse()
+    MODEL.clear()
+    MODEL.update(MODELS[args.model])
+    if args.layers is None:
+        args.layers = MODEL["layers"]
+    METRIC = f"GPTQ W4A16 wall-clock s ({MODEL['label']} shape)"
+    SPARSE_METRIC = f"SparseGPT 2:4 wall-clock s ({MODEL['label']} shape)"
     if args.impl == "reference":
         run_reference(args)
         return
