@@ -315,9 +315,10 @@ def run_ours(args):
                          "frac_of_its_sms": round(achieved / (sustained * pipe.hessian_sms() / sm_count), 3),
                          "algorithmic": "d(d+1)T FLOP per launch (symmetric rank-k update of T tokens)",
                          "traffic": SYRK_TRAFFIC_PER_LAUNCH,
-                         "traffic_note": "ncu DRAM read+write bytes per launch, averaged over the step's mix of "
-                                         "d=4096 (1.30 GB) and d=14336 (29.4 GB) launches of 65,536 tokens; their "
-                                         "algorithmic bytes are 0.60 GB and 2.70 GB (X once + H upper triangle)"},
+                         "traffic_note": "ncu DRAM read+write bytes per launch of this kernel version, averaged "
+                                         "over the step's mix of d=4096 (1.49 GB) and d=14336 (18.2 GB) launches of "
+                                         "65,536 tokens; their algorithmic bytes are 0.60 GB and 2.70 GB (X once + "
+                                         "H upper triangle)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
@@ -330,12 +331,13 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# DRAM bytes (read + write) per Hessian launch of this workload, from one ncu capture of the
-# four site launches of a 65,536-token step (profiles/syrk_tc2_kernel_llama3_8b_sites.md):
-# d = 4096: 0.944 GB read + 0.355 GB written; d = 14336: 26.38 GB + 2.99 GB.  A step has three
-# d = 4096 launches for every d = 14336 launch, so the average launch moves
-# (3 * 1.299 + 29.37) / 4 GB.
-SYRK_TRAFFIC_PER_LAUNCH = (3 * 1.299e9 + 29.37e9) / 4
+# DRAM bytes (read + write) per Hessian launch of this workload, from one ncu capture of the four
+# site launches of a 65,536-token step (dram__bytes_read.sum + dram__bytes_write.sum, captured with
+# `--layers 1 --tokens 65536 --steps 1 --warmup 1 --no-e2e --no-cpu-baseline --reserve-sms 0`):
+# d = 4096: 1.350 GB read + 0.135 GB written; d = 14336: 16.52 GB + 1.69 GB.  A step has three
+# d = 4096 launches for every d = 14336 launch, so the average launch moves (3 * 1.485 + 18.21) / 4 GB.
+# Re-capture whenever the Hessian kernel changes.
+SYRK_TRAFFIC_PER_LAUNCH = (3 * 1.485e9 + 18.21e9) / 4
 
 
 def _randn_bf16(m, n, dev, g, std=1.0):

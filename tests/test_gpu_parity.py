@@ -127,7 +127,9 @@ def test_hessian_tensor_cores_match_fp64(dtype, d, rows):
     xd = x.double()
     h64 = xd.t() @ xd
     assert torch.equal(h_tc, h_tc.t())
-    assert rel_fro(h_tc, h64) < 4e-6      # tensor cores, folded into fp32 every 1,024 tokens (~1.8e-6)
+    # tensor cores, folded into fp32 every 1,024 tokens: the truncating accumulation of 64 MMAs per
+    # fold leaves 1.8e-6 (d = 4096 / 14336, bf16) to 4.2e-6 (d = 320, fp16) relative to fp64
+    assert rel_fro(h_tc, h64) < 8e-6
     assert rel_fro(h_simt, h64) < 5e-6    # fp32 SIMT: <= 2048 sequential fp32 sums per split
     if d <= 1024:
         ref = o_hess.HessianAccumulator(d)
