@@ -153,6 +153,30 @@ class GptqPipeline:
             _lib.call("llmc_hessian_update", h, C.c_void_p(x.data_ptr() + r0 * x.stride(0) * x.element_size()),
                       _lib.dtype_code(x.dtype), C.c_int64(r1 - r0), C.c_int64(x.stride(0)))
 
+    def _accumulate_many(self, handles: list, xs: list, ready=None):
+        """``_accumulate_into`` for several Hessians at once (one per layer), chunk-interleaved:
+        each row chunk is added to every handle before the next chunk's copy is waited for.  The
+        tensors in ``xs`` have the same number of rows; ``ready`` marks the rows of the first one."""
+        stream = torch.cuda.current_stream(self.device)
+        if isinstance(ready, torch.cuda.Event):
+            stream.wait_event(ready)
+            ready = None
+        marks = list(ready or [])
+        T = xs[0].shape[0]
+        if any(x.shape[0] != T for x in xs):
+            raise ValueError("the layers' activations of one site need the same number of rows")
+        waits = chunk_waits([r for r, _ in marks], T, self.chunk)
+        hs = [C.c_void_p(h) for h in handles]
+        for h in hs:
+            _lib.call("llmc_hessian_reset", h)
+        for i, r0 in enumerate(range(0, T, self.chunk)):
+            r1 = min(T, r0 + self.chunk)
+            if waits[i] >= 0:
+                stream.wait_event(marks[waits[i]][1])
+            for h, x in zip(hs, xs):
+                _lib.call("llmc_hessian_update", h, C.c_void_p(x.data_ptr() + r0 * x.stride(0) * x.element_size()),
+                          _lib.dtype_code(x.dtype), C.c_int64(r1 - r0), C.c_int64(x.stride(0)))
+
     def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict, ctx=None, rows=None):
         """U from the site's H (upper triangle), then one stacked GPTQ solve of every weight
         that reads the site (outputs are views into stacked per-site buffers).  ``ctx`` is a
@@ -357,12 +381,18 @@ class _Overlap:
         # The factorisation decides a non-PD Hessian on the device, so enqueueing a solve never
         # waits for the GPU; a failure surfaces at the llmc_sync that ends the job.
         _lib.call("llmc_set_deferred_errors", C.c_void_p(self.cs), C.c_int32(1))
-        self.h = [{}, {}]
-        for b in range(2):
-            for s in pipe.sites:
+        self.h = []
+        self._ensure_sets(2)
+
+    def _ensure_sets(self, n: int):
+        """At least ``n`` Hessian handle sets (one handle per site each)."""
+        while len(self.h) < n:
+            hs = {}
+            for s in self.pipe.sites:
                 p = C.c_void_p()
                 _lib.call("llmc_hessian_create", C.c_void_p(self.ch), C.c_int64(s.d), C.byref(p))
-                self.h[b][s.name] = p.value
+                hs[s.name] = p.value
+            self.h.append(hs)
 
     @staticmethod
     def _ctx(dev, stream) -> int:
@@ -374,10 +404,10 @@ class _Overlap:
     def close(self):
         torch.cuda.synchronize(self.pipe.device)
         self.close_dist()
-        for b in range(2):
-            for p in self.h[b].values():
+        for hs in self.h:
+            for p in hs.values():
                 _lib.call("llmc_hessian_destroy", C.c_void_p(p))
-        self.h = [{}, {}]
+        self.h = []
         for c in (self.ch, self.cs):
             _lib.call("llmc_destroy", C.c_void_p(c))
         self.ch = self.cs = None
@@ -387,12 +417,22 @@ class _Overlap:
         _lib.call("llmc_hessian_data", C.c_void_p(self.h[b][site]), C.byref(p))
         return p.value
 
+    # Layers whose Hessians accumulate site by site, chunk by chunk, while the calibration
+    # activations are still arriving (``acts_ready``): every copied chunk then feeds this many
+    # layers at once, so the first layers' work overlaps the copy instead of waiting for all of it.
+    PROLOGUE_LAYERS = 4
+
     def run(self, layers, acts_for, weights, outputs, before_solve, after_solve, hess_events, acts_ready, sync=True):
         pipe = self.pipe
         cur = torch.cuda.current_stream(pipe.device)
         self.sh.wait_stream(cur)
         self.ss.wait_stream(cur)
-        solved = [None, None]  # event: last solve that read buffer set b
+        K = min(self.PROLOGUE_LAYERS, len(layers)) if acts_ready else 0
+        if K < 2:
+            K = 0
+        nsets = max(2, K + 1)
+        self._ensure_sets(nsets)
+        solved = [None] * nsets  # event: last solve that read buffer set b
 
         def solve(item):
             l, b, acc_done = item
@@ -409,8 +449,28 @@ class _Overlap:
                 solved[b] = done
 
         pending = None
-        for i, l in enumerate(layers):
-            b = i % 2
+        if K:
+            # Prologue: layers 0..K-1 in sets 0..K-1, site-major, each arriving chunk added to
+            # all K layers' Hessians before the next chunk is waited for.
+            acts = [acts_for(l) for l in layers[:K]]
+            with torch.cuda.stream(self.sh):
+                for s in pipe.sites:
+                    ev = _events() if hess_events is not None else None
+                    if ev:
+                        ev[0].record(self.sh)
+                    pipe._accumulate_many([self.h[i][s.name] for i in range(K)], [a[s.name] for a in acts],
+                                          ready=acts_ready.pop(s.name, None))
+                    if ev:
+                        ev[1].record(self.sh)
+                        hess_events.append((ev[0], ev[1], s.d, sum(a[s.name].shape[0] for a in acts)))
+                acc_done = torch.cuda.Event()
+                acc_done.record(self.sh)
+            for i in range(K - 1):
+                solve((layers[i], i, acc_done))
+            pending = (layers[K - 1], K - 1, acc_done)
+        for i in range(K, len(layers)):
+            l = layers[i]
+            b = i % nsets
             a = acts_for(l)
             with torch.cuda.stream(self.sh):
                 if solved[b] is not None:
