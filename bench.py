@@ -960,7 +960,8 @@ def run_smooth_awq(args):
     """--workload smoothquant: per layer of a Llama-2-7B shape (hidden 4096, intermediate 11008,
     32 layers, 256 x 2048 = 524,288 calibration tokens), the activation absmax of the attention
     and MLP inputs, SmoothQuant (alpha 0.5) of input_layernorm -> q/k/v and post_attention_layernorm
-    -> gate/up, and W8A8's int8 per-channel weight quantisation of all seven weights.
+    -> gate/up, W8A8's int8 per-channel weight quantisation of all seven weights, and W8A8's int8
+    per-token quantisation of the two activation inputs (codes and per-token scales).
     --workload awq: per layer of a Llama-3-8B shape (128 x 2048 = 262,144 tokens), the activation
     absmax of the same two inputs, the AWQ 20-point grid search (RTN asym int4 g128) and the
     scale apply for q/k/v and gate/up.  Both are HBM-bound: throughput = algorithmic bytes /
@@ -1008,6 +1009,10 @@ def run_smooth_awq(args):
     codes = {k: torch.empty(m, n, dtype=torch.uint8, device=dev) for k, (m, n) in shapes.items()}
     scales = {k: torch.empty(m, 1, dtype=torch.float32, device=dev) for k, (m, n) in shapes.items()}
     zps = {k: torch.empty(m, 1, dtype=torch.int32, device=dev) for k, (m, n) in shapes.items()}
+    act_codes = act_scales = None
+    if not awq:
+        act_codes = torch.empty(T, hid, dtype=torch.int8, device=dev)
+        act_scales = torch.empty(T, dtype=torch.float32, device=dev)
 
     def step():
         c = C.c_void_p(_lib.ctx_for(0))
@@ -1032,6 +1037,10 @@ def run_smooth_awq(args):
                     _lib.call("llmc_rtn_quantize", c, _lib.ptr(w[key]), _lib.DTYPE_BF16, C.c_int64(m), C.c_int64(n),
                               C.c_int64(n), C.byref(q8), _lib.ptr(codes[key]), _lib.ptr(scales[key]),
                               _lib.ptr(zps[key]), C.c_void_p(0))
+                for x in acts:  # the A side of W8A8: int8 per token, symmetric
+                    _lib.call("llmc_act_quant_per_token", c, _lib.ptr(x), _lib.DTYPE_BF16, C.c_int64(T), C.c_int64(hid),
+                              C.c_int64(hid), C.c_int32(8), C.c_int32(1), _lib.ptr(act_codes), C.c_int64(hid),
+                              _lib.ptr(act_scales), C.c_void_p(0), C.c_void_p(0), C.c_int64(hid))
 
     # algorithmic bytes of one step
     absmax_b = 2 * T * hid * 2
@@ -1041,6 +1050,7 @@ def run_smooth_awq(args):
     else:
         params = sum(m * n for m, n in shapes.values())
         per_layer = absmax_b + 3 * bal + 4 * hid * 2 + params * 3 + sum(m for m, _ in shapes.values()) * 8
+        per_layer += 2 * (T * hid * 2 + T * hid + T * 4)  # per-token: read x, write codes and scales
     step_bytes = per_layer * L
     launches0 = _lib.launch_count(0)
     for _ in range(args.warmup):
@@ -1060,7 +1070,8 @@ def run_smooth_awq(args):
     _, _, hbm, src = peaks()
     gbs = step_bytes / (ms * 1e-3) / 1e9
     name = ("AWQ grid search (20 points, int4 g128) + scale apply throughput (Llama-3-8B shape)" if awq else
-            "SmoothQuant (alpha 0.5) + W8A8 int8 per-channel weights throughput (Llama-2-7B shape)")
+            "SmoothQuant (alpha 0.5) + W8A8 (int8 per-channel weights, int8 per-token activations) throughput "
+            "(Llama-2-7B shape)")
     line = {"metric": name, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -1068,7 +1079,7 @@ def run_smooth_awq(args):
                        "bytes_per_step": int(step_bytes),
                        "activations": "two [tokens, 4096] bf16 inputs, 1 % of channels heavy-tailed x50",
                        "l2": "inputs larger than L2"},
-            "roofline": {"kernel": "awq_err_kernel" if awq else "col_absmax_kernel", "bound": "hbm",
+            "roofline": {"kernel": "awq_err_group_kernel" if awq else "col_absmax_kernel", "bound": "hbm",
                          "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 3),
                          "peak_note": f"{src} HBM copy bandwidth; whole-step bytes over step time", "traffic": None},
             "gpu_launches": warm_launches * args.steps, "clocks": clk}

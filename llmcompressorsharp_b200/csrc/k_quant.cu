@@ -504,6 +504,126 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
     }
 }
 
+// bf16 RTN to packed nibbles (num_bits <= 4, no dequantised output): rtn_bf16_kernel's exact
+// integer path with fewer integer-pipe instructions per element.
+//   * f = x * rcp(s); an element whose f lies within 4 units in the last place of a bf16
+//     rounding midpoint takes the op-by-op chain (as in rtn_bf16_kernel).  The test is one
+//     multiply-add (the low 16 bits of f, shifted up) and one unsigned compare.
+//   * bf16(f) by Veltkamp splitting, c = f * (2^16 + 1), bf16(f) = c - (c - f): rounding to
+//     nearest on 8 significant bits on the floating-point pipe (T. J. Dekker, "A floating-point
+//     technique for extending the available precision", 1971).  Its tie-breaking may differ
+//     from round-to-even, but ties are exactly the midpoint elements sent to the chain.
+//   * rint by adding 1.5 * 2^23, then the clamp to [qmin - zp, qmax - zp] on that float (only in
+//     warps whose segments can reach the grid's ends); the code nibble (q - zp) & 0xF is the low
+//     nibble of the sum's bit pattern.
+//   * Nibbles are gathered with byte permutes, two 32-bit words per eight columns.
+__global__ void __launch_bounds__(NT) rtn_bf16_nib_kernel(const __nv_bfloat16* x, SegGeom g, FastDiv fd, int bits,
+                                                          int sym, int tensor_mode, float* scales, int32_t* zps,
+                                                          uint8_t* codes) {
+    constexpr int VEC = 8;
+    const int L = g.L;
+    const uint32_t gpb = NT / L;
+    const uint32_t total = (uint32_t)(g.rows * g.nseg);
+    const uint32_t lg = threadIdx.x / L;
+    const int sub = lane_id() % L;
+    const int64_t seglen = g.gs < g.cols ? g.gs : g.cols;
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    const int64_t crow = code_row_bytes(bits, g.cols);
+    const __nv_bfloat162 pinf = __float2bfloat162_rn(INFINITY), ninf = __float2bfloat162_rn(-INFINITY);
+    constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
+    for (uint32_t base = blockIdx.x * gpb; base < total; base += gridDim.x * gpb) {
+        const uint32_t seg = base + lg;
+        const bool active = seg < total;
+        const uint32_t sg = active ? seg : 0;
+        const uint32_t r = fastdiv(sg, fd);
+        const int64_t c0 = (int64_t)(sg - r * (uint32_t)g.nseg) * seglen;
+        const __nv_bfloat16* row = x + (int64_t)r * g.ld + c0;
+        uint4 w[RV];
+        __nv_bfloat162 mn2[2] = {pinf, pinf}, mx2[2] = {ninf, ninf};
+        if (active) {
+#pragma unroll
+            for (int j = 0; j < RV; j++) w[j] = *reinterpret_cast<const uint4*>(row + (int64_t)(j * L + sub) * VEC);
+#pragma unroll
+            for (int j = 0; j < RV; j++) {
+                const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(&ww[k]);
+                    mn2[k & 1] = __hmin2_nan(mn2[k & 1], p);
+                    mx2[k & 1] = __hmax2_nan(mx2[k & 1], p);
+                }
+            }
+        }
+        const __nv_bfloat162 mnp = __hmin2_nan(mn2[0], mn2[1]), mxp = __hmax2_nan(mx2[0], mx2[1]);
+        float smin = fmin_nan(__low2float(mnp), __high2float(mnp));
+        float smax = fmax_nan(__low2float(mxp), __high2float(mxp));
+        for (int off = L / 2; off > 0; off >>= 1) {
+            smin = fmin_nan(smin, __shfl_xor_sync(0xffffffffu, smin, off));
+            smax = fmax_nan(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+        }
+        float s;
+        int z;
+        if (tensor_mode) {
+            s = scales[0];
+            z = zps[0];
+        } else {
+            affine_params(smin, smax, bits, sym, &s, &z);
+            if (active && sub == 0) {
+                scales[seg] = s;
+                zps[seg] = z;
+            }
+        }
+        const float zf = (float)z;
+        const float rcp = __frcp_rn(s);
+        const float k = 1.f + 0x1p-20f;
+        const float hi = fmaxf(smax, 0.f) * rcp * k + zf;  // NaN / Inf fail the tests below
+        const float lo = fminf(smin, 0.f) * rcp * k + zf;
+        const bool fast = hi <= 256.f && lo >= -256.f;
+        // The clamp can act only if some quotient of the segment rounds beyond the grid.
+        const bool clamp = !(hi <= qmax + 0.25f && lo >= qmin - 0.25f);
+        const bool warp_clamp = __any_sync(0xffffffffu, active && clamp);
+        const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
+        if (!active) continue;
+        uint8_t* crow_p = codes + (int64_t)r * crow;
+#pragma unroll
+        for (int j = 0; j < RV; j++) {
+            const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
+            const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+            uint32_t u[VEC];
+            bool slow = !fast;
+#pragma unroll
+            for (int i = 0; i < VEC; i++) {
+                const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+                const float f = __fmul_rn(xv, rcp);
+                // low 16 bits of f within 4 of 0x8000  <=>  (bits(f) - 0x7FFC) * 2^16 <= 8 * 2^16 (mod 2^32)
+                slow |= (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u;
+                const float cc = __fmul_rn(f, 65537.f);
+                const float b16 = __fsub_rn(cc, __fsub_rn(cc, f));
+                float rf = __fadd_rn(b16, MAGIC);
+                if (warp_clamp) rf = fminf(fmaxf(rf, cmin), cmax);
+                u[i] = __float_as_uint(rf);
+            }
+            if (slow) {
+#pragma unroll
+                for (int i = 0; i < VEC; i++) {
+                    const float xv =
+                        (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+                    const float f = __fmul_rn(xv, rcp);
+                    if (!fast || (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u) {
+                        const FqOut e = fq_chain_call<__nv_bfloat16>(xv, s, zf, qmin, qmax);
+                        u[i] = (uint32_t)((e.code - z) & 0xF);
+                    }
+                }
+            }
+            // byte b of the output holds columns 2b (high nibble) and 2b + 1 (low nibble)
+            const uint32_t ev = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);
+            const uint32_t od = __byte_perm(__byte_perm(u[1], u[3], 0x0040), __byte_perm(u[5], u[7], 0x0040), 0x5410);
+            *reinterpret_cast<uint32_t*>(crow_p + c / 2) = ((ev << 4) & 0xF0F0F0F0u) | (od & 0x0F0F0F0Fu);
+        }
+    }
+}
+
 template <typename T>
 __global__ void fake_quant_flat_kernel(const T* x, int64_t n, float s, float zf, float qmin, float qmax, T* out,
                                        int32_t* codes) {
@@ -627,6 +747,11 @@ llmc_status launch_rtn(llmc_ctx* ctx, const void* x, int64_t m, int64_t n, int64
         if (vec_ok<T>(x, ldw, gs, n) && deq_ok && codes_ok && codes_al && reg_ok) {
             g.L = (int)lanes;
             const FastDiv fd = make_fastdiv((uint32_t)g.nseg);
+            if (!deq && codes && bits <= 4) {
+                rtn_bf16_nib_kernel<<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
+                    reinterpret_cast<const T*>(x), g, fd, bits, sym, tensor_mode, scales, zps, codes);
+                return check_launch(ctx, "rtn_bf16_nib");
+            }
             if (deq)
                 rtn_bf16_kernel<true><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
                     reinterpret_cast<const T*>(x), g, fd, bits, sym, tensor_mode, scales, zps, codes,
