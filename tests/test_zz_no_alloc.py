@@ -74,13 +74,16 @@ def test_noalloc_call_allocates_no_device_memory():
     """The property the entry exists for.  On a fresh context (empty workspace) the calls after
     the first one leave the device's free memory unchanged, while the workspace observer on the
     same context has to grow its workspace (a cudaMalloc that shows in the free memory), which
-    shows that the check would see an allocation."""
+    shows that the check would see an allocation.  The control input has 1 Mi rows, so that
+    workspace (two floats a row, 8 MiB) is larger than the 2 MiB pages the driver hands out;
+    a small cudaMalloc can be served from a page the context already holds."""
     lib = _lib.load()
     c = C.c_void_p()
     assert lib.llmc_init(0, C.byref(c)) == 0, _lib.last_error()
     try:
         assert lib.llmc_set_stream(c, C.c_void_p(torch.cuda.current_stream().cuda_stream or 1)) == 0
         x = torch.randn(8192, 1024, device="cuda")
+        y = torch.randn(1 << 20, 4, device="cuda")  # control input for the workspace observer
         mn = torch.zeros(1, device="cuda")
         mx = torch.zeros(1, device="cuda")
         args = (_lib.ptr(x), _lib.dtype_code(x.dtype), C.c_int64(x.shape[0]), C.c_int64(x.shape[1]),
@@ -98,11 +101,13 @@ def test_noalloc_call_allocates_no_device_memory():
         torch.cuda.synchronize()
         assert torch.cuda.mem_get_info()[0] == free0
         assert float(mn) == float(x.min()) and float(mx) == float(x.max())
-        st = lib.llmc_observer_minmax(c, *args, _lib.STRATEGY["tensor"], C.c_int64(x.shape[1]), _lib.ptr(mn),
-                                      _lib.ptr(mx), 0)
+        st = lib.llmc_observer_minmax(c, _lib.ptr(y), _lib.dtype_code(y.dtype), C.c_int64(y.shape[0]),
+                                      C.c_int64(y.shape[1]), C.c_int64(y.stride(0)), _lib.STRATEGY["tensor"],
+                                      C.c_int64(y.shape[1]), _lib.ptr(mn), _lib.ptr(mx), 0)
         assert st == 0, _lib.last_error()
         torch.cuda.synchronize()
         assert torch.cuda.mem_get_info()[0] < free0
+        assert float(mn) == float(y.min()) and float(mx) == float(y.max())
     finally:
         lib.llmc_destroy(c)
 
