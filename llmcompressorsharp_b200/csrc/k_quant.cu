@@ -505,18 +505,66 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
 }
 
 // bf16 RTN to packed nibbles (num_bits <= 4, no dequantised output): rtn_bf16_kernel's exact
-// integer path with fewer integer-pipe instructions per element.
+// integer path with fewer instructions per element.  Each 32-bit word holds two bf16 columns,
+// and the two are carried through the paired fp32 instructions of sm_100 (FMUL2 / FFMA2 /
+// FADD2, each component rounded exactly as its scalar form).
 //   * f = x * rcp(s); an element whose f lies within 4 units in the last place of a bf16
-//     rounding midpoint takes the op-by-op chain (as in rtn_bf16_kernel).  The test is one
-//     multiply-add (the low 16 bits of f, shifted up) and one unsigned compare.
+//     rounding midpoint takes the op-by-op chain (as in rtn_bf16_kernel).  The test takes the
+//     low 16 bits of f, shifted up and offset, min-accumulated over a vector's eight elements
+//     and compared once.
 //   * bf16(f) by Veltkamp splitting, c = f * (2^16 + 1), bf16(f) = c - (c - f): rounding to
 //     nearest on 8 significant bits on the floating-point pipe (T. J. Dekker, "A floating-point
-//     technique for extending the available precision", 1971).  Its tie-breaking may differ
-//     from round-to-even, but ties are exactly the midpoint elements sent to the chain.
+//     technique for extending the available precision", 1971).  Each difference is one fused
+//     multiply-add by -1 (the product is exact, so the one rounding is the subtraction's).  Its
+//     tie-breaking may differ from round-to-even, but ties are exactly the midpoint elements
+//     sent to the chain.
 //   * rint by adding 1.5 * 2^23, then the clamp to [qmin - zp, qmax - zp] on that float (only in
-//     warps whose segments can reach the grid's ends); the code nibble (q - zp) & 0xF is the low
-//     nibble of the sum's bit pattern.
+//     warps whose segments can reach the grid's ends: a separate instantiation of the element
+//     loop); the code nibble (q - zp) & 0xF is the low nibble of the sum's bit pattern.
 //   * Nibbles are gathered with byte permutes, two 32-bit words per eight columns.
+template <bool CLAMP>
+__device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
+                                           float zf, int z, float qmin, float qmax, uint8_t* dst) {
+    constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
+    const float2 rcp2 = make_float2(rcp, rcp), k2 = make_float2(65537.f, 65537.f);
+    const float2 neg1 = make_float2(-1.f, -1.f), magic2 = make_float2(MAGIC, MAGIC);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t u[8];
+    uint32_t near = 0xFFFFFFFFu;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float2 xv = make_float2(__uint_as_float(ww[k] << 16), __uint_as_float(ww[k] & 0xFFFF0000u));
+        const float2 f = __fmul2_rn(xv, rcp2);
+        // low 16 bits of f within 4 of 0x8000  <=>  (bits(f) - 0x7FFC) * 2^16 <= 8 * 2^16 (mod 2^32)
+        near = min(near, __float_as_uint(f.x) * 65536u - 0x7FFC0000u);
+        near = min(near, __float_as_uint(f.y) * 65536u - 0x7FFC0000u);
+        const float2 c = __fmul2_rn(f, k2);
+        const float2 b16 = __ffma2_rn(__ffma2_rn(f, neg1, c), neg1, c);  // c - (c - f)
+        float2 rf = __fadd2_rn(b16, magic2);
+        if constexpr (CLAMP) {
+            rf.x = fminf(fmaxf(rf.x, cmin), cmax);
+            rf.y = fminf(fmaxf(rf.y, cmin), cmax);
+        }
+        u[2 * k] = __float_as_uint(rf.x);
+        u[2 * k + 1] = __float_as_uint(rf.y);
+    }
+    if (!fast || near <= 0x80000u) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+            const float f = __fmul_rn(xv, rcp);
+            if (!fast || (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u) {
+                const FqOut e = fq_chain_call<__nv_bfloat16>(xv, s, zf, qmin, qmax);
+                u[i] = (uint32_t)((e.code - z) & 0xF);
+            }
+        }
+    }
+    // byte b of the output holds columns 2b (high nibble) and 2b + 1 (low nibble)
+    const uint32_t ev = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);
+    const uint32_t od = __byte_perm(__byte_perm(u[1], u[3], 0x0040), __byte_perm(u[5], u[7], 0x0040), 0x5410);
+    *reinterpret_cast<uint32_t*>(dst) = ((ev << 4) & 0xF0F0F0F0u) | (od & 0x0F0F0F0Fu);
+}
+
 __global__ void __launch_bounds__(NT) rtn_bf16_nib_kernel(const __nv_bfloat16* x, SegGeom g, FastDiv fd, int bits,
                                                           int sym, int tensor_mode, float* scales, int32_t* zps,
                                                           uint8_t* codes) {
@@ -586,40 +634,18 @@ __global__ void __launch_bounds__(NT) rtn_bf16_nib_kernel(const __nv_bfloat16* x
         const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
         if (!active) continue;
         uint8_t* crow_p = codes + (int64_t)r * crow;
+        if (warp_clamp) {
 #pragma unroll
-        for (int j = 0; j < RV; j++) {
-            const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
-            const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
-            uint32_t u[VEC];
-            bool slow = !fast;
-#pragma unroll
-            for (int i = 0; i < VEC; i++) {
-                const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
-                const float f = __fmul_rn(xv, rcp);
-                // low 16 bits of f within 4 of 0x8000  <=>  (bits(f) - 0x7FFC) * 2^16 <= 8 * 2^16 (mod 2^32)
-                slow |= (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u;
-                const float cc = __fmul_rn(f, 65537.f);
-                const float b16 = __fsub_rn(cc, __fsub_rn(cc, f));
-                float rf = __fadd_rn(b16, MAGIC);
-                if (warp_clamp) rf = fminf(fmaxf(rf, cmin), cmax);
-                u[i] = __float_as_uint(rf);
+            for (int j = 0; j < RV; j++) {
+                const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
+                nib_vector<true>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, crow_p + c / 2);
             }
-            if (slow) {
+        } else {
 #pragma unroll
-                for (int i = 0; i < VEC; i++) {
-                    const float xv =
-                        (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
-                    const float f = __fmul_rn(xv, rcp);
-                    if (!fast || (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u) {
-                        const FqOut e = fq_chain_call<__nv_bfloat16>(xv, s, zf, qmin, qmax);
-                        u[i] = (uint32_t)((e.code - z) & 0xF);
-                    }
-                }
+            for (int j = 0; j < RV; j++) {
+                const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
+                nib_vector<false>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, crow_p + c / 2);
             }
-            // byte b of the output holds columns 2b (high nibble) and 2b + 1 (low nibble)
-            const uint32_t ev = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);
-            const uint32_t od = __byte_perm(__byte_perm(u[1], u[3], 0x0040), __byte_perm(u[5], u[7], 0x0040), 0x5410);
-            *reinterpret_cast<uint32_t*>(crow_p + c / 2) = ((ev << 4) & 0xF0F0F0F0u) | (od & 0x0F0F0F0Fu);
         }
     }
 }

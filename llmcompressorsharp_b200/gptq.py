@@ -192,7 +192,7 @@ class GPTQModifier(ModifierBase):
         self._hooks = ActivationHookManager()
         self._acc = {}
         self._alias = {}
-        owners: dict[tuple, HessianAccumulator] = {}
+        owners: dict[tuple, tuple] = {}  # key -> (accumulator, the input it saw)
         for wname in self.targeted_names(state):
             lname = wname[: -len(".weight")] if wname.endswith(".weight") else wname
             module = state.named_modules.get(lname)
@@ -216,14 +216,19 @@ class GPTQModifier(ModifierBase):
 
         def hook(mod, inputs, output):
             x = inputs[0]
-            key = (x.data_ptr(), tuple(x.shape), x.dtype, x._version)
-            owner = owners.get(key)
+            # Same tensor = same address, shape, strides, dtype and in-place version.  The entry
+            # holds x itself: while it stands, the caching allocator cannot give x's memory to
+            # a later tensor (say the next norm's output after x was freed), which would
+            # otherwise match the key with different data.
+            key = (x.data_ptr(), tuple(x.shape), tuple(x.stride()), x.dtype, x._version)
+            entry = owners.get(key)
+            owner = entry[0] if entry is not None else None
             if owner is None:
                 if id(acc) in alias:
                     raise InvalidOperationError("GPTQ share_inputs: a module that shared its input earlier "
                                                 "received a different input")
                 owners.clear()
-                owners[key] = acc
+                owners[key] = (acc, x)
                 acc.update(x)
             elif owner is not acc:
                 prev = alias.get(id(acc))

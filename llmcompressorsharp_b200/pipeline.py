@@ -11,8 +11,8 @@ Overlap (one GPU): ``run`` pipelines the layers over two library contexts on two
 While layer l is solved (Cholesky factor + GPTQ, mostly latency-bound kernels) on the solve
 stream, layer l+1's Hessians accumulate on the Hessian stream; the Hessian context's
 persistent kernel is capped to ``sm_count - reserve_sms`` SMs so the solve always finds SMs
-free.  Hessians are double-buffered (two handle sets), and events order every hand-off:
-solve(l) waits for accumulate(l), and accumulate(l+2) waits for solve(l) before it resets
+free.  Hessians rotate through three handle sets, and events order every hand-off:
+solve(l) waits for accumulate(l), and accumulate(l+3) waits for solve(l) before it resets
 the buffer set they share.
 
 Multi-GPU: calibration tokens are split across ranks; each rank accumulates its partial
@@ -356,7 +356,7 @@ def _events():
 
 
 class _Overlap:
-    """Two library contexts, two streams and two Hessian handle sets for ``GptqPipeline.run``."""
+    """Two library contexts, two streams and three Hessian handle sets for ``GptqPipeline.run``."""
 
     def __init__(self, pipe: GptqPipeline, reserve_sms: int):
         self.pipe = pipe
@@ -430,7 +430,10 @@ class _Overlap:
         K = min(self.PROLOGUE_LAYERS, len(layers)) if acts_ready else 0
         if K < 2:
             K = 0
-        nsets = max(2, K + 1)
+        # Three sets: the solve of layer l may run up to two layers' accumulation long before
+        # layer l + 3 needs its set back, which absorbs solves that run long (the factorisation
+        # of a layer whose Cholesky needs the damping fallback, launch jitter on the reserve).
+        nsets = max(3, K + 1)
         self._ensure_sets(nsets)
         solved = [None] * nsets  # event: last solve that read buffer set b
 

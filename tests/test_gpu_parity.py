@@ -880,6 +880,51 @@ def test_gptq_modifier_shared_inputs_match_separate():
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
 
 
+def test_gptq_modifier_shared_inputs_through_a_decoder_forward():
+    """A decoder forward frees its temporaries between Linear calls, so the caching allocator
+    hands a later tensor (the post-attention norm's output) the memory of an earlier one (the
+    o-projection's input, same shape and dtype).  Sharing must key on the tensor, not on a
+    recycled address: per-weight Hessians and shared ones give the same weights."""
+    from llmcompressorsharp_b200 import CompressionSession, CompressionState, GPTQConfig, GPTQModifier, SessionStatus
+    from llmcompressorsharp_b200.calibration import LlamaForCalibration, LlamaShape, calibration_batches, drive
+
+    shape = LlamaShape(hidden=128, intermediate=256, heads=4, kv_heads=2, layers=2, vocab=512)
+    model = LlamaForCalibration(shape, dtype=torch.float32, device=DEV, seed=3)
+    batches = list(calibration_batches(shape.vocab, 6, 64, 2, seed=4, device=DEV))
+    cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=64, block_size=64)
+    outs = []
+    for share in (False, True):
+        state = CompressionState({k: v.detach().clone() for k, v in model.linear_weights().items()})
+        state.named_modules = model.linear_modules()
+        session = CompressionSession([GPTQModifier(cfg, share_inputs=share)])
+        assert session.run(state, drive(model, batches)) == SessionStatus.COMPLETED, session.failure
+        outs.append(state.named_weights)
+    for k in outs[0]:
+        assert torch.equal(outs[0][k], outs[1][k]), k
+
+
+def test_gptq_modifier_shared_inputs_tell_a_transposed_view_apart():
+    """x and x.T of a square x share address, shape and dtype but not data."""
+    from llmcompressorsharp_b200 import CompressionState, GPTQConfig, GPTQModifier
+
+    a = torch.nn.Linear(64, 16, bias=False).to(DEV)
+    b = torch.nn.Linear(64, 16, bias=False).to(DEV)
+    outs = []
+    for share in (False, True):
+        st = CompressionState({"a.weight": a.weight.detach().clone(), "b.weight": b.weight.detach().clone()})
+        st.named_modules = {"a": a, "b": b}
+        mod = GPTQModifier(GPTQConfig(num_bits=4, strategy="group", group_size=32, symmetric=False), share_inputs=share)
+        mod.initialize(st)
+        mod.on_start(st)
+        x = torch.randn(64, 64, device=DEV, generator=torch.Generator(DEV).manual_seed(6))
+        a(x)
+        b(x.T)
+        mod.on_end(st)
+        mod.finalize(st)
+        outs.append((st.named_weights["a.weight"], st.named_weights["b.weight"]))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
 # --------------------------------------------------------------------------- SmoothQuant / AWQ / SparseGPT
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
