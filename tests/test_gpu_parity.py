@@ -1050,15 +1050,42 @@ def test_pipeline_sparsegpt_matches_oracle():
                 assert rel_fro(got["wq"], rout) < 1e-3
 
 
-def test_awq_search_matches_oracle():
+@pytest.mark.parametrize("strategy,gs,m", [("group", 128, 128), ("group", 256, 300), ("group", 64, 40),
+                                           ("channel", 0, 96)])
+def test_awq_search_matches_oracle(strategy, gs, m):
+    """The one-pass group kernel (4 columns a lane for groups of up to 128, 8 up to 256; row
+    counts that leave warps idle) and the per-point kernel (channel scales)."""
     from llmcompressorsharp_b200 import RtnConfig, awq_search
 
-    w = (torch.randn(128, 512, generator=gen(8)) * 0.02).to(torch.bfloat16)
+    w = (torch.randn(m, 512, generator=gen(8)) * 0.02).to(torch.bfloat16)
     a = (torch.rand(512, generator=gen(9)) * 3 + 0.1) * torch.where(torch.rand(512, generator=gen(10)) < 0.02, 30.0, 1.0)
-    cfg = RtnConfig(4, False, "group", group_size=128)
+    cfg = RtnConfig(4, False, strategy, group_size=gs)
     s, k, mse = awq_search(w.to(DEV), a.to(DEV), 20, cfg)
-    rs, rk, rmse = o_awq.awq_search(w, a.numpy(), 20, o_rtn.RtnConfig(4, False, "group", group_size=128))
+    rs, rk, rmse = o_awq.awq_search(w, a.numpy(), 20, o_rtn.RtnConfig(4, False, strategy, group_size=gs))
     assert np.allclose(mse.cpu().numpy(), np.asarray(rmse), rtol=1e-4)
     assert k == rk or abs(rmse[k - 1] / rmse[rk - 1] - 1) < 1e-4
     if k == rk:
         assert rel_fro(s, rs) < 1e-6
+
+
+def test_awq_search_without_best_k_reads_nothing_back():
+    """best_k NULL: the call only enqueues work; best_s and the per-point mse equal the
+    synchronising call's."""
+    import ctypes as C
+
+    from llmcompressorsharp_b200 import RtnConfig, _lib, awq_search
+    from llmcompressorsharp_b200.quantization import ctx
+
+    w = (torch.randn(256, 1024, generator=gen(18)) * 0.02).to(torch.bfloat16).to(DEV)
+    a = (torch.rand(1024, generator=gen(19)) * 3 + 0.1).to(DEV)
+    cfg = RtnConfig(4, True, "group", group_size=128)
+    s, k, mse = awq_search(w, a, 20, cfg)
+    s2 = torch.empty_like(s)
+    mse2 = torch.empty_like(mse)
+    qc = cfg.to_c()
+    _lib.call("llmc_awq_search", C.c_void_p(ctx(w.device)), _lib.ptr(w), _lib.dtype_code(w.dtype), C.c_int64(256),
+              C.c_int64(1024), C.c_int64(1024), _lib.ptr(a), C.c_int32(20), C.byref(qc), _lib.ptr(s2), _lib.ptr(mse2),
+              None)
+    torch.cuda.synchronize()
+    assert torch.equal(s2, s) and torch.equal(mse2, mse)
+    assert int(torch.argmin(mse)) + 1 == k

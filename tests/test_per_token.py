@@ -61,3 +61,38 @@ def test_per_token_rejects_wide_codes():
 
     with pytest.raises(ArgumentOutOfRangeError):
         quantize_per_token(torch.ones(2, 8, device=DEV), 9, True)
+
+
+@pytest.mark.parametrize("bits,sym", [(8, True), (8, False), (4, True), (4, False)])
+@pytest.mark.parametrize("rows,cols", [(333, 4096), (1000, 2048), (64, 256), (50, 768)])
+def test_per_token_codes_only_bf16_rows_in_registers(bits, sym, rows, cols):
+    """Codes without fake-quantised values for bf16 rows of up to 4,096 columns (a multiple of
+    256) take the register-resident kernel; codes, scales and zero-points equal the oracle's.
+    A few hundred thousand elements per case put some quotients near a bf16 rounding midpoint,
+    the elements that kernel hands to the op-by-op chain; a row of exact midpoints forces it."""
+    from llmcompressorsharp_b200 import quantize_per_token
+
+    x = acts(rows, cols, torch.bfloat16, rows + cols + bits)
+    if rows > 5:
+        # symmetric grids: absmax 63.5 (int8) or 3.5 (int4) gives scale 1/2, so the other
+        # entries, (k + 1/2) / 2, divide to exact half-integers (ties of the rounding)
+        half = 127.0 if bits == 8 else 7.0
+        x[5] = (((torch.arange(cols) % 8) - 4.0) * 0.5 + 0.25).to(torch.bfloat16)
+        x[5, 0] = half / 2
+    codes, scales, zps, deq = quantize_per_token(x.to(DEV), bits, sym, want_values=False)
+    assert deq is None
+    rdeq, rcodes, rs, rz = o_pt.quantize_per_token(x, bits, sym)
+    assert np.array_equal(scales.cpu().numpy(), rs)
+    assert np.array_equal(zps.cpu().numpy(), rz.astype(np.int32))
+    assert torch.equal(codes.cpu().to(torch.int32), rcodes)
+
+
+def test_per_token_codes_only_nan_row_bf16():
+    from llmcompressorsharp_b200 import quantize_per_token
+
+    x = acts(24, 1024, torch.bfloat16, 77)
+    x[3, 100] = float("nan")
+    codes, scales, _, _ = quantize_per_token(x.to(DEV), 8, True)
+    _, rcodes, rs, _ = o_pt.quantize_per_token(x, 8, True)
+    assert np.array_equal(scales.cpu().numpy(), rs, equal_nan=True)
+    assert torch.equal(codes.cpu().to(torch.int32), rcodes)
