@@ -522,8 +522,16 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
 //     warps whose segments can reach the grid's ends: a separate instantiation of the element
 //     loop); the code nibble (q - zp) & 0xF is the low nibble of the sum's bit pattern.
 //   * Nibbles are gathered with byte permutes, two 32-bit words per eight columns.
-// The kernel is bounded to 64 registers (four 256-thread blocks per SM): on 224 Llama-3-8B
-// weights that ran 4 % faster than the unbounded 72-register build (three blocks per SM).
+// A lane holds NRV 8-column vectors of one segment, so the segment's L = length / (8 NRV) lanes
+// each repeat its parameter math (min / max, scale, zero-point, reciprocal) once per 8 NRV
+// elements.  The launch bound follows the registers that holds: four 256-thread blocks per SM
+// at NRV = 4 (64 registers; on 224 Llama-3-8B weights that ran 4 % faster than the unbounded
+// 72-register build), three at 8, two at 16.
+// Largest NRV the launch picks (16: a whole 128-column group in one lane).
+#ifndef NIB_RV_MAX
+#define NIB_RV_MAX 16
+#endif
+
 template <bool CLAMP>
 __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
                                            float zf, int z, float qmin, float qmax, uint8_t* dst) {
@@ -567,9 +575,10 @@ __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin
     *reinterpret_cast<uint32_t*>(dst) = ((ev << 4) & 0xF0F0F0F0u) | (od & 0x0F0F0F0Fu);
 }
 
-__global__ void __launch_bounds__(NT, 4) rtn_bf16_nib_kernel(const __nv_bfloat16* x, SegGeom g, FastDiv fd, int bits,
-                                                          int sym, int tensor_mode, float* scales, int32_t* zps,
-                                                          uint8_t* codes) {
+template <int NRV>
+__global__ void __launch_bounds__(NT, NRV <= 4 ? 4 : (NRV <= 8 ? 3 : 2))
+    rtn_bf16_nib_kernel(const __nv_bfloat16* x, SegGeom g, FastDiv fd, int bits, int sym, int tensor_mode,
+                        float* scales, int32_t* zps, uint8_t* codes) {
     constexpr int VEC = 8;
     const int L = g.L;
     const uint32_t gpb = NT / L;
@@ -589,13 +598,13 @@ __global__ void __launch_bounds__(NT, 4) rtn_bf16_nib_kernel(const __nv_bfloat16
         const uint32_t r = fastdiv(sg, fd);
         const int64_t c0 = (int64_t)(sg - r * (uint32_t)g.nseg) * seglen;
         const __nv_bfloat16* row = x + (int64_t)r * g.ld + c0;
-        uint4 w[RV];
+        uint4 w[NRV];
         __nv_bfloat162 mn2[2] = {pinf, pinf}, mx2[2] = {ninf, ninf};
         if (active) {
 #pragma unroll
-            for (int j = 0; j < RV; j++) w[j] = *reinterpret_cast<const uint4*>(row + (int64_t)(j * L + sub) * VEC);
+            for (int j = 0; j < NRV; j++) w[j] = *reinterpret_cast<const uint4*>(row + (int64_t)(j * L + sub) * VEC);
 #pragma unroll
-            for (int j = 0; j < RV; j++) {
+            for (int j = 0; j < NRV; j++) {
                 const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
@@ -638,13 +647,13 @@ __global__ void __launch_bounds__(NT, 4) rtn_bf16_nib_kernel(const __nv_bfloat16
         uint8_t* crow_p = codes + (int64_t)r * crow;
         if (warp_clamp) {
 #pragma unroll
-            for (int j = 0; j < RV; j++) {
+            for (int j = 0; j < NRV; j++) {
                 const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
                 nib_vector<true>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, crow_p + c / 2);
             }
         } else {
 #pragma unroll
-            for (int j = 0; j < RV; j++) {
+            for (int j = 0; j < NRV; j++) {
                 const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
                 nib_vector<false>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, crow_p + c / 2);
             }
@@ -776,8 +785,18 @@ llmc_status launch_rtn(llmc_ctx* ctx, const void* x, int64_t m, int64_t n, int64
             g.L = (int)lanes;
             const FastDiv fd = make_fastdiv((uint32_t)g.nseg);
             if (!deq && codes && bits <= 4) {
-                rtn_bf16_nib_kernel<<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(
-                    reinterpret_cast<const T*>(x), g, fd, bits, sym, tensor_mode, scales, zps, codes);
+                // Vectors per lane: as many as a segment holds, up to NIB_RV_MAX, so fewer lanes
+                // share (and repeat) a segment's parameter math.
+                int nrv = NIB_RV_MAX;
+                while (nrv > RV && seglen % ((int64_t)nrv * V) != 0) nrv /= 2;
+                g.L = (int)(seglen / ((int64_t)nrv * V));
+#define LLMC_NIB(NRV)                                                                                  \
+    rtn_bf16_nib_kernel<NRV><<<grid_for(ctx, total, NT / g.L), NT, 0, ctx->stream>>>(                  \
+        reinterpret_cast<const T*>(x), g, fd, bits, sym, tensor_mode, scales, zps, codes)
+                if (nrv == 16) LLMC_NIB(16);
+                else if (nrv == 8) LLMC_NIB(8);
+                else LLMC_NIB(RV);
+#undef LLMC_NIB
                 return check_launch(ctx, "rtn_bf16_nib");
             }
             if (deq)
