@@ -161,6 +161,23 @@ __global__ void __launch_bounds__(32 * WARPS) act_token_kernel(const T* x, int64
 //     pattern plus zp.
 constexpr int REG_NV = 16;
 
+// The op-by-op chain for all eight codes of a vector, packed: one out-of-line copy, so the
+// unrolled element loops that call it stay small enough for the instruction cache.
+__device__ __noinline__ uint2 token_chain8(uint4 w, float s, float rcp, float zf, int z, float qmin, float qmax,
+                                           int iqmin, int iqmax) {
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t u[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+        int code;
+        quant_elem<__nv_bfloat16>(xv, s, rcp, zf, z, qmin, qmax, iqmin, iqmax, false, &code);
+        u[i] = (uint32_t)code;
+    }
+    return make_uint2(__byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410),
+                      __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410));
+}
+
 template <bool CLAMP>
 __device__ __forceinline__ uint2 token_codes8(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
                                               float zf, int z, float qmin, float qmax, int iqmin, int iqmax) {
@@ -186,15 +203,7 @@ __device__ __forceinline__ uint2 token_codes8(const uint4& w, float rcp, float c
         u[2 * k] = __float_as_uint(rf.x) + (uint32_t)z;
         u[2 * k + 1] = __float_as_uint(rf.y) + (uint32_t)z;
     }
-    if (!fast || near <= 0x80000u) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
-            int code;
-            quant_elem<__nv_bfloat16>(xv, s, rcp, zf, z, qmin, qmax, iqmin, iqmax, false, &code);
-            u[i] = (uint32_t)code;
-        }
-    }
+    if (!fast || near <= 0x80000u) return token_chain8(w, s, rcp, zf, z, qmin, qmax, iqmin, iqmax);
     return make_uint2(__byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410),
                       __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410));
 }

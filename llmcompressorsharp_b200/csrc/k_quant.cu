@@ -532,6 +532,23 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
 #define NIB_RV_MAX 16
 #endif
 
+// The op-by-op chain for all eight columns of a vector, packed as nib_vector packs them: one
+// out-of-line copy, so the unrolled element loops that call it stay small.
+__device__ __noinline__ uint32_t nib_chain8(uint4 w, float s, float zf, int z, float qmin, float qmax) {
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t u[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
+        int code;
+        fq_chain<__nv_bfloat16>(xv, s, zf, qmin, qmax, &code);
+        u[i] = (uint32_t)((code - z) & 0xF);
+    }
+    const uint32_t ev = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);
+    const uint32_t od = __byte_perm(__byte_perm(u[1], u[3], 0x0040), __byte_perm(u[5], u[7], 0x0040), 0x5410);
+    return ((ev << 4) & 0xF0F0F0F0u) | (od & 0x0F0F0F0Fu);
+}
+
 template <bool CLAMP>
 __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
                                            float zf, int z, float qmin, float qmax, uint8_t* dst) {
@@ -559,15 +576,8 @@ __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin
         u[2 * k + 1] = __float_as_uint(rf.y);
     }
     if (!fast || near <= 0x80000u) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
-            const float f = __fmul_rn(xv, rcp);
-            if (!fast || (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u) {
-                const FqOut e = fq_chain_call<__nv_bfloat16>(xv, s, zf, qmin, qmax);
-                u[i] = (uint32_t)((e.code - z) & 0xF);
-            }
-        }
+        *reinterpret_cast<uint32_t*>(dst) = nib_chain8(w, s, zf, z, qmin, qmax);
+        return;
     }
     // byte b of the output holds columns 2b (high nibble) and 2b + 1 (low nibble)
     const uint32_t ev = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);

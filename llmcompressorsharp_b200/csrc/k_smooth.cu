@@ -140,6 +140,13 @@ __global__ void recip_kernel(const float* x, int64_t n, float* out) {
 // added in fp32 first, then once in double).  W is read from memory once instead of twice per
 // grid point.  The error divides by multiplying with 1 / s_k (within one unit in the last place of
 // the quotient), so the sums differ from the per-point kernel's by about 1e-7 relative.
+// The op-by-op chain out of line (the one-pass kernel's rare midpoint elements): one copy instead
+// of one per unrolled column.
+__device__ __noinline__ float fq_chain_f32(float v, float s, float zf, float qmin, float qmax) {
+    int code;
+    return fq_chain<float>(v, s, zf, qmin, qmax, &code);
+}
+
 constexpr int AWQ_WARPS = NT / 32;
 constexpr int AWQ_PER = 8;  // columns per lane: groups of up to 256
 
@@ -203,11 +210,10 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
                 const int col = lane + 32 * i;
                 if (col >= L) continue;
                 float fq;
-                int code;
                 const float f = __fmul_rn(v[i], rsc);
                 const float fr = rintf(f);
                 if (!rs_ok || fabsf(fabsf(__fsub_rn(f, fr)) - 0.5f) <= fabsf(f) * 4.8e-7f + 1e-30f) {
-                    fq = fq_chain<float>(v[i], sc, zf, qmin, qmax, &code);
+                    fq = fq_chain_f32(v[i], sc, zf, qmin, qmax);
                 } else {
                     float t = __fadd_rn(fr, zf);
                     t = (t < qmin) ? qmin : ((t > qmax) ? qmax : t);
