@@ -526,10 +526,13 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
 // each repeat its parameter math (min / max, scale, zero-point, reciprocal) once per 8 NRV
 // elements.  The launch bound follows the registers that holds: four 256-thread blocks per SM
 // at NRV = 4 (64 registers; on 224 Llama-3-8B weights that ran 4 % faster than the unbounded
-// 72-register build), three at 8, two at 16.
-// Largest NRV the launch picks (16: a whole 128-column group in one lane).
+// 72-register build), three at 8, two at 16.  On those weights (g128, so L = 4, 2, 1 lanes a
+// group) NRV = 4 ran at 2,426 GB/s, 8 at 1,890 and 16 at 1,144: with fewer lanes a group, one
+// load instruction of a warp covers fewer whole 32-byte sectors and fewer warps are resident,
+// which costs more than the repeated parameter math saves.
+// Largest NRV the launch picks.
 #ifndef NIB_RV_MAX
-#define NIB_RV_MAX 16
+#define NIB_RV_MAX 4
 #endif
 
 // The op-by-op chain for all eight columns of a vector, packed as nib_vector packs them: one

@@ -140,11 +140,54 @@ __global__ void recip_kernel(const float* x, int64_t n, float* out) {
 // added in fp32 first, then once in double).  W is read from memory once instead of twice per
 // grid point.  The error divides by multiplying with 1 / s_k (within one unit in the last place of
 // the quotient), so the sums differ from the per-point kernel's by about 1e-7 relative.
-// The op-by-op chain out of line (the one-pass kernel's rare midpoint elements): one copy instead
-// of one per unrolled column.
-__device__ __noinline__ float fq_chain_f32(float v, float s, float zf, float qmin, float qmax) {
-    int code;
-    return fq_chain<float>(v, s, zf, qmin, qmax, &code);
+// Squared error of one (row, group) segment held by a warp (PER columns a lane) for one grid
+// point: min / max of W * s_k, the affine parameters, the fake-quantised value and
+// (FQ / s_k - W)^2 summed over the lane's columns in fp32.
+template <int PER>
+__device__ __forceinline__ float awq_seg_err(const float (&w)[PER], const float* sv, const float* rv, int lane, int L,
+                                             int bits, int sym, float qmin, float qmax) {
+    float v[PER];
+    float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int col = lane + 32 * i;
+        v[i] = col < L ? __fmul_rn(w[i], sv[col]) : 0.f;
+        if (col < L) {
+            mn = fmin_nan(mn, v[i]);
+            mx = fmax_nan(mx, v[i]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    float sc;
+    int z;
+    affine_params(mn, mx, bits, sym, &sc, &z);
+    const float zf = (float)z;
+    const float rsc = __frcp_rn(sc);
+    const bool rs_ok = fabsf(rsc) <= 3.0e38f && rsc != 0.f;
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int col = lane + 32 * i;
+        if (col >= L) continue;
+        float fq;
+        const float f = __fmul_rn(v[i], rsc);
+        const float fr = rintf(f);
+        if (!rs_ok || fabsf(fabsf(__fsub_rn(f, fr)) - 0.5f) <= fabsf(f) * 4.8e-7f + 1e-30f) {
+            int code;
+            fq = fq_chain<float>(v[i], sc, zf, qmin, qmax, &code);
+        } else {
+            float t = __fadd_rn(fr, zf);
+            t = (t < qmin) ? qmin : ((t > qmax) ? qmax : t);
+            fq = __fmul_rn(__fsub_rn(t, zf), sc);
+        }
+        const float e = __fsub_rn(__fmul_rn(fq, rv[col]), w[i]);
+        part = __fmaf_rn(e, e, part);
+    }
+    return part;
 }
 
 constexpr int AWQ_WARPS = NT / 32;
@@ -171,58 +214,26 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
     __syncthreads();
     float qmin, qmax;
     qrange(bits, sym, &qmin, &qmax);
-    for (int64_t r = (int64_t)blockIdx.y * AWQ_WARPS + warp; r < m; r += (int64_t)gridDim.y * AWQ_WARPS) {
-        float w[PER];
+    // Two rows per pass (r and r + stride; a missing second row is all zeros, whose error is 0):
+    // the two rows' chains per grid point (shuffles, affine parameters, reciprocal, elements) are
+    // independent, so their latencies overlap.
+    const int64_t stride = (int64_t)gridDim.y * AWQ_WARPS;
+    for (int64_t r = (int64_t)blockIdx.y * AWQ_WARPS + warp; r < m; r += 2 * stride) {
+        const int64_t r2 = r + stride;
+        float w[PER], w2[PER];
 #pragma unroll
         for (int i = 0; i < PER; i++) {
             const int col = lane + 32 * i;
             w[i] = col < L ? to_f<T>(W[r * ldw + c0 + col]) : 0.f;
+            w2[i] = (col < L && r2 < m) ? to_f<T>(W[r2 * ldw + c0 + col]) : 0.f;
         }
 #pragma unroll 1
         for (int k = 0; k < grid_pts; k++) {
             const float* sv = ss + k * gs;
             const float* rv = rs + k * gs;
-            float v[PER];
-            float mn = INFINITY, mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < PER; i++) {
-                const int col = lane + 32 * i;
-                v[i] = col < L ? __fmul_rn(w[i], sv[col]) : 0.f;
-                if (col < L) {
-                    mn = fmin_nan(mn, v[i]);
-                    mx = fmax_nan(mx, v[i]);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-                mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            }
-            float sc;
-            int z;
-            affine_params(mn, mx, bits, sym, &sc, &z);
-            const float zf = (float)z;
-            const float rsc = __frcp_rn(sc);
-            const bool rs_ok = fabsf(rsc) <= 3.0e38f && rsc != 0.f;
-            float part = 0.f;
-#pragma unroll
-            for (int i = 0; i < PER; i++) {
-                const int col = lane + 32 * i;
-                if (col >= L) continue;
-                float fq;
-                const float f = __fmul_rn(v[i], rsc);
-                const float fr = rintf(f);
-                if (!rs_ok || fabsf(fabsf(__fsub_rn(f, fr)) - 0.5f) <= fabsf(f) * 4.8e-7f + 1e-30f) {
-                    fq = fq_chain_f32(v[i], sc, zf, qmin, qmax);
-                } else {
-                    float t = __fadd_rn(fr, zf);
-                    t = (t < qmin) ? qmin : ((t > qmax) ? qmax : t);
-                    fq = __fmul_rn(__fsub_rn(t, zf), sc);
-                }
-                const float e = __fsub_rn(__fmul_rn(fq, rv[col]), w[i]);
-                part = __fmaf_rn(e, e, part);
-            }
-            acc[k * 32] += (double)part;
+            const float p1 = awq_seg_err<PER>(w, sv, rv, lane, L, bits, sym, qmin, qmax);
+            const float p2 = awq_seg_err<PER>(w2, sv, rv, lane, L, bits, sym, qmin, qmax);
+            acc[k * 32] += (double)p1 + (double)p2;
         }
     }
     __syncthreads();
