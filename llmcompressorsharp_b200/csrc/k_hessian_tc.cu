@@ -608,12 +608,29 @@ constexpr int SYRK_UNIT_KB = 256;
 constexpr int SYRK_COUNTER_WORD = 8;
 
 // Token splits for the dynamic order: about SYRK_UNIT_KB k-blocks per unit, at most 16 splits,
-// and >= 32 k-blocks per unit when split.
-int unit_splits(int kb_total) {
-    int s = (kb_total + SYRK_UNIT_KB / 2) / SYRK_UNIT_KB;
-    if (s > 16) s = 16;
-    while (s > 1 && (kb_total + s - 1) / s < 32) s--;
-    return s < 1 ? 1 : s;
+// and >= 32 k-blocks per unit when split.  From there up to half as many splits again may be
+// added when that fills the last wave of `pairs` better (units are dealt one at a time, so the
+// launch ends with a partly filled wave of equal units): at d = 4,096 on 58 pairs, 4 splits give
+// 9.38 waves of units (0.938 of the last wave's slots used over the launch), 5 give 11.72 (0.977).
+int unit_splits(int kb_total, int ntiles, int pairs) {
+    int s0 = (kb_total + SYRK_UNIT_KB / 2) / SYRK_UNIT_KB;
+    if (s0 > 16) s0 = 16;
+    while (s0 > 1 && (kb_total + s0 - 1) / s0 < 32) s0--;
+    if (s0 < 1) s0 = 1;
+    if (pairs < 1) return s0;
+    int best = s0;
+    double best_eff = 0.0;
+    for (int s = s0; s <= 16 && s <= s0 + s0 / 2; s++) {
+        if (s > 1 && (kb_total + s - 1) / s < 32) break;
+        const long long units = (long long)ntiles * s;
+        const long long waves = (units + pairs - 1) / pairs;
+        const double eff = (double)units / ((double)waves * pairs);
+        if (eff > best_eff + 1e-3) {
+            best_eff = eff;
+            best = s;
+        }
+    }
+    return best;
 }
 
 // Token splits: balance the last wave over `cap` workers while keeping >= 32 k-blocks (2048
@@ -752,7 +769,7 @@ llmc_status syrk_tc(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64
             }
             if (n != p.ntiles) return fail(LLMC_ERR_INTERNAL, "syrk pair tile order: %d of %d tiles", n, p.ntiles);
             p.kb_total = a.kb_total;
-            p.splits = SYRK_DYNAMIC ? unit_splits(p.kb_total) : pick_splits(p.ntiles, p.kb_total, pcap);
+            p.splits = SYRK_DYNAMIC ? unit_splits(p.kb_total, p.ntiles, pcap) : pick_splits(p.ntiles, p.kb_total, pcap);
             p.kb_per_split = (p.kb_total + p.splits - 1) / p.splits;
             p.err = ctx->dflags + 2;
             p.next_unit = ctx->dflags + SYRK_COUNTER_WORD;

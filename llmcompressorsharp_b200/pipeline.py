@@ -451,11 +451,17 @@ class _Overlap:
                 done.record(self.ss)
                 solved[b] = done
 
+        def hessian_limit(whole_gpu: bool):
+            # Accumulations enqueued before the first solve have no solve beside them: they
+            # take every SM (the limit is read when a launch is enqueued).
+            _lib.call("llmc_set_sm_limit", C.c_void_p(self.ch), C.c_int32(0 if whole_gpu else self.hessian_sms))
+
         pending = None
         if K:
             # Prologue: layers 0..K-1 in sets 0..K-1, site-major, each arriving chunk added to
             # all K layers' Hessians before the next chunk is waited for.
             acts = [acts_for(l) for l in layers[:K]]
+            hessian_limit(True)
             with torch.cuda.stream(self.sh):
                 for s in pipe.sites:
                     ev = _events() if hess_events is not None else None
@@ -468,6 +474,7 @@ class _Overlap:
                         hess_events.append((ev[0], ev[1], s.d, sum(a[s.name].shape[0] for a in acts)))
                 acc_done = torch.cuda.Event()
                 acc_done.record(self.sh)
+            hessian_limit(False)
             for i in range(K - 1):
                 solve((layers[i], i, acc_done))
             pending = (layers[K - 1], K - 1, acc_done)
@@ -475,6 +482,9 @@ class _Overlap:
             l = layers[i]
             b = i % nsets
             a = acts_for(l)
+            first = pending is None  # nothing solves beside this accumulation
+            if first:
+                hessian_limit(True)
             with torch.cuda.stream(self.sh):
                 if solved[b] is not None:
                     self.sh.wait_event(solved[b])
@@ -488,6 +498,8 @@ class _Overlap:
                         hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
                 acc_done = torch.cuda.Event()
                 acc_done.record(self.sh)
+            if first:
+                hessian_limit(False)
             if pending is not None:
                 solve(pending)
             pending = (l, b, acc_done)
