@@ -103,7 +103,7 @@ class GptqPipeline:
         """Kernels launched so far by the library contexts this pipeline uses."""
         n = _lib.launch_count(self.device.index)
         if self.overlap is not None:
-            for c in (self.overlap.ch, self.overlap.cs):
+            for c in [self.overlap.ch] + self.overlap.solve_contexts():
                 v = C.c_int64()
                 _lib.call("llmc_launch_count", C.c_void_p(c), C.byref(v))
                 n += int(v.value)
@@ -177,13 +177,16 @@ class GptqPipeline:
                 _lib.call("llmc_hessian_update", h, C.c_void_p(x.data_ptr() + r0 * x.stride(0) * x.element_size()),
                           _lib.dtype_code(x.dtype), C.c_int64(r1 - r0), C.c_int64(x.stride(0)))
 
-    def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict, ctx=None, rows=None):
+    def solve_site(self, site: SiteSpec, h_ptr: int, weights: dict, outputs: dict, ctx=None, rows=None, u=None,
+                   work=None):
         """U from the site's H (upper triangle), then one stacked GPTQ solve of every weight
         that reads the site (outputs are views into stacked per-site buffers).  ``ctx`` is a
         library context bound to the stream to run on (default: torch's current stream).
         ``rows`` = (r0, r1) solves only those rows of the site's stack (rows are independent
         given U); the stacked outputs are written at the same rows.  Row ranges need a
-        per-row strategy (channel or group)."""
+        per-row strategy (channel or group).  ``u`` (d * d fp32) and ``work`` (the stack's rows
+        * d fp32) are scratch buffers for this call; by default the pipeline's own, so solves
+        that run at the same time on other streams pass their own."""
         from .distributed import stack_slices
 
         d = site.d
@@ -198,15 +201,16 @@ class GptqPipeline:
             raise ValueError(f"row range [{r0}, {r1}) outside the stack of {M} rows")
         if rows is not None and self.solver == "gptq" and self.cfg.strategy == "tensor":
             raise ValueError("row-sharded solves need a per-row strategy (channel or group)")
+        u = self.u if u is None else u
         _lib.call("llmc_chol_inverse", ctx, C.c_void_p(h_ptr), C.c_int64(d), C.c_int64(d),
-                  C.c_float(self.cfg.dampening_frac), 1, _lib.ptr(self.u), C.c_int64(d), 1)
+                  C.c_float(self.cfg.dampening_frac), 1, _lib.ptr(u), C.c_int64(d), 1)
         if r1 == r0:
             return
         parts = stack_slices(ms, r0, r1)  # [(weight index, first row, rows)]
         st = outputs[_stack_key(site)]
         wq = st.get("wq")
         if wq is None:
-            wq = self.work[: (r1 - r0) * d].view(r1 - r0, d)
+            wq = (self.work if work is None else work)[: (r1 - r0) * d].view(r1 - r0, d)
         else:
             wq = wq[r0:r1]
         if self.solver == "sparsegpt":
@@ -215,7 +219,7 @@ class GptqPipeline:
                 w = weights[names[i]]
                 _lib.call("llmc_sparsegpt_prune", ctx,
                           C.c_void_p(w.data_ptr() + a * w.stride(0) * w.element_size()), _lib.dtype_code(w.dtype),
-                          C.c_int64(m), C.c_int64(d), C.c_int64(w.stride(0)), _lib.ptr(self.u), C.c_int64(d),
+                          C.c_int64(m), C.c_int64(d), C.c_int64(w.stride(0)), _lib.ptr(u), C.c_int64(d),
                           C.byref(self.qc), C.c_void_p(wq.data_ptr() + q0 * d * 4), C.c_int64(d),
                           C.c_void_p(st["mask"].data_ptr() + (r0 + q0) * d))
                 q0 += m
@@ -227,7 +231,7 @@ class GptqPipeline:
         lp = (C.c_int64 * k)(*[w.stride(0) for w in ws])
         codes, scales, zps = st["codes"], st["scales"], st["zero_points"]
         _lib.call("llmc_gptq_quantize_batch", ctx, C.c_int32(k), wp, mp, lp, _lib.dtype_code(ws[0].dtype),
-                  C.c_int64(d), _lib.ptr(self.u), C.c_int64(d), C.byref(self.qc), _lib.ptr(wq), C.c_int64(d),
+                  C.c_int64(d), _lib.ptr(u), C.c_int64(d), C.byref(self.qc), _lib.ptr(wq), C.c_int64(d),
                   C.c_void_p(codes.data_ptr() + r0 * codes.stride(0) * codes.element_size()),
                   C.c_void_p(scales.data_ptr() + r0 * (scales.stride(0) if scales.dim() > 1 else 1) * 4),
                   C.c_void_p(zps.data_ptr() + r0 * (zps.stride(0) if zps.dim() > 1 else 1) * 4))
@@ -356,7 +360,9 @@ def _events():
 
 
 class _Overlap:
-    """Two library contexts, two streams and three Hessian handle sets for ``GptqPipeline.run``."""
+    """Library contexts and streams for ``GptqPipeline.run``: one for the Hessians, one that
+    orders each layer's solve (and the caller's copies around it), one per site for the site
+    solves that run side by side; and rotating Hessian handle sets."""
 
     def __init__(self, pipe: GptqPipeline, reserve_sms: int):
         self.pipe = pipe
@@ -381,6 +387,20 @@ class _Overlap:
         # The factorisation decides a non-PD Hessian on the device, so enqueueing a solve never
         # waits for the GPU; a failure surfaces at the llmc_sync that ends the job.
         _lib.call("llmc_set_deferred_errors", C.c_void_p(self.cs), C.c_int32(1))
+        # One stream, context and scratch set per site for ``run``: a layer's sites are
+        # independent given their Hessians, so their solves (chains of mostly small, dependent
+        # launches) run side by side on the reserved SMs instead of one after another.
+        self.site_streams, self.site_ctx, self.site_u, self.site_work = [], [], [], []
+        for site in pipe.sites:
+            st = torch.cuda.Stream(dev, priority=lo)
+            c = self._ctx(dev, st)
+            _lib.call("llmc_set_sm_limit", C.c_void_p(c), C.c_int32(self.solve_sms))
+            _lib.call("llmc_set_deferred_errors", C.c_void_p(c), C.c_int32(1))
+            self.site_streams.append(st)
+            self.site_ctx.append(c)
+            self.site_u.append(torch.empty(site.d * site.d, dtype=torch.float32, device=dev))
+            self.site_work.append(torch.empty(sum(m for _, m in site.weights) * site.d, dtype=torch.float32,
+                                              device=dev))
         self.h = []
         self._ensure_sets(2)
 
@@ -408,9 +428,17 @@ class _Overlap:
             for p in hs.values():
                 _lib.call("llmc_hessian_destroy", C.c_void_p(p))
         self.h = []
-        for c in (self.ch, self.cs):
+        for c in [self.ch, self.cs] + self.site_ctx:
             _lib.call("llmc_destroy", C.c_void_p(c))
         self.ch = self.cs = None
+        self.site_ctx, self.site_streams, self.site_u, self.site_work = [], [], [], []
+
+    def solve_contexts(self) -> list:
+        return [self.cs] + list(self.site_ctx)
+
+    def _set_solve_limit(self, sms: int):
+        for c in self.solve_contexts():
+            _lib.call("llmc_set_sm_limit", C.c_void_p(c), C.c_int32(sms))
 
     def _data(self, b: int, site: str) -> int:
         p = C.c_void_p()
@@ -443,8 +471,19 @@ class _Overlap:
                 self.ss.wait_event(acc_done)
                 if before_solve is not None:
                     before_solve(l)
-                for s in pipe.sites:
-                    pipe.solve_site(s, self._data(b, s.name), weights[l], outputs[l], ctx=C.c_void_p(self.cs))
+                start = torch.cuda.Event()
+                start.record(self.ss)
+            # each site on its own stream, all joined back into the solve stream
+            for j, s in enumerate(pipe.sites):
+                st = self.site_streams[j]
+                st.wait_event(start)
+                with torch.cuda.stream(st):
+                    pipe.solve_site(s, self._data(b, s.name), weights[l], outputs[l], ctx=C.c_void_p(self.site_ctx[j]),
+                                    u=self.site_u[j], work=self.site_work[j])
+                    fin = torch.cuda.Event()
+                    fin.record(st)
+                self.ss.wait_event(fin)
+            with torch.cuda.stream(self.ss):
                 if after_solve is not None:
                     after_solve(l)
                 done = torch.cuda.Event()
@@ -506,11 +545,11 @@ class _Overlap:
         if pending is not None:
             # The last layer's solve waits for the last accumulation, so nothing else runs beside
             # it: lift the solve context's SM limit (persistent grids over the whole GPU) for it.
-            _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(0))
+            self._set_solve_limit(0)
             try:
                 solve(pending)
             finally:
-                _lib.call("llmc_set_sm_limit", C.c_void_p(self.cs), C.c_int32(self.solve_sms))
+                self._set_solve_limit(self.solve_sms)
         cur.wait_stream(self.sh)
         cur.wait_stream(self.ss)
         if sync:
@@ -519,7 +558,7 @@ class _Overlap:
     def check(self):
         """Waits for the solve stream and raises the first deferred device error (a Hessian
         that was not positive definite, a bounded wait that gave up) of either context."""
-        for c in (self.cs, self.ch):
+        for c in self.solve_contexts() + [self.ch]:
             _lib.call("llmc_sync", C.c_void_p(c))
 
     # ---- one process per GPU ------------------------------------------------------------------
