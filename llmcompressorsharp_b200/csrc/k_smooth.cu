@@ -246,6 +246,117 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
     }
 }
 
+// The one-pass search with several rows a warp (2-byte weights; group width a multiple of PER
+// and a divisor of n): a (row, group) segment takes L = gs / PER lanes holding PER consecutive
+// columns each, so a warp covers 32 / L rows at once and one instruction stream serves all of
+// them.  Per grid point and lane that shares the min / max shuffles (log2 L rounds), the affine
+// parameters and the reciprocal among PER elements instead of gs / 32, and reads s_k and 1 / s_k
+// as 16-byte vectors.  Rows past m are all zeros (error 0).  The arithmetic per element is
+// awq_seg_err's.
+template <typename T, int PER>
+__global__ void __launch_bounds__(NT) awq_err_rows_kernel(const T* W, int64_t m, int64_t n, int64_t ldw, int gs,
+                                                          const float* sk, const float* rsk, int grid_pts, int bits,
+                                                          int sym, double* sums) {
+    extern __shared__ __align__(16) unsigned char awq_smem[];
+    double* accs = reinterpret_cast<double*>(awq_smem);           // [warps][grid_pts][32]
+    float* ss = reinterpret_cast<float*>(accs + (size_t)AWQ_WARPS * grid_pts * 32);  // [grid_pts][gs]
+    float* rs = ss + (size_t)grid_pts * gs;                        // [grid_pts][gs]
+    const int64_t c0 = (int64_t)blockIdx.x * gs;
+    for (int t = threadIdx.x; t < grid_pts * gs; t += NT) {
+        const int k = t / gs, i = t % gs;
+        ss[t] = sk[(int64_t)k * n + c0 + i];
+        rs[t] = rsk[(int64_t)k * n + c0 + i];
+    }
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int L = gs / PER;        // lanes a segment (power of two)
+    const int rpw = 32 / L;        // rows a warp
+    const int sub = lane % L, rsub = lane / L;
+    double* acc = accs + (size_t)warp * grid_pts * 32 + lane;
+    for (int k = 0; k < grid_pts; k++) acc[k * 32] = 0.0;
+    __syncthreads();
+    float qmin, qmax;
+    qrange(bits, sym, &qmin, &qmax);
+    const int64_t stride = (int64_t)gridDim.y * AWQ_WARPS * rpw;
+    for (int64_t rb = ((int64_t)blockIdx.y * AWQ_WARPS + warp) * rpw; rb < m; rb += stride) {
+        const int64_t r = rb + rsub;
+        float w[PER];
+        if (r < m) {
+            const uint4* src = reinterpret_cast<const uint4*>(W + r * ldw + c0 + (int64_t)sub * PER);
+#pragma unroll
+            for (int q = 0; q < PER / 8; q++) {
+                const uint4 u = src[q];
+                const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+                for (int i = 0; i < 8; i++) w[q * 8 + i] = to_f<T>(h[i]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < PER; i++) w[i] = 0.f;
+        }
+#pragma unroll 1
+        for (int k = 0; k < grid_pts; k++) {
+            const float4* sv = reinterpret_cast<const float4*>(ss + k * gs + sub * PER);
+            const float4* rv = reinterpret_cast<const float4*>(rs + k * gs + sub * PER);
+            float v[PER];
+            float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < PER / 4; q++) {
+                const float4 s4 = sv[q];
+                v[4 * q + 0] = __fmul_rn(w[4 * q + 0], s4.x);
+                v[4 * q + 1] = __fmul_rn(w[4 * q + 1], s4.y);
+                v[4 * q + 2] = __fmul_rn(w[4 * q + 2], s4.z);
+                v[4 * q + 3] = __fmul_rn(w[4 * q + 3], s4.w);
+            }
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                mn = fmin_nan(mn, v[i]);
+                mx = fmax_nan(mx, v[i]);
+            }
+            for (int o = L / 2; o > 0; o >>= 1) {
+                mn = fmin_nan(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+                mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            }
+            float sc;
+            int z;
+            affine_params(mn, mx, bits, sym, &sc, &z);
+            const float zf = (float)z;
+            const float rsc = __frcp_rn(sc);
+            const bool rs_ok = fabsf(rsc) <= 3.0e38f && rsc != 0.f;
+            float part = 0.f;
+#pragma unroll
+            for (int q = 0; q < PER / 4; q++) {
+                const float4 r4 = rv[q];
+                const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int e_i = 4 * q + i;
+                    float fq;
+                    const float f = __fmul_rn(v[e_i], rsc);
+                    const float fr = rintf(f);
+                    if (!rs_ok || fabsf(fabsf(__fsub_rn(f, fr)) - 0.5f) <= fabsf(f) * 4.8e-7f + 1e-30f) {
+                        int code;
+                        fq = fq_chain<float>(v[e_i], sc, zf, qmin, qmax, &code);
+                    } else {
+                        float t = __fadd_rn(fr, zf);
+                        t = (t < qmin) ? qmin : ((t > qmax) ? qmax : t);
+                        fq = __fmul_rn(__fsub_rn(t, zf), sc);
+                    }
+                    const float e = __fsub_rn(__fmul_rn(fq, rr[i]), w[e_i]);
+                    part = __fmaf_rn(e, e, part);
+                }
+            }
+            acc[k * 32] += (double)part;
+        }
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < grid_pts; k += NT) {
+        double t = 0.0;
+        for (int wq = 0; wq < AWQ_WARPS; wq++)
+            for (int l = 0; l < 32; l++) t += accs[((size_t)wq * grid_pts + k) * 32 + l];
+        atomicAdd(sums + k, t);
+    }
+}
+
 __global__ void awq_pick_kernel(const double* sums, int grid_pts, double denom, const float* sk, int64_t n, double* mse_out,
                                 float* best_s, int* best_k) {
     __shared__ int kbest;
@@ -365,6 +476,50 @@ llmc_status awq_search(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64
         recip_kernel<<<grid_for(ctx, (int64_t)grid_pts * n), NT, 0, ctx->stream>>>(sk, (int64_t)grid_pts * n, rsk);
         LLMC_TRY(check_launch(ctx, "recip"));
         const int64_t ngroups = (n + gs - 1) / gs;
+        // Several rows a warp: 2-byte weights in 16-byte rows, whole groups of 16 (or 8) * 2^j
+        // columns.
+        auto pow2 = [](int64_t v) { return v >= 1 && (v & (v - 1)) == 0; };
+        int rper = 0;
+        if ((dtype == LLMC_DTYPE_BF16 || dtype == LLMC_DTYPE_F16) && n % gs == 0 && (uintptr_t)W % 16 == 0 &&
+            ldw % 8 == 0) {
+            if (gs % 16 == 0 && pow2(gs / 16) && gs / 16 <= 32) rper = 16;
+            else if (gs % 8 == 0 && pow2(gs / 8) && gs / 8 <= 32) rper = 8;
+        }
+        if (rper) {
+            static bool rattr[64][2][2];
+            const int di = dtype == LLMC_DTYPE_BF16 ? 0 : 1, qi = rper == 16 ? 0 : 1;
+            const int64_t rows_per_block = (int64_t)AWQ_WARPS * (32 / (gs / rper));
+            const int64_t rmax = (m + rows_per_block - 1) / rows_per_block;
+#define LLMC_AWQR(T, PER)                                                                                         \
+    do {                                                                                                          \
+        auto kern = awq_err_rows_kernel<T, PER>;                                                                  \
+        if (!rattr[ctx->device][di][qi]) {                                                                        \
+            LLMC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));    \
+            rattr[ctx->device][di][qi] = true;                                                                    \
+        }                                                                                                         \
+        int per_sm = 0;                                                                                           \
+        LLMC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem));                    \
+        const int64_t slots = (int64_t)ctx->sm_count * (per_sm > 0 ? per_sm : 1);                                \
+        int64_t ry = slots / ngroups;                                                                             \
+        if (ry > rmax) ry = rmax;                                                                                 \
+        if (ry < 1) ry = 1;                                                                                       \
+        if (ry > 65535) ry = 65535;                                                                               \
+        kern<<<dim3((unsigned)ngroups, (unsigned)ry), NT, smem, ctx->stream>>>((const T*)W, m, n, ldw, (int)gs, sk, \
+                                                                              rsk, grid_pts, cfg->num_bits,       \
+                                                                              cfg->symmetric, sums);              \
+    } while (0)
+            if (dtype == LLMC_DTYPE_BF16) {
+                if (rper == 16) LLMC_AWQR(__nv_bfloat16, 16);
+                else LLMC_AWQR(__nv_bfloat16, 8);
+            } else {
+                if (rper == 16) LLMC_AWQR(__half, 16);
+                else LLMC_AWQR(__half, 8);
+            }
+#undef LLMC_AWQR
+            LLMC_TRY(check_launch(ctx, "awq_err_rows"));
+            goto picked;
+        }
+        {
         const int64_t ry_max = (m + AWQ_WARPS - 1) / AWQ_WARPS;
         static bool attr[64][3][2];
         const int ti = dtype == LLMC_DTYPE_F32 ? 0 : (dtype == LLMC_DTYPE_BF16 ? 1 : 2);
@@ -397,6 +552,7 @@ llmc_status awq_search(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64
         }
 #undef LLMC_AWQ1
         LLMC_TRY(check_launch(ctx, "awq_err_group"));
+        }
     } else {
         for (int k = 0; k < grid_pts; k++) {
             const float* s = sk + (int64_t)k * n;
@@ -418,6 +574,7 @@ llmc_status awq_search(llmc_ctx* ctx, const void* W, int dtype, int64_t m, int64
             LLMC_TRY(check_launch(ctx, "awq_err"));
         }
     }
+picked:
     awq_pick_kernel<<<1, NT, 0, ctx->stream>>>(sums, grid_pts, (double)m * (double)n, sk, n, mse_out, best_s, kdev);
     LLMC_TRY(check_launch(ctx, "awq_pick"));
     if (!best_k) return LLMC_OK;  // best_s and mse_out are written in stream order

@@ -1050,14 +1050,17 @@ def test_pipeline_sparsegpt_matches_oracle():
                 assert rel_fro(got["wq"], rout) < 1e-3
 
 
-@pytest.mark.parametrize("strategy,gs,m", [("group", 128, 128), ("group", 256, 300), ("group", 64, 40),
-                                           ("channel", 0, 96)])
-def test_awq_search_matches_oracle(strategy, gs, m):
-    """The one-pass group kernel (4 columns a lane for groups of up to 128, 8 up to 256; row
-    counts that leave warps idle) and the per-point kernel (channel scales)."""
+@pytest.mark.parametrize("strategy,gs,m,dtype", [("group", 128, 128, torch.bfloat16), ("group", 256, 300, torch.bfloat16),
+                                                 ("group", 64, 40, torch.bfloat16), ("group", 128, 70, torch.float16),
+                                                 ("group", 128, 96, torch.float32), ("group", 256, 33, torch.float32),
+                                                 ("channel", 0, 96, torch.bfloat16)])
+def test_awq_search_matches_oracle(strategy, gs, m, dtype):
+    """The one-pass kernels: several rows a warp for 2-byte weights (row counts that leave rows
+    of a warp empty), one row a warp with 4 or 8 columns a lane otherwise (fp32); and the
+    per-point kernel (channel scales)."""
     from llmcompressorsharp_b200 import RtnConfig, awq_search
 
-    w = (torch.randn(m, 512, generator=gen(8)) * 0.02).to(torch.bfloat16)
+    w = (torch.randn(m, 512, generator=gen(8)) * 0.02).to(dtype)
     a = (torch.rand(512, generator=gen(9)) * 3 + 0.1) * torch.where(torch.rand(512, generator=gen(10)) < 0.02, 30.0, 1.0)
     cfg = RtnConfig(4, False, strategy, group_size=gs)
     s, k, mse = awq_search(w.to(DEV), a.to(DEV), 20, cfg)
