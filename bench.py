@@ -69,7 +69,7 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--reserve-sms", type=int, default=32,
+    p.add_argument("--reserve-sms", type=int, default=28,
                    help="1 GPU: SMs kept free of the Hessian kernel for the overlapped solve (0 = no overlap)")
     return p.parse_args()
 

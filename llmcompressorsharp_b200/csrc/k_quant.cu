@@ -535,17 +535,29 @@ __global__ void __launch_bounds__(NT) rtn_bf16_kernel(const __nv_bfloat16* x, Se
 #define NIB_RV_MAX 4
 #endif
 
-// The op-by-op chain for all eight columns of a vector, packed as nib_vector packs them: one
-// out-of-line copy, so the unrolled element loops that call it stay small.
-__device__ __noinline__ uint32_t nib_chain8(uint4 w, float s, float zf, int z, float qmin, float qmax) {
+// A vector holding an element near a bf16 rounding midpoint (or a segment off the fast path):
+// those elements take the op-by-op chain, the others nib_vector's arithmetic with the clamp;
+// packed as nib_vector packs.  One out-of-line copy, so the unrolled element loops that call it
+// stay small.
+__device__ __noinline__ uint32_t nib_chain8(uint4 w, float rcp, bool fast, float s, float zf, int z, float qmin,
+                                            float qmax) {
+    constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
+    const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
     uint32_t u[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
-        int code;
-        fq_chain<__nv_bfloat16>(xv, s, zf, qmin, qmax, &code);
-        u[i] = (uint32_t)((code - z) & 0xF);
+        const float f = __fmul_rn(xv, rcp);
+        if (!fast || (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u) {
+            int code;
+            fq_chain<__nv_bfloat16>(xv, s, zf, qmin, qmax, &code);
+            u[i] = (uint32_t)((code - z) & 0xF);
+        } else {
+            const float c = __fmul_rn(f, 65537.f);
+            const float b16 = __fsub_rn(c, __fsub_rn(c, f));
+            u[i] = __float_as_uint(fminf(fmaxf(__fadd_rn(b16, MAGIC), cmin), cmax));
+        }
     }
     const uint32_t ev = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);
     const uint32_t od = __byte_perm(__byte_perm(u[1], u[3], 0x0040), __byte_perm(u[5], u[7], 0x0040), 0x5410);
@@ -579,7 +591,7 @@ __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin
         u[2 * k + 1] = __float_as_uint(rf.y);
     }
     if (!fast || near <= 0x80000u) {
-        *reinterpret_cast<uint32_t*>(dst) = nib_chain8(w, s, zf, z, qmin, qmax);
+        *reinterpret_cast<uint32_t*>(dst) = nib_chain8(w, rcp, fast, s, zf, z, qmin, qmax);
         return;
     }
     // byte b of the output holds columns 2b (high nibble) and 2b + 1 (low nibble)
@@ -652,8 +664,22 @@ __global__ void __launch_bounds__(NT, NRV <= 4 ? 4 : (NRV <= 8 ? 3 : 2))
         const float hi = fmaxf(smax, 0.f) * rcp * k + zf;  // NaN / Inf fail the tests below
         const float lo = fminf(smin, 0.f) * rcp * k + zf;
         const bool fast = hi <= 256.f && lo >= -256.f;
-        // The clamp can act only if some quotient of the segment rounds beyond the grid.
-        const bool clamp = !(hi <= qmax + 0.25f && lo >= qmin - 0.25f);
+        // The clamp can act only if some element's rounded quotient lies beyond the grid.  On
+        // the fast path x -> rint(bf16(x * rcp)) is monotone (rounded products with rcp > 0,
+        // round to nearest, rint), so the segment's extremes bound every element's code; an
+        // extreme near a bf16 rounding midpoint (where the split's tie-breaking may differ)
+        // counts as reaching the grid's end.  Elements near a midpoint take the exact chain,
+        // which clamps by itself.
+        bool clamp = true;
+        if (fast) {
+            const float fx = __fmul_rn(smax, rcp), fn = __fmul_rn(smin, rcp);
+            const bool mid = (__float_as_uint(fx) * 65536u - 0x7FFC0000u) <= 0x80000u ||
+                             (__float_as_uint(fn) * 65536u - 0x7FFC0000u) <= 0x80000u;
+            const float cx = __fmul_rn(fx, 65537.f), cn = __fmul_rn(fn, 65537.f);
+            const float qx = __fsub_rn(__fadd_rn(__fsub_rn(cx, __fsub_rn(cx, fx)), MAGIC), MAGIC);
+            const float qn = __fsub_rn(__fadd_rn(__fsub_rn(cn, __fsub_rn(cn, fn)), MAGIC), MAGIC);
+            clamp = mid || __fadd_rn(qx, zf) > qmax || __fadd_rn(qn, zf) < qmin;
+        }
         const bool warp_clamp = __any_sync(0xffffffffu, active && clamp);
         const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
         if (!active) continue;

@@ -302,10 +302,12 @@ __global__ void __launch_bounds__(NT) awq_err_rows_kernel(const T* W, int64_t m,
 #pragma unroll
             for (int q = 0; q < PER / 4; q++) {
                 const float4 s4 = sv[q];
-                v[4 * q + 0] = __fmul_rn(w[4 * q + 0], s4.x);
-                v[4 * q + 1] = __fmul_rn(w[4 * q + 1], s4.y);
-                v[4 * q + 2] = __fmul_rn(w[4 * q + 2], s4.z);
-                v[4 * q + 3] = __fmul_rn(w[4 * q + 3], s4.w);
+                const float2 a = __fmul2_rn(make_float2(w[4 * q + 0], w[4 * q + 1]), make_float2(s4.x, s4.y));
+                const float2 c = __fmul2_rn(make_float2(w[4 * q + 2], w[4 * q + 3]), make_float2(s4.z, s4.w));
+                v[4 * q + 0] = a.x;
+                v[4 * q + 1] = a.y;
+                v[4 * q + 2] = c.x;
+                v[4 * q + 3] = c.y;
             }
 #pragma unroll
             for (int i = 0; i < PER; i++) {
@@ -322,29 +324,41 @@ __global__ void __launch_bounds__(NT) awq_err_rows_kernel(const T* W, int64_t m,
             const float zf = (float)z;
             const float rsc = __frcp_rn(sc);
             const bool rs_ok = fabsf(rsc) <= 3.0e38f && rsc != 0.f;
-            float part = 0.f;
+            // Pairs of columns on the paired fp32 instructions (each component rounded as its
+            // scalar form); rint(f) as (f + 1.5 * 2^23) - 1.5 * 2^23, exact for |f| < 2^22 (larger
+            // |f|, and quotients near a half-integer, take the chain).
+            const float2 rsc2 = make_float2(rsc, rsc), sc2 = make_float2(sc, sc);
+            const float2 zf2 = make_float2(zf, zf), nzf2 = make_float2(-zf, -zf);
+            const float2 mg2 = make_float2(12582912.f, 12582912.f), nmg2 = make_float2(-12582912.f, -12582912.f);
+            const float2 neg1 = make_float2(-1.f, -1.f);
+            float2 part2 = make_float2(0.f, 0.f);
 #pragma unroll
             for (int q = 0; q < PER / 4; q++) {
                 const float4 r4 = rv[q];
-                const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int e_i = 4 * q + i;
-                    float fq;
-                    const float f = __fmul_rn(v[e_i], rsc);
-                    const float fr = rintf(f);
-                    if (!rs_ok || fabsf(fabsf(__fsub_rn(f, fr)) - 0.5f) <= fabsf(f) * 4.8e-7f + 1e-30f) {
+                for (int h = 0; h < 2; h++) {
+                    const int e0 = 4 * q + 2 * h;
+                    const float2 f = __fmul2_rn(make_float2(v[e0], v[e0 + 1]), rsc2);
+                    const float2 fr = __fadd2_rn(__fadd2_rn(f, mg2), nmg2);
+                    const float2 d = __ffma2_rn(fr, neg1, f);  // f - fr
+                    float2 t = __fadd2_rn(fr, zf2);
+                    t.x = fminf(fmaxf(t.x, qmin), qmax);
+                    t.y = fminf(fmaxf(t.y, qmin), qmax);
+                    float2 fq = __fmul2_rn(__fadd2_rn(t, nzf2), sc2);
+                    if (!rs_ok || !(fabsf(f.x) < 4194304.f) || fabsf(fabsf(d.x) - 0.5f) <= fabsf(f.x) * 4.8e-7f + 1e-30f) {
                         int code;
-                        fq = fq_chain<float>(v[e_i], sc, zf, qmin, qmax, &code);
-                    } else {
-                        float t = __fadd_rn(fr, zf);
-                        t = (t < qmin) ? qmin : ((t > qmax) ? qmax : t);
-                        fq = __fmul_rn(__fsub_rn(t, zf), sc);
+                        fq.x = fq_chain<float>(v[e0], sc, zf, qmin, qmax, &code);
                     }
-                    const float e = __fsub_rn(__fmul_rn(fq, rr[i]), w[e_i]);
-                    part = __fmaf_rn(e, e, part);
+                    if (!rs_ok || !(fabsf(f.y) < 4194304.f) || fabsf(fabsf(d.y) - 0.5f) <= fabsf(f.y) * 4.8e-7f + 1e-30f) {
+                        int code;
+                        fq.y = fq_chain<float>(v[e0 + 1], sc, zf, qmin, qmax, &code);
+                    }
+                    const float2 pr = __fmul2_rn(fq, h ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y));
+                    const float2 e = __ffma2_rn(make_float2(w[e0], w[e0 + 1]), neg1, pr);  // fq / s_k - w
+                    part2 = __ffma2_rn(e, e, part2);
                 }
             }
+            const float part = __fadd_rn(part2.x, part2.y);
             acc[k * 32] += (double)part;
         }
     }

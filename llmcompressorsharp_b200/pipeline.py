@@ -84,7 +84,7 @@ class GptqPipeline:
                                 device=device)
         self.overlap = None
 
-    def enable_overlap(self, reserve_sms: int = 32):
+    def enable_overlap(self, reserve_sms: int = 28):
         """Switch ``run`` to the two-stream schedule described in the module docstring;
         ``reserve_sms`` SMs are kept free of the persistent Hessian kernel for the solve."""
         if self.overlap is None:
