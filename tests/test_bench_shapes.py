@@ -108,3 +108,34 @@ def test_gate_up_stack_at_m28672():
             gptq_bars(w_cpu[name], out["wq"], out["scales"], out["zero_points"], wq_r, s_r, z_r, h_ref)
     finally:
         pipe.close()
+
+
+def test_factor_at_d28672_against_fp64():
+    """Llama-3-70B's widest site (down_proj input, d = 28,672): the Hessian of 32,768 bf16 rows
+    (fewer rows than columns, so H' is only as well conditioned as the damping makes it) and
+    U = chol(H'^-1)^T from llmc_chol_inverse(want_upper = 1), against the same chain of
+    HessianInverseSolver.cs:44-92 / GptqBlockQuantizer.cs:105-118 in fp64 on the device
+    (torch.linalg, used here only as the checker: the CPU oracle's fp32 chain takes too long at
+    this width).  H' is the oracle's damping of the device's H.  Bar: U within 1e-4 relative
+    Frobenius on a sample of 256 rows, and nothing below the diagonal."""
+    from llmcompressorsharp_b200 import HessianAccumulator, HessianInverseSolver
+
+    d = 28672
+    x = activations(32768, d, 28672)
+    acc = HessianAccumulator(d, DEV)
+    acc.update(x)
+    del x
+    u_dev = HessianInverseSolver.upper(acc.raw(), 0.01, upper_only=True)
+    h = acc.get_hessian()
+    acc.dispose()
+    hd = o_hess.damped(h, 0.01).double()
+    del h
+    low = torch.linalg.cholesky(hd)
+    del hd
+    hinv = torch.cholesky_inverse(low)
+    del low
+    u_ref = torch.linalg.cholesky(hinv, upper=True)
+    del hinv
+    rows = torch.randperm(d, generator=torch.Generator().manual_seed(3))[:256].to(DEV)
+    assert rel_fro(u_dev[rows], u_ref[rows]) < 1e-4
+    assert torch.count_nonzero(torch.tril(u_dev, -1)) == 0
