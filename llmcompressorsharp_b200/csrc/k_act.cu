@@ -161,26 +161,61 @@ __global__ void __launch_bounds__(32 * WARPS) act_token_kernel(const T* x, int64
 //     pattern plus zp.
 constexpr int REG_NV = 16;
 
-// The op-by-op chain for all eight codes of a vector, packed: one out-of-line copy, so the
-// unrolled element loops that call it stay small enough for the instruction cache.
-__device__ __noinline__ uint2 token_chain8(uint4 w, float s, float rcp, float zf, int z, float qmin, float qmax,
+// A vector holding an element near a bf16 rounding midpoint (or a row off the fast path): those
+// elements take the op-by-op chain, the others token_codes8's arithmetic with the clamp; packed
+// as token_codes8 packs.  One out-of-line copy, called from the batched rewrite below.
+__device__ __noinline__ uint2 token_chain8(uint4 w, float s, float rcp, bool fast, int z, float qmin, float qmax,
                                            int iqmin, int iqmax) {
+    constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
+    const float zf = (float)z;
+    const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
     uint32_t u[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const float xv = (i & 1) ? __uint_as_float(ww[i / 2] & 0xFFFF0000u) : __uint_as_float(ww[i / 2] << 16);
-        int code;
-        quant_elem<__nv_bfloat16>(xv, s, rcp, zf, z, qmin, qmax, iqmin, iqmax, false, &code);
-        u[i] = (uint32_t)code;
+        const float f = __fmul_rn(xv, rcp);
+        if (!fast || (__float_as_uint(f) * 65536u - 0x7FFC0000u) <= 0x80000u) {
+            int code;
+            quant_elem<__nv_bfloat16>(xv, s, rcp, zf, z, qmin, qmax, iqmin, iqmax, false, &code);
+            u[i] = (uint32_t)code;
+        } else {
+            const float c = __fmul_rn(f, 65537.f);
+            const float b16 = __fsub_rn(c, __fsub_rn(c, f));
+            u[i] = __float_as_uint(fminf(fmaxf(__fadd_rn(b16, MAGIC), cmin), cmax)) + (uint32_t)z;
+        }
     }
     return make_uint2(__byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410),
                       __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410));
 }
 
+// Vectors that need the chain are queued per warp in shared memory and rewritten in batches,
+// one vector a lane: a branch to the chain costs the whole warp the chain's time whenever any
+// lane takes it, and a 4,096-column row holds 512 vectors, of which a few percent hold an
+// element near a midpoint.
+constexpr int TOK_QCAP = 32;
+struct TokQueue {
+    uint4 w[TOK_QCAP];
+    float s[TOK_QCAP], rcp[TOK_QCAP];
+    int z[TOK_QCAP];
+    int64_t off[TOK_QCAP];  // byte offset of the vector's codes; bit 62 set: the row is off the fast path
+};
+
+__device__ __forceinline__ void token_flush(TokQueue& q, int count, float qmin, float qmax, int iqmin, int iqmax,
+                                            uint8_t* codes) {
+    __syncwarp();  // the fast-path stores of these vectors came from other lanes of this warp
+    const int lane = threadIdx.x & 31;
+    if (lane < count) {
+        const int64_t o = q.off[lane];
+        const bool fast = (o & (int64_t(1) << 62)) == 0;
+        *reinterpret_cast<uint2*>(codes + (o & ~(int64_t(1) << 62))) =
+            token_chain8(q.w[lane], q.s[lane], q.rcp[lane], fast, q.z[lane], qmin, qmax, iqmin, iqmax);
+    }
+    __syncwarp();
+}
+
 template <bool CLAMP>
-__device__ __forceinline__ uint2 token_codes8(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
-                                              float zf, int z, float qmin, float qmax, int iqmin, int iqmax) {
+__device__ __forceinline__ uint2 token_codes8(const uint4& w, float rcp, float cmin, float cmax, int z, bool* near_mid) {
     constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
     const float2 rcp2 = make_float2(rcp, rcp), k2 = make_float2(65537.f, 65537.f);
     const float2 neg1 = make_float2(-1.f, -1.f), magic2 = make_float2(MAGIC, MAGIC);
@@ -203,7 +238,7 @@ __device__ __forceinline__ uint2 token_codes8(const uint4& w, float rcp, float c
         u[2 * k] = __float_as_uint(rf.x) + (uint32_t)z;
         u[2 * k + 1] = __float_as_uint(rf.y) + (uint32_t)z;
     }
-    if (!fast || near <= 0x80000u) return token_chain8(w, s, rcp, zf, z, qmin, qmax, iqmin, iqmax);
+    *near_mid = near <= 0x80000u;
     return make_uint2(__byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410),
                       __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410));
 }
@@ -219,6 +254,9 @@ __global__ void __launch_bounds__(32 * WARPS) act_token_bf16_reg_kernel(const __
     qrange(bits, sym, &qmin, &qmax);
     const int iqmin = (int)qmin, iqmax = (int)qmax;
     const __nv_bfloat162 pinf = __float2bfloat162_rn(INFINITY), ninf = __float2bfloat162_rn(-INFINITY);
+    __shared__ TokQueue queues[WARPS];
+    TokQueue& q = queues[threadIdx.x / 32];
+    int qn = 0;  // queued vectors of this warp (the same in every lane)
     for (int64_t r = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32; r < rows; r += (int64_t)gridDim.x * WARPS) {
         const __nv_bfloat16* row = x + r * ld;
         uint4 w[REG_NV];
@@ -262,21 +300,36 @@ __global__ void __launch_bounds__(32 * WARPS) act_token_bf16_reg_kernel(const __
         // parameters are the same in every lane, so the branch is uniform).
         const bool clamp = !(hi <= qmax + 0.25f && lo >= qmin - 0.25f);
         const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
-        uint8_t* crow = codes + r * ldc;
-        if (clamp) {
+        const int64_t crow = r * ldc;
 #pragma unroll
-            for (int j = 0; j < REG_NV; j++)
-                if (j < nv)
-                    *reinterpret_cast<uint2*>(crow + (int64_t)(j * 32 + lane) * 8) =
-                        token_codes8<true>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, iqmin, iqmax);
-        } else {
-#pragma unroll
-            for (int j = 0; j < REG_NV; j++)
-                if (j < nv)
-                    *reinterpret_cast<uint2*>(crow + (int64_t)(j * 32 + lane) * 8) =
-                        token_codes8<false>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, iqmin, iqmax);
+        for (int j = 0; j < REG_NV; j++) {
+            if (j < nv) {  // nv is the same in every lane
+                const int64_t off = crow + (int64_t)(j * 32 + lane) * 8;
+                bool near_mid;
+                *reinterpret_cast<uint2*>(codes + off) = clamp ? token_codes8<true>(w[j], rcp, cmin, cmax, z, &near_mid)
+                                                               : token_codes8<false>(w[j], rcp, cmin, cmax, z, &near_mid);
+                const bool slow = !fast || near_mid;
+                const unsigned mask = __ballot_sync(0xffffffffu, slow);
+                if (mask) {
+                    const int n = __popc(mask);
+                    if (qn + n > TOK_QCAP) {
+                        token_flush(q, qn, qmin, qmax, iqmin, iqmax, codes);
+                        qn = 0;
+                    }
+                    if (slow) {
+                        const int pos = qn + __popc(mask & ((1u << lane) - 1u));
+                        q.w[pos] = w[j];
+                        q.s[pos] = s;
+                        q.rcp[pos] = rcp;
+                        q.z[pos] = z;
+                        q.off[pos] = off | (fast ? int64_t(0) : (int64_t(1) << 62));
+                    }
+                    qn += n;
+                }
+            }
         }
     }
+    if (qn) token_flush(q, qn, qmin, qmax, iqmin, iqmax, codes);
 }
 
 template <typename T>

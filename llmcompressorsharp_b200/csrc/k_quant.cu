@@ -565,8 +565,7 @@ __device__ __noinline__ uint32_t nib_chain8(uint4 w, float rcp, bool fast, float
 }
 
 template <bool CLAMP>
-__device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin, float cmax, bool fast, float s,
-                                           float zf, int z, float qmin, float qmax, uint8_t* dst) {
+__device__ __forceinline__ bool nib_vector(const uint4& w, float rcp, float cmin, float cmax, bool fast, uint8_t* dst) {
     constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
     const float2 rcp2 = make_float2(rcp, rcp), k2 = make_float2(65537.f, 65537.f);
     const float2 neg1 = make_float2(-1.f, -1.f), magic2 = make_float2(MAGIC, MAGIC);
@@ -590,14 +589,39 @@ __device__ __forceinline__ void nib_vector(const uint4& w, float rcp, float cmin
         u[2 * k] = __float_as_uint(rf.x);
         u[2 * k + 1] = __float_as_uint(rf.y);
     }
-    if (!fast || near <= 0x80000u) {
-        *reinterpret_cast<uint32_t*>(dst) = nib_chain8(w, rcp, fast, s, zf, z, qmin, qmax);
-        return;
-    }
     // byte b of the output holds columns 2b (high nibble) and 2b + 1 (low nibble)
     const uint32_t ev = __byte_perm(__byte_perm(u[0], u[2], 0x0040), __byte_perm(u[4], u[6], 0x0040), 0x5410);
     const uint32_t od = __byte_perm(__byte_perm(u[1], u[3], 0x0040), __byte_perm(u[5], u[7], 0x0040), 0x5410);
     *reinterpret_cast<uint32_t*>(dst) = ((ev << 4) & 0xF0F0F0F0u) | (od & 0x0F0F0F0Fu);
+    // a vector near a midpoint (or off the fast path) is rewritten later by nib_chain8
+    return !fast || near <= 0x80000u;
+}
+
+// Vectors that need the exact chain are queued per warp in shared memory and rewritten in
+// batches, one vector a lane: in SIMT a branch to the chain costs the whole warp the chain's
+// time whenever any lane takes it, and on 4-bit weights about 1 % of 8-column vectors (so most
+// warp iterations of 128 vectors) hold an element near a bf16 rounding midpoint.
+constexpr int NIB_QCAP = 32;  // queued vectors a warp
+struct NibQueue {
+    uint4 w[NIB_QCAP];
+    float s[NIB_QCAP], rcp[NIB_QCAP];
+    int z[NIB_QCAP];
+    int64_t off[NIB_QCAP];  // byte offset of the vector's codes; bit 62 set: the segment is off the fast path
+};
+
+// Rewrites the queue's count vectors (lane i takes entry i) and empties it.  The fast-path
+// stores of those vectors came from other lanes of this warp: __syncwarp orders them first.
+__device__ __forceinline__ void nib_flush(NibQueue& q, int count, float qmin, float qmax, uint8_t* codes) {
+    __syncwarp();
+    const int lane = lane_id();
+    if (lane < count) {
+        const int64_t o = q.off[lane];
+        const bool fast = (o & (int64_t(1) << 62)) == 0;
+        const int z = q.z[lane];
+        *reinterpret_cast<uint32_t*>(codes + (o & ~(int64_t(1) << 62))) =
+            nib_chain8(q.w[lane], q.rcp[lane], fast, q.s[lane], (float)z, z, qmin, qmax);
+    }
+    __syncwarp();
 }
 
 template <int NRV>
@@ -616,6 +640,9 @@ __global__ void __launch_bounds__(NT, NRV <= 4 ? 4 : (NRV <= 8 ? 3 : 2))
     const int64_t crow = code_row_bytes(bits, g.cols);
     const __nv_bfloat162 pinf = __float2bfloat162_rn(INFINITY), ninf = __float2bfloat162_rn(-INFINITY);
     constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
+    __shared__ NibQueue queues[NT / 32];
+    NibQueue& q = queues[threadIdx.x / 32];
+    int qn = 0;  // queued vectors of this warp (the same in every lane)
     for (uint32_t base = blockIdx.x * gpb; base < total; base += gridDim.x * gpb) {
         const uint32_t seg = base + lg;
         const bool active = seg < total;
@@ -682,22 +709,36 @@ __global__ void __launch_bounds__(NT, NRV <= 4 ? 4 : (NRV <= 8 ? 3 : 2))
         }
         const bool warp_clamp = __any_sync(0xffffffffu, active && clamp);
         const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
-        if (!active) continue;
-        uint8_t* crow_p = codes + (int64_t)r * crow;
-        if (warp_clamp) {
+        const int64_t crow_off = (int64_t)r * crow;
+        // every lane reaches the ballots (inactive lanes store nothing and queue nothing)
 #pragma unroll
-            for (int j = 0; j < NRV; j++) {
-                const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
-                nib_vector<true>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, crow_p + c / 2);
+        for (int j = 0; j < NRV; j++) {
+            const int64_t off = crow_off + (c0 + (int64_t)(j * L + sub) * VEC) / 2;
+            bool slow = false;
+            if (active) {
+                slow = warp_clamp ? nib_vector<true>(w[j], rcp, cmin, cmax, fast, codes + off)
+                                  : nib_vector<false>(w[j], rcp, cmin, cmax, fast, codes + off);
             }
-        } else {
-#pragma unroll
-            for (int j = 0; j < NRV; j++) {
-                const int64_t c = c0 + (int64_t)(j * L + sub) * VEC;
-                nib_vector<false>(w[j], rcp, cmin, cmax, fast, s, zf, z, qmin, qmax, crow_p + c / 2);
+            const unsigned mask = __ballot_sync(0xffffffffu, slow);
+            if (mask) {
+                const int n = __popc(mask);
+                if (qn + n > NIB_QCAP) {
+                    nib_flush(q, qn, qmin, qmax, codes);
+                    qn = 0;
+                }
+                if (slow) {
+                    const int pos = qn + __popc(mask & ((1u << lane_id()) - 1u));
+                    q.w[pos] = w[j];
+                    q.s[pos] = s;
+                    q.rcp[pos] = rcp;
+                    q.z[pos] = z;
+                    q.off[pos] = off | (fast ? int64_t(0) : (int64_t(1) << 62));
+                }
+                qn += n;
             }
         }
     }
+    if (qn) nib_flush(q, qn, qmin, qmax, codes);
 }
 
 template <typename T>

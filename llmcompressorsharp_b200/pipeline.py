@@ -450,6 +450,35 @@ class _Overlap:
     # layers at once, so the first layers' work overlaps the copy instead of waiting for all of it.
     PROLOGUE_LAYERS = 4
 
+    def _enqueue_solve(self, l, h_ptrs: dict, weights, outputs, wait_ev, before_solve, after_solve, rows_for=None):
+        """Enqueue the solve of layer l: the solve stream waits for ``wait_ev`` and runs the
+        caller's ``before_solve``; each site then solves on its own stream and context (from the
+        Hessian at ``h_ptrs[site]``; ``rows_for(site)`` picks a row range); the solve stream
+        joins them and runs ``after_solve``.  Returns the event that marks the layer solved."""
+        pipe = self.pipe
+        with torch.cuda.stream(self.ss):
+            self.ss.wait_event(wait_ev)
+            if before_solve is not None:
+                before_solve(l)
+            start = torch.cuda.Event()
+            start.record(self.ss)
+        for j, s in enumerate(pipe.sites):
+            st = self.site_streams[j]
+            st.wait_event(start)
+            with torch.cuda.stream(st):
+                pipe.solve_site(s, h_ptrs[s.name], weights[l], outputs[l], ctx=C.c_void_p(self.site_ctx[j]),
+                                rows=rows_for(s) if rows_for is not None else None, u=self.site_u[j],
+                                work=self.site_work[j])
+                fin = torch.cuda.Event()
+                fin.record(st)
+            self.ss.wait_event(fin)
+        with torch.cuda.stream(self.ss):
+            if after_solve is not None:
+                after_solve(l)
+            done = torch.cuda.Event()
+            done.record(self.ss)
+        return done
+
     def run(self, layers, acts_for, weights, outputs, before_solve, after_solve, hess_events, acts_ready, sync=True):
         pipe = self.pipe
         cur = torch.cuda.current_stream(pipe.device)
@@ -467,28 +496,8 @@ class _Overlap:
 
         def solve(item):
             l, b, acc_done = item
-            with torch.cuda.stream(self.ss):
-                self.ss.wait_event(acc_done)
-                if before_solve is not None:
-                    before_solve(l)
-                start = torch.cuda.Event()
-                start.record(self.ss)
-            # each site on its own stream, all joined back into the solve stream
-            for j, s in enumerate(pipe.sites):
-                st = self.site_streams[j]
-                st.wait_event(start)
-                with torch.cuda.stream(st):
-                    pipe.solve_site(s, self._data(b, s.name), weights[l], outputs[l], ctx=C.c_void_p(self.site_ctx[j]),
-                                    u=self.site_u[j], work=self.site_work[j])
-                    fin = torch.cuda.Event()
-                    fin.record(st)
-                self.ss.wait_event(fin)
-            with torch.cuda.stream(self.ss):
-                if after_solve is not None:
-                    after_solve(l)
-                done = torch.cuda.Event()
-                done.record(self.ss)
-                solved[b] = done
+            solved[b] = self._enqueue_solve(l, {s.name: self._data(b, s.name) for s in pipe.sites}, weights, outputs,
+                                            acc_done, before_solve, after_solve)
 
         def hessian_limit(whole_gpu: bool):
             # Accumulations enqueued before the first solve have no solve beside them: they
@@ -608,20 +617,13 @@ class _Overlap:
 
         def solve(item):
             _, l, b, rd = item
-            with torch.cuda.stream(self.ss):
-                self.ss.wait_event(rd)
-                if before_solve is not None:
-                    before_solve(l)
-                for s in pipe.sites:
-                    p = C.c_void_p()
-                    _lib.call("llmc_hessian_data", C.c_void_p(sets[b][s.name]), C.byref(p))
-                    shard = row_shard(sum(m for _, m in s.weights), world, rank) if rows else None
-                    pipe.solve_site(s, p.value, weights[l], outputs[l], ctx=C.c_void_p(self.cs), rows=shard)
-                if after_solve is not None:
-                    after_solve(l)
-                done = torch.cuda.Event()
-                done.record(self.ss)
-                released[b] = done
+            ptrs = {}
+            for s in pipe.sites:
+                p = C.c_void_p()
+                _lib.call("llmc_hessian_data", C.c_void_p(sets[b][s.name]), C.byref(p))
+                ptrs[s.name] = p.value
+            rows_for = (lambda s: row_shard(sum(m for _, m in s.weights), world, rank)) if rows else None
+            released[b] = self._enqueue_solve(l, ptrs, weights, outputs, rd, before_solve, after_solve, rows_for)
 
         layers = list(layers)
         for i, l in enumerate(layers):
