@@ -410,33 +410,46 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
                     ready[k].append((r1, ev))
         return ready
 
+    out_stream = torch.cuda.Stream(dev)
+
+    def copy_weights():
+        """Host->device copy of every owned layer's weights on the copy stream, after the
+        activations, one event per layer: the solve of layer l waits only for its own."""
+        evs = {}
+        with torch.cuda.stream(copy_stream):
+            for l in mine:
+                for k in weights[l]:
+                    weights[l][k].copy_(h_w[l][k], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+                evs[l] = ev
+        return evs
+
     def e2e_step():
         ready = copy_acts()
-        if world == 1:
-            def load_weights(l):
-                for k in weights[l]:
-                    weights[l][k].copy_(h_w[l][k], non_blocking=True)
+        if world == 1 or hbufs is None:  # one GPU, or the pipelined multi-GPU job
+            wev = copy_weights()
+            out_stream.wait_stream(torch.cuda.current_stream(dev))
 
-            def store_outputs(l):
-                for k, o in stacked[l].items():
-                    for f, t in o.items():
-                        h_out[l][k][f].copy_(t, non_blocking=True)
+            def load_weights(l):  # runs on the solve stream
+                torch.cuda.current_stream(dev).wait_event(wev[l])
 
-            pipe.run(mine, acts, weights, outputs, before_solve=load_weights, after_solve=store_outputs,
-                     acts_ready=ready)
-            return
-        if hbufs is None:  # pipelined multi-GPU job
-            def load_weights_d(l):
-                for k in weights[l]:
-                    weights[l][k].copy_(h_w[l][k], non_blocking=True)
+            def store_outputs(l):  # device->host on its own stream, beside the next solve
+                done = torch.cuda.Event()
+                done.record()
+                out_stream.wait_event(done)
+                with torch.cuda.stream(out_stream):
+                    for k, o in stacked[l].items():
+                        for f, t in o.items():
+                            h_out[l][k][f].copy_(t, non_blocking=True)
 
-            def store_outputs_d(l):
-                for k, o in stacked[l].items():
-                    for f, t in o.items():
-                        h_out[l][k][f].copy_(t, non_blocking=True)
-
-            pipe.run_distributed(range(args.layers), acts, weights, outputs, world, rank,
-                                 before_solve=load_weights_d, after_solve=store_outputs_d, acts_ready=ready)
+            if world == 1:
+                pipe.run(mine, acts, weights, outputs, before_solve=load_weights, after_solve=store_outputs,
+                         acts_ready=ready)
+            else:
+                pipe.run_distributed(range(args.layers), acts, weights, outputs, world, rank,
+                                     before_solve=load_weights, after_solve=store_outputs, acts_ready=ready)
+            torch.cuda.current_stream(dev).wait_stream(out_stream)
             return
         for l in range(args.layers):
             for s in sites:
