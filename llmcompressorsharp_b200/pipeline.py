@@ -661,8 +661,15 @@ class _Overlap:
                 released[b] = rd
             while queue and queue[0][0] + self.DIST_LAG <= i:
                 solve(queue.pop(0))
-        while queue:
-            solve(queue.pop(0))
+        if queue:
+            # Solves enqueued after the last accumulation and reduction have nothing to share
+            # the GPU with: persistent grids over every SM.
+            self._set_solve_limit(0)
+            try:
+                while queue:
+                    solve(queue.pop(0))
+            finally:
+                self._set_solve_limit(self.solve_sms)
         for st in (self.sh, self.ss, self.sc):
             cur.wait_stream(st)
         if sync:
