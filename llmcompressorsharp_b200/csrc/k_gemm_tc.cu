@@ -280,6 +280,11 @@ constexpr int P_OUT_BYTES = 32 * 32 * 4;         // epilogue box per warp: 32 ro
 constexpr int P_SMEM_BYTES = P_SMEM_MAIN + P_EPI * P_OUT_BYTES + 1024 + 256;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory above the per-block limit");
 constexpr int P_TMEM_COLS = 2 * P_BN;
+// k-blocks (128 K-elements, 48 MMAs) per TMEM accumulation of the pair kernel.  Each fold is a
+// TMEM read of the whole accumulator and a hand-off across the pair; at 2 k-blocks the folds
+// and hand-offs took a large share of the MMA time.  The tensor core's truncating accumulation
+// then spans 128 K-elements between fp32 folds.
+constexpr int P_KF = 4;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap ahi, const __grid_constant__ CUtensorMap alo,
@@ -354,7 +359,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
             kb0 = s0;
             kb1 = s1;
         }
-        const int nchunks = (kb1 - kb0 + KF - 1) / KF;
+        const int nchunks = (kb1 - kb0 + P_KF - 1) / P_KF;
         const int64_t m0 = pm0 + (int64_t)rank * 128;   // this CTA's rows
         const int64_t nb = n0 + (int64_t)rank * 128;    // this CTA's half of the B panel
 
@@ -384,7 +389,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
                     if (!mbar_wait(&tempty[b], ((c_it >> 1) & 1u) ^ 1u, abort_flag, a.err, a.wait_limit)) break;
                     tc_fence_after();
                     const uint32_t dst = tmem + (uint32_t)(b * P_BN);
-                    const int k0 = kb0 + c * KF, k1 = min(kb1, k0 + KF);
+                    const int k0 = kb0 + c * P_KF, k1 = min(kb1, k0 + P_KF);
                     bool ok = true;
                     for (int kb = k0; kb < k1; kb++, mma_it++) {
                         const int s = mma_it % STAGES;
@@ -439,7 +444,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_NT, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+                if (lane == 0) mbar_arrive_cluster_cta(mapa_shared(smem_u32(&tempty[b]), 0));
             }
             const int64_t r = m0 + q * 32 + lane;
             const int64_t c0 = n0 + h * 128;

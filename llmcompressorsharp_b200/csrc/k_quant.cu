@@ -710,15 +710,22 @@ __global__ void __launch_bounds__(NT, NRV <= 4 ? 4 : (NRV <= 8 ? 3 : 2))
         const bool warp_clamp = __any_sync(0xffffffffu, active && clamp);
         const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
         const int64_t crow_off = (int64_t)r * crow;
-        // every lane reaches the ballots (inactive lanes store nothing and queue nothing)
+        // every lane reaches the votes (inactive lanes store nothing and queue nothing)
+        unsigned slow_bits = 0;  // bit j: vector j needs the chain
+        if (active) {
+#pragma unroll
+            for (int j = 0; j < NRV; j++) {
+                uint8_t* dst = codes + crow_off + (c0 + (int64_t)(j * L + sub) * VEC) / 2;
+                const bool slow = warp_clamp ? nib_vector<true>(w[j], rcp, cmin, cmax, fast, dst)
+                                             : nib_vector<false>(w[j], rcp, cmin, cmax, fast, dst);
+                slow_bits |= slow ? (1u << j) : 0u;
+            }
+        }
+        if (!__any_sync(0xffffffffu, slow_bits != 0)) continue;  // the common case: one vote
 #pragma unroll
         for (int j = 0; j < NRV; j++) {
             const int64_t off = crow_off + (c0 + (int64_t)(j * L + sub) * VEC) / 2;
-            bool slow = false;
-            if (active) {
-                slow = warp_clamp ? nib_vector<true>(w[j], rcp, cmin, cmax, fast, codes + off)
-                                  : nib_vector<false>(w[j], rcp, cmin, cmax, fast, codes + off);
-            }
+            const bool slow = (slow_bits >> j) & 1u;
             const unsigned mask = __ballot_sync(0xffffffffu, slow);
             if (mask) {
                 const int n = __popc(mask);
