@@ -705,13 +705,13 @@ def test_pipeline_chunked_copy_matches_resident(reserve):
     """Activations copied in from pinned host memory on another stream, with one event per
     copied row range (acts_ready in its list form), give the same outputs as the same job on
     resident activations: scales and zero-points (from W alone) equal, codes equal up to the
-    order of the Hessian's split-K additions.  With five layers the overlapped schedule runs its
-    copy-time prologue (the first four layers' Hessians fed chunk by chunk, site by site) and then
+    order of the Hessian's split-K additions.  With eight layers the overlapped schedule runs its
+    copy-time prologue (the first six layers' Hessians fed chunk by chunk, site by site) and then
     its layer-by-layer loop."""
     from llmcompressorsharp_b200 import GPTQConfig
     from llmcompressorsharp_b200.pipeline import GptqPipeline
 
-    sites, acts, weights = _pipeline_case(seed=52, layers=5, tokens=10000)
+    sites, acts, weights = _pipeline_case(seed=52, layers=8, tokens=10000)
     cfg = GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=128)
     outs = []
     for mode in ("resident", "copied"):
