@@ -243,37 +243,96 @@ __device__ __forceinline__ uint2 token_codes8(const uint4& w, float rcp, float c
                       __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410));
 }
 
-__global__ void __launch_bounds__(32 * WARPS) act_token_bf16_reg_kernel(const __nv_bfloat16* x, int64_t rows,
-                                                                        int64_t cols, int64_t ld, int bits, int sym,
-                                                                        uint8_t* codes, int64_t ldc, float* scales,
-                                                                        int32_t* zps) {
+// The row kernel streams its rows through shared memory: while a warp quantises row r, row
+// r + stride is already on its way (cp.async, 16 bytes a lane and vector) into the other half of
+// the warp's double buffer, so each warp keeps a row of loads in flight through its compute.
+// Each lane copies and later reads only its own 16-byte slots, so cp.async.wait_group alone
+// orders the data for it; the buffer a copy overwrites was read one iteration earlier.  The
+// loops over a row's vectors read the stage and are unrolled only a little: with the row held in
+// registers and every loop fully unrolled (16 vectors x 2 clamp variants) the kernel's code no
+// longer fit the instruction cache (ncu: "no instruction" the top stall, issue active 35 %).
+constexpr int RWARPS = 4;                                   // warps (rows in flight) a block
+constexpr int RSTAGE = REG_NV * 32;                         // uint4 slots of one row buffer
+constexpr size_t REG_SMEM = (size_t)RWARPS * 2 * RSTAGE * 16 + RWARPS * sizeof(TokQueue);
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+
+template <bool CLAMP>
+__device__ __forceinline__ void token_row_codes(const uint4* rowbuf, int nv, int lane, int64_t crow, float rcp,
+                                                float cmin, float cmax, bool fast, float s, int z, float qmin,
+                                                float qmax, int iqmin, int iqmax, uint8_t* codes, TokQueue& q,
+                                                int& qn) {
+#pragma unroll 2
+    for (int j = 0; j < nv; j++) {  // nv is the same in every lane
+        const uint4 w = rowbuf[j * 32 + lane];
+        const int64_t off = crow + (int64_t)(j * 32 + lane) * 8;
+        bool near_mid;
+        *reinterpret_cast<uint2*>(codes + off) = token_codes8<CLAMP>(w, rcp, cmin, cmax, z, &near_mid);
+        const bool slow = !fast || near_mid;
+        const unsigned mask = __ballot_sync(0xffffffffu, slow);
+        if (mask) {
+            const int n = __popc(mask);
+            if (qn + n > TOK_QCAP) {
+                token_flush(q, qn, qmin, qmax, iqmin, iqmax, codes);
+                qn = 0;
+            }
+            if (slow) {
+                const int pos = qn + __popc(mask & ((1u << lane) - 1u));
+                q.w[pos] = w;
+                q.s[pos] = s;
+                q.rcp[pos] = rcp;
+                q.z[pos] = z;
+                q.off[pos] = off | (fast ? int64_t(0) : (int64_t(1) << 62));
+            }
+            qn += n;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(32 * RWARPS) act_token_bf16_reg_kernel(const __nv_bfloat16* x, int64_t rows,
+                                                                         int64_t cols, int64_t ld, int bits, int sym,
+                                                                         uint8_t* codes, int64_t ldc, float* scales,
+                                                                         int32_t* zps) {
     constexpr float MAGIC = 12582912.f;
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
     const int nv = (int)(cols / 256);  // vectors per lane
     float qmin, qmax;
     qrange(bits, sym, &qmin, &qmax);
     const int iqmin = (int)qmin, iqmax = (int)qmax;
     const __nv_bfloat162 pinf = __float2bfloat162_rn(INFINITY), ninf = __float2bfloat162_rn(-INFINITY);
-    __shared__ TokQueue queues[WARPS];
-    TokQueue& q = queues[threadIdx.x / 32];
+    extern __shared__ __align__(16) unsigned char tok_smem[];
+    uint4* stage = reinterpret_cast<uint4*>(tok_smem) + (size_t)warp * 2 * RSTAGE;
+    TokQueue* queues = reinterpret_cast<TokQueue*>(tok_smem + (size_t)RWARPS * 2 * RSTAGE * 16);
+    TokQueue& q = queues[warp];
     int qn = 0;  // queued vectors of this warp (the same in every lane)
-    for (int64_t r = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32; r < rows; r += (int64_t)gridDim.x * WARPS) {
-        const __nv_bfloat16* row = x + r * ld;
-        uint4 w[REG_NV];
-#pragma unroll
-        for (int j = 0; j < REG_NV; j++)
-            if (j < nv) w[j] = *reinterpret_cast<const uint4*>(row + (int64_t)(j * 32 + lane) * 8);
+    const int64_t stride = (int64_t)gridDim.x * RWARPS;
+    auto prefetch = [&](int64_t rr, int buf) {
+        const __nv_bfloat16* src = x + rr * ld;
+        uint4* dst = stage + buf * RSTAGE;
+#pragma unroll 4
+        for (int j = 0; j < nv; j++) cp_async16(dst + j * 32 + lane, src + (int64_t)(j * 32 + lane) * 8);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    int64_t r = (int64_t)blockIdx.x * RWARPS + warp;
+    if (r < rows) prefetch(r, 0);
+    for (int it = 0; r < rows; r += stride, it++) {
+        const uint4* rowbuf = stage + (it & 1) * RSTAGE;
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        if (r + stride < rows) prefetch(r + stride, (it & 1) ^ 1);
         __nv_bfloat162 mn2 = pinf, mx2 = ninf;
+#pragma unroll 4
+        for (int j = 0; j < nv; j++) {
+            const uint4 w = rowbuf[j * 32 + lane];
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int j = 0; j < REG_NV; j++) {
-            if (j < nv) {
-                const uint32_t ww[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(&ww[k]);
-                    mn2 = __hmin2_nan(mn2, p);
-                    mx2 = __hmax2_nan(mx2, p);
-                }
+            for (int k = 0; k < 4; k++) {
+                const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(&ww[k]);
+                mn2 = __hmin2_nan(mn2, p);
+                mx2 = __hmax2_nan(mx2, p);
             }
         }
         float mn = fmin_nan(__low2float(mn2), __high2float(mn2));
@@ -300,34 +359,12 @@ __global__ void __launch_bounds__(32 * WARPS) act_token_bf16_reg_kernel(const __
         // parameters are the same in every lane, so the branch is uniform).
         const bool clamp = !(hi <= qmax + 0.25f && lo >= qmin - 0.25f);
         const float cmin = MAGIC + (qmin - zf), cmax = MAGIC + (qmax - zf);
-        const int64_t crow = r * ldc;
-#pragma unroll
-        for (int j = 0; j < REG_NV; j++) {
-            if (j < nv) {  // nv is the same in every lane
-                const int64_t off = crow + (int64_t)(j * 32 + lane) * 8;
-                bool near_mid;
-                *reinterpret_cast<uint2*>(codes + off) = clamp ? token_codes8<true>(w[j], rcp, cmin, cmax, z, &near_mid)
-                                                               : token_codes8<false>(w[j], rcp, cmin, cmax, z, &near_mid);
-                const bool slow = !fast || near_mid;
-                const unsigned mask = __ballot_sync(0xffffffffu, slow);
-                if (mask) {
-                    const int n = __popc(mask);
-                    if (qn + n > TOK_QCAP) {
-                        token_flush(q, qn, qmin, qmax, iqmin, iqmax, codes);
-                        qn = 0;
-                    }
-                    if (slow) {
-                        const int pos = qn + __popc(mask & ((1u << lane) - 1u));
-                        q.w[pos] = w[j];
-                        q.s[pos] = s;
-                        q.rcp[pos] = rcp;
-                        q.z[pos] = z;
-                        q.off[pos] = off | (fast ? int64_t(0) : (int64_t(1) << 62));
-                    }
-                    qn += n;
-                }
-            }
-        }
+        if (clamp)
+            token_row_codes<true>(rowbuf, nv, lane, r * ldc, rcp, cmin, cmax, fast, s, z, qmin, qmax, iqmin, iqmax, codes,
+                                  q, qn);
+        else
+            token_row_codes<false>(rowbuf, nv, lane, r * ldc, rcp, cmin, cmax, fast, s, z, qmin, qmax, iqmin, iqmax,
+                                   codes, q, qn);
     }
     if (qn) token_flush(q, qn, qmin, qmax, iqmin, iqmax, codes);
 }
@@ -346,7 +383,17 @@ llmc_status launch(llmc_ctx* ctx, const void* x, int64_t rows, int64_t cols, int
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
         if (vec && codes && !deq && cols % 256 == 0 && cols <= 256 * REG_NV && (uintptr_t)codes % 8 == 0 &&
             ldc % 8 == 0) {
-            act_token_bf16_reg_kernel<<<(unsigned)blocks, 32 * WARPS, 0, ctx->stream>>>(
+            static bool attr[64];
+            if (ctx->device < 0 || ctx->device >= 64) return fail(LLMC_ERR_UNSUPPORTED, "device index");
+            if (!attr[ctx->device]) {
+                LLMC_CUDA_TRY(cudaFuncSetAttribute(act_token_bf16_reg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)REG_SMEM));
+                attr[ctx->device] = true;
+            }
+            int64_t rblocks = (rows + RWARPS - 1) / RWARPS;
+            const int64_t rcap = (int64_t)ctx->sm_count * 8;
+            if (rblocks > rcap) rblocks = rcap;
+            act_token_bf16_reg_kernel<<<(unsigned)rblocks, 32 * RWARPS, REG_SMEM, ctx->stream>>>(
                 reinterpret_cast<const __nv_bfloat16*>(x), rows, cols, ld, bits, sym, codes, ldc, scales, zps);
             return check_launch(ctx, "act_token_bf16_reg");
         }
