@@ -246,6 +246,52 @@ __global__ void __launch_bounds__(NT) awq_err_group_kernel(const T* W, int64_t m
     }
 }
 
+// Squared errors of a lane's PER columns for one grid point, pairs of columns on the paired fp32
+// instructions (each component rounded as its scalar form): f = v * rcp(s), rint(f) as
+// (f + 1.5 * 2^23) - 1.5 * 2^23, fq = (clamp(rint(f) + zp) - zp) * s, e = fq * (1 / s_k) - w.
+// The chain replaces fq where the quotient may round otherwise than v / s: within 4.8e-7 |f| of a
+// half-integer, |f| >= 2^22 (where the rint trick no longer holds; caught by the same bound), a
+// NaN, or a scale without a finite reciprocal.  The clamp runs only in warps that need it.
+template <int PER, bool CLAMP>
+__device__ __forceinline__ float2 awq_pairs(const float (&v)[PER], const float (&w)[PER], const float4* rv, float rsc,
+                                            float sc, float zf, float qmin, float qmax, bool rs_ok) {
+    const float2 rsc2 = make_float2(rsc, rsc), sc2 = make_float2(sc, sc);
+    const float2 zf2 = make_float2(zf, zf), nzf2 = make_float2(-zf, -zf);
+    const float2 mg2 = make_float2(12582912.f, 12582912.f), nmg2 = make_float2(-12582912.f, -12582912.f);
+    const float2 neg1 = make_float2(-1.f, -1.f);
+    float2 part2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < PER / 4; q++) {
+        const float4 r4 = rv[q];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int e0 = 4 * q + 2 * h;
+            const float2 f = __fmul2_rn(make_float2(v[e0], v[e0 + 1]), rsc2);
+            const float2 fr = __fadd2_rn(__fadd2_rn(f, mg2), nmg2);
+            const float2 d = __ffma2_rn(fr, neg1, f);  // f - fr
+            float2 t = __fadd2_rn(fr, zf2);
+            if constexpr (CLAMP) {
+                t.x = fminf(fmaxf(t.x, qmin), qmax);
+                t.y = fminf(fmaxf(t.y, qmin), qmax);
+            }
+            float2 fq = __fmul2_rn(__fadd2_rn(t, nzf2), sc2);
+            // |d| <= 0.5, so "within 4.8e-7 |f| of a half-integer" is |d| + 4.8e-7 |f| >= 0.5
+            if (!rs_ok || !(fmaf(fabsf(f.x), 4.8e-7f, fabsf(d.x)) < 0.5f)) {
+                int code;
+                fq.x = fq_chain<float>(v[e0], sc, zf, qmin, qmax, &code);
+            }
+            if (!rs_ok || !(fmaf(fabsf(f.y), 4.8e-7f, fabsf(d.y)) < 0.5f)) {
+                int code;
+                fq.y = fq_chain<float>(v[e0 + 1], sc, zf, qmin, qmax, &code);
+            }
+            const float2 pr = __fmul2_rn(fq, h ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y));
+            const float2 e = __ffma2_rn(make_float2(w[e0], w[e0 + 1]), neg1, pr);  // fq / s_k - w
+            part2 = __ffma2_rn(e, e, part2);
+        }
+    }
+    return part2;
+}
+
 // The one-pass search with several rows a warp (2-byte weights; group width a multiple of PER
 // and a divisor of n): a (row, group) segment takes L = gs / PER lanes holding PER consecutive
 // columns each, so a warp covers 32 / L rows at once and one instruction stream serves all of
@@ -324,40 +370,22 @@ __global__ void __launch_bounds__(NT) awq_err_rows_kernel(const T* W, int64_t m,
             const float zf = (float)z;
             const float rsc = __frcp_rn(sc);
             const bool rs_ok = fabsf(rsc) <= 3.0e38f && rsc != 0.f;
-            // Pairs of columns on the paired fp32 instructions (each component rounded as its
-            // scalar form); rint(f) as (f + 1.5 * 2^23) - 1.5 * 2^23, exact for |f| < 2^22 (larger
-            // |f|, and quotients near a half-integer, take the chain).
-            const float2 rsc2 = make_float2(rsc, rsc), sc2 = make_float2(sc, sc);
-            const float2 zf2 = make_float2(zf, zf), nzf2 = make_float2(-zf, -zf);
-            const float2 mg2 = make_float2(12582912.f, 12582912.f), nmg2 = make_float2(-12582912.f, -12582912.f);
-            const float2 neg1 = make_float2(-1.f, -1.f);
-            float2 part2 = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int q = 0; q < PER / 4; q++) {
-                const float4 r4 = rv[q];
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const int e0 = 4 * q + 2 * h;
-                    const float2 f = __fmul2_rn(make_float2(v[e0], v[e0 + 1]), rsc2);
-                    const float2 fr = __fadd2_rn(__fadd2_rn(f, mg2), nmg2);
-                    const float2 d = __ffma2_rn(fr, neg1, f);  // f - fr
-                    float2 t = __fadd2_rn(fr, zf2);
-                    t.x = fminf(fmaxf(t.x, qmin), qmax);
-                    t.y = fminf(fmaxf(t.y, qmin), qmax);
-                    float2 fq = __fmul2_rn(__fadd2_rn(t, nzf2), sc2);
-                    if (!rs_ok || !(fabsf(f.x) < 4194304.f) || fabsf(fabsf(d.x) - 0.5f) <= fabsf(f.x) * 4.8e-7f + 1e-30f) {
-                        int code;
-                        fq.x = fq_chain<float>(v[e0], sc, zf, qmin, qmax, &code);
-                    }
-                    if (!rs_ok || !(fabsf(f.y) < 4194304.f) || fabsf(fabsf(d.y) - 0.5f) <= fabsf(f.y) * 4.8e-7f + 1e-30f) {
-                        int code;
-                        fq.y = fq_chain<float>(v[e0 + 1], sc, zf, qmin, qmax, &code);
-                    }
-                    const float2 pr = __fmul2_rn(fq, h ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y));
-                    const float2 e = __ffma2_rn(make_float2(w[e0], w[e0 + 1]), neg1, pr);  // fq / s_k - w
-                    part2 = __ffma2_rn(e, e, part2);
-                }
+            // The clamp to [qmin, qmax] can act only if an extreme's code leaves the grid: on the
+            // fast path v -> rint(v * rcp(s)) is monotone, so the segment's extremes bound every
+            // element; an extreme near a half-integer (or off the fast path) counts as leaving.
+            bool clamp_need = true;
+            if (rs_ok) {
+                const float fx = __fmul_rn(mx, rsc), fn = __fmul_rn(mn, rsc);
+                const float rx = __fsub_rn(__fadd_rn(fx, 12582912.f), 12582912.f);
+                const float rn = __fsub_rn(__fadd_rn(fn, 12582912.f), 12582912.f);
+                const bool tie = !(fmaf(fabsf(fx), 4.8e-7f, fabsf(__fsub_rn(fx, rx))) < 0.5f) ||
+                                 !(fmaf(fabsf(fn), 4.8e-7f, fabsf(__fsub_rn(fn, rn))) < 0.5f);
+                clamp_need = tie || __fadd_rn(rx, zf) > qmax || __fadd_rn(rn, zf) < qmin;
             }
+            const float2 pr2 = __any_sync(0xffffffffu, clamp_need)
+                                   ? awq_pairs<PER, true>(v, w, rv, rsc, sc, zf, qmin, qmax, rs_ok)
+                                   : awq_pairs<PER, false>(v, w, rv, rsc, sc, zf, qmin, qmax, rs_ok);
+            const float2 part2 = pr2;
             const float part = __fadd_rn(part2.x, part2.y);
             acc[k * 32] += (double)part;
         }
