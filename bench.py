@@ -331,7 +331,7 @@ def run_ours(args):
                          "algorithmic": "d(d+1)T FLOP per launch (symmetric rank-k update of T tokens)",
                          "traffic": SYRK_TRAFFIC_PER_LAUNCH,
                          "traffic_note": "ncu DRAM read+write bytes per launch of this kernel version, averaged "
-                                         "over the step's mix of d=4096 (1.49 GB) and d=14336 (18.2 GB) launches of "
+                                         "over the step's mix of d=4096 (1.47 GB) and d=14336 (20.4 GB) launches of "
                                          "65,536 tokens; their algorithmic bytes are 0.60 GB and 2.70 GB (X once + "
                                          "H upper triangle)"},
             "cpu_baseline": cpu,
@@ -347,12 +347,12 @@ def run_ours(args):
 
 
 # DRAM bytes (read + write) per Hessian launch of this workload, from one ncu capture of the four
-# site launches of a 65,536-token step (dram__bytes_read.sum + dram__bytes_write.sum, captured with
-# `--layers 1 --tokens 65536 --steps 1 --warmup 1 --no-e2e --no-cpu-baseline --reserve-sms 0`):
-# d = 4096: 1.350 GB read + 0.135 GB written; d = 14336: 16.52 GB + 1.69 GB.  A step has three
-# d = 4096 launches for every d = 14336 launch, so the average launch moves (3 * 1.485 + 18.21) / 4 GB.
-# Re-capture whenever the Hessian kernel changes.
-SYRK_TRAFFIC_PER_LAUNCH = (3 * 1.485e9 + 18.21e9) / 4
+# site launches of a 65,536-token step at the default SM reserve (dram__bytes_read.sum +
+# dram__bytes_write.sum, captured with `--layers 1 --tokens 65536 --steps 1 --warmup 1 --no-e2e
+# --no-cpu-baseline`): d = 4096: 1.341 GB read + 0.131 GB written; d = 14336: 18.33 GB + 2.11 GB.
+# A step has three d = 4096 launches for every d = 14336 launch, so the average launch moves
+# (3 * 1.472 + 20.44) / 4 GB.  Re-capture whenever the Hessian kernel changes.
+SYRK_TRAFFIC_PER_LAUNCH = (3 * 1.472e9 + 20.44e9) / 4
 
 
 def _randn_bf16(m, n, dev, g, std=1.0):
