@@ -452,11 +452,13 @@ class _Overlap:
     # 9.66 / 9.58 / 9.46 / 9.41 s with 2 / 3 / 4 / 6 layers (one box, 1,300 MHz).
     PROLOGUE_LAYERS = 6
 
-    def _enqueue_solve(self, l, h_ptrs: dict, weights, outputs, wait_ev, before_solve, after_solve, rows_for=None):
+    def _enqueue_solve(self, l, h_ptrs: dict, weights, outputs, wait_ev, before_solve, after_solve, rows_for=None,
+                       site_waits=None):
         """Enqueue the solve of layer l: the solve stream waits for ``wait_ev`` and runs the
         caller's ``before_solve``; each site then solves on its own stream and context (from the
-        Hessian at ``h_ptrs[site]``; ``rows_for(site)`` picks a row range); the solve stream
-        joins them and runs ``after_solve``.  Returns the event that marks the layer solved."""
+        Hessian at ``h_ptrs[site]``, once ``site_waits[site]`` has completed when given;
+        ``rows_for(site)`` picks a row range); the solve stream joins them and runs
+        ``after_solve``.  Returns the event that marks the layer solved."""
         pipe = self.pipe
         with torch.cuda.stream(self.ss):
             self.ss.wait_event(wait_ev)
@@ -467,6 +469,8 @@ class _Overlap:
         for j, s in enumerate(pipe.sites):
             st = self.site_streams[j]
             st.wait_event(start)
+            if site_waits is not None:
+                st.wait_event(site_waits[s.name])
             with torch.cuda.stream(st):
                 pipe.solve_site(s, h_ptrs[s.name], weights[l], outputs[l], ctx=C.c_void_p(self.site_ctx[j]),
                                 rows=rows_for(s) if rows_for is not None else None, u=self.site_u[j],
@@ -497,9 +501,15 @@ class _Overlap:
         solved = [None] * nsets  # event: last solve that read buffer set b
 
         def solve(item):
-            l, b, acc_done = item
+            # item: (layer, set, event of the first site accumulated, events of every site)
+            l, b, first_ev, site_evs = item
             solved[b] = self._enqueue_solve(l, {s.name: self._data(b, s.name) for s in pipe.sites}, weights, outputs,
-                                            acc_done, before_solve, after_solve)
+                                            first_ev, before_solve, after_solve, site_waits=site_evs)
+
+        def accumulated(s, evs):
+            ev = torch.cuda.Event()
+            ev.record(self.sh)
+            evs[s.name] = ev
 
         def hessian_limit(whole_gpu: bool):
             # Accumulations enqueued before the first solve have no solve beside them: they
@@ -512,8 +522,9 @@ class _Overlap:
             # all K layers' Hessians before the next chunk is waited for.
             acts = [acts_for(l) for l in layers[:K]]
             hessian_limit(True)
+            site_evs = {}
             with torch.cuda.stream(self.sh):
-                for s in pipe.sites:
+                for s in pipe.sites:  # the copy's site order
                     ev = _events() if hess_events is not None else None
                     if ev:
                         ev[0].record(self.sh)
@@ -522,12 +533,16 @@ class _Overlap:
                     if ev:
                         ev[1].record(self.sh)
                         hess_events.append((ev[0], ev[1], s.d, sum(a[s.name].shape[0] for a in acts)))
-                acc_done = torch.cuda.Event()
-                acc_done.record(self.sh)
+                    accumulated(s, site_evs)
             hessian_limit(False)
+            first_ev = site_evs[pipe.sites[0].name]
             for i in range(K - 1):
-                solve((layers[i], i, acc_done))
-            pending = (layers[K - 1], K - 1, acc_done)
+                solve((layers[i], i, first_ev, site_evs))
+            pending = (layers[K - 1], K - 1, first_ev, site_evs)
+        # Widest site first: its solve (the longest: the largest factorisation and GPTQ sweep)
+        # starts while the narrower sites of the layer still accumulate, and each site's solve
+        # waits only for its own Hessian.
+        order = sorted(pipe.sites, key=lambda s: -s.d)
         for i in range(K, len(layers)):
             l = layers[i]
             b = i % nsets
@@ -535,10 +550,11 @@ class _Overlap:
             first = pending is None  # nothing solves beside this accumulation
             if first:
                 hessian_limit(True)
+            site_evs = {}
             with torch.cuda.stream(self.sh):
                 if solved[b] is not None:
                     self.sh.wait_event(solved[b])
-                for s in pipe.sites:
+                for s in order:
                     ev = _events() if hess_events is not None else None
                     if ev:
                         ev[0].record(self.sh)
@@ -546,13 +562,12 @@ class _Overlap:
                     if ev:
                         ev[1].record(self.sh)
                         hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
-                acc_done = torch.cuda.Event()
-                acc_done.record(self.sh)
+                    accumulated(s, site_evs)
             if first:
                 hessian_limit(False)
             if pending is not None:
                 solve(pending)
-            pending = (l, b, acc_done)
+            pending = (l, b, site_evs[order[0].name], site_evs)
         if pending is not None:
             # The last layer's solve waits for the last accumulation, so nothing else runs beside
             # it: lift the solve context's SM limit (persistent grids over the whole GPU) for it.
