@@ -246,12 +246,29 @@ class GPTQModifier(ModifierBase):
         if not self._acc:
             return
         alias = self._alias
+        # Factor every distinct Hessian first, with the device context's errors deferred: the
+        # factorisations are enqueued back to back (none reads a flag back to the host), and one
+        # llmc_sync per device then raises the first failure before any weight is replaced.
         ucache: dict[int, torch.Tensor] = {}
-        for wname, acc in self._acc.items():
+        srcs = {}
+        for acc in self._acc.values():
             src = alias.get(id(acc), acc)
-            key = id(src)
-            if key not in ucache:
-                ucache[key] = HessianInverseSolver.upper(src.raw(), self.config.dampening_frac, upper_only=True)
+            srcs.setdefault(id(src), src)
+        by_dev: dict = {}
+        for key, src in srcs.items():
+            by_dev.setdefault(src.raw().device, []).append((key, src))
+        for dev, items in by_dev.items():
+            c = C.c_void_p(ctx(dev))
+            _lib.call("llmc_set_deferred_errors", c, C.c_int32(1))
+            try:
+                with torch.cuda.device(dev):
+                    for key, src in items:
+                        ucache[key] = HessianInverseSolver.upper(src.raw(), self.config.dampening_frac, upper_only=True)
+                _lib.call("llmc_sync", c)
+            finally:
+                _lib.call("llmc_set_deferred_errors", c, C.c_int32(0))
+        for wname, acc in self._acc.items():
+            key = id(alias.get(id(acc), acc))
             w = state.named_weights[wname]
             res = gptq_quantize_u(w, ucache[key], self.config)
             state.named_weights[wname] = res.wq if w.is_cuda else res.wq.cpu()

@@ -903,6 +903,37 @@ def test_gptq_modifier_shared_inputs_through_a_decoder_forward():
         assert torch.equal(outs[0][k], outs[1][k]), k
 
 
+def test_gptq_modifier_non_pd_hessian_raises_before_any_weight_changes():
+    """Undamped Hessians with a dead input channel are singular.  The modifier factors every
+    distinct Hessian with the context's errors deferred and checks once: the failure surfaces as
+    NotPositiveDefiniteError (the reference would fall back to a pseudo-inverse, which this
+    library does not provide for non-zero matrices) and no weight has been replaced."""
+    from llmcompressorsharp_b200 import CompressionState, GPTQConfig, GPTQModifier
+    from llmcompressorsharp_b200.errors import NotPositiveDefiniteError
+
+    a = torch.nn.Linear(64, 16, bias=False).to(DEV)
+    b = torch.nn.Linear(64, 8, bias=False).to(DEV)
+    wa, wb = a.weight.detach().clone(), b.weight.detach().clone()
+    st = CompressionState({"a.weight": wa.clone(), "b.weight": wb.clone()})
+    st.named_modules = {"a": a, "b": b}
+    mod = GPTQModifier(GPTQConfig(num_bits=4, strategy="group", group_size=32, symmetric=False,
+                                  dampening_frac=0.0))
+    mod.initialize(st)
+    mod.on_start(st)
+    x = torch.randn(256, 64, device=DEV, generator=torch.Generator(DEV).manual_seed(8))
+    a(x)
+    xb = x.clone()
+    xb[:, 5] = 0.0  # b's Hessian: row and column 5 are zero, a zero pivot without damping
+    b(xb)
+    with pytest.raises(NotPositiveDefiniteError):
+        mod.on_end(st)
+    assert torch.equal(st.named_weights["a.weight"], wa) and torch.equal(st.named_weights["b.weight"], wb)
+    # the device context is usable afterwards (its deferred-error mode was restored)
+    from llmcompressorsharp_b200 import HessianInverseSolver
+    u = HessianInverseSolver.upper(torch.eye(8, device=DEV) * 2, 0.01)
+    assert torch.isfinite(u).all()
+
+
 def test_gptq_modifier_shared_inputs_tell_a_transposed_view_apart():
     """x and x.T of a square x share address, shape and dtype but not data."""
     from llmcompressorsharp_b200 import CompressionState, GPTQConfig, GPTQModifier
