@@ -93,8 +93,11 @@ __device__ __forceinline__ void chol32_step(float (&r)[32], int lane, int& bad) 
         bad = 1;
         piv = 1.f;
     }
-    const float s = __fsqrt_rn(piv);
-    const float inv_s = __frcp_rn(s);
+    // 1 / sqrt(piv) from the SFU (within 2 ulp) and sqrt(piv) as piv times it: this step is on
+    // the block's critical path, and the correctly rounded square root and reciprocal each cost
+    // several times the latency; the factor's error bars (1e-4 relative on U) are far wider.
+    const float inv_s = rsqrtf(piv);
+    const float s = __fmul_rn(piv, inv_s);
     r[K] = (lane == K) ? s : ((lane > K) ? __fmul_rn(r[K], inv_s) : 0.f);
 #pragma unroll
     for (int j = K + 1; j < 32; j++) {
@@ -124,8 +127,8 @@ __device__ __forceinline__ void invert_diag32(const float* sL, float* sX, int c0
         float acc = 0.f;
 #pragma unroll
         for (int k = 0; k < i; k++) acc = fmaf(Li[k], x[k], acc);  // x[k] = 0 for k < lane
-        const float lii = Li[i];
-        x[i] = (i < lane) ? 0.f : ((i == lane) ? __frcp_rn(lii) : __fdiv_rn(-acc, lii));
+        const float rii = __frcp_rn(Li[i]);  // independent of acc: off the substitution chain
+        x[i] = (i < lane) ? 0.f : ((i == lane) ? rii : __fmul_rn(-acc, rii));
     }
 #pragma unroll
     for (int i = 0; i < 32; i++) sX[(c0 + i) * BLD + c0 + lane] = x[i];
