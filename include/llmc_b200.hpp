@@ -93,7 +93,21 @@ class Context {
     Context& operator=(const Context&) = delete;
     llmc_ctx* get() const { return ctx_; }
     int device() const { return device_; }
+    // Waits for the context's stream and raises its first deferred device error.
     void Synchronize() const { Check(llmc_sync(ctx_)); }
+    // Extensions (no reference counterpart): the stream the context's work is ordered on, an SM
+    // cap for its persistent grids (0: the whole GPU), the tries of a bounded device wait
+    // (negative: the default), device-side "not positive definite" decisions reported by
+    // Synchronize, and the number of kernels it has launched.
+    void SetStream(cudaStream_t stream) { Check(llmc_set_stream(ctx_, (void*)stream)); }
+    void SetSmLimit(int sms) { Check(llmc_set_sm_limit(ctx_, sms)); }
+    void SetWaitLimit(int64_t tries) { Check(llmc_set_wait_limit(ctx_, tries)); }
+    void SetDeferredErrors(bool on) { Check(llmc_set_deferred_errors(ctx_, on ? 1 : 0)); }
+    int64_t LaunchCount() const {
+        int64_t n = 0;
+        Check(llmc_launch_count(ctx_, &n));
+        return n;
+    }
 
    private:
     llmc_ctx* ctx_ = nullptr;
@@ -581,6 +595,70 @@ struct SmoothQuant {
                                 (int32_t)smooth.dtype(), balance.data(), (int32_t)balance.dtype(), balance.shape()[0],
                                 balance.last(), alpha, static_cast<float*>(s.data())));
         return s.ToHost();
+    }
+};
+
+// ---- AWQ's apply step with a given scale (algorithm-mapping.md:243-248) -------------------------
+struct ScaleApply {
+    // smooth /= s (skipped when smooth is null), balance *= s, in the weights' dtypes.
+    static void Apply(Context& ctx, const DeviceTensor& s, DeviceTensor* smooth, DeviceTensor& balance) {
+        if (balance.dim() != 2 || s.numel() != balance.last() || s.dtype() != DType::Float32)
+            throw ArgumentException("balance must be 2-D and s fp32 [balance's last dim]");
+        Check(llmc_scale_apply(ctx.get(), static_cast<const float*>(s.data()), smooth ? smooth->data() : nullptr,
+                               smooth ? (int32_t)smooth->dtype() : 0, balance.data(), (int32_t)balance.dtype(),
+                               balance.shape()[0], balance.last()));
+    }
+};
+
+// ---- per-token activation quantisation (extension: W8A8's activation side) ---------------------
+struct PerTokenResult {
+    std::vector<uint8_t> Codes;       // [tokens, hidden]; two's complement for a symmetric grid
+    std::vector<float> Scales;        // [tokens]
+    std::vector<int32_t> ZeroPoints;  // [tokens]
+};
+
+struct PerTokenQuantizer {
+    // x [tokens, hidden] (any leading shape folded into tokens); one min-max observer a row.
+    static PerTokenResult Quantize(Context& ctx, const DeviceTensor& x, int numBits = 8, bool symmetric = true) {
+        const int64_t cols = x.last(), rows = x.numel() / cols;
+        DeviceBytes codes((size_t)(rows * cols)), scales((size_t)rows * 4), zps((size_t)rows * 4);
+        Check(llmc_act_quant_per_token(ctx.get(), x.data(), (int32_t)x.dtype(), rows, cols, cols, numBits,
+                                       symmetric ? 1 : 0, static_cast<uint8_t*>(codes.data()), cols,
+                                       static_cast<float*>(scales.data()), static_cast<int32_t*>(zps.data()), nullptr,
+                                       cols));
+        return PerTokenResult{codes.ToHost<uint8_t>(), scales.ToHost<float>(), zps.ToHost<int32_t>()};
+    }
+};
+
+// ---- GPTQ activation order (extension: the reference rejects ActOrder) -------------------------
+struct ActOrder {
+    // Columns in decreasing diag(H) (stable, NaN first); H fp32 [d, d].
+    static std::vector<int32_t> Permutation(Context& ctx, const DeviceTensor& hessian) {
+        if (hessian.dim() != 2 || hessian.shape()[0] != hessian.shape()[1] || hessian.dtype() != DType::Float32)
+            throw ArgumentException("Hessian must be a square fp32 2-D tensor");
+        const int64_t d = hessian.shape()[0];
+        DeviceBytes perm((size_t)d * 4);
+        Check(llmc_gptq_act_order_perm(ctx.get(), static_cast<const float*>(hessian.data()), d, d,
+                                       static_cast<int32_t*>(perm.data())));
+        return perm.ToHost<int32_t>();
+    }
+};
+
+// ---- per-tensor min/max without device allocation (no reference counterpart) -------------------
+struct NoAllocObserver {
+    // For callers that may not allocate device memory mid-run (a hook on a model's stream, a
+    // host allocator with a fixed budget): writes min / max into the caller's fp32 [1] device
+    // tensors (updating them with accumulate) and allocates nothing; rows <= 65,536; calls that
+    // overlap on the GPU share one static buffer and race.
+    static void MinMax(Context& ctx, const DeviceTensor& x, DeviceTensor& minOut, DeviceTensor& maxOut,
+                       bool accumulate = false) {
+        if (minOut.numel() != 1 || maxOut.numel() != 1 || minOut.dtype() != DType::Float32 ||
+            maxOut.dtype() != DType::Float32)
+            throw ArgumentException("min / max must be fp32 tensors of one element");
+        const int64_t cols = x.last(), rows = x.numel() / cols;
+        Check(llmc_observer_minmax_tensor_noalloc(ctx.get(), x.data(), (int32_t)x.dtype(), rows, cols, cols,
+                                                  static_cast<float*>(minOut.data()),
+                                                  static_cast<float*>(maxOut.data()), accumulate ? 1 : 0));
     }
 };
 

@@ -257,6 +257,53 @@ std::vector<std::pair<std::string, std::function<void(Context&)>>> tests() {
                          },
                          "ActOrder");
                  }});
+    // ---- extensions of the mirror (no reference test): context controls, per-token codes, AWQ's
+    // apply step, activation order, the allocation-free observer
+    t.push_back({"Context.ControlsAndLaunchCount", [](Context& c) {
+                     const int64_t n0 = c.LaunchCount();
+                     c.SetSmLimit(16);
+                     c.SetWaitLimit(-1);
+                     c.SetDeferredErrors(true);
+                     HessianAccumulator acc(c, 8);
+                     acc.Update(DeviceTensor::FromHost(std::vector<float>(64, 1.f), {8, 8}));
+                     c.Synchronize();
+                     c.SetDeferredErrors(false);
+                     c.SetSmLimit(0);
+                     Assert(c.LaunchCount() > n0, "launch count grows");
+                     Assert(acc.GetHessian().ToHost()[0] == 8.f, "H[0][0]");
+                 }});
+    t.push_back({"PerTokenQuantizer.SymmetricInt8", [](Context& c) {
+                     // row 0 absmax 127 -> scale 1; row 1 absmax 254 -> scale 2
+                     auto r = PerTokenQuantizer::Quantize(c, DeviceTensor::FromHost({127, -64, 3, 0, 254, -127, 7, 1}, {2, 4}));
+                     Near(r.Scales[0], 1.f, 0.f, "scale 0");
+                     Near(r.Scales[1], 2.f, 0.f, "scale 1");
+                     Assert((int8_t)r.Codes[0] == 127 && (int8_t)r.Codes[1] == -64 && (int8_t)r.Codes[2] == 3, "row 0");
+                     // 254 / 2 = 127; -127 / 2 = -63.5 -> -64 (half to even); 7 / 2 = 3.5 -> 4; 1 / 2 -> 0
+                     Assert((int8_t)r.Codes[4] == 127 && (int8_t)r.Codes[5] == -64 && (int8_t)r.Codes[6] == 4 &&
+                                (int8_t)r.Codes[7] == 0,
+                            "row 1");
+                 }});
+    t.push_back({"ScaleApply.BalanceTimesSmoothOver", [](Context& c) {
+                     auto s = DeviceTensor::FromHost({2, 4}, {2});
+                     auto smooth = DeviceTensor::FromHost({8, 8}, {2});
+                     auto balance = DeviceTensor::FromHost({1, 1, 0.5f, 0.25f}, {2, 2});
+                     ScaleApply::Apply(c, s, &smooth, balance);
+                     const std::vector<float> sm = smooth.ToHost(), bal = balance.ToHost();
+                     Assert(sm[0] == 4.f && sm[1] == 2.f, "smooth / s");
+                     Assert(bal[0] == 2.f && bal[1] == 4.f && bal[2] == 1.f && bal[3] == 1.f, "balance * s");
+                 }});
+    t.push_back({"ActOrder.DecreasingDiagonal", [](Context& c) {
+                     auto h = DeviceTensor::FromHost({1, 0, 0, 0, 3, 0, 0, 0, 2}, {3, 3});
+                     const std::vector<int32_t> want = {1, 2, 0};
+                     Assert(ActOrder::Permutation(c, h) == want, "order by diag(H) descending");
+                 }});
+    t.push_back({"NoAllocObserver.MinMax", [](Context& c) {
+                     DeviceTensor mn({1}, DType::Float32), mx({1}, DType::Float32);
+                     NoAllocObserver::MinMax(c, DeviceTensor::FromHost({-3, 5, 2, 0.5f}, {2, 2}), mn, mx);
+                     Assert(mn.ToHost()[0] == -3.f && mx.ToHost()[0] == 5.f, "min / max");
+                     NoAllocObserver::MinMax(c, DeviceTensor::FromHost({-1, 9}, {1, 2}), mn, mx, true);
+                     Assert(mn.ToHost()[0] == -3.f && mx.ToHost()[0] == 9.f, "running min / max");
+                 }});
     return t;
 }
 
