@@ -399,7 +399,7 @@ def run_e2e(args, pipe, sites, acts, weights, outputs, mine, world, rank, local,
         copy_stream.wait_stream(torch.cuda.current_stream(dev))
         ready = {}
         with torch.cuda.stream(copy_stream):
-            for k in acts:
+            for k in [s.name for s in pipe.site_order() if s.name in acts]:
                 T = acts[k].shape[0]
                 ready[k] = []
                 for r0 in range(0, T, args.chunk):

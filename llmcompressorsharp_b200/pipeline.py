@@ -281,6 +281,13 @@ class GptqPipeline:
             self.accumulate(s, acts[s.name])
             self.solve_site(s, self.hessian_ptr(s.name), weights, outputs)
 
+    def site_order(self):
+        """The order in which the overlapped schedule accumulates a layer's sites: widest first.
+        A caller that copies the activations in (``acts_ready``) copies them in this order, so
+        that the site with the most Hessian work per copied byte starts first and hides the rest
+        of the copy."""
+        return sorted(self.sites, key=lambda s: -s.d)
+
     def run_distributed(self, layers, acts, weights, outputs, world: int, rank: int, group=None, before_solve=None,
                         after_solve=None, hess_events=None, acts_ready=None, shard: str = "layers", sync: bool = True):
         """``run`` for one process per GPU (NCCL process group initialised by the caller):
@@ -452,6 +459,31 @@ class _Overlap:
     # 9.66 / 9.58 / 9.46 / 9.41 s with 2 / 3 / 4 / 6 layers (one box, 1,300 MHz).
     PROLOGUE_LAYERS = 6
 
+    def site_order(self):
+        return self.pipe.site_order()
+
+    def _hessian_whole_gpu(self, whole_gpu: bool):
+        # Accumulations enqueued before the first solve have no solve beside them: they take
+        # every SM (the limit is read when a launch is enqueued).
+        _lib.call("llmc_set_sm_limit", C.c_void_p(self.ch), C.c_int32(0 if whole_gpu else self.hessian_sms))
+
+    def _prologue(self, set_ids, sets, acts, acts_ready, hess_events, after_site):
+        """Accumulates len(set_ids) layers at once on the current stream, site by site in
+        ``site_order``, chunk-interleaved: each copied chunk of a site's activations is added to
+        every layer's Hessian (``sets[set_ids[i]]``, from ``acts[i]``) before the next chunk is
+        waited for.  ``after_site(site)`` runs on the stream after each site."""
+        pipe = self.pipe
+        for s in self.site_order():
+            ev = _events() if hess_events is not None else None
+            if ev:
+                ev[0].record()
+            pipe._accumulate_many([sets[b][s.name] for b in set_ids], [a[s.name] for a in acts],
+                                  ready=acts_ready.pop(s.name, None))
+            if ev:
+                ev[1].record()
+                hess_events.append((ev[0], ev[1], s.d, sum(a[s.name].shape[0] for a in acts)))
+            after_site(s)
+
     def _enqueue_solve(self, l, h_ptrs: dict, weights, outputs, wait_ev, before_solve, after_solve, rows_for=None,
                        site_waits=None):
         """Enqueue the solve of layer l: the solve stream waits for ``wait_ev`` and runs the
@@ -511,11 +543,11 @@ class _Overlap:
             ev.record(self.sh)
             evs[s.name] = ev
 
-        def hessian_limit(whole_gpu: bool):
-            # Accumulations enqueued before the first solve have no solve beside them: they
-            # take every SM (the limit is read when a launch is enqueued).
-            _lib.call("llmc_set_sm_limit", C.c_void_p(self.ch), C.c_int32(0 if whole_gpu else self.hessian_sms))
-
+        hessian_limit = self._hessian_whole_gpu
+        # Widest site first: its solve (the longest: the largest factorisation and GPTQ sweep)
+        # starts while the narrower sites of the layer still accumulate, and each site's solve
+        # waits only for its own Hessian.
+        order = self.site_order()
         pending = None
         if K:
             # Prologue: layers 0..K-1 in sets 0..K-1, site-major, each arriving chunk added to
@@ -524,25 +556,13 @@ class _Overlap:
             hessian_limit(True)
             site_evs = {}
             with torch.cuda.stream(self.sh):
-                for s in pipe.sites:  # the copy's site order
-                    ev = _events() if hess_events is not None else None
-                    if ev:
-                        ev[0].record(self.sh)
-                    pipe._accumulate_many([self.h[i][s.name] for i in range(K)], [a[s.name] for a in acts],
-                                          ready=acts_ready.pop(s.name, None))
-                    if ev:
-                        ev[1].record(self.sh)
-                        hess_events.append((ev[0], ev[1], s.d, sum(a[s.name].shape[0] for a in acts)))
-                    accumulated(s, site_evs)
+                self._prologue(list(range(K)), self.h, acts, acts_ready, hess_events,
+                               lambda s: accumulated(s, site_evs))
             hessian_limit(False)
-            first_ev = site_evs[pipe.sites[0].name]
+            first_ev = site_evs[order[0].name]
             for i in range(K - 1):
                 solve((layers[i], i, first_ev, site_evs))
             pending = (layers[K - 1], K - 1, first_ev, site_evs)
-        # Widest site first: its solve (the longest: the largest factorisation and GPTQ sweep)
-        # starts while the narrower sites of the layer still accumulate, and each site's solve
-        # waits only for its own Hessian.
-        order = sorted(pipe.sites, key=lambda s: -s.d)
         for i in range(K, len(layers)):
             l = layers[i]
             b = i % nsets
@@ -594,17 +614,17 @@ class _Overlap:
     # host; one layer of lag keeps the next accumulation ahead of the solve in the launch order.
     DIST_LAG = 1
 
-    def _dist_sets(self):
+    def _dist_sets(self, n: int):
         if not getattr(self, "hd", None):
             self.hd = []
-            for _ in range(self.DIST_SETS):
-                hs = {}
-                for s in self.pipe.sites:
-                    p = C.c_void_p()
-                    _lib.call("llmc_hessian_create", C.c_void_p(self.ch), C.c_int64(s.d), C.byref(p))
-                    hs[s.name] = p.value
-                self.hd.append(hs)
             self.sc = torch.cuda.Stream(self.pipe.device)
+        while len(self.hd) < n:
+            hs = {}
+            for s in self.pipe.sites:
+                p = C.c_void_p()
+                _lib.call("llmc_hessian_create", C.c_void_p(self.ch), C.c_int64(s.d), C.byref(p))
+                hs[s.name] = p.value
+            self.hd.append(hs)
         return self.hd
 
     def close_dist(self):
@@ -625,12 +645,19 @@ class _Overlap:
         from .distributed import layer_owner, row_shard
 
         pipe = self.pipe
-        sets = self._dist_sets()
+        layers = list(layers)
+        K = min(self.PROLOGUE_LAYERS, len(layers)) if acts_ready else 0
+        if K < 2:
+            K = 0
+        # The prologue's K sets are reused only after their reductions (and owned solves): keep
+        # half the steady-state sets free beyond them.
+        sets = self._dist_sets(max(self.DIST_SETS, K + self.DIST_SETS // 2))
         cur = torch.cuda.current_stream(pipe.device)
         for st in (self.sh, self.ss, self.sc):
             st.wait_stream(cur)
         released = [None] * len(sets)  # event after which set b may be overwritten
         queue = []                      # owned layers waiting to be solved: (index, layer, set, reduce event)
+        order = self.site_order()
 
         def solve(item):
             _, l, b, rd = item
@@ -642,23 +669,13 @@ class _Overlap:
             rows_for = (lambda s: row_shard(sum(m for _, m in s.weights), world, rank)) if rows else None
             released[b] = self._enqueue_solve(l, ptrs, weights, outputs, rd, before_solve, after_solve, rows_for)
 
-        layers = list(layers)
-        for i, l in enumerate(layers):
-            b = i % len(sets)
-            a = acts_for(l)
+        def reduce(i, l, b):
+            # Issued from the Hessian stream (NCCL waits for the accumulation); the copy stream
+            # records when the reduction is done.  Every rank issues the same reductions in the
+            # same order.
             with torch.cuda.stream(self.sh):
-                if released[b] is not None:
-                    self.sh.wait_event(released[b])
-                for s in pipe.sites:
-                    ev = _events() if hess_events is not None else None
-                    if ev:
-                        ev[0].record(self.sh)
-                    pipe._accumulate_into(sets[b][s.name], a[s.name], ready=acts_ready.pop(s.name, None))
-                    if ev:
-                        ev[1].record(self.sh)
-                        hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
                 works = []
-                for s in pipe.sites:
+                for s in order:
                     p = C.c_void_p()
                     _lib.call("llmc_hessian_data", C.c_void_p(sets[b][s.name]), C.byref(p))
                     h = torch.as_tensor(_HView(p.value, s.d), device=pipe.device)
@@ -678,6 +695,33 @@ class _Overlap:
                 released[b] = rd
             while queue and queue[0][0] + self.DIST_LAG <= i:
                 solve(queue.pop(0))
+
+        if K:
+            # Prologue, as on one GPU: layers 0..K-1 accumulate together while this rank's
+            # activations are still arriving, on every SM; their reductions follow.
+            self._hessian_whole_gpu(True)
+            with torch.cuda.stream(self.sh):
+                self._prologue(list(range(K)), sets, [acts_for(l) for l in layers[:K]], acts_ready, hess_events,
+                               lambda s: None)
+            self._hessian_whole_gpu(False)
+            for i in range(K):
+                reduce(i, layers[i], i)
+        for i in range(K, len(layers)):
+            l = layers[i]
+            b = i % len(sets)
+            a = acts_for(l)
+            with torch.cuda.stream(self.sh):
+                if released[b] is not None:
+                    self.sh.wait_event(released[b])
+                for s in order:
+                    ev = _events() if hess_events is not None else None
+                    if ev:
+                        ev[0].record(self.sh)
+                    pipe._accumulate_into(sets[b][s.name], a[s.name], ready=acts_ready.pop(s.name, None))
+                    if ev:
+                        ev[1].record(self.sh)
+                        hess_events.append((ev[0], ev[1], s.d, a[s.name].shape[0]))
+            reduce(i, l, b)
         if queue:
             # Solves enqueued after the last accumulation and reduction have nothing to share
             # the GPU with: persistent grids over every SM.

@@ -1,10 +1,12 @@
-"""Two-rank pipeline job for tests/test_multi_gpu.py (run under torchrun, one GPU per rank).
+"""Pipeline job for tests/test_multi_gpu.py (run under torchrun, one GPU per rank).
 
 Every rank builds the same seeded calibration set and weights, keeps its token shard, and runs
 ``GptqPipeline.run_distributed`` in the mode given on the command line; it then solves the
 whole job on its own GPU from the full token set and compares what it is responsible for
-(its owned layers, or its rows of every layer) with that single-GPU result.  Exit status 0
-means every comparison held."""
+(its owned layers, or its rows of every layer) with that single-GPU result.  With a second
+argument ``copied`` the shard starts in pinned host memory and is copied in chunk by chunk on
+another stream while the job runs (``acts_ready``), over enough layers that the prologue runs
+and its Hessian sets are reused.  Exit status 0 means every comparison held."""
 
 import datetime
 import os
@@ -22,12 +24,13 @@ from llmcompressorsharp_b200.pipeline import GptqPipeline, SiteSpec, _stack_key 
 
 def main():
     mode = sys.argv[1]
+    copied = len(sys.argv) > 2 and sys.argv[2] == "copied"
     world, rank, local = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     sites = [SiteSpec("a", 256, [("w1", 320), ("w2", 64)]), SiteSpec("b", 512, [("w3", 256)])]
-    layers, tokens = 4, 12000
+    layers, tokens = (10 if copied else 4), 12000
     g = torch.Generator().manual_seed(60)
     acts = {s.name: torch.randn(tokens, s.d, generator=g).to(torch.bfloat16).to(dev) for s in sites}
     weights = {l: {w: (torch.randn(m, s.d, generator=g) * 0.02).to(torch.bfloat16).to(dev)
@@ -39,7 +42,23 @@ def main():
     pipe = GptqPipeline(sites, cfg, dev, chunk_rows=4096).enable_overlap(24)
     mine = list(range(layers)) if mode == "rows" else owned_layers(range(layers), world, rank)
     outs = {l: pipe.alloc_outputs(weights[l]) for l in mine}
-    pipe.run_distributed(range(layers), shard, weights, outs, world, rank, shard=mode)
+    ready = None
+    if copied:
+        host = {k: v.cpu().pin_memory() for k, v in shard.items()}
+        shard = {k: torch.empty_like(v) for k, v in shard.items()}
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(torch.cuda.current_stream(dev))
+        ready = {}
+        with torch.cuda.stream(cs):
+            for s in pipe.site_order():
+                T, ready[s.name] = shard[s.name].shape[0], []
+                for r0 in range(0, T, 1500):
+                    r1 = min(T, r0 + 1500)
+                    shard[s.name][r0:r1].copy_(host[s.name][r0:r1], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    ready[s.name].append((r1, ev))
+    pipe.run_distributed(range(layers), shard, weights, outs, world, rank, shard=mode, acts_ready=ready)
     torch.cuda.synchronize()
     pipe.close()
 

@@ -1,5 +1,5 @@
-"""Multi-GPU on two GPUs (skipped when fewer are visible), each rank run by torchrun: the
-layer-owner and the row-sharded partitions of ``GptqPipeline.run_distributed`` against a
+"""Multi-GPU on two GPUs (skipped when fewer are visible; one case runs one rank), each rank run
+by torchrun: the layer-owner and the row-sharded partitions of ``GptqPipeline.run_distributed`` against a
 single-GPU solve of the same job (tests/mgpu_pipeline_job.py), and the C-ABI Hessian
 reductions over NCCL (tests/mgpu_hessian_job.py)."""
 
@@ -29,6 +29,21 @@ def test_two_rank_pipeline_matches_single_gpu(mode):
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "tests", "mgpu_pipeline_job.py"), mode]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("nproc", [1, 2])
+def test_pipeline_with_copied_activations_matches_single_gpu(nproc):
+    """The distributed schedule's prologue (several layers accumulated while the activations
+    are still being copied in) and the reuse of its Hessian sets; one rank runs on one GPU."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < nproc:
+        pytest.skip(f"needs {nproc} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", str(nproc), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "mgpu_pipeline_job.py"), "layers", "copied"]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
 
