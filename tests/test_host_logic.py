@@ -110,3 +110,18 @@ def test_chunk_waits():
     assert chunk_waits([3000, 6000, 9000, 10000], 10000, 4096) == [1, 2, 3]
     # marks finer than chunks and one mark short of the end: the last mark covers the rest
     assert chunk_waits([1, 2, 3, 4, 5], 12, 4) == [3, 4, -1]
+
+
+def test_site_order_widest_first_and_stable():
+    """The overlapped schedule's site order (GptqPipeline.site_order): widest first, ties in the
+    model's order, so every rank of a distributed job issues its reductions in the same order."""
+    from types import SimpleNamespace
+
+    from llmcompressorsharp_b200.pipeline import GptqPipeline, llama_sites
+
+    sites = llama_sites(4096, 14336, 32, 8)
+    order = [s.name for s in GptqPipeline.site_order(SimpleNamespace(sites=sites))]
+    assert order == ["down_in", "attn_in", "o_in", "mlp_in"]
+    wide = llama_sites(8192, 4096, 64, 8)  # intermediate narrower than hidden
+    assert [s.name for s in GptqPipeline.site_order(SimpleNamespace(sites=wide))] == ["attn_in", "o_in", "mlp_in",
+                                                                                        "down_in"]
