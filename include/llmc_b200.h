@@ -106,8 +106,9 @@ llmc_status llmc_set_wait_limit(llmc_ctx* ctx, int64_t tries);
  * matrix still gives the zero factor (pinv(0) = 0, HessianInverseSolver.cs:85-91) and
  * llmc_upper_factor still falls back to U = Hinv (GptqBlockQuantizer.cs:112-118), while any
  * other non-PD input gets a zero factor and LLMC_ERR_NOT_PD from the next llmc_sync (or from
- * any call that reads results back) instead of from the call itself.  on = 0 (the default)
- * restores the synchronous reporting.  No reference counterpart: it lets one host thread
+ * any call that reads results back) instead of from the call itself; the pseudo-inverse
+ * fallback needs the synchronous path, so a host factors such a Hessian again with deferred
+ * errors off.  on = 0 (the default) restores the synchronous reporting.  No reference counterpart: it lets one host thread
  * enqueue a layer's solve while other streams keep running. */
 llmc_status llmc_set_deferred_errors(llmc_ctx* ctx, int32_t on);
 llmc_status llmc_sync(llmc_ctx* ctx);
@@ -168,9 +169,13 @@ llmc_status llmc_hessian_reduce(llmc_hessian* h, void* comm, int32_t root);
  *   want_upper = 1: out = U, upper triangular with U^T U = H'^-1          (GPTQ's factor; computed
  *                   directly as the inverse of the reversed-order Cholesky factor of H')
  * upper_only = 1 reads only the upper triangle of H (as llmc_hessian_data leaves it).
- * Non-positive-definite H': when H' is all zeros the reference's pinv fallback gives 0 and so
- * does this call; any other non-PD input returns LLMC_ERR_NOT_PD.  Reads one flag back to
- * the host (synchronises the stream). */
+ * Non-positive-definite H' (no Cholesky factor): the reference's fallback Hinv = pinv(H')
+ * (HessianInverseSolver.cs:85-91), computed from the symmetric eigendecomposition of H' with
+ * torch.linalg.pinv's default cutoff (|lambda| > eps(fp32) * d * max |lambda| kept); cuSOLVER
+ * is opened at the first such call.  The all-zero matrix gives 0 without the eigensolver.  With
+ * want_upper = 1 the result is then GPTQ's factor of that Hinv: chol(Hinv)^T, or Hinv itself
+ * when it has no Cholesky factor (GptqBlockQuantizer.cs:105-118).  LLMC_ERR_NOT_PD only if the
+ * eigensolver does not converge.  Reads one flag back to the host (synchronises the stream). */
 llmc_status llmc_chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, float damp,
                               int32_t upper_only, float* out, int64_t ldo, int32_t want_upper);
 /* U = chol(Hinv)^T with the reference's fallback U = Hinv when Hinv is not PD

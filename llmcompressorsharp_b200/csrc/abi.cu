@@ -107,8 +107,8 @@ llmc_status device_error_check(llmc_ctx* ctx) {
                     "affected calls are incomplete");
     if (not_pd)
         return fail(LLMC_ERR_NOT_PD, "a damped Hessian factorised with deferred errors was not positive definite "
-                    "(its factor was written as zeros); pseudo-inverse fallback is only available for the "
-                    "all-zero matrix");
+                    "(its factor was written as zeros); the pseudo-inverse fallback runs on the synchronous "
+                    "path: factor it again with deferred errors off");
     return LLMC_OK;
 }
 

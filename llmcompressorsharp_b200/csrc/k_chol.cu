@@ -436,7 +436,7 @@ llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, 
     }
     if (not_pd) {
         // HessianInverseSolver.cs:85-91 falls back to pinv(H').  pinv of the zero matrix is
-        // zero (the no-calibration-data case); anything else is reported.
+        // zero (the no-calibration-data case, answered without the eigensolver).
         LLMC_CUDA_TRY(cudaMemsetAsync(ctx->dflags, 0, 2 * sizeof(int), ctx->stream));
         prep_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(H, d, ldh, upper_only, 0, lam, w.A, d);
         LLMC_TRY(check_launch(ctx, "prep"));
@@ -448,8 +448,12 @@ llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, 
             LLMC_CUDA_TRY(cudaMemset2DAsync(out, ldo * sizeof(float), 0, d * sizeof(float), d, ctx->stream));
             return LLMC_OK;
         }
-        return fail(LLMC_ERR_NOT_PD, "damped Hessian (d=%lld) is not positive definite; pseudo-inverse fallback "
-                    "is only available for the all-zero matrix", (long long)d);
+        LLMC_TRY(pinv_symmetric(ctx, w.A, w.I, d, out, ldo));
+        if (!want_upper) return LLMC_OK;
+        // GPTQ's factor of that Hinv (GptqBlockQuantizer.cs:105-118): chol(Hinv)^T, or Hinv itself
+        // when it has no Cholesky factor (the usual case for a pseudo-inverse).  In place: the
+        // factorisation reads its input into the workspace first.
+        return upper_factor(ctx, out, d, ldo, out, ldo);
     }
     if (want_upper) {
         remap_kernel<<<grid_for(ctx, dd), 256, 0, ctx->stream>>>(w.I, d, d, 0, out, ldo);

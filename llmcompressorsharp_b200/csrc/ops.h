@@ -50,6 +50,9 @@ inline int64_t n_groups(int strategy, int64_t n, int64_t gs) {
 llmc_status chol_inverse(llmc_ctx* ctx, const float* H, int64_t d, int64_t ldh, float damp, int upper_only,
                          float* out, int64_t ldo, int want_upper);
 llmc_status upper_factor(llmc_ctx* ctx, const float* hinv, int64_t d, int64_t ldh, float* out, int64_t ldo);
+// pinv of a symmetric matrix given by the lower triangle of A (d x d row-major, overwritten),
+// torch.linalg.pinv's default cutoff; B is d x d scratch (pinv.cu).  Synchronises the stream.
+llmc_status pinv_symmetric(llmc_ctx* ctx, float* A, float* B, int64_t d, float* out, int64_t ldo);
 
 // ---- per-token activation quantisation (k_act.cu) ------------------------------------------
 llmc_status act_quant_per_token(llmc_ctx* ctx, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,

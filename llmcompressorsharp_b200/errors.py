@@ -35,8 +35,9 @@ class NotSupportedError(LlmcError, NotImplementedError):
 
 
 class NotPositiveDefiniteError(LlmcError):
-    """Cholesky failed and no device fallback applies (HessianInverseSolver's pinv path for a
-    non-zero matrix)."""
+    """A Hessian factorised with deferred errors had no Cholesky factor (factoring it again
+    synchronously takes HessianInverseSolver's pinv fallback), or the eigensolver inside that
+    fallback did not converge."""
 
     status = 4
 

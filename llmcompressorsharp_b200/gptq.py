@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 from ._device import ctx, supported_dtype, target_device, to_device
-from .errors import ArgumentError, InvalidOperationError, NotSupportedError
+from .errors import ArgumentError, InvalidOperationError, NotPositiveDefiniteError, NotSupportedError
 from .hessian import ActivationHookManager, HessianAccumulator, HessianInverseSolver, upper_factor
 from .session import CompressionState, ModifierBase
 
@@ -248,7 +248,10 @@ class GPTQModifier(ModifierBase):
         alias = self._alias
         # Factor every distinct Hessian first, with the device context's errors deferred: the
         # factorisations are enqueued back to back (none reads a flag back to the host), and one
-        # llmc_sync per device then raises the first failure before any weight is replaced.
+        # llmc_sync per device then reports whether any Hessian had no Cholesky factor.  Those
+        # devices factor their Hessians again synchronously, which takes the reference's
+        # pseudo-inverse fallback (HessianInverseSolver.cs:85-91); every weight is replaced only
+        # after all factors exist.
         ucache: dict[int, torch.Tensor] = {}
         srcs = {}
         for acc in self._acc.values():
@@ -260,13 +263,20 @@ class GPTQModifier(ModifierBase):
         for dev, items in by_dev.items():
             c = C.c_void_p(ctx(dev))
             _lib.call("llmc_set_deferred_errors", c, C.c_int32(1))
+            redo = False
             try:
                 with torch.cuda.device(dev):
                     for key, src in items:
                         ucache[key] = HessianInverseSolver.upper(src.raw(), self.config.dampening_frac, upper_only=True)
                 _lib.call("llmc_sync", c)
+            except NotPositiveDefiniteError:
+                redo = True
             finally:
                 _lib.call("llmc_set_deferred_errors", c, C.c_int32(0))
+            if redo:
+                with torch.cuda.device(dev):
+                    for key, src in items:
+                        ucache[key] = HessianInverseSolver.upper(src.raw(), self.config.dampening_frac, upper_only=True)
         for wname, acc in self._acc.items():
             key = id(alias.get(id(acc), acc))
             w = state.named_weights[wname]

@@ -79,10 +79,12 @@ def test_deferred_non_pd_reported_at_sync_and_cleared():
         assert "not positive definite" in _lib.last_error()
         assert torch.count_nonzero(u) == 0
         assert lib.llmc_sync(c) == 0  # the word was cleared
-        # the synchronous path reports the same input at the call
+        # the synchronous path takes the pinv fallback instead: pinv(-I) = -I, which has no
+        # Cholesky factor, so U = Hinv (HessianInverseSolver.cs:85-91, GptqBlockQuantizer.cs:112-118)
         assert lib.llmc_set_deferred_errors(c, 0) == 0
-        st, _ = _upper(lib, c, h, damp=0.0)
-        assert st == NOT_PD
+        st, u = _upper(lib, c, h, damp=0.0)
+        assert st == 0, _lib.last_error()
+        assert float((u + torch.eye(256, device="cuda")).abs().max()) < 1e-5
     finally:
         lib.llmc_destroy(c)
 
