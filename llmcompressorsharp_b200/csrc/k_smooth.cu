@@ -39,8 +39,9 @@ __global__ void __launch_bounds__(NT) col_absmax_kernel(const T* x, int64_t rows
         atomicMax(reinterpret_cast<int*>(out + c0 + i), __float_as_int(mx[i]));
 }
 
-// MathF.Pow result: pow evaluated in double and rounded once to float (the correctly
-// rounded single-precision power that the host C library returns in practice).
+// MathF.Pow result taken as the correctly rounded single-precision power: pow evaluated in
+// double and rounded once to float.  The host C library's powf usually returns the same value
+// but does not guarantee it, so agreement with the reference is exact only where it does.
 __device__ __forceinline__ float powf_cr(float a, float b) { return (float)pow((double)a, (double)b); }
 
 __global__ void smooth_scales_kernel(const float* act, const float* wmax, int64_t n, float alpha, float* s) {
