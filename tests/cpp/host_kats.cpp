@@ -110,6 +110,15 @@ std::vector<std::pair<std::string, std::function<void(Context&)>>> tests() {
                                                                    0.01f).ToHost();
                      for (float v : h) Assert(v == 0.f, "zero");
                  }});
+    t.push_back({"HessianInverseSolver.SingularFallsBackToPinv", [](Context& c) {  // :85-91
+                     // diag(2, 0, 4, 0) has no Cholesky factor; pinv keeps the non-zero eigenvalues.
+                     std::vector<float> h(16, 0.f);
+                     h[0] = 2.f;
+                     h[10] = 4.f;
+                     const auto p = HessianInverseSolver::Compute(c, DeviceTensor::FromHost(h, {4, 4}), 0.f).ToHost();
+                     for (int i = 0; i < 16; i++)
+                         Near(p[i], i == 0 ? 0.5f : (i == 10 ? 0.25f : 0.f), 1e-6f, "pinv(diag(2, 0, 4, 0))");
+                 }});
     t.push_back({"HessianInverseSolver.NonSquareThrows", [](Context& c) {  // :72-78
                      Throws<ArgumentException>(
                          [&] { HessianInverseSolver::Compute(c, DeviceTensor::FromHost(std::vector<float>(12, 1.f), {3, 4}), 0.01f); },

@@ -387,6 +387,15 @@ def test_gptq_no_batches_is_rtn():  # GPTQModifierTests.cs:92-110: H = 0 -> pinv
     assert torch.equal(wq, out)
 
 
+def test_inverse_singular_is_pinv():  # derived KAT, HessianInverseSolver.cs:85-91: no Cholesky factor -> pinv(H')
+    h = torch.diag(torch.tensor([2.0, 0.0, 4.0, 0.0]))
+    assert torch.allclose(hessian.hessian_inverse(h, 0.0), torch.diag(torch.tensor([0.5, 0.0, 0.25, 0.0])), atol=1e-7)
+    neg = -torch.eye(3)  # indefinite: pinv is the inverse, and U falls back to Hinv (GptqBlockQuantizer.cs:112-118)
+    hinv = hessian.hessian_inverse(neg, 0.0)
+    assert torch.allclose(hinv, -torch.eye(3), atol=1e-7)
+    assert torch.equal(hessian.upper_factor(hinv), hinv)
+
+
 def test_gptq_identity_hinv_is_rtn():  # derived KAT: Hinv = I -> U = I -> no cross-column coupling
     g = torch.Generator().manual_seed(4)
     w = torch.randn(16, 40, generator=g)
