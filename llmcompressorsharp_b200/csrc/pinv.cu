@@ -6,7 +6,11 @@
 // symmetric A the singular values are the |lambda| of its eigenvalues and the result is
 //   pinv(A) = sum_k [|lambda_k| > tol] v_k v_k^T / lambda_k,
 // which is what this computes: eigenvalues and eigenvectors from cuSOLVER's symmetric
-// eigensolver (syevd), then one scaling kernel and one 3xTF32 GEMM (V^T (D V)).  cuSOLVER is
+// eigensolver (syevd), then one scaling kernel and one 3xTF32 GEMM (V^T (D V)).  Rows and
+// columns of an exactly zero row of the matrix (a dead input channel) are set to exactly zero,
+// their value in exact arithmetic (the eigensolver, like an SVD, leaves rounding residue there),
+// so that GPTQ's later Cholesky of the result meets a zero pivot at that channel and takes the
+// U = Hinv fallback, as exact arithmetic does.  cuSOLVER is
 // opened with dlopen at the first call, so the library has no link-time dependency on it;
 // cusolverDn.h supplies the types only.  A rare, synchronous path: it waits for the eigensolver's
 // status and allocates its own scratch.
@@ -73,6 +77,28 @@ __global__ void pinv_scale_kernel(const float* V, const float* w, int64_t d, flo
     }
 }
 
+// nz[i] = 1 when row i of the symmetric matrix (its lower triangle in A) holds a non-zero entry.
+__global__ void pinv_nonzero_rows_kernel(const float* A, int64_t d, int* nz) {
+    const int64_t total = d * d;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / d, j = t % d;
+        if (j <= i && A[t] != 0.f) {
+            nz[i] = 1;
+            nz[j] = 1;
+        }
+    }
+}
+
+// A row (and column) that is exactly zero in the matrix is an exact null direction, so it is
+// exactly zero in the pseudo-inverse; the eigensolver leaves rounding residue there instead.
+__global__ void pinv_zero_dead_kernel(const int* nz, int64_t d, float* out, int64_t ldo) {
+    const int64_t total = d * d;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t / d, j = t % d;
+        if (!nz[i] || !nz[j]) out[i * ldo + j] = 0.f;
+    }
+}
+
 struct SolverHandle {
     const SolverApi* api = nullptr;
     cusolverDnHandle_t h = nullptr;
@@ -109,9 +135,15 @@ llmc_status pinv_symmetric(llmc_ctx* ctx, float* A, float* B, int64_t d, float* 
     const cublasFillMode_t uplo = CUBLAS_FILL_MODE_UPPER;
     DeviceScratch wbuf, wsp;
     const size_t w_floats = ((size_t)d + 63) / 64 * 64;
-    LLMC_CUDA_TRY(cudaMalloc(&wbuf.p, w_floats * sizeof(float) + 64));
+    LLMC_CUDA_TRY(cudaMalloc(&wbuf.p, 2 * w_floats * sizeof(float) + 64));
     float* w = static_cast<float*>(wbuf.p);
-    int* info = reinterpret_cast<int*>(w + w_floats);
+    int* nz = reinterpret_cast<int*>(w + w_floats);
+    int* info = nz + w_floats;
+    const int64_t blocks = std::max<int64_t>(
+        std::min<int64_t>(((int64_t)d * d + 255) / 256, (int64_t)ctx->sm_count * 8), 1);
+    LLMC_CUDA_TRY(cudaMemsetAsync(nz, 0, (size_t)d * sizeof(int), ctx->stream));
+    pinv_nonzero_rows_kernel<<<(int)blocks, 256, 0, ctx->stream>>>(A, d, nz);
+    LLMC_TRY(check_launch(ctx, "pinv_nonzero_rows"));
     int lwork = 0;
     if (sh.api->syevd_buffer(sh.h, CUSOLVER_EIG_MODE_VECTOR, uplo, n, A, n, w, &lwork) != CUSOLVER_STATUS_SUCCESS)
         return fail(LLMC_ERR_CUDA, "pinv: cusolverDnSsyevd_bufferSize failed");
@@ -126,13 +158,14 @@ llmc_status pinv_symmetric(llmc_ctx* ctx, float* A, float* B, int64_t d, float* 
         return fail(LLMC_ERR_NOT_PD, "damped Hessian (d=%lld) is not positive definite and its pseudo-inverse "
                     "failed: the symmetric eigensolver did not converge (info %d)", (long long)d, hinfo);
     const float rtol = (float)((double)FLT_EPSILON * (double)d);
-    const int64_t blocks = std::min<int64_t>(((int64_t)d * d + 255) / 256, (int64_t)ctx->sm_count * 8);
-    pinv_scale_kernel<<<(int)std::max<int64_t>(blocks, 1), 256, 0, ctx->stream>>>(A, w, d, rtol, B);
+    pinv_scale_kernel<<<(int)blocks, 256, 0, ctx->stream>>>(A, w, d, rtol, B);
     LLMC_TRY(check_launch(ctx, "pinv_scale"));
     // out = V^T (D V), V with the eigenvectors as rows.
     GemmArgs g{d, d, d, A, d, 1, LLMC_DTYPE_F32, B, d, 0, LLMC_DTYPE_F32, out, ldo, 1.f, 0.f};
     LLMC_TRY(gemm_f32(ctx, g));
-    // pinv_scale_kernel reads the eigenvalues from wbuf, freed on return.
+    pinv_zero_dead_kernel<<<(int)blocks, 256, 0, ctx->stream>>>(nz, d, out, ldo);
+    LLMC_TRY(check_launch(ctx, "pinv_zero_dead"));
+    // The kernels read the eigenvalues and the row flags from wbuf, freed on return.
     LLMC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     return LLMC_OK;
 }

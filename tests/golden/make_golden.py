@@ -6,7 +6,7 @@ known-answer tests (tests/test_oracle_kats.py).  The fixtures freeze those outpu
 suite checks that the oracle still reproduces them, and the GPU suite checks the CUDA path
 against them without running the oracle.
 
-    python tests/golden/make_golden.py      # rewrites tests/golden/*.npz
+    python tests/golden/make_golden.py [name ...]   # rewrites tests/golden/*.npz (or those named)
 """
 
 import os
@@ -18,7 +18,8 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
-from oracle import gptq as o_gptq, hessian as o_hess, rtn as o_rtn, sparsegpt as o_sp  # noqa: E402
+from oracle import awq as o_awq, gptq as o_gptq, hessian as o_hess, pertoken as o_pt, rtn as o_rtn  # noqa: E402
+from oracle import smoothquant as o_sq, sparsegpt as o_sp  # noqa: E402
 
 
 def gen(seed):
@@ -55,14 +56,52 @@ def cases():
     # SparseGPT 2:4 on the same weight and factor
     ps, pm = o_sp.sparsegpt_prune_u(wg, ug, 128, 0.5, 2, 4)
     out["sparsegpt_2_4"] = {"w": wg.numpy(), "u": ug.numpy(), "out": ps.numpy(), "mask": pm.numpy()}
+    # the pinv fallback: an undamped Hessian with a dead input channel, d = 96
+    xs = torch.randn(400, 96, generator=gen(7))
+    xs[:, 11] = 0.0
+    hs = xs.t() @ xs
+    hinv_s = o_hess.hessian_inverse(hs, 0.0)
+    out["pinv_dead_channel"] = {"h": hs.numpy(), "hinv": hinv_s.numpy(), "u": o_hess.upper_factor(hinv_s).numpy()}
+    # GPTQ with activation order and static groups (asym int4 g64) on a 48 x 192 bf16 weight
+    xa = torch.randn(768, 192, generator=gen(8)) * torch.exp(0.5 * torch.randn(192, generator=gen(9)))
+    ha = xa.t() @ xa
+    wa = (torch.randn(48, 192, generator=gen(10)) * 0.02).to(torch.bfloat16)
+    acfg = o_gptq.GPTQConfig(num_bits=4, symmetric=False, strategy="group", group_size=64, block_size=128)
+    wq_a, c_a, s_a, z_a, p_a = o_gptq.gptq_quantize_act_order(wa, ha, 0.01, acfg)
+    out["gptq_act_order_g64"] = {"w": wa.float().numpy(), "h": ha.numpy(), "wq": wq_a.numpy(), "codes": c_a.numpy(),
+                                 "scales": np.asarray(s_a, np.float32), "zps": np.asarray(z_a, np.int64),
+                                 "perm": p_a.numpy()}
+    # per-token int8 (symmetric) of bf16 activations with outlier channels and an all-zero row
+    xt = torch.randn(96, 640, generator=gen(11)) * torch.where(torch.rand(640, generator=gen(12)) < 0.02, 40.0, 1.0)
+    xt[5] = 0.0
+    xt = xt.to(torch.bfloat16)
+    deq_t, c_t, s_t, z_t = o_pt.quantize_per_token(xt, 8, True)
+    out["per_token_int8_sym"] = {"x": xt.float().numpy(), "deq": deq_t.float().numpy(), "codes": c_t.numpy(),
+                                 "scales": np.asarray(s_t, np.float32), "zps": np.asarray(z_t, np.int64)}
+    # SmoothQuant alpha = 0.5 on bf16 layer norm / q-k-v weights
+    am = (torch.rand(256, generator=gen(13)) * 3 + 0.1) * torch.where(torch.rand(256, generator=gen(14)) < 0.03, 25.0, 1.0)
+    sw = (1.0 + 0.1 * torch.randn(256, generator=gen(15))).to(torch.bfloat16)
+    bw = (torch.randn(384, 256, generator=gen(16)) * 0.02).to(torch.bfloat16)
+    ns, nb, sc = o_sq.apply_mapping(sw, bw, am.numpy(), 0.5)
+    out["smoothquant_a05"] = {"act_max": am.numpy(), "smooth": sw.float().numpy(), "balance": bw.float().numpy(),
+                              "new_smooth": ns.float().numpy(), "new_balance": nb.float().numpy(), "s": sc}
+    # AWQ: 20-point grid search, asym int4 g128, on a 64 x 512 bf16 weight
+    ww = (torch.randn(64, 512, generator=gen(17)) * 0.02).to(torch.bfloat16)
+    aw = (torch.rand(512, generator=gen(18)) * 3 + 0.1) * torch.where(torch.rand(512, generator=gen(19)) < 0.02, 30.0, 1.0)
+    rs, rk, rmse = o_awq.awq_search(ww, aw.numpy(), 20, o_rtn.RtnConfig(4, False, "group", group_size=128))
+    out["awq_g128"] = {"w": ww.float().numpy(), "act_max": aw.numpy(), "s": np.asarray(rs, np.float32),
+                       "k": np.asarray(rk, np.int64), "mse": np.asarray(rmse, np.float64)}
     return out
 
 
-def main():
+def main(names=None):
+    """Writes every fixture, or only ``names`` (so that the others keep their bytes)."""
     for name, arrays in cases().items():
+        if names and name not in names:
+            continue
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)
         print(name, {k: v.shape for k, v in arrays.items()})
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])
