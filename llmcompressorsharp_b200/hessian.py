@@ -90,15 +90,18 @@ class HessianAccumulator:
 
 
 class HessianInverseSolver:
-    """HessianInverseSolver.Compute (:44-92) on the device."""
+    """HessianInverseSolver.Compute (:44-108) on the device."""
 
     @staticmethod
     def compute(hessian: torch.Tensor, damping_frac: float) -> torch.Tensor:
+        """(H + damp*mean(diag H)*I)^-1; pinv of that matrix when it has no Cholesky factor (:85-91)."""
         return _chol(hessian, damping_frac, want_upper=False)
 
     @staticmethod
     def upper(hessian: torch.Tensor, damping_frac: float, upper_only: bool = False) -> torch.Tensor:
-        """U with U^T U = (H + damp*mean(diag H)*I)^-1 in one factorisation (the factor GPTQ needs)."""
+        """U with U^T U = (H + damp*mean(diag H)*I)^-1 in one factorisation (the factor GPTQ needs).
+        Without a Cholesky factor: GPTQ's factor of the pinv fallback, chol(Hinv)^T or Hinv itself
+        (GptqBlockQuantizer.cs:105-118)."""
         return _chol(hessian, damping_frac, want_upper=True, upper_only=upper_only)
 
 
