@@ -12,6 +12,9 @@
  *   PerChannelMinMaxObserver  PerChannelMinMaxObserver.cs:15-112
  *   FakeQuantize              FakeQuantize.cs:22-38
  *   Int4PackedTensor          Int4PackedTensor.cs:47-161
+ *   TargetMatcher, ModifierBase, CompressionState (Core/Modifiers, Core/Compression)
+ *   GPTQModifier              GPTQModifier.cs:28-155
+ *   RtnModifier               RtnModifier.cs:44-122
  * Tensors are DeviceTensor: a device buffer owned by the host code (the role TorchSharp's
  * CUDA tensors play for the C# primitives), row-major, float32 / bfloat16 / float16.
  * Exceptions mirror .NET's: ArgumentNullException, ArgumentException,
@@ -31,6 +34,7 @@
 #include <string>
 #include <utility>
 #include <limits>
+#include <memory>
 #include <vector>
 
 #include "llmc_b200.h"
@@ -227,6 +231,12 @@ class HessianAccumulator {
         return n;
     }
     int InFeatures() const { return d_; }
+    // The accumulator's own fp32 [d, d] buffer (upper triangle authoritative), no copy.
+    const float* Data() const {
+        float* p = nullptr;
+        Check(llmc_hessian_data(h_, &p));
+        return p;
+    }
     // Multi-GPU: sum the partial H and sample counts of a token-sharded calibration set over
     // an NCCL communicator (an ncclComm_t), on every rank or onto `root`.
     void AllReduce(void* ncclComm) { Check(llmc_hessian_allreduce(h_, ncclComm)); }
@@ -738,6 +748,258 @@ class NcclCommunicator {
 
    private:
     void* comm_ = nullptr;
+};
+
+// ---- modifiers (Core/Modifiers, Core/Compression, Algorithms/Gptq, Algorithms/Rtn) ---------------
+struct ModifierLifecycleException : InvalidOperationException {
+    explicit ModifierLifecycleException(const std::string& m) : InvalidOperationException(m) {}
+};
+
+// TargetMatcher.cs:22-86: ignore patterns win; no targets matches every name; a pattern without
+// '*' matches exactly, and '*' matches any run of characters (dots and slashes included).
+struct TargetMatcher {
+    static bool MatchesPattern(const std::string& name, const std::string& pattern) {
+        if (pattern.empty()) return false;
+        if (pattern.find('*') == std::string::npos) return name == pattern;
+        // Glob match with backtracking to the last '*'.
+        size_t n = 0, p = 0, star = std::string::npos, mark = 0;
+        while (n < name.size()) {
+            if (p < pattern.size() && pattern[p] == '*') {
+                star = p++;
+                mark = n;
+            } else if (p < pattern.size() && pattern[p] == name[n]) {
+                p++;
+                n++;
+            } else if (star != std::string::npos) {
+                p = star + 1;
+                n = ++mark;
+            } else {
+                return false;
+            }
+        }
+        while (p < pattern.size() && pattern[p] == '*') p++;
+        return p == pattern.size();
+    }
+    static bool Matches(const std::string& name, const std::vector<std::string>& targets,
+                        const std::vector<std::string>& ignore) {
+        for (const auto& pat : ignore)
+            if (MatchesPattern(name, pat)) return false;
+        if (targets.empty()) return true;
+        for (const auto& pat : targets)
+            if (MatchesPattern(name, pat)) return true;
+        return false;
+    }
+};
+
+// CompressionState.cs:17-65.  NamedWeights keep the host's insertion order, as the C# dictionary
+// enumerates.  The C# NamedModules (modules the modifiers hook) become the layer names whose
+// inputs the host feeds to the modifiers' Observe(layerName, x): the call the hook lambda makes
+// (ActivationHookManager.cs:47-51).
+struct CompressionState {
+    std::vector<std::pair<std::string, DeviceTensor>> NamedWeights;
+    std::vector<std::string> NamedModules;
+    bool HasNamedModules = false;
+
+    DeviceTensor& Weight(const std::string& name) {
+        for (auto& kv : NamedWeights)
+            if (kv.first == name) return kv.second;
+        throw ArgumentException("no weight named " + name);
+    }
+    bool HasModule(const std::string& layer) const {
+        for (const auto& m : NamedModules)
+            if (m == layer) return true;
+        return false;
+    }
+};
+
+// ModifierBase.cs:47-180: the lifecycle checks and the hooks a modifier implements.
+class ModifierBase {
+   public:
+    ModifierBase(std::string name, std::vector<std::string> targets, std::vector<std::string> ignore)
+        : name_(std::move(name)), targets_(std::move(targets)), ignore_(std::move(ignore)) {}
+    virtual ~ModifierBase() = default;
+    const std::string& Name() const { return name_; }
+
+    void Initialize(CompressionState& state) {
+        if (initialized_) throw ModifierLifecycleException("Modifier '" + name_ + "' was initialized twice.");
+        initialized_ = true;
+        OnInitialize(state);
+    }
+    void OnStart(CompressionState& state) {
+        EnsureInitialized();
+        if (started_) throw ModifierLifecycleException("Modifier '" + name_ + "' was started twice.");
+        started_ = true;
+        OnStartCore(state);
+    }
+    void OnBatch(CompressionState& state) {
+        EnsureStarted();
+        if (ended_) throw ModifierLifecycleException("Modifier '" + name_ + "' received a batch after OnEnd.");
+        OnBatchCore(state);
+    }
+    void OnEnd(CompressionState& state) {
+        EnsureStarted();
+        if (ended_) throw ModifierLifecycleException("Modifier '" + name_ + "' was ended twice.");
+        ended_ = true;
+        OnEndCore(state);
+    }
+    void Finalize(CompressionState& state) {
+        if (!initialized_) throw ModifierLifecycleException("Modifier '" + name_ + "' was finalized before being initialized.");
+        if (finalized_) throw ModifierLifecycleException("Modifier '" + name_ + "' was finalized twice.");
+        finalized_ = true;
+        OnFinalizeCore(state);
+    }
+
+   protected:
+    virtual void OnInitialize(CompressionState&) {}
+    virtual void OnStartCore(CompressionState&) {}
+    virtual void OnBatchCore(CompressionState&) {}
+    virtual void OnEndCore(CompressionState&) = 0;
+    virtual void OnFinalizeCore(CompressionState&) {}
+    std::vector<std::string> TargetedNames(const CompressionState& state) const {
+        std::vector<std::string> out;
+        for (const auto& kv : state.NamedWeights)
+            if (TargetMatcher::Matches(kv.first, targets_, ignore_)) out.push_back(kv.first);
+        return out;
+    }
+
+   private:
+    void EnsureInitialized() const {
+        if (!initialized_) throw ModifierLifecycleException("Modifier '" + name_ + "' was used before Initialize.");
+    }
+    void EnsureStarted() const {
+        EnsureInitialized();
+        if (!started_) throw ModifierLifecycleException("Modifier '" + name_ + "' was used before OnStart.");
+    }
+    std::string name_;
+    std::vector<std::string> targets_, ignore_;
+    bool initialized_ = false, started_ = false, ended_ = false, finalized_ = false;
+};
+
+// GPTQModifier.cs:28-155: one accumulator per targeted weight whose layer the host observes;
+// OnEnd factors every Hessian and replaces each weight by its fp32 fake-quantised solve.  The
+// factorisations are enqueued with the context's errors deferred and checked once; a Hessian
+// without a Cholesky factor is factored again synchronously, which takes the reference's pinv
+// fallback (HessianInverseSolver.cs:85-91).
+class GPTQModifier : public ModifierBase {
+   public:
+    GPTQModifier(Context& ctx, GPTQConfig config, std::vector<std::string> targets = {},
+                 std::vector<std::string> ignore = {})
+        : ModifierBase("GPTQ", std::move(targets), std::move(ignore)), ctx_(&ctx), cfg_(config) {}
+
+    // The hook: x is the input of layer `layerName` ([..., inFeatures]).
+    void Observe(const std::string& layerName, const DeviceTensor& x) {
+        for (auto& a : acc_)
+            if (a.first == layerName + ".weight" || a.first == layerName) a.second->Update(x);
+    }
+
+   protected:
+    void OnInitialize(CompressionState&) override {
+        if (cfg_.ActOrder)
+            throw NotSupportedException("GPTQConfig.ActOrder=true is not yet implemented. Column reordering by Hessian "
+                                        "diagonal is deferred to a future release.");
+    }
+    void OnStartCore(CompressionState& state) override {
+        if (!state.HasNamedModules)
+            throw InvalidOperationException("GPTQModifier requires CompressionState.NamedModules to be populated.");
+        acc_.clear();
+        for (const auto& name : TargetedNames(state)) {
+            const std::string suffix = ".weight";
+            const bool has = name.size() >= suffix.size() && name.compare(name.size() - suffix.size(), suffix.size(), suffix) == 0;
+            const std::string layer = has ? name.substr(0, name.size() - suffix.size()) : name;
+            if (!state.HasModule(layer)) continue;
+            const DeviceTensor& w = state.Weight(name);
+            acc_.emplace_back(name, std::make_unique<HessianAccumulator>(*ctx_, (int)w.last()));
+        }
+    }
+    void OnEndCore(CompressionState& state) override {
+        std::vector<DeviceTensor> us;
+        for (auto& a : acc_) us.emplace_back(std::vector<int64_t>{a.second->InFeatures(), a.second->InFeatures()}, DType::Float32);
+        auto factor_all = [&] {
+            for (size_t i = 0; i < acc_.size(); i++) {
+                const int64_t d = acc_[i].second->InFeatures();
+                Check(llmc_chol_inverse(ctx_->get(), acc_[i].second->Data(), d, d, cfg_.DampeningFrac, 1,
+                                        static_cast<float*>(us[i].data()), d, 1));
+            }
+        };
+        ctx_->SetDeferredErrors(true);
+        bool redo = false;
+        try {
+            factor_all();
+            ctx_->Synchronize();
+        } catch (const LlmcException& e) {
+            if (e.status != LLMC_ERR_NOT_PD) {
+                ctx_->SetDeferredErrors(false);
+                throw;
+            }
+            redo = true;
+        }
+        ctx_->SetDeferredErrors(false);
+        if (redo) factor_all();
+        const llmc_qconfig c = cfg_.ToC();
+        for (size_t i = 0; i < acc_.size(); i++) {
+            DeviceTensor& w = state.Weight(acc_[i].first);
+            const int64_t m = w.shape()[0], n = w.shape()[1];
+            const int64_t per_row = cfg_.Strategy == QuantizationStrategy::Group ? (n + cfg_.GroupSize - 1) / cfg_.GroupSize : 1;
+            const int64_t nparams = cfg_.Strategy == QuantizationStrategy::PerTensor ? 1 : m * per_row;
+            DeviceTensor scales({nparams}, DType::Float32), zps({nparams}, DType::Float32);
+            DeviceTensor out({m, n}, DType::Float32);
+            Check(llmc_gptq_quantize(ctx_->get(), w.data(), (int32_t)w.dtype(), m, n, n,
+                                     static_cast<const float*>(us[i].data()), n, &c, static_cast<float*>(out.data()), n,
+                                     nullptr, static_cast<float*>(scales.data()), static_cast<int32_t*>(zps.data())));
+            w = std::move(out);
+        }
+    }
+    void OnFinalizeCore(CompressionState&) override { acc_.clear(); }
+
+   private:
+    Context* ctx_;
+    GPTQConfig cfg_;
+    std::vector<std::pair<std::string, std::unique_ptr<HessianAccumulator>>> acc_;
+};
+
+// RtnModifier.cs:44-122: each targeted weight replaced by its fake-quantised value in its dtype.
+// Any rank: per tensor the weight is one [1, numel] row; per channel (axis 0) it is
+// [shape[0], numel / shape[0]], one channel a row; the group extension needs a 2-D weight.
+class RtnModifier : public ModifierBase {
+   public:
+    RtnModifier(Context& ctx, RtnConfig config, std::vector<std::string> targets = {},
+                std::vector<std::string> ignore = {})
+        : ModifierBase("RTN", std::move(targets), std::move(ignore)), ctx_(&ctx), cfg_(config) {}
+
+   protected:
+    void OnEndCore(CompressionState& state) override {
+        for (const auto& name : TargetedNames(state)) {
+            if (cfg_.Strategy == QuantizationStrategy::PerToken)  // RtnModifier.cs:69-70
+                throw NotSupportedException("PerToken strategy applies to activations, not weights.");
+            DeviceTensor& w = state.Weight(name);
+            const int64_t numel = w.numel();
+            if (numel == 0) continue;
+            int64_t m = 1, n = numel;
+            if (cfg_.Strategy == QuantizationStrategy::PerChannel) {
+                m = w.dim() == 0 ? 1 : w.shape()[0];
+                n = numel / m;
+            } else if (cfg_.Strategy == QuantizationStrategy::Group) {
+                if (w.dim() != 2) throw ArgumentException("the group strategy needs a 2-D weight");
+                m = w.shape()[0];
+                n = w.shape()[1];
+            }
+            const llmc_qconfig c = cfg_.ToC();
+            const int64_t per_row =
+                cfg_.Strategy == QuantizationStrategy::Group ? (n + cfg_.GroupSize - 1) / cfg_.GroupSize : 1;
+            const int64_t nparams = cfg_.Strategy == QuantizationStrategy::PerTensor ? 1 : m * per_row;
+            const int64_t row_bytes = cfg_.NumBits <= 4 ? (n + 1) / 2 : n;
+            DeviceBytes codes((size_t)(m * row_bytes)), scales((size_t)nparams * 4), zps((size_t)nparams * 4);
+            DeviceTensor deq(w.shape(), w.dtype());
+            Check(llmc_rtn_quantize(ctx_->get(), w.data(), (int32_t)w.dtype(), m, n, n, &c,
+                                    static_cast<uint8_t*>(codes.data()), static_cast<float*>(scales.data()),
+                                    static_cast<int32_t*>(zps.data()), deq.data()));
+            w = std::move(deq);
+        }
+    }
+
+   private:
+    Context* ctx_;
+    RtnConfig cfg_;
 };
 
 }  // namespace llmcs

@@ -313,6 +313,140 @@ std::vector<std::pair<std::string, std::function<void(Context&)>>> tests() {
                      NoAllocObserver::MinMax(c, DeviceTensor::FromHost({-1, 9}, {1, 2}), mn, mx, true);
                      Assert(mn.ToHost()[0] == -3.f && mx.ToHost()[0] == 9.f, "running min / max");
                  }});
+    // ---- TargetMatcher / ModifierBase / GPTQModifierTests.cs / RtnModifierTests.cs / EndToEndRecipeTests.cs
+    t.push_back({"TargetMatcher.GlobsAndIgnore", [](Context&) {  // TargetMatcher.cs:22-86
+                     Assert(TargetMatcher::Matches("model.layers.0.q_proj.weight", {"model.*"}, {}), "glob");
+                     Assert(!TargetMatcher::Matches("model.lm_head.weight", {"model.*"}, {"model.lm_head.*"}), "ignore wins");
+                     Assert(TargetMatcher::Matches("anything", {}, {}), "no targets match all");
+                     Assert(TargetMatcher::Matches("a.b", {"a.b"}, {}) && !TargetMatcher::Matches("a.bc", {"a.b"}, {}), "exact");
+                     Assert(TargetMatcher::Matches("x.q_proj.weight", {"*q_proj*"}, {}), "two stars");
+                     Assert(!TargetMatcher::Matches("x", {""}, {}), "empty pattern");
+                 }});
+    t.push_back({"ModifierBase.LifecycleOrder", [](Context& c) {  // ModifierBase.cs:47-180
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("w", DeviceTensor::FromHost({1, 2}, {2}));
+                     RtnModifier m(c, RtnConfig{8, true, QuantizationStrategy::PerTensor});
+                     Throws<ModifierLifecycleException>([&] { m.OnStart(st); }, "start before initialize");
+                     m.Initialize(st);
+                     Throws<ModifierLifecycleException>([&] { m.Initialize(st); }, "initialize twice");
+                     Throws<ModifierLifecycleException>([&] { m.OnEnd(st); }, "end before start");
+                     m.OnStart(st);
+                     m.OnEnd(st);
+                     Throws<ModifierLifecycleException>([&] { m.OnBatch(st); }, "batch after end");
+                     m.Finalize(st);
+                     Throws<ModifierLifecycleException>([&] { m.Finalize(st); }, "finalize twice");
+                 }});
+    t.push_back({"RtnModifier.TargetsAndIgnore", [](Context& c) {  // EndToEndRecipeTests.cs:41-101 (its RTN stage)
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("model.layer.0.weight", DeviceTensor::FromHost({1, 2, 3, 4, 5, 6, 7, 8}, {8}));
+                     st.NamedWeights.emplace_back("model.lm_head.weight", DeviceTensor::FromHost({100, 200, 300}, {3}));
+                     RtnModifier m(c, RtnConfig{8, true, QuantizationStrategy::PerTensor}, {"model.*"}, {"model.lm_head.*"});
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     m.OnEnd(st);
+                     m.Finalize(st);
+                     Assert(st.Weight("model.lm_head.weight").ToHost() == std::vector<float>({100, 200, 300}), "ignored");
+                     const auto q = st.Weight("model.layer.0.weight").ToHost();
+                     const float scale = 8.f / 127.f;  // Observer.cs:60-64, symmetric int8
+                     for (int i = 0; i < 8; i++) {
+                         const float want = std::nearbyint((float)(i + 1) / scale) * scale;
+                         Near(q[i], want, 1e-6f, "fake-quantised value " + std::to_string(i));
+                     }
+                 }});
+    t.push_back({"RtnModifier.PerTokenThrows", [](Context& c) {  // RtnModifier.cs:69-70
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("w", DeviceTensor::FromHost({1, 2}, {1, 2}));
+                     RtnModifier m(c, RtnConfig{8, true, QuantizationStrategy::PerToken});
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     Throws<NotSupportedException>([&] { m.OnEnd(st); }, "PerToken");
+                 }});
+    t.push_back({"GPTQModifier.RequiresNamedModules", [](Context& c) {  // GPTQModifierTests.cs:108-122
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("linear.weight", DeviceTensor::FromHost(std::vector<float>(12, 0.5f), {3, 4}));
+                     GPTQModifier m(c, GPTQConfig{});
+                     Assert(m.Name() == "GPTQ", "name");
+                     m.Initialize(st);
+                     Throws<InvalidOperationException>([&] { m.OnStart(st); }, "NamedModules");
+                 }});
+    t.push_back({"GPTQModifier.ActOrderThrows", [](Context& c) {  // GPTQModifierTests.cs:124-136
+                     CompressionState st;
+                     GPTQConfig cfg;
+                     cfg.ActOrder = true;
+                     GPTQModifier m(c, cfg);
+                     Throws<NotSupportedException>([&] { m.Initialize(st); }, "ActOrder");
+                 }});
+    t.push_back({"GPTQModifier.NoBatchesIsRtn", [](Context& c) {  // GPTQModifierTests.cs:89-106: H = 0
+                     const std::vector<float> w = {0.3f, -1.2f, 0.05f, 2.0f, -0.7f, 0.9f, 1.13f, -0.4f, 0.6f, -2.2f, 0.15f, 0.8f};
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("linear.weight", DeviceTensor::FromHost(w, {3, 4}));
+                     st.NamedModules = {"linear"};
+                     st.HasNamedModules = true;
+                     GPTQConfig cfg;
+                     cfg.NumBits = 8;
+                     cfg.Strategy = QuantizationStrategy::PerTensor;
+                     cfg.BlockSize = 4;
+                     GPTQModifier m(c, cfg);
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     m.OnEnd(st);
+                     m.Finalize(st);
+                     const auto got = st.Weight("linear.weight").ToHost();
+                     // pinv(0) = 0, U = Hinv = 0, every pivot skipped: the RTN fake-quantisation.
+                     const auto want = Rtn::Quantize(c, DeviceTensor::FromHost(w, {3, 4}), RtnConfig{8, true, QuantizationStrategy::PerTensor})
+                                           .Dequantized.ToHost();
+                     for (size_t i = 0; i < w.size(); i++) Near(got[i], want[i], 0.f, "RTN value " + std::to_string(i));
+                 }});
+    t.push_back({"GPTQModifier.ObservedLayerAt16BitIsClose", [](Context& c) {  // GPTQModifierTests.cs:58-87
+                     std::vector<float> w(12), x(24);
+                     for (int i = 0; i < 12; i++) w[i] = std::sin(0.7f * i + 0.3f);
+                     for (int i = 0; i < 24; i++) x[i] = std::cos(1.3f * i) + 0.1f * i;
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("linear.weight", DeviceTensor::FromHost(w, {3, 4}));
+                     st.NamedModules = {"linear"};
+                     st.HasNamedModules = true;
+                     GPTQConfig cfg;
+                     cfg.NumBits = 16;
+                     GPTQModifier m(c, cfg);
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     for (int b = 0; b < 3; b++) {
+                         m.Observe("linear", DeviceTensor::FromHost(std::vector<float>(x.begin() + 8 * b, x.begin() + 8 * b + 8), {2, 4}));
+                         m.OnBatch(st);
+                     }
+                     m.OnEnd(st);
+                     m.Finalize(st);
+                     const auto got = st.Weight("linear.weight").ToHost();
+                     for (int i = 0; i < 12; i++) Near(got[i], w[i], 1e-3f, "16-bit GPTQ value " + std::to_string(i));
+                 }});
+    t.push_back({"GPTQModifier.SingularHessianTakesPinv", [](Context& c) {  // HessianInverseSolver.cs:85-91
+                     std::vector<float> w(32), x(64 * 8);
+                     for (int i = 0; i < 32; i++) w[i] = 0.05f * std::sin(1.1f * i);
+                     for (int i = 0; i < 64 * 8; i++) x[i] = (i % 8 == 3) ? 0.f : std::sin(0.37f * i) + std::cos(0.11f * i * i);
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("fc.weight", DeviceTensor::FromHost(w, {4, 8}));
+                     st.NamedModules = {"fc"};
+                     st.HasNamedModules = true;
+                     GPTQConfig cfg;
+                     cfg.DampeningFrac = 0.f;  // no damping: the dead input channel 3 leaves H singular
+                     GPTQModifier m(c, cfg);
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     m.Observe("fc", DeviceTensor::FromHost(x, {64, 8}));
+                     m.OnEnd(st);
+                     m.Finalize(st);
+                     const auto got = st.Weight("fc.weight").ToHost();
+                     // The reference's composition: Hinv = pinv(H) (HessianInverseSolver.Compute), then
+                     // GptqBlockQuantizer.Quantize with its U = chol(Hinv)^T or U = Hinv.
+                     HessianAccumulator acc(c, 8);
+                     acc.Update(DeviceTensor::FromHost(x, {64, 8}));
+                     auto hinv = HessianInverseSolver::Compute(c, acc.GetHessian(), 0.f);
+                     const auto want = GptqBlockQuantizer::Quantize(c, DeviceTensor::FromHost(w, {4, 8}), hinv, cfg).ToHost();
+                     for (int i = 0; i < 32; i++) {
+                         Assert(std::isfinite(got[i]), "finite");
+                         Near(got[i], want[i], 1e-6f, "value " + std::to_string(i));
+                     }
+                 }});
     return t;
 }
 
