@@ -15,6 +15,7 @@
  *   TargetMatcher, ModifierBase, CompressionState (Core/Modifiers, Core/Compression)
  *   GPTQModifier              GPTQModifier.cs:28-155
  *   RtnModifier               RtnModifier.cs:44-122
+ *   SmoothQuantModifier       SmoothQuantModifier.cs:15-182
  * Tensors are DeviceTensor: a device buffer owned by the host code (the role TorchSharp's
  * CUDA tensors play for the C# primitives), row-major, float32 / bfloat16 / float16.
  * Exceptions mirror .NET's: ArgumentNullException, ArgumentException,
@@ -799,7 +800,16 @@ struct CompressionState {
     std::vector<std::pair<std::string, DeviceTensor>> NamedWeights;
     std::vector<std::string> NamedModules;
     bool HasNamedModules = false;
+    // CompressionState.LayerActivations: this batch's activations by key, owned by the host,
+    // which keeps them alive across the OnBatch / OnEnd call that reads them.
+    std::vector<std::pair<std::string, const DeviceTensor*>> LayerActivations;
+    bool HasLayerActivations = false;
 
+    const DeviceTensor* Activation(const std::string& key) const {
+        for (const auto& kv : LayerActivations)
+            if (kv.first == key) return kv.second;
+        return nullptr;
+    }
     DeviceTensor& Weight(const std::string& name) {
         for (auto& kv : NamedWeights)
             if (kv.first == name) return kv.second;
@@ -1000,6 +1010,90 @@ class RtnModifier : public ModifierBase {
    private:
     Context* ctx_;
     RtnConfig cfg_;
+};
+
+// SmoothQuantModifier.cs:15-182 with SmoothQuantConfig / SmoothQuantMapping
+// (Configs/SmoothQuantConfig.cs): per mapping, the running per-channel |x| max of the activation
+// key over the batches, then smooth /= s and balance *= s in the weights' dtypes.  The running
+// maxima stay on the device (llmc_act_absmax folds each batch in).
+struct SmoothQuantMapping {
+    std::string SmoothWeight, BalanceWeight, ActivationKey;
+};
+struct SmoothQuantConfig {
+    float SmoothingStrength = 0.5f;
+    std::vector<SmoothQuantMapping> Mappings;
+    std::vector<std::string> Targets, Ignore;
+};
+
+class SmoothQuantModifier : public ModifierBase {
+   public:
+    SmoothQuantModifier(Context& ctx, SmoothQuantConfig config)
+        : ModifierBase("SmoothQuant", config.Targets, config.Ignore), ctx_(&ctx), cfg_(std::move(config)) {
+        if (cfg_.SmoothingStrength < 0.f || cfg_.SmoothingStrength > 1.f)
+            throw ArgumentOutOfRangeException("SmoothingStrength (alpha) must be in [0, 1].");
+    }
+
+   protected:
+    void OnInitialize(CompressionState&) override { running_.clear(); }
+    void OnBatchCore(CompressionState& state) override {
+        if (!state.HasLayerActivations) return;
+        for (const auto& mp : cfg_.Mappings)
+            if (const DeviceTensor* x = state.Activation(mp.ActivationKey)) Update(mp.ActivationKey, *x);
+    }
+    void OnEndCore(CompressionState& state) override {
+        for (const auto& mp : cfg_.Mappings) Apply(state, mp);
+    }
+
+   private:
+    DeviceTensor* Running(const std::string& key) {
+        for (auto& kv : running_)
+            if (kv.first == key) return &kv.second;
+        return nullptr;
+    }
+    void Update(const std::string& key, const DeviceTensor& x) {
+        const int64_t cols = x.last();
+        DeviceTensor* r = Running(key);
+        const bool first = r == nullptr;
+        if (first) {
+            running_.emplace_back(key, DeviceTensor({cols}, DType::Float32));
+            r = &running_.back().second;
+        } else if (r->numel() != cols) {
+            throw InvalidOperationException("SmoothQuant: activation feature dim changed for '" + key + "': expected " +
+                                            std::to_string(r->numel()) + ", got " + std::to_string(cols) + ".");
+        }
+        SmoothQuant::UpdateActivationMax(*ctx_, x, *r, !first);
+    }
+    void Apply(CompressionState& state, const SmoothQuantMapping& mp) {
+        const DeviceTensor* x = state.HasLayerActivations ? state.Activation(mp.ActivationKey) : nullptr;
+        if (!x) {
+            if (!Running(mp.ActivationKey))
+                throw InvalidOperationException("SmoothQuant: no activation collected for '" + mp.ActivationKey +
+                                                "'. Populate CompressionState.LayerActivations.");
+        } else if (!Running(mp.ActivationKey)) {
+            Update(mp.ActivationKey, *x);
+        }
+        const DeviceTensor& actMax = *Running(mp.ActivationKey);
+        DeviceTensor& smooth = state.Weight(mp.SmoothWeight);
+        if (smooth.dim() != 1)
+            throw InvalidOperationException("SmoothQuant: smooth weight '" + mp.SmoothWeight + "' must be 1-D (got rank " +
+                                            std::to_string(smooth.dim()) + ").");
+        DeviceTensor& balance = state.Weight(mp.BalanceWeight);
+        if (balance.dim() != 2)
+            throw InvalidOperationException("SmoothQuant: balance weight '" + mp.BalanceWeight +
+                                            "' must be 2-D (got rank " + std::to_string(balance.dim()) + ").");
+        const int64_t hidden = smooth.shape()[0];
+        if (actMax.numel() != hidden)
+            throw InvalidOperationException("SmoothQuant: activation hidden dim " + std::to_string(actMax.numel()) +
+                                            " does not match smooth weight " + std::to_string(hidden) + ".");
+        if (balance.shape()[1] != hidden)
+            throw InvalidOperationException("SmoothQuant: balance weight last dim " + std::to_string(balance.shape()[1]) +
+                                            " does not match hidden " + std::to_string(hidden) + ".");
+        SmoothQuant::ApplyMapping(*ctx_, actMax, smooth, balance, cfg_.SmoothingStrength);
+    }
+
+    Context* ctx_;
+    SmoothQuantConfig cfg_;
+    std::vector<std::pair<std::string, DeviceTensor>> running_;
 };
 
 }  // namespace llmcs

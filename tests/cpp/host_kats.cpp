@@ -447,6 +447,77 @@ std::vector<std::pair<std::string, std::function<void(Context&)>>> tests() {
                          Near(got[i], want[i], 1e-6f, "value " + std::to_string(i));
                      }
                  }});
+    t.push_back({"SmoothQuantModifier.OutputPreservedAndScaled", [](Context& c) {  // SmoothQuantModifierTests.cs:26-76
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("norm.weight", DeviceTensor::FromHost({2, 4}, {2}));
+                     st.NamedWeights.emplace_back("proj.weight", DeviceTensor::FromHost({1, 1, 1, 1}, {2, 2}));
+                     const DeviceTensor act = DeviceTensor::FromHost({1, 4, -0.5f, -2}, {2, 2});
+                     st.LayerActivations = {{"proj", &act}};
+                     st.HasLayerActivations = true;
+                     SmoothQuantConfig cfg;
+                     cfg.SmoothingStrength = 0.5f;
+                     cfg.Mappings = {{"norm.weight", "proj.weight", "proj"}};
+                     SmoothQuantModifier m(c, cfg);
+                     Assert(m.Name() == "SmoothQuant", "name");
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     m.OnBatch(st);
+                     m.OnEnd(st);
+                     m.Finalize(st);
+                     const auto g = st.Weight("norm.weight").ToHost(), w = st.Weight("proj.weight").ToHost();
+                     Near(g[0], 2.f, 1e-4f, "g0");
+                     Near(g[1], 2.f, 1e-4f, "g1");
+                     Near(w[0], 1.f, 1e-4f, "w00");
+                     Near(w[1], 2.f, 1e-4f, "w01");
+                     Near(w[2], 1.f, 1e-4f, "w10");
+                     Near(w[3], 2.f, 1e-4f, "w11");
+                 }});
+    t.push_back({"SmoothQuantModifier.PreservesIdentity", [](Context& c) {  // SmoothQuantModifierTests.cs:78-123
+                     const std::vector<float> g = {1, 2, 3}, w = {0.5f, 1, -1, 2, -0.5f, 0.25f}, x = {0.1f, 0.5f, -1, 0.2f, -0.3f, 0.7f};
+                     std::vector<float> xg(6), yref(4, 0.f);
+                     for (int r = 0; r < 2; r++)
+                         for (int k = 0; k < 3; k++) xg[3 * r + k] = x[3 * r + k] * g[k];
+                     for (int r = 0; r < 2; r++)
+                         for (int o = 0; o < 2; o++)
+                             for (int k = 0; k < 3; k++) yref[2 * r + o] += xg[3 * r + k] * w[3 * o + k];
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("g.weight", DeviceTensor::FromHost(g, {3}));
+                     st.NamedWeights.emplace_back("proj.weight", DeviceTensor::FromHost(w, {2, 3}));
+                     const DeviceTensor act = DeviceTensor::FromHost(xg, {2, 3});
+                     st.LayerActivations = {{"proj", &act}};
+                     st.HasLayerActivations = true;
+                     SmoothQuantConfig cfg;
+                     cfg.Mappings = {{"g.weight", "proj.weight", "proj"}};
+                     SmoothQuantModifier m(c, cfg);
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     m.OnBatch(st);
+                     m.OnEnd(st);
+                     m.Finalize(st);
+                     const auto gn = st.Weight("g.weight").ToHost(), wn = st.Weight("proj.weight").ToHost();
+                     for (int r = 0; r < 2; r++)
+                         for (int o = 0; o < 2; o++) {
+                             float y = 0.f;
+                             for (int k = 0; k < 3; k++) y += x[3 * r + k] * gn[k] * wn[3 * o + k];
+                             Near(y, yref[2 * r + o], 1e-4f, "y");
+                         }
+                 }});
+    t.push_back({"SmoothQuantModifier.AlphaOutOfRangeThrows", [](Context& c) {  // SmoothQuantModifier.cs:25-31
+                     SmoothQuantConfig cfg;
+                     cfg.SmoothingStrength = 1.5f;
+                     Throws<ArgumentOutOfRangeException>([&] { SmoothQuantModifier m(c, cfg); }, "alpha");
+                 }});
+    t.push_back({"SmoothQuantModifier.NoActivationThrows", [](Context& c) {  // SmoothQuantModifier.cs:118-127
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("norm.weight", DeviceTensor::FromHost({2, 4}, {2}));
+                     st.NamedWeights.emplace_back("proj.weight", DeviceTensor::FromHost({1, 1, 1, 1}, {2, 2}));
+                     SmoothQuantConfig cfg;
+                     cfg.Mappings = {{"norm.weight", "proj.weight", "proj"}};
+                     SmoothQuantModifier m(c, cfg);
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     Throws<InvalidOperationException>([&] { m.OnEnd(st); }, "no activation");
+                 }});
     return t;
 }
 
