@@ -16,6 +16,8 @@
  *   GPTQModifier              GPTQModifier.cs:28-155
  *   RtnModifier               RtnModifier.cs:44-122
  *   SmoothQuantModifier       SmoothQuantModifier.cs:15-182
+ *   SparseGPTModifier, AWQModifier (the reference's plans: phase-4c-sparsegpt.md,
+ *                             algorithm-mapping.md:214-249)
  * Tensors are DeviceTensor: a device buffer owned by the host code (the role TorchSharp's
  * CUDA tensors play for the C# primitives), row-major, float32 / bfloat16 / float16.
  * Exceptions mirror .NET's: ArgumentNullException, ArgumentException,
@@ -1093,6 +1095,127 @@ class SmoothQuantModifier : public ModifierBase {
 
     Context* ctx_;
     SmoothQuantConfig cfg_;
+    std::vector<std::pair<std::string, DeviceTensor>> running_;
+};
+
+// SparseGPT as a recipe type (the plan, phase-4c-sparsegpt.md:1559-1567,1652-1655): calibration
+// as GPTQModifier; OnEnd prunes each observed weight against its site's U and writes it back in
+// its own dtype (a weight with no calibration rows stays as it is).
+struct SparseGPTConfig {
+    float Sparsity = 0.5f;
+    int MaskN = 0, MaskM = 0;  // 0:0 unstructured; 2:4 for the N:M structure
+    int BlockSize = 128;
+    float DampeningFrac = 0.01f;
+    std::vector<std::string> Targets, Ignore;
+};
+
+class SparseGPTModifier : public ModifierBase {
+   public:
+    SparseGPTModifier(Context& ctx, SparseGPTConfig config)
+        : ModifierBase("SparseGPT", config.Targets, config.Ignore), ctx_(&ctx), cfg_(std::move(config)) {}
+
+    void Observe(const std::string& layerName, const DeviceTensor& x) {
+        for (auto& a : acc_)
+            if (a.first == layerName + ".weight" || a.first == layerName) a.second->Update(x);
+    }
+
+   protected:
+    void OnStartCore(CompressionState& state) override {
+        if (!state.HasNamedModules)
+            throw InvalidOperationException("SparseGPTModifier requires CompressionState.NamedModules to be populated.");
+        acc_.clear();
+        for (const auto& name : TargetedNames(state)) {
+            const std::string suffix = ".weight";
+            const bool has = name.size() >= suffix.size() && name.compare(name.size() - suffix.size(), suffix.size(), suffix) == 0;
+            const std::string layer = has ? name.substr(0, name.size() - suffix.size()) : name;
+            if (!state.HasModule(layer)) continue;
+            acc_.emplace_back(name, std::make_unique<HessianAccumulator>(*ctx_, (int)state.Weight(name).last()));
+        }
+    }
+    void OnEndCore(CompressionState& state) override {
+        for (auto& a : acc_) {
+            if (a.second->SampleCount() == 0) continue;
+            const int64_t d = a.second->InFeatures();
+            DeviceTensor u({d, d}, DType::Float32);
+            Check(llmc_chol_inverse(ctx_->get(), a.second->Data(), d, d, cfg_.DampeningFrac, 1,
+                                    static_cast<float*>(u.data()), d, 1));
+            DeviceTensor& w = state.Weight(a.first);
+            SparseGPTResult r = SparseGPT::Prune(*ctx_, w, u, cfg_.Sparsity, cfg_.MaskN, cfg_.MaskM, cfg_.BlockSize);
+            if (w.dtype() == DType::Float32) {
+                w = std::move(r.Pruned);
+            } else {  // round to the weight's dtype (nearest even), as the plan's .to(dtype)
+                w = DeviceTensor::FromHost(r.Pruned.ToHost(), w.shape(), w.dtype());
+            }
+        }
+    }
+    void OnFinalizeCore(CompressionState&) override { acc_.clear(); }
+
+   private:
+    Context* ctx_;
+    SparseGPTConfig cfg_;
+    std::vector<std::pair<std::string, std::unique_ptr<HessianAccumulator>>> acc_;
+};
+
+// AWQ as a recipe type (algorithm-mapping.md:214-249): per mapping, the running activation
+// |x| max (as SmoothQuantModifier), then at OnEnd the grid search on the balance weight and the
+// chosen scale applied (smooth /= s when a smooth weight is named, balance *= s).
+struct AWQConfig {
+    RtnConfig Quant{4, false, QuantizationStrategy::Group, 128};
+    int NGrid = 20;
+    std::vector<SmoothQuantMapping> Mappings;
+    std::vector<std::string> Targets, Ignore;
+};
+
+class AWQModifier : public ModifierBase {
+   public:
+    AWQModifier(Context& ctx, AWQConfig config)
+        : ModifierBase("AWQ", config.Targets, config.Ignore), ctx_(&ctx), cfg_(std::move(config)) {}
+    // The grid point (1-based) chosen for each balance weight.
+    std::vector<std::pair<std::string, int>> Chosen;
+
+   protected:
+    void OnInitialize(CompressionState&) override {
+        running_.clear();
+        Chosen.clear();
+    }
+    void OnBatchCore(CompressionState& state) override {
+        if (!state.HasLayerActivations) return;
+        for (const auto& mp : cfg_.Mappings)
+            if (const DeviceTensor* x = state.Activation(mp.ActivationKey)) Update(mp.ActivationKey, *x);
+    }
+    void OnEndCore(CompressionState& state) override {
+        for (const auto& mp : cfg_.Mappings) {
+            if (!Running(mp.ActivationKey)) {
+                const DeviceTensor* x = state.HasLayerActivations ? state.Activation(mp.ActivationKey) : nullptr;
+                if (!x) throw InvalidOperationException("AWQ: no activation collected for '" + mp.ActivationKey + "'.");
+                Update(mp.ActivationKey, *x);
+            }
+            DeviceTensor& balance = state.Weight(mp.BalanceWeight);
+            const AwqResult r = AWQ::Search(*ctx_, balance, *Running(mp.ActivationKey), cfg_.NGrid, cfg_.Quant);
+            Chosen.emplace_back(mp.BalanceWeight, r.BestK);
+            const DeviceTensor s = DeviceTensor::FromHost(r.BestScale, {(int64_t)r.BestScale.size()});
+            ScaleApply::Apply(*ctx_, s, mp.SmoothWeight.empty() ? nullptr : &state.Weight(mp.SmoothWeight), balance);
+        }
+    }
+
+   private:
+    DeviceTensor* Running(const std::string& key) {
+        for (auto& kv : running_)
+            if (kv.first == key) return &kv.second;
+        return nullptr;
+    }
+    void Update(const std::string& key, const DeviceTensor& x) {
+        DeviceTensor* r = Running(key);
+        const bool first = r == nullptr;
+        if (first) {
+            running_.emplace_back(key, DeviceTensor({x.last()}, DType::Float32));
+            r = &running_.back().second;
+        }
+        SmoothQuant::UpdateActivationMax(*ctx_, x, *r, !first);
+    }
+
+    Context* ctx_;
+    AWQConfig cfg_;
     std::vector<std::pair<std::string, DeviceTensor>> running_;
 };
 

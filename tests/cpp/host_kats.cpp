@@ -518,6 +518,68 @@ std::vector<std::pair<std::string, std::function<void(Context&)>>> tests() {
                      m.OnStart(st);
                      Throws<InvalidOperationException>([&] { m.OnEnd(st); }, "no activation");
                  }});
+    t.push_back({"SparseGPTModifier.TwoFourMask", [](Context& c) {  // phase-4c-sparsegpt.md:1584-1656 (2:4)
+                     std::vector<float> w(32), x(64 * 8);
+                     for (int i = 0; i < 32; i++) w[i] = 0.05f * std::sin(1.7f * i + 0.2f);
+                     for (int i = 0; i < 64 * 8; i++) x[i] = std::sin(0.37f * i) + std::cos(0.11f * i * i);
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("fc.weight", DeviceTensor::FromHost(w, {4, 8}, DType::BFloat16));
+                     st.NamedWeights.emplace_back("other.weight", DeviceTensor::FromHost(w, {4, 8}));
+                     st.NamedModules = {"fc", "other"};
+                     st.HasNamedModules = true;
+                     SparseGPTConfig cfg;
+                     cfg.MaskN = 2;
+                     cfg.MaskM = 4;
+                     SparseGPTModifier m(c, cfg);
+                     Assert(m.Name() == "SparseGPT", "name");
+                     m.Initialize(st);
+                     m.OnStart(st);
+                     m.Observe("fc", DeviceTensor::FromHost(x, {64, 8}));  // "other" sees no calibration rows
+                     m.OnEnd(st);
+                     m.Finalize(st);
+                     Assert(st.Weight("fc.weight").dtype() == DType::BFloat16, "dtype kept");
+                     const auto p = st.Weight("fc.weight").ToHost();
+                     for (int r = 0; r < 4; r++)
+                         for (int g = 0; g < 2; g++) {
+                             int zeros = 0;
+                             for (int k = 0; k < 4; k++) zeros += p[8 * r + 4 * g + k] == 0.f;
+                             Assert(zeros >= 2, "2:4 group " + std::to_string(r) + "," + std::to_string(g));
+                         }
+                     Assert(st.Weight("other.weight").ToHost() == w, "no calibration rows: unchanged");
+                 }});
+    t.push_back({"AWQModifier.SearchesAndApplies", [](Context& c) {  // algorithm-mapping.md:214-249
+                     const int n = 128, m = 4, rows = 16;
+                     std::vector<float> w(m * n), g(n), x(rows * n);
+                     for (int i = 0; i < m * n; i++) w[i] = 0.02f * std::sin(0.9f * i + 0.1f);
+                     for (int i = 0; i < n; i++) g[i] = 1.f + 0.1f * std::cos(0.5f * i);
+                     for (int i = 0; i < rows * n; i++) x[i] = std::sin(0.23f * i) * ((i % n) % 17 == 0 ? 20.f : 1.f);
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("norm.weight", DeviceTensor::FromHost(g, {n}));
+                     st.NamedWeights.emplace_back("proj.weight", DeviceTensor::FromHost(w, {m, n}));
+                     const DeviceTensor act = DeviceTensor::FromHost(x, {rows, n});
+                     st.LayerActivations = {{"proj", &act}};
+                     st.HasLayerActivations = true;
+                     AWQConfig cfg;
+                     cfg.Mappings = {{"norm.weight", "proj.weight", "proj"}};
+                     AWQModifier mod(c, cfg);
+                     mod.Initialize(st);
+                     mod.OnStart(st);
+                     mod.OnBatch(st);
+                     mod.OnEnd(st);
+                     mod.Finalize(st);
+                     Assert(mod.Chosen.size() == 1 && mod.Chosen[0].first == "proj.weight", "one mapping");
+                     DeviceTensor amax({n}, DType::Float32);
+                     SmoothQuant::UpdateActivationMax(c, act, amax, false);
+                     const AwqResult want = AWQ::Search(c, DeviceTensor::FromHost(w, {m, n}), amax, 20, cfg.Quant);
+                     Assert(mod.Chosen[0].second == want.BestK && want.BestK >= 1 && want.BestK <= 20, "grid point");
+                     const auto gn = st.Weight("norm.weight").ToHost(), wn = st.Weight("proj.weight").ToHost();
+                     for (int i = 0; i < n; i++) {
+                         Near(gn[i], g[i] / want.BestScale[i], 1e-6f * std::fabs(g[i] / want.BestScale[i]) + 1e-30f, "smooth / s");
+                         for (int r = 0; r < m; r++)
+                             Near(wn[r * n + i], w[r * n + i] * want.BestScale[i],
+                                  1e-6f * std::fabs(w[r * n + i] * want.BestScale[i]) + 1e-30f, "balance * s");
+                     }
+                 }});
     return t;
 }
 
