@@ -18,6 +18,7 @@
  *   SmoothQuantModifier       SmoothQuantModifier.cs:15-182
  *   SparseGPTModifier, AWQModifier (the reference's plans: phase-4c-sparsegpt.md,
  *                             algorithm-mapping.md:214-249)
+ *   CompressionSession        CompressionSession.cs
  * Tensors are DeviceTensor: a device buffer owned by the host code (the role TorchSharp's
  * CUDA tensors play for the C# primitives), row-major, float32 / bfloat16 / float16.
  * Exceptions mirror .NET's: ArgumentNullException, ArgumentException,
@@ -33,6 +34,8 @@
 
 #include <cstdint>
 #include <cstring>
+#include <exception>
+#include <functional>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -1217,6 +1220,59 @@ class AWQModifier : public ModifierBase {
     Context* ctx_;
     AWQConfig cfg_;
     std::vector<std::pair<std::string, DeviceTensor>> running_;
+};
+
+// CompressionSession.cs: every modifier initialised and started, each calibration batch handed to
+// every modifier's OnBatch, then OnEnd; any exception ends the run as Failed (kept in Failure)
+// and the initialised modifiers are finalised either way.  A C++ host has no tensor batches for
+// the session to pass through: `forward(state, index)` runs its own forward for batch `index`
+// (feeding GPTQModifier::Observe or state.LayerActivations) before the OnBatch calls.
+enum class SessionStatus { NotStarted, Running, Completed, Failed };
+
+class CompressionSession {
+   public:
+    explicit CompressionSession(std::vector<ModifierBase*> modifiers) : modifiers_(std::move(modifiers)) {
+        for (auto* m : modifiers_)
+            if (!m) throw ArgumentNullException("modifiers must not be null");
+    }
+    SessionStatus Status() const { return status_; }
+    std::exception_ptr Failure() const { return failure_; }
+
+    SessionStatus Run(CompressionState& state, int batches, const std::function<void(CompressionState&, int)>& forward) {
+        if (status_ != SessionStatus::NotStarted)
+            throw InvalidOperationException("CompressionSession.Run may only be called once.");
+        status_ = SessionStatus::Running;
+        std::vector<ModifierBase*> initialized;
+        try {
+            for (auto* m : modifiers_) {
+                m->Initialize(state);
+                initialized.push_back(m);
+            }
+            for (auto* m : modifiers_) m->OnStart(state);
+            for (int i = 0; i < batches; i++) {
+                if (forward) forward(state, i);
+                for (auto* m : modifiers_) m->OnBatch(state);
+            }
+            for (auto* m : modifiers_) m->OnEnd(state);
+            status_ = SessionStatus::Completed;
+        } catch (...) {
+            status_ = SessionStatus::Failed;
+            failure_ = std::current_exception();
+        }
+        for (auto* m : initialized) {
+            try {
+                m->Finalize(state);
+            } catch (...) {
+                if (status_ != SessionStatus::Failed) throw;  // kept: the run's own failure wins
+            }
+        }
+        return status_;
+    }
+
+   private:
+    std::vector<ModifierBase*> modifiers_;
+    SessionStatus status_ = SessionStatus::NotStarted;
+    std::exception_ptr failure_;
 };
 
 }  // namespace llmcs

@@ -580,6 +580,42 @@ std::vector<std::pair<std::string, std::function<void(Context&)>>> tests() {
                                   1e-6f * std::fabs(w[r * n + i] * want.BestScale[i]) + 1e-30f, "balance * s");
                      }
                  }});
+    t.push_back({"CompressionSession.CompletesFailsAndRunsOnce", [](Context& c) {  // CompressionSession.cs
+                     // GPTQ over two batches fed by the host's forward, then RTN of the other weight.
+                     std::vector<float> w(12);
+                     for (int i = 0; i < 12; i++) w[i] = std::sin(0.7f * i + 0.3f);
+                     CompressionState st;
+                     st.NamedWeights.emplace_back("linear.weight", DeviceTensor::FromHost(w, {3, 4}));
+                     st.NamedWeights.emplace_back("head.weight", DeviceTensor::FromHost({1, 2, 3, 4, 5, 6, 7, 8}, {8}));
+                     st.NamedModules = {"linear"};
+                     st.HasNamedModules = true;
+                     GPTQConfig gc;
+                     gc.NumBits = 16;
+                     GPTQModifier gptq(c, gc, {"linear.*"});
+                     RtnModifier rtn(c, RtnConfig{8, true, QuantizationStrategy::PerTensor}, {"head.*"});
+                     CompressionSession session({&gptq, &rtn});
+                     int fed = 0;
+                     const auto status = session.Run(st, 2, [&](CompressionState&, int b) {
+                         std::vector<float> x(8);
+                         for (int i = 0; i < 8; i++) x[i] = std::cos(1.3f * (i + 8 * b)) + 0.1f * i;
+                         gptq.Observe("linear", DeviceTensor::FromHost(x, {2, 4}));
+                         fed++;
+                     });
+                     Assert(status == SessionStatus::Completed && fed == 2, "completed");
+                     const auto q = st.Weight("linear.weight").ToHost();
+                     for (int i = 0; i < 12; i++) Near(q[i], w[i], 1e-3f, "16-bit GPTQ");
+                     const auto h = st.Weight("head.weight").ToHost();
+                     const float scale = 8.f / 127.f;
+                     for (int i = 0; i < 8; i++) Near(h[i], std::nearbyint((float)(i + 1) / scale) * scale, 1e-6f, "RTN");
+                     Throws<InvalidOperationException>([&] { session.Run(st, 0, nullptr); }, "run once");
+                     // A modifier that throws: the session fails, keeps the exception, finalises.
+                     CompressionState bad;
+                     bad.NamedWeights.emplace_back("linear.weight", DeviceTensor::FromHost(w, {3, 4}));
+                     GPTQModifier needsModules(c, GPTQConfig{});
+                     CompressionSession s2({&needsModules});
+                     Assert(s2.Run(bad, 1, nullptr) == SessionStatus::Failed, "failed");
+                     Throws<InvalidOperationException>([&] { std::rethrow_exception(s2.Failure()); }, "failure kept");
+                 }});
     return t;
 }
 
