@@ -1,6 +1,7 @@
 """The C++ host mirror (include/llmc_b200.hpp): it compiles and links against the library
-here (no GPU needed), and its known-answer test program (tests/cpp/host_kats.cpp) passes on
-the GPU."""
+here (no GPU needed), its host logic (tests/cpp/host_logic.cpp: target matching, the modifier
+lifecycle, the session, the status mapping) passes on the CPU, and its known-answer test program
+(tests/cpp/host_kats.cpp) passes on the GPU."""
 
 import os
 import shutil
@@ -12,16 +13,16 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 
-def _build(out_dir) -> str:
+def _build(out_dir, name: str = "host_kats") -> str:
     from llmcompressorsharp_b200 import build
 
     lib = build.build()
     gxx = shutil.which("g++")
     if gxx is None:
         pytest.skip("g++ not available")
-    exe = os.path.join(str(out_dir), "host_kats")
+    exe = os.path.join(str(out_dir), name)
     cmd = [gxx, "-std=c++17", "-O1", "-Wall", "-I", os.path.join(ROOT, "include"), "-I", os.path.join(CUDA, "include"),
-           os.path.join(ROOT, "tests", "cpp", "host_kats.cpp"), "-o", exe, "-L", os.path.dirname(lib), "-lllmc_b200",
+           os.path.join(ROOT, "tests", "cpp", name + ".cpp"), "-o", exe, "-L", os.path.dirname(lib), "-lllmc_b200",
            "-L", os.path.join(CUDA, "lib64"), "-lcudart", "-Wl,-rpath," + os.path.dirname(lib),
            "-Wl,-rpath," + os.path.join(CUDA, "lib64")]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -32,6 +33,13 @@ def _build(out_dir) -> str:
 def test_cpp_host_mirror_compiles_and_links(tmp_path):
     exe = _build(tmp_path)
     assert os.path.exists(exe)
+
+
+def test_cpp_host_logic(tmp_path):
+    exe = _build(tmp_path, "host_logic")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    assert " 0 failed" in r.stdout
 
 
 @pytest.mark.gpu
