@@ -131,15 +131,21 @@ def upper_factor(hinv: torch.Tensor) -> torch.Tensor:
 
 
 class ForwardHookHandle:
-    """ForwardHookHandle.cs:14-33 — disposing removes the hook (idempotent)."""
+    """ForwardHookHandle.cs:14-33 — disposing removes the hook (idempotent).  ``remover`` is the
+    removal action: a callable, or torch's hook handle (its ``remove``)."""
 
     def __init__(self, remover):
+        if remover is None:
+            raise ArgumentError("remove action must not be null")
         self._remover = remover
 
     def dispose(self):
         if self._remover is not None:
-            self._remover.remove()
-            self._remover = None
+            r, self._remover = self._remover, None
+            if callable(r):
+                r()
+            else:
+                r.remove()
 
 
 class ActivationHookManager:

@@ -88,7 +88,7 @@ def test_rtn_config_rejects_token():
         RtnConfig(strategy="token").to_c()
 
 
-def test_gptq_config_defaults():  # GPTQConfig.cs:22-59
+def test_gptq_config_defaults():  # GPTQConfig.cs:22-59, GPTQConfigTests.cs:16-56
     from llmcompressorsharp_b200.gptq import GPTQConfig
 
     c = GPTQConfig()
@@ -125,3 +125,59 @@ def test_site_order_widest_first_and_stable():
     wide = llama_sites(8192, 4096, 64, 8)  # intermediate narrower than hidden
     assert [s.name for s in GptqPipeline.site_order(SimpleNamespace(sites=wide))] == ["attn_in", "o_in", "mlp_in",
                                                                                         "down_in"]
+
+
+class _CountingAccumulator:
+    """Stands in for HessianAccumulator (which needs the GPU) where only the hook path is tested."""
+
+    def __init__(self, in_features):
+        self.in_features = in_features
+        self.sample_count = 0
+
+    def update(self, x):
+        assert x.shape[-1] == self.in_features
+        self.sample_count += x.numel() // self.in_features
+
+
+def test_activation_hooks():  # ActivationHookManagerTests.cs:22-117
+    from llmcompressorsharp_b200.errors import ArgumentError
+    from llmcompressorsharp_b200.hessian import ActivationHookManager
+
+    lin = torch.nn.Linear(4, 2)
+    acc = _CountingAccumulator(4)
+    mgr = ActivationHookManager()
+    mgr.register_for(lin, acc)
+    lin(torch.tensor([[1.0, 2.0, 3.0, 4.0]]))
+    assert acc.sample_count == 1  # :22-36
+    l1, l2 = torch.nn.Linear(3, 4), torch.nn.Linear(4, 2)
+    a1, a2 = _CountingAccumulator(3), _CountingAccumulator(4)
+    mgr.register_for(l1, a1)
+    mgr.register_for(l2, a2)
+    l2(l1(torch.tensor([[1.0, 2.0, 3.0]])))
+    assert (a1.sample_count, a2.sample_count) == (1, 1)  # :38-56
+    mgr.clear()  # :78-99: cleared hooks stop, re-registration works
+    lin(torch.ones(1, 4))
+    assert acc.sample_count == 1
+    mgr.register_for(lin, acc)
+    lin(torch.ones(1, 4))
+    assert acc.sample_count == 2
+    mgr.dispose()  # :58-76
+    lin(torch.ones(1, 4))
+    assert acc.sample_count == 2
+    with pytest.raises(ArgumentError):  # :101-117
+        ActivationHookManager().register_for(None, acc)
+    with pytest.raises(ArgumentError):
+        ActivationHookManager().register_for(lin, None)
+
+
+def test_forward_hook_handle():  # ForwardHookHandleTests.cs:14-40
+    from llmcompressorsharp_b200.errors import ArgumentError
+    from llmcompressorsharp_b200.hessian import ForwardHookHandle
+
+    calls = []
+    h = ForwardHookHandle(lambda: calls.append(1))
+    h.dispose()
+    h.dispose()
+    assert calls == [1]
+    with pytest.raises(ArgumentError):
+        ForwardHookHandle(None)
