@@ -34,9 +34,16 @@ def test_safetensors_round_trip(tmp_path):
         assert torch.equal(lib[k], ts[k]), k
 
 
-def test_safetensors_writer_mirrors_reference(tmp_path):
+def test_safetensors_writer_mirrors_reference(tmp_path):  # SafetensorsWriterTests.cs (all three cases)
     from llmcompressorsharp_b200.errors import ArgumentError
 
+    kat = CompressionState({"a.weight": torch.tensor([-1.0, 0.0, 1.0, 2.0]), "b.weight": torch.tensor([[1.0, 2.0], [3.0, 4.0]])})
+    pk = str(tmp_path / "kat.safetensors")
+    SafetensorsWriter.save(kat, pk)
+    assert os.path.getsize(pk) > 0
+    back = SafetensorsWriter.load(pk)
+    assert back["a.weight"].tolist() == [-1.0, 0.0, 1.0, 2.0] and list(back["a.weight"].shape) == [4]
+    assert list(back["b.weight"].shape) == [2, 2]
     state = CompressionState({"model.layers.0.mlp.down_proj.weight": torch.ones(2, 3)})
     p = str(tmp_path / "m.safetensors")
     SafetensorsWriter.save(state, p)
