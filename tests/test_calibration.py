@@ -119,3 +119,56 @@ def test_forward_matches_the_transformers_llama():
         a = ours(ids)
         b = hf(input_ids=ids).last_hidden_state
     assert torch.allclose(a, b, atol=1e-5, rtol=1e-5), float((a - b).abs().max())
+
+
+# --- structural tests of the reference's model classes (Llama*Tests.cs), on this calibration model
+def _tiny():
+    from llmcompressorsharp_b200.calibration import LlamaShape
+
+    return LlamaShape(hidden=16, intermediate=24, heads=4, kv_heads=2, layers=2, vocab=50)
+
+
+def test_rmsnorm_kats():  # LlamaRMSNormTests.cs:17-56
+    from llmcompressorsharp_b200.calibration import RMSNorm
+
+    n = RMSNorm(8, 1e-6, torch.float32, "cpu")
+    x = torch.randn(2, 4, 8, generator=torch.Generator().manual_seed(3))
+    y = n(x)
+    assert list(y.shape) == [2, 4, 8]
+    assert abs(float(y.pow(2).mean(-1).mean()) - 1.0) < 1e-3  # unit weight -> unit RMS rows
+    assert float(n(torch.zeros(1, 8)).abs().max()) < 1e-5
+    assert [list(p.shape) for p in n.parameters()] == [[8]]
+
+
+def test_rotary_kats():  # LlamaRotaryEmbeddingTests.cs:17-70
+    from llmcompressorsharp_b200.calibration import LlamaForCalibration, _rope
+
+    m = LlamaForCalibration(_tiny(), dtype=torch.float32)
+    cos, sin = m.rope_tables(4, torch.float32)
+    q = torch.randn(1, 2, 4, 4, generator=torch.Generator().manual_seed(4))
+    r = _rope(q, cos, sin)
+    assert list(r.shape) == [1, 2, 4, 4]
+    # each (i, i + half) pair is rotated, so its magnitude is kept
+    half = q.shape[-1] // 2
+    mag = lambda t: t[..., :half].pow(2) + t[..., half:].pow(2)  # noqa: E731
+    assert torch.allclose(mag(r), mag(q), atol=1e-3)
+    assert float((r[:, :, 0] - q[:, :, 0]).abs().max()) < 1e-5  # position 0 is the identity
+
+
+def test_model_submodules_kats():  # LlamaMLPTests.cs, LlamaAttentionTests.cs, LlamaDecoderLayerTests.cs
+    from llmcompressorsharp_b200.calibration import LlamaForCalibration
+
+    m = LlamaForCalibration(_tiny(), dtype=torch.float32)
+    layer = m.model.layers[0]
+    mlp = {n for n, _ in layer.mlp.named_parameters()}
+    assert mlp == {"gate_proj.weight", "up_proj.weight", "down_proj.weight"}  # three Linear layers, no bias
+    attn = {n for n, _ in layer.self_attn.named_parameters()}
+    assert attn == {"q_proj.weight", "k_proj.weight", "v_proj.weight", "o_proj.weight"}
+    names = {n for n, _ in layer.named_children()}
+    assert {"input_layernorm", "self_attn", "post_attention_layernorm", "mlp"} <= names
+    top = {n for n, _ in m.model.named_children()}
+    assert {"embed_tokens", "layers", "norm"} <= top  # no lm_head: calibration stops at the decoder
+    cos, sin = m.rope_tables(5, torch.float32)
+    x = torch.randn(2, 5, 16, generator=torch.Generator().manual_seed(5))
+    y = layer(x, cos, sin)
+    assert list(y.shape) == [2, 5, 16] and float((y - x).abs().max()) > 1e-5  # residual adds something
