@@ -130,6 +130,31 @@ std::vector<std::pair<std::string, std::function<void()>>> tests() {
                      }
                      Check(LLMC_OK);
                  }});
+    t.push_back({"Configs.DefaultsAndCLayout", [] {  // GPTQConfig.cs:22-59, GPTQConfigTests.cs:16-56
+                     GPTQConfig g;
+                     Assert(g.NumBits == 4 && g.Symmetric && g.Strategy == QuantizationStrategy::PerChannel &&
+                                g.ChannelAxis == 0 && g.BlockSize == 128 && !g.ActOrder,
+                            "GPTQ defaults");
+                     Assert(g.DampeningFrac > 0.0099f && g.DampeningFrac < 0.0101f, "damp 0.01");
+                     g.NumBits = 99;  // no validation in the config itself
+                     g.BlockSize = 64;
+                     g.Strategy = QuantizationStrategy::Group;
+                     g.GroupSize = 32;
+                     const llmc_qconfig c = g.ToC();
+                     Assert(c.num_bits == 99 && c.block_size == 64 && c.strategy == LLMC_STRATEGY_GROUP && c.group_size == 32 &&
+                                c.symmetric == 1 && c.act_order == 0,
+                            "GPTQ to C");
+                     const llmc_qconfig r = RtnConfig{8, false, QuantizationStrategy::PerTensor, 128}.ToC();
+                     Assert(r.num_bits == 8 && r.symmetric == 0 && r.strategy == LLMC_STRATEGY_TENSOR, "RTN to C");
+                     SmoothQuantConfig sq;
+                     Assert(sq.SmoothingStrength == 0.5f && sq.Mappings.empty(), "SmoothQuant defaults");
+                     AWQConfig aw;
+                     Assert(aw.NGrid == 20 && aw.Quant.NumBits == 4 && !aw.Quant.Symmetric &&
+                                aw.Quant.Strategy == QuantizationStrategy::Group && aw.Quant.GroupSize == 128,
+                            "AWQ defaults");
+                     SparseGPTConfig sp;
+                     Assert(sp.Sparsity == 0.5f && sp.MaskN == 0 && sp.MaskM == 0 && sp.BlockSize == 128, "SparseGPT defaults");
+                 }});
     return t;
 }
 
