@@ -1146,7 +1146,7 @@ class SparseGPTModifier : public ModifierBase {
             SparseGPTResult r = SparseGPT::Prune(*ctx_, w, u, cfg_.Sparsity, cfg_.MaskN, cfg_.MaskM, cfg_.BlockSize);
             if (w.dtype() == DType::Float32) {
                 w = std::move(r.Pruned);
-            } else {  // round to the weight's dtype (nearest even), as the plan's .to(dtype)
+            } else {  // round to the weight's dtype (nearest even, one host round trip), as the plan's .to(dtype)
                 w = DeviceTensor::FromHost(r.Pruned.ToHost(), w.shape(), w.dtype());
             }
         }
